@@ -1,0 +1,335 @@
+"""Decode benchmark (BASELINE.json metric: decode tokens/s and % of the HBM roofline).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--layers L] ...
+
+Default workload: BASELINE config 1, the full 36-layer Qwen3-4B architecture (seeded random-init
+BF16 weights, tied embeddings), batch 1, a 128-token uniform-random prompt, greedy decode. A "step"
+is one decode step (one token per sequence) through the captured CUDA graph of the engine's
+hand-written kernels. The timed region holds exactly K steps bracketed by barrier + synchronize,
+measured with CUDA events on the launching stream; each step streams ~8 GB of weights, far more
+than the 126 MB L2, so no flush is needed between steps.
+
+With --gpus N > 1 (one process per GPU under torchrun) every rank runs its own replica of the
+workload (batch-sharded, no collective on the hot path); value = tokens of all ranks / max-over-ranks
+time.
+
+--impl reference times the reference's own CPU implementation of the path on the host cores: the
+plain Transformers greedy loop (the reference's tier 0, engine/engine.py:963-972, restated in
+oracle/native.py over this image's transformers) on the same model and prompt.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+sys.path.insert(0, os.path.join(REPO, "htn-2026_b200"))
+
+METRIC = "decode tokens/s (bs1 latency ms/token; bs64 aggregate) and % of HBM roofline"
+
+
+def _args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--layers", type=int, default=36)
+    p.add_argument("--batch", type=int, default=1, help="sequences per GPU")
+    p.add_argument("--prompt", type=int, default=128)
+    p.add_argument("--new", type=int, default=256)
+    p.add_argument("--cpu-steps", type=int, default=16, help="decode steps in the CPU baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def _peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def weight_bytes(cfg) -> int:
+    H, I, V, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"], cfg["num_hidden_layers"]
+    nq, nkv, D = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"]
+    layer = 2 * ((nq + 2 * nkv) * D * H + H * nq * D + 2 * I * H + H * I) + 2 * (2 * H + 2 * D)
+    return L * layer + 2 * V * H + 2 * H
+
+
+def kv_bytes_per_token(cfg) -> int:
+    return cfg["num_hidden_layers"] * 2 * cfg["num_key_value_heads"] * cfg["head_dim"] * 2
+
+
+class Clocks:
+    """nvidia-smi sampler over the timed region (SM clock, throttle reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"qd_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def make_model(layers: int):
+    from decode_b200 import synth
+
+    cfg = synth.qwen3_config(layers)
+    return synth.make_state_dict(cfg, seed=0), cfg
+
+
+def cpu_reference(state, cfg, prompt, steps: int, threads: int | None = None):
+    """Time the reference's Transformers greedy loop (oracle.native) on the host cores."""
+    import torch
+
+    from oracle import native
+
+    threads = threads or os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    model = native.build_model(state, cfg)
+    t0 = time.perf_counter()
+    _, _, times = native.greedy(model, prompt, steps + 1, keep_logits=False)
+    total = time.perf_counter() - t0
+    dec = times[1:]
+    return {"value": len(prompt) * len(dec) / sum(dec), "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port", "ttft_s": times[0], "decode_ms_per_step": 1e3 * sum(dec) / len(dec),
+            "sample": f"Transformers CPU greedy decode (reference tier 0 restated), {cfg['num_hidden_layers']} layers, "
+                      f"batch {len(prompt)}, prompt {len(prompt[0])}, {len(dec)} decode steps after prefill "
+                      f"({total:.1f} s total)"}
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    state, cfg = make_model(a.layers)
+    from decode_b200 import synth
+
+    prompt = synth.random_prompt(a.batch, a.prompt, cfg["vocab_size"], seed=0)
+    steps = max(1, min(a.steps, a.cpu_steps))
+    r = cpu_reference(state, cfg, prompt, steps)
+    out = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": a.gpus,
+           "steps": steps, "warmup": 1, "ms_per_step": r["decode_ms_per_step"], "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights, "
+           "uniform-random prompt)",
+           "config": {"workload": f"BASELINE config 1 (Qwen3-4B arch, {a.layers} layers, batch {a.batch}, prompt "
+                                  f"{a.prompt}) on host CPU", "batch": a.batch, "prompt": a.prompt, "layers": a.layers},
+           "cpu_baseline": {"value": r["value"], "unit": "tokens/s", "cores": r["cores"], "kind": "port",
+                            "sample": r["sample"]},
+           "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def gu_kernel_roofline(eng, st, launches_per_layer=3):
+    """Average duration of the gate_up GEMV (the largest decode kernel, 99.6 MB of weights per launch)
+    measured with CUDA events on its launching stream, cycling through all layers' weights."""
+    import torch
+
+    L = eng.n_layers
+    stream = torch.cuda.current_stream()
+    for i in range(min(L, 4)):
+        st.gu(st.x, eng.w_gu[i], st.act, norm_w=eng.ln2[i], pdl=False)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 0
+    s.record(stream)
+    for _ in range(launches_per_layer):
+        for i in range(L):
+            st.gu(st.x, eng.w_gu[i], st.act, norm_w=eng.ln2[i], pdl=False)
+            n += 1
+    e.record(stream)
+    e.synchronize()
+    ms = s.elapsed_time(e) / n
+    nbytes = 2 * (2 * eng.inter) * eng.hidden + 2 * st.B * eng.hidden + 2 * st.B * eng.inter
+    return ms, nbytes
+
+
+def _traffic_from_profile():
+    path = os.path.join(REPO, "profiles", "gemv_gate_up_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+def run_ours(a):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device(f"cuda:{local}"))
+    import engine as E
+    from decode_b200 import synth
+
+    state, cfg = make_model(a.layers)
+    eng = E.Engine.from_state_dict(state, cfg, f"cuda:{local}")
+    B, S = a.batch, a.prompt
+    W, K = a.warmup, a.steps
+    N = max(a.new, W + K + 1)
+    prompt = synth.random_prompt(B, S, cfg["vocab_size"], seed=rank)
+    st = eng._build(B, S, N)
+
+    # ---------------- device-timed decode steps (graph replays)
+    with torch.inference_mode():
+        st.ids.copy_(torch.tensor(prompt, dtype=torch.int64))
+        st.pos.fill_(S)
+        st.prefill_graph.replay()
+        for _ in range(W):
+            st.decode_graph.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        stream = torch.cuda.current_stream()
+        t_s, t_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(local) as clk:
+            t_s.record(stream)
+            for _ in range(K):
+                st.decode_graph.replay()
+            t_e.record(stream)
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        eng.check_device_errors(st)
+    ms = t_s.elapsed_time(t_e)
+    ms_max = ms
+    if world > 1:
+        tt = torch.tensor([ms], device=f"cuda:{local}")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_max = float(tt.item())
+    ms_step = ms_max / K
+    value = world * B * K / (ms_max / 1e3)
+
+    # ---------------- end to end through the public API (host lists in, host lists out)
+    e2e = None
+    if not a.no_e2e:
+        n_e2e = a.new
+        list(eng.generate(prompt, n_e2e))  # untimed: builds and captures the (B, S, n_e2e) shape
+        stamps = []
+        t0 = time.perf_counter()
+        for _ in eng.generate(prompt, n_e2e):
+            stamps.append(time.perf_counter())
+        total = stamps[-1] - t0
+        dec = stamps[-1] - stamps[0]
+        e2e_val = B * (n_e2e - 1) / dec if n_e2e > 1 else 0.0
+        if world > 1:
+            tt = torch.tensor([e2e_val], device=f"cuda:{local}")
+            dist.all_reduce(tt, op=dist.ReduceOp.MIN)
+            e2e_val = float(tt.item()) * world
+        e2e = {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": round(B * S * 8 / n_e2e, 1),
+               "d2h_bytes_per_step": B * 8, "ttft_ms": 1e3 * (stamps[0] - t0),
+               "total_tokens_per_s_incl_prefill": world * B * n_e2e / total,
+               "note": "decode tokens/s between the first and last yield of Engine.generate (host prompt list in, "
+                       "host token lists out); the prompt upload is amortised over the steps in h2d_bytes_per_step"}
+
+    # ---------------- roofline of the dominant kernel (gate_up GEMV) and of the whole step
+    peak, peak_kind = _peaks()
+    gu_ms, gu_bytes = gu_kernel_roofline(eng, st)
+    achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+    prof = _traffic_from_profile()
+    roofline = {"bound": "hbm", "kernel": "qd gemv gate_up+SwiGLU (99.6 MB weights/launch)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "peak_kind": peak_kind, "avg_launch_us": round(gu_ms * 1e3, 2), "algorithmic_bytes": gu_bytes,
+                "traffic": (prof or {}).get("traffic_bytes_per_launch")}
+    L_avg = S + W + K / 2
+    step_bytes = weight_bytes(cfg) + B * kv_bytes_per_token(cfg) * (L_avg + 1)
+    step_gbs = step_bytes / (ms_step / 1e3) / 1e9
+
+    cpu = None
+    if rank == 0 and not a.no_cpu_baseline:
+        try:
+            cpu = cpu_reference(state, cfg, prompt, a.cpu_steps)
+        except Exception as exc:  # a baseline failure must not hide the GPU number
+            cpu = {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"failed: {repr(exc)[:200]}"}
+
+    if rank == 0:
+        out = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": K,
+               "warmup": W, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init BF16 weights, "
+               "uniform-random prompt ids)",
+               "config": {"workload": f"BASELINE config {'1' if (a.layers == 36 and B == 1) else 'custom'}: Qwen3-4B "
+                                      f"arch {a.layers} layers, batch {B}/GPU, prompt {S}, greedy decode steps",
+                          "batch_per_gpu": B, "global_batch": B * world, "prompt": S, "layers": a.layers,
+                          "parallelism": f"batch-sharded replicas x{world} (no collective)",
+                          "l2": "inputs larger than L2 (~8 GB of weights per step)"},
+               "roofline": roofline,
+               "step_roofline": {"bytes_per_step": step_bytes, "achieved": round(step_gbs, 1), "peak": peak,
+                                 "unit": "GB/s", "frac": round(step_gbs / peak, 4),
+                                 "roofline_tokens_per_s": round(world * B * peak * 1e9 / step_bytes, 1)},
+               "clocks": clk.summary(), "e2e": e2e, "cpu_baseline": cpu,
+               "gpu_launches": K * (2 + 5 * a.layers)}
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    a = _args()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

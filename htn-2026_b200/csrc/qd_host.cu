@@ -1,0 +1,57 @@
+// Library identification, error reporting and the shared launch helper.
+#include <cstdarg>
+#include <cstdio>
+
+#include "qd_host.h"
+
+namespace qd {
+
+static thread_local char g_msg[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int host_sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev >= 0 && dev < 64 && cached[dev] > 0) return cached[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  if (dev >= 0 && dev < 64) cached[dev] = n;
+  return n;
+}
+
+int launch_kernel(const void* func, dim3 grid, dim3 block, int smem, int pdl, cudaStream_t stream, void* arg) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  void* args[1] = {arg};
+  cudaError_t e = cudaLaunchKernelExC(&cfg, func, args);
+  if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "launch: %s", cudaGetErrorString(e));
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "launch: %s", cudaGetErrorString(e));
+  return QD_OK;
+}
+
+}  // namespace qd
+
+extern "C" const char* qd_version(void) { return "qd_decode 0.1 (sm_100a)"; }
+extern "C" const char* qd_last_error(void) { return qd::g_msg; }
+extern "C" int qd_sm_count(int* out) {
+  if (!out) return qd::set_error(QD_ERR_ARG, "null out");
+  *out = qd::host_sm_count();
+  return QD_OK;
+}

@@ -1,0 +1,21 @@
+// Host-side helpers shared by the C-ABI translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/qd_decode.h"
+
+namespace qd {
+
+// Record a message for qd_last_error() (thread-local) and return `code`.
+int set_error(int code, const char* fmt, ...);
+// SM count of the current device (cached per device).
+int host_sm_count();
+// cudaLaunchKernelEx of a kernel whose only parameter is the struct at `arg`; `pdl` adds the
+// programmatic-stream-serialization attribute so the kernel may start before its predecessor ends.
+int launch_kernel(const void* func, dim3 grid, dim3 block, int smem, int pdl, cudaStream_t stream, void* arg);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace qd

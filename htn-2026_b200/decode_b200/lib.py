@@ -1,0 +1,90 @@
+"""ctypes binding of libqd_decode.so (the C ABI declared in include/qd_decode.h).
+
+The library is the only compute path of the decode step: there is no CPU or PyTorch fallback.
+If it is missing or fails to load, `load()` raises; build it with `python -m decode_b200.build`.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+from . import build as _build
+
+_LIB = None
+
+c_void_p, c_int, c_int64, c_float = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+P_I64 = ctypes.POINTER(ctypes.c_int64)
+P_INT = ctypes.POINTER(ctypes.c_int)
+
+# name -> (restype, argtypes); every function declared in include/qd_decode.h
+PROTOTYPES = {
+    "qd_version": (ctypes.c_char_p, []),
+    "qd_last_error": (ctypes.c_char_p, []),
+    "qd_sm_count": (c_int, [P_INT]),
+    "qd_packed_bytes": (c_int64, [c_int64, c_int64]),
+    "qd_pack_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64,
+                             c_void_p]),
+    "qd_embed": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_void_p, c_int, c_void_p]),
+    "qd_gemv_plan": (c_int, [c_int64, c_int64, c_int, c_int, P_INT, P_I64]),
+    "qd_gemv": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_void_p, c_int64,
+                        c_void_p, c_float, c_int, c_int, c_void_p, c_int64, c_void_p, c_int, c_void_p]),
+    "qd_qkv_rope_append": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_float, c_void_p,
+                                   c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p,
+                                   c_void_p, c_int64, c_int64, c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int,
+                                   c_void_p]),
+    "qd_lm_head_plan": (c_int, [c_int64, c_int64, c_int, c_int, P_INT, P_I64]),
+    "qd_lm_head_argmax": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_void_p, c_float, c_void_p,
+                                  c_void_p, c_int, c_void_p, c_int64, c_int, c_void_p, c_int64, c_void_p, c_int,
+                                  c_void_p]),
+    "qd_attn_plan": (c_int, [c_int, c_int, c_int64, c_int, P_INT, P_I64, P_I64]),
+    "qd_attn_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64,
+                               c_int64, c_int64, c_int, c_int64, c_float, c_void_p, c_int64, c_void_p, c_int,
+                               c_void_p]),
+}
+
+QD_OK, QD_ERR_ARG, QD_ERR_SCRATCH, QD_ERR_CUDA, QD_ERR_UNSUPPORTED = 0, 1, 2, 3, 4
+QD_EPI_STORE, QD_EPI_RES, QD_EPI_SWIGLU = 0, 1, 2
+DEVERR = {1: "wait for a weight block timed out", 2: "wait for a free ring slot timed out",
+          4: "drain of in-flight copies timed out", 8: "token id out of range",
+          16: "decode position outside the cache"}
+
+
+class QDError(RuntimeError):
+    def __init__(self, fn: str, code: int, msg: str):
+        super().__init__(f"{fn} failed with code {code}: {msg}")
+        self.code = code
+
+
+def lib_path() -> str:
+    return os.environ.get("QD_DECODE_LIB", _build.LIB)
+
+
+def load(path: str | None = None) -> ctypes.CDLL:
+    """Load (once) and return the library; raises if it is missing."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    path = path or lib_path()
+    if not os.path.exists(path):
+        raise RuntimeError(f"libqd_decode.so not found at {path}; build it with `python -m decode_b200.build` "
+                           "(there is no fallback path)")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in PROTOTYPES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _LIB = lib
+    return lib
+
+
+def call(name: str, *args) -> None:
+    """Call an int-returning entry point and raise QDError on a non-zero status."""
+    lib = load()
+    rc = getattr(lib, name)(*args)
+    if rc != QD_OK:
+        raise QDError(name, rc, lib.qd_last_error().decode(errors="replace"))
+
+
+def describe_device_error(code: int) -> str:
+    return ", ".join(msg for bit, msg in DEVERR.items() if code & bit) or f"unknown ({code})"

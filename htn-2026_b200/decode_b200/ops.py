@@ -1,0 +1,191 @@
+"""Python wrappers over the C ABI, shaped like the reference's kernel wrapper classes.
+
+  pack_matrix / PackedMatrix   engine/engine.py:255-282 (weight packing)
+  embed                        engine/kernels/fast.py:73-76 (embed_ss)
+  Gemv                         engine/kernels/fast.py:173-213 (FastGemm) / gemv.py:157-248 (Gemv)
+  QkvRopeAppend                FastGemm "qkv" + the q/k-norm/RoPE/KV-append of FastAttention (fast.py:240-293)
+  LmHeadArgmax                 engine/kernels/fast.py:439-465 (FastLmHead) / gemv.py:251-287
+  DecodeAttention              engine/kernels/decode_attn.py:89-119 / FastAttention (fast.py:353-376)
+
+Each object owns its scratch buffer (split-K partials and tickets, zero-filled once) and launches
+on the current torch CUDA stream, so calls are graph-capturable. Tensors must be CUDA tensors.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import lib as L
+
+BF16 = torch.bfloat16
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _check_bf16(*ts):
+    for t in ts:
+        if t is not None:
+            assert t.is_cuda and t.dtype == BF16, f"expected a CUDA BF16 tensor, got {t.dtype} on {t.device}"
+
+
+def sm_count() -> int:
+    n = ctypes.c_int(0)
+    L.call("qd_sm_count", ctypes.byref(n))
+    return n.value
+
+
+# ------------------------------------------------------------------------------------ packing
+def packed_rows(n: int) -> int:
+    return (n + 127) // 128 * 128
+
+
+def new_packed(n_rows: int, k: int, device, count: int | None = None) -> torch.Tensor:
+    """Uninitialised packed storage for one matrix [n_rows, k] (or `count` stacked matrices)."""
+    elems = packed_rows(n_rows) * k
+    shape = (elems,) if count is None else (count, elems)
+    return torch.zeros(shape, dtype=BF16, device=device)
+
+
+def pack_rows(src: torch.Tensor, dst: torch.Tensor, n_dst_rows: int, span: int | None = None,
+              group_stride: int = 0, row_offset: int = 0) -> None:
+    """Copy row-major src [n, k] into rows (j // span) * group_stride + row_offset + j % span of the
+    packed destination (a flat BF16 tensor holding [n_dst_rows, k])."""
+    _check_bf16(src, dst)
+    n, k = src.shape
+    assert src.stride(1) == 1
+    L.call("qd_pack_rows", _ptr(src), src.stride(0), n, k, _ptr(dst), n_dst_rows, span or n, group_stride,
+           row_offset, _stream())
+
+
+def pack_matrix(w: torch.Tensor) -> torch.Tensor:
+    """Packed copy of a row-major [n, k] weight (rows padded to a multiple of 128 with zeros)."""
+    n, k = w.shape
+    out = new_packed(n, k, w.device)
+    pack_rows(w.contiguous(), out, packed_rows(n))
+    return out
+
+
+def pack_gate_up(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Gate/up matrix packed interleaved for the SwiGLU epilogue: each 128-row group holds 64 gate rows
+    followed by the 64 up rows of the same outputs."""
+    inter, k = gate.shape
+    assert up.shape == gate.shape and inter % 64 == 0
+    if out is None:
+        out = new_packed(2 * inter, k, gate.device)
+    pack_rows(gate.contiguous(), out, 2 * inter, 64, 128, 0)
+    pack_rows(up.contiguous(), out, 2 * inter, 64, 128, 64)
+    return out
+
+
+# ------------------------------------------------------------------------------------ kernels
+class _ErrWord:
+    """Device int32 word the kernels OR their bounded-wait / token-range failures into."""
+
+    def __init__(self, device):
+        self.t = torch.zeros((1,), dtype=torch.int32, device=device)
+
+    @property
+    def ptr(self):
+        return _ptr(self.t)
+
+
+def embed(tok: torch.Tensor, e_packed: torch.Tensor, vocab: int, x: torch.Tensor, err: torch.Tensor | None = None,
+          pdl: bool = True) -> torch.Tensor:
+    """x[i] = E[tok[i]] (tok int64 [m], x [m, k] BF16)."""
+    assert tok.dtype == torch.int64 and tok.is_cuda
+    m, k = x.shape
+    L.call("qd_embed", _ptr(tok), _ptr(e_packed), vocab, k, m, _ptr(x), x.stride(0), _ptr(err), int(pdl), _stream())
+    return x
+
+
+class Gemv:
+    """out[m, :] (+epilogue) = norm?(x)[m, k] @ W^T for a packed W [n, k]; see qd_gemv."""
+
+    STORE, RES, SWIGLU = L.QD_EPI_STORE, L.QD_EPI_RES, L.QD_EPI_SWIGLU
+
+    def __init__(self, m: int, n: int, k: int, epilogue: int, device, grid: int = 0, eps: float = 1e-6):
+        self.m, self.n, self.k, self.epilogue, self.eps = m, n, k, epilogue, eps
+        g, nbytes = ctypes.c_int(0), ctypes.c_int64(0)
+        L.call("qd_gemv_plan", n, k, m, grid, ctypes.byref(g), ctypes.byref(nbytes))
+        self.grid = g.value
+        self.scratch = torch.zeros((max(1, nbytes.value),), dtype=torch.uint8, device=device)
+
+    def __call__(self, x, w, out, res=None, norm_w=None, err=None, pdl=True):
+        _check_bf16(x, w, out, res, norm_w)
+        assert x.shape[0] == self.m and x.stride(1) == 1 and out.stride(1) == 1
+        L.call("qd_gemv", _ptr(x), x.stride(0), _ptr(w), self.n, self.k, self.m, _ptr(out), out.stride(0),
+               _ptr(res), res.stride(0) if res is not None else 0, _ptr(norm_w), self.eps, self.epilogue, self.grid,
+               _ptr(self.scratch), self.scratch.numel(), _ptr(err), int(pdl), _stream())
+        return out
+
+
+class QkvRopeAppend:
+    """Packed QKV projection of RMSNorm(x) with per-head q/k RMSNorm, RoPE at *pos and the K/V append."""
+
+    def __init__(self, m: int, k: int, nq: int, nkv: int, device, grid: int = 0, eps: float = 1e-6):
+        self.m, self.k, self.nq, self.nkv, self.eps = m, k, nq, nkv, eps
+        self.n = (nq + 2 * nkv) * 128
+        g, nbytes = ctypes.c_int(0), ctypes.c_int64(0)
+        L.call("qd_gemv_plan", self.n, k, m, grid, ctypes.byref(g), ctypes.byref(nbytes))
+        self.grid = g.value
+        self.scratch = torch.zeros((max(1, nbytes.value),), dtype=torch.uint8, device=device)
+
+    def __call__(self, x, w, norm_w, q_norm, k_norm, cos, sin, pos, q_out, k_cache, v_cache, raw_out=None,
+                 err=None, pdl=True):
+        _check_bf16(x, w, norm_w, q_norm, k_norm, cos, sin, q_out, k_cache, v_cache, raw_out)
+        assert pos.dtype == torch.int64 and k_cache.stride(2) == 128 and k_cache.stride() == v_cache.stride()
+        L.call("qd_qkv_rope_append", _ptr(x), x.stride(0), _ptr(w), self.k, self.m, _ptr(norm_w), self.eps,
+               _ptr(q_norm), _ptr(k_norm), _ptr(cos), _ptr(sin), _ptr(pos), k_cache.shape[2], self.nq, self.nkv,
+               _ptr(q_out),
+               _ptr(k_cache), _ptr(v_cache), k_cache.stride(0), k_cache.stride(1), _ptr(raw_out), self.grid,
+               _ptr(self.scratch), self.scratch.numel(), _ptr(err), int(pdl), _stream())
+        return q_out
+
+
+class LmHeadArgmax:
+    """tok[m] = argmax(bf16(RMSNorm(x) @ E^T)) (lowest index on ties); optionally *pos += 1 and logits."""
+
+    def __init__(self, m: int, vocab: int, k: int, device, grid: int = 0, eps: float = 1e-6):
+        self.m, self.vocab, self.k, self.eps = m, vocab, k, eps
+        g, nbytes = ctypes.c_int(0), ctypes.c_int64(0)
+        L.call("qd_lm_head_plan", vocab, k, m, grid, ctypes.byref(g), ctypes.byref(nbytes))
+        self.grid = g.value
+        self.scratch = torch.zeros((max(1, nbytes.value),), dtype=torch.uint8, device=device)
+
+    def __call__(self, x, e_packed, norm_w, tok, pos=None, inc_pos=False, logits=None, err=None, pdl=True):
+        _check_bf16(x, e_packed, norm_w, logits)
+        assert tok.dtype == torch.int64
+        L.call("qd_lm_head_argmax", _ptr(x), x.stride(0), _ptr(e_packed), self.vocab, self.k, self.m, _ptr(norm_w),
+               self.eps, _ptr(tok), _ptr(pos), int(inc_pos), _ptr(logits),
+               logits.stride(0) if logits is not None else 0, self.grid, _ptr(self.scratch), self.scratch.numel(),
+               _ptr(err), int(pdl), _stream())
+        return tok
+
+
+class DecodeAttention:
+    """Split-K GQA flash-decode + LSE merge for a fixed (batch, capacity); see qd_attn_decode."""
+
+    def __init__(self, batch: int, nq: int, nkv: int, capacity: int, device, grid: int = 0):
+        self.batch, self.nq, self.nkv, self.capacity = batch, nq, nkv, capacity
+        s, ch, nbytes = ctypes.c_int(0), ctypes.c_int64(0), ctypes.c_int64(0)
+        L.call("qd_attn_plan", batch, nkv, capacity, grid, ctypes.byref(s), ctypes.byref(ch), ctypes.byref(nbytes))
+        self.splits, self.chunk = s.value, ch.value
+        self.scratch = torch.zeros((max(1, nbytes.value),), dtype=torch.uint8, device=device)
+        self.scale = 1.0 / math.sqrt(128)
+
+    def __call__(self, q, k_cache, v_cache, pos, out, err=None, pdl=True):
+        _check_bf16(q, k_cache, v_cache, out)
+        assert k_cache.shape[2] == self.capacity and k_cache.stride() == v_cache.stride()
+        L.call("qd_attn_decode", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(pos), _ptr(out), self.batch, self.nq,
+               self.nkv, self.capacity, k_cache.stride(0), k_cache.stride(1), self.splits, self.chunk, self.scale,
+               _ptr(self.scratch), self.scratch.numel(), _ptr(err), int(pdl), _stream())
+        return out

@@ -1,0 +1,378 @@
+"""Qwen3 greedy decode engine for NVIDIA B200 (sm_100a).
+
+Drop-in for the reference's `engine/engine.py`: the same `Engine(model_path)` constructor and
+`generate(input_ids, max_new_tokens)` generator (engine/engine.py:232-293, :1105-1132; contract in
+QWEN_ENGINE_CONTRACT.md): it yields exactly `max_new_tokens` lists, one token id per sequence in
+input order, ignores end-of-sequence ids, and yields nothing for max_new_tokens <= 0.
+
+Decode runs entirely in the hand-written CUDA library (decode_b200/libqd_decode.so, C ABI in
+include/qd_decode.h); there is no Triton, no tier fallback and no CPU path. One decode step is
+1 + 5 x layers + 1 launches, captured once per shape in a CUDA graph:
+
+  embed          x = E[tok]
+  per layer      qkv   RMSNorm(x) @ Wqkv^T, per-head q/k RMSNorm + RoPE(pos), K/V appended at pos
+                 attn  split-K GQA flash-decode over [0, pos] + log-sum-exp merge
+                 o     x = bf16(x + bf16(attn @ Wo^T))
+                 gu    act = bf16(silu(bf16 g)) * bf16 u with g, u = RMSNorm(x) @ [Wg; Wu]^T
+                 down  x = bf16(x + bf16(act @ Wd^T))
+  lm head        tok = argmax(bf16(RMSNorm(x) @ E^T)), pos += 1
+
+Weights are packed once at load into the kernels' blocked layout (decode_b200/ops.py). The prompt
+forward (prefill, engine/engine.py:550-592) still uses PyTorch (cuBLAS GEMMs + SDPA) on row-major
+copies of the weights and writes the same KV cache; it is captured in a CUDA graph too. The stream
+loop keeps the GPU one step ahead of the host like engine/engine.py:719-757.
+"""
+
+from __future__ import annotations
+
+import gc
+import os
+import sys
+import time
+
+import torch
+import torch.nn.functional as F
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+from decode_b200 import lib as qdlib  # noqa: E402
+from decode_b200 import ops  # noqa: E402
+from decode_b200.loader import load_checkpoint  # noqa: E402
+
+DEVICE = os.environ.get("ENGINE_DEVICE", "cuda:0")
+BF16 = torch.bfloat16
+MAX_BATCH = 8             # the streaming GEMV keeps up to 8 activation rows in registers
+PREFILL_TOKENS = 16384    # prefill processes at most this many tokens per row chunk (engine/engine.py:79)
+USE_GRAPHS = os.environ.get("ENGINE_GRAPHS", "1") != "0"
+USE_PDL = os.environ.get("ENGINE_PDL", "1") != "0"
+
+
+def log(msg):
+    print(f"[engine] {msg}", file=sys.stderr, flush=True)
+
+
+def rope_tables(cap: int, head_dim: int, theta: float):
+    """cos, sin [cap, head_dim] BF16, computed on the CPU exactly as transformers'
+    Qwen3RotaryEmbedding does (fp32 inv_freq, fp32 matmul, cat(freqs, freqs), cos/sin, cast)."""
+    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).to(dtype=torch.float) / head_dim))
+    pos = torch.arange(cap)[None]
+    freqs = (inv_freq[None, :, None].float() @ pos[:, None, :].float()).transpose(1, 2)
+    emb = torch.cat((freqs, freqs), dim=-1)
+    return emb.cos()[0].to(BF16).contiguous(), emb.sin()[0].to(BF16).contiguous()
+
+
+def _rms(x, w, eps, heads=1):
+    """Qwen3RMSNorm with the reference's cast placement (engine/engine.py:505-509)."""
+    n = w.numel()
+    xf = x[:, : heads * n].reshape(x.shape[0], heads, n).to(torch.float32)
+    xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return w * xf.to(BF16)
+
+
+def _rotate_half(x):
+    half = x.shape[-1] // 2
+    return torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+
+
+class _State:
+    """Everything shape-dependent for one (batch, prompt length, new tokens)."""
+
+    def __init__(self, eng: "Engine", B: int, S: int, N: int):
+        dev = eng.device
+        self.B, self.S, self.N = B, S, N
+        cap = self.capacity = S + N
+        Lyr, H, I = eng.n_layers, eng.hidden, eng.inter
+        nq, nkv, D = eng.nq, eng.nkv, eng.head_dim
+        self.k_all = torch.zeros((Lyr, B, nkv, cap, D), dtype=BF16, device=dev)
+        self.v_all = torch.zeros((Lyr, B, nkv, cap, D), dtype=BF16, device=dev)
+        cos, sin = rope_tables(cap, D, eng.theta)
+        self.cos, self.sin = cos.to(dev), sin.to(dev)
+        self.ids = torch.zeros((B, S), dtype=torch.int64, device=dev)
+        self.tok = torch.zeros((B,), dtype=torch.int64, device=dev)
+        self.pos = torch.zeros((1,), dtype=torch.int64, device=dev)
+        self.err = torch.zeros((1,), dtype=torch.int32, device=dev)
+        self.x = torch.zeros((B, H), dtype=BF16, device=dev)
+        self.q = torch.zeros((B, nq, D), dtype=BF16, device=dev)
+        self.attn_out = torch.zeros((B, nq, D), dtype=BF16, device=dev)
+        self.act = torch.zeros((B, I), dtype=BF16, device=dev)
+        self.logits = None
+        self.qkv = ops.QkvRopeAppend(B, H, nq, nkv, dev, eps=eng.eps)
+        self.attn = ops.DecodeAttention(B, nq, nkv, cap, dev)
+        self.o = ops.Gemv(B, H, nq * D, ops.Gemv.RES, dev, eps=eng.eps)
+        self.gu = ops.Gemv(B, 2 * I, H, ops.Gemv.SWIGLU, dev, eps=eng.eps)
+        self.down = ops.Gemv(B, H, I, ops.Gemv.RES, dev, eps=eng.eps)
+        self.lm = ops.LmHeadArgmax(B, eng.vocab, H, dev, eps=eng.eps)
+        self.rows = max(1, min(B, PREFILL_TOKENS // S))
+        pin = torch.cuda.is_available()
+        self.host = torch.empty((max(N, 1), B), dtype=torch.int64, pin_memory=pin)
+        self.ids_host = torch.empty((B, S), dtype=torch.int64, pin_memory=pin)
+        self.events = [torch.cuda.Event() for _ in range(max(N, 1))]
+        self.prefill_graph = self.decode_graph = None
+        self.prefill_logits = None
+
+
+class Engine:
+    def __init__(self, model_path: str, device: str | None = None) -> None:
+        t0 = time.perf_counter()
+        state, cfg = load_checkpoint(model_path, "cpu")
+        self._setup(state, cfg, device or DEVICE)
+        self.load_s = time.perf_counter() - t0
+        log(f"loaded {model_path} in {self.load_s:.1f}s: {self.n_layers} layers, {qdlib.load().qd_version().decode()}")
+
+    @classmethod
+    def from_state_dict(cls, state: dict, cfg: dict, device: str | None = None) -> "Engine":
+        """Build from Hugging Face-named BF16 tensors (CPU or CUDA) and a config dict."""
+        eng = cls.__new__(cls)
+        t0 = time.perf_counter()
+        eng._setup(state, cfg, device or DEVICE)
+        eng.load_s = time.perf_counter() - t0
+        return eng
+
+    # ------------------------------------------------------------------ weights
+    def _setup(self, state: dict, cfg: dict, device: str) -> None:
+        qdlib.load()  # fail loudly before anything else if the CUDA library is missing
+        if not torch.cuda.is_available():
+            raise RuntimeError("the decode engine needs a CUDA device (sm_100a); there is no CPU path")
+        torch.backends.cuda.matmul.allow_tf32 = False
+        torch.backends.cudnn.allow_tf32 = False
+        self.device = torch.device(device)
+        torch.cuda.set_device(self.device)
+        self.cfg = dict(cfg)
+        self.n_layers = cfg["num_hidden_layers"]
+        self.hidden = H = cfg["hidden_size"]
+        self.inter = I = cfg["intermediate_size"]
+        self.nq, self.nkv = cfg["num_attention_heads"], cfg["num_key_value_heads"]
+        self.head_dim = D = cfg.get("head_dim") or H // self.nq
+        self.vocab = cfg["vocab_size"]
+        self.eps = float(cfg["rms_norm_eps"])
+        self.theta = float(cfg.get("rope_theta", 5e6))
+        if D != 128 or self.nq != 4 * self.nkv or H % 64 or I % 64 or self.nq * D % 64:
+            raise NotImplementedError("kernels are built for head_dim 128, 4 query heads per KV head, "
+                                      "hidden/intermediate multiples of 64")
+        dev = self.device
+        get = lambda name: state[name].to(dev, BF16)  # noqa: E731
+        Lyr = self.n_layers
+        nq_rows, nkv_rows = self.nq * D, self.nkv * D
+        n_qkv = nq_rows + 2 * nkv_rows
+        # row-major copies for the PyTorch prefill; packed copies for the decode kernels
+        self.embed_rm = get("model.embed_tokens.weight")
+        self.lm_rm = get("lm_head.weight") if ("lm_head.weight" in state and not cfg.get("tie_word_embeddings", True)) \
+            else self.embed_rm
+        self.final_norm = get("model.norm.weight")
+        self.ln1 = torch.empty((Lyr, H), dtype=BF16, device=dev)
+        self.ln2 = torch.empty((Lyr, H), dtype=BF16, device=dev)
+        self.qn = torch.empty((Lyr, D), dtype=BF16, device=dev)
+        self.kn = torch.empty((Lyr, D), dtype=BF16, device=dev)
+        self.w_qkv_rm = torch.empty((Lyr, n_qkv, H), dtype=BF16, device=dev)
+        self.w_o_rm = torch.empty((Lyr, H, nq_rows), dtype=BF16, device=dev)
+        self.w_gu_rm = torch.empty((Lyr, 2 * I, H), dtype=BF16, device=dev)
+        self.w_down_rm = torch.empty((Lyr, H, I), dtype=BF16, device=dev)
+        self.w_qkv = ops.new_packed(n_qkv, H, dev, Lyr)
+        self.w_o = ops.new_packed(H, nq_rows, dev, Lyr)
+        self.w_gu = ops.new_packed(2 * I, H, dev, Lyr)
+        self.w_down = ops.new_packed(H, I, dev, Lyr)
+        with torch.no_grad():
+            for i in range(Lyr):
+                p = f"model.layers.{i}."
+                self.ln1[i].copy_(state[p + "input_layernorm.weight"])
+                self.ln2[i].copy_(state[p + "post_attention_layernorm.weight"])
+                self.qn[i].copy_(state[p + "self_attn.q_norm.weight"])
+                self.kn[i].copy_(state[p + "self_attn.k_norm.weight"])
+                self.w_qkv_rm[i, :nq_rows].copy_(state[p + "self_attn.q_proj.weight"])
+                self.w_qkv_rm[i, nq_rows:nq_rows + nkv_rows].copy_(state[p + "self_attn.k_proj.weight"])
+                self.w_qkv_rm[i, nq_rows + nkv_rows:].copy_(state[p + "self_attn.v_proj.weight"])
+                self.w_o_rm[i].copy_(state[p + "self_attn.o_proj.weight"])
+                self.w_gu_rm[i, :I].copy_(state[p + "mlp.gate_proj.weight"])
+                self.w_gu_rm[i, I:].copy_(state[p + "mlp.up_proj.weight"])
+                self.w_down_rm[i].copy_(state[p + "mlp.down_proj.weight"])
+                ops.pack_rows(self.w_qkv_rm[i], self.w_qkv[i], n_qkv)
+                ops.pack_rows(self.w_o_rm[i], self.w_o[i], H)
+                ops.pack_gate_up(self.w_gu_rm[i, :I], self.w_gu_rm[i, I:], self.w_gu[i])
+                ops.pack_rows(self.w_down_rm[i], self.w_down[i], H)
+            self.e_packed = ops.pack_matrix(self.lm_rm)
+            if self.lm_rm is not self.embed_rm:
+                raise NotImplementedError("untied LM head: the embedding gather reads the packed LM matrix")
+        torch.cuda.synchronize()
+        self.state = None
+        self.sm_count = ops.sm_count()
+
+    # ------------------------------------------------------------------ model step
+    def _prefill(self, st: _State) -> torch.Tensor:
+        """Prompt forward in row chunks (engine/engine.py:550-592): K/V [0, S) into the cache, first
+        token into st.tok; returns the last position's logits [B, V]."""
+        B, S = st.B, st.S
+        H, D, nq, nkv = self.hidden, self.head_dim, self.nq, self.nkv
+        cos = st.cos[:S][None, None]
+        sin = st.sin[:S][None, None]
+        last_layer = self.n_layers - 1
+        outs = []
+        for r0 in range(0, B, st.rows):
+            r1 = min(B, r0 + st.rows)
+            b, M = r1 - r0, (r1 - r0) * S
+            x = F.embedding(st.ids[r0:r1], self.embed_rm).view(M, H)
+            for i in range(self.n_layers):
+                kc, vc = st.k_all[i, r0:r1], st.v_all[i, r0:r1]
+                h = _rms(x, self.ln1[i], self.eps).view(M, H)
+                qkv = F.linear(h, self.w_qkv_rm[i])
+                q = _rms(qkv, self.qn[i], self.eps, nq).view(b, S, nq, D).transpose(1, 2)
+                k = _rms(qkv[:, nq * D:], self.kn[i], self.eps, nkv).view(b, S, nkv, D).transpose(1, 2)
+                v = qkv[:, (nq + nkv) * D:].view(b, S, nkv, D).transpose(1, 2)
+                q = (q * cos) + (_rotate_half(q) * sin)
+                k = (k * cos) + (_rotate_half(k) * sin)
+                kc[:, :, :S].copy_(k)
+                vc[:, :, :S].copy_(v)
+                if i == last_layer:
+                    a = F.scaled_dot_product_attention(q[:, :, -1:].contiguous(), kc[:, :, :S], vc[:, :, :S],
+                                                       scale=D ** -0.5, enable_gqa=True)
+                    x = x.view(b, S, H)[:, -1] + F.linear(a.reshape(b, nq * D), self.w_o_rm[i])
+                    h = _rms(x, self.ln2[i], self.eps).view(b, H)
+                    gu = F.linear(h, self.w_gu_rm[i])
+                    x = x + F.linear(F.silu(gu[:, :self.inter]) * gu[:, self.inter:], self.w_down_rm[i])
+                    break
+                a = F.scaled_dot_product_attention(q.contiguous(), kc[:, :, :S], vc[:, :, :S], is_causal=True,
+                                                   scale=D ** -0.5, enable_gqa=True)
+                x = x + F.linear(a.transpose(1, 2).reshape(M, nq * D), self.w_o_rm[i])
+                h = _rms(x, self.ln2[i], self.eps).view(M, H)
+                gu = F.linear(h, self.w_gu_rm[i])
+                x = x + F.linear(F.silu(gu[:, :self.inter]) * gu[:, self.inter:], self.w_down_rm[i])
+            outs.append(F.linear(_rms(x, self.final_norm, self.eps).view(b, H), self.lm_rm))
+        logits = outs[0] if len(outs) == 1 else torch.cat(outs, 0)
+        st.tok.copy_(torch.argmax(logits, dim=-1))
+        return logits
+
+    def _decode_step(self, st: _State, logits: torch.Tensor | None = None) -> None:
+        """One token per sequence at st.pos: 1 + 5 * layers + 1 kernel launches, all in libqd_decode."""
+        pdl, err = USE_PDL, st.err
+        ops.embed(st.tok, self.e_packed, self.vocab, st.x, err, pdl)
+        for i in range(self.n_layers):
+            kc, vc = st.k_all[i], st.v_all[i]
+            st.qkv(st.x, self.w_qkv[i], self.ln1[i], self.qn[i], self.kn[i], st.cos, st.sin, st.pos, st.q, kc, vc,
+                   err=err, pdl=pdl)
+            st.attn(st.q, kc, vc, st.pos, st.attn_out, err=err, pdl=pdl)
+            st.o(st.attn_out.view(st.B, -1), self.w_o[i], st.x, res=st.x, err=err, pdl=pdl)
+            st.gu(st.x, self.w_gu[i], st.act, norm_w=self.ln2[i], err=err, pdl=pdl)
+            st.down(st.act, self.w_down[i], st.x, res=st.x, err=err, pdl=pdl)
+        st.lm(st.x, self.e_packed, self.final_norm, st.tok, st.pos, inc_pos=True, logits=logits, err=err, pdl=pdl)
+
+    def check_device_errors(self, st: _State) -> None:
+        code = int(st.err.item())
+        if code:
+            st.err.zero_()
+            raise RuntimeError(f"decode kernels reported a device error: {qdlib.describe_device_error(code)}")
+
+    # ------------------------------------------------------------------ shapes, graphs
+    def _build(self, B: int, S: int, N: int) -> _State:
+        if B > MAX_BATCH:
+            raise NotImplementedError(f"batch {B} > {MAX_BATCH}: the tensor-core skinny GEMM path is not built yet")
+        self.state = None
+        gc.collect()
+        torch.cuda.empty_cache()
+        st = _State(self, B, S, N)
+        t0 = time.perf_counter()
+        with torch.inference_mode():
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    self._prefill(st)
+                    if N > 1:
+                        st.pos.fill_(S)
+                        self._decode_step(st)
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            self.check_device_errors(st)
+            if USE_GRAPHS:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    st.prefill_logits = self._prefill(st)
+                st.prefill_graph = g
+                if N > 1:
+                    st.pos.fill_(S)
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g):
+                        self._decode_step(st)
+                    st.decode_graph = g
+            torch.cuda.synchronize()
+        st.build_s = time.perf_counter() - t0
+        self.state = st
+        return st
+
+    def _stream(self, st: _State, input_ids, N: int, timing: list | None = None):
+        """Greedy stream of N steps; keeps the GPU one step ahead of the host (engine/engine.py:719-757)."""
+        B, S = st.B, st.S
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(N)] \
+            if timing is not None else None
+        with torch.inference_mode():
+            st.ids_host.copy_(torch.tensor(input_ids, dtype=torch.int64))
+            st.ids.copy_(st.ids_host, non_blocking=True)
+            st.pos.fill_(S)
+            if ev:
+                ev[0][0].record()
+            if st.prefill_graph is not None:
+                st.prefill_graph.replay()
+            else:
+                st.prefill_logits = self._prefill(st)
+            if ev:
+                ev[0][1].record()
+            st.host[0].copy_(st.tok, non_blocking=True)
+            st.events[0].record()
+        for t in range(1, N):
+            with torch.inference_mode():
+                if ev:
+                    ev[t][0].record()
+                if st.decode_graph is not None:
+                    st.decode_graph.replay()
+                else:
+                    self._decode_step(st)
+                if ev:
+                    ev[t][1].record()
+                st.host[t].copy_(st.tok, non_blocking=True)
+                st.events[t].record()
+            st.events[t - 1].synchronize()
+            yield st.host[t - 1].tolist()
+        st.events[N - 1].synchronize()
+        self.check_device_errors(st)
+        if ev:
+            timing.extend(a.elapsed_time(b) for a, b in ev)
+        yield st.host[N - 1].tolist()
+
+    # ------------------------------------------------------------------ API
+    def generate(self, input_ids: list[list[int]], max_new_tokens: int):
+        N = int(max_new_tokens)
+        if N <= 0:
+            return
+        B, S = len(input_ids), len(input_ids[0])
+        if B < 1 or S < 1 or any(len(r) != S for r in input_ids):
+            raise ValueError("input_ids must be a non-empty batch of equal-length rows")
+        st = self.state
+        if st is None or (st.B, st.S, st.N) != (B, S, N):
+            st = self._build(B, S, N)
+        gc_was = gc.isenabled()
+        gc.disable()
+        try:
+            yield from self._stream(st, input_ids, N)
+        finally:
+            if gc_was:
+                gc.enable()
+
+    def generate_with_logits(self, input_ids: list[list[int]], max_new_tokens: int):
+        """Test hook: eager (un-graphed) greedy run returning (tokens [B][N], list of N host logits [B, V])."""
+        N = int(max_new_tokens)
+        B, S = len(input_ids), len(input_ids[0])
+        st = self.state
+        if st is None or (st.B, st.S, st.N) != (B, S, N):
+            st = self._build(B, S, N)
+        buf = torch.empty((B, self.vocab), dtype=BF16, device=self.device)
+        toks, logits = [], []
+        with torch.inference_mode():
+            st.ids.copy_(torch.tensor(input_ids, dtype=torch.int64))
+            st.pos.fill_(S)
+            lg = self._prefill(st)
+            toks.append(st.tok.tolist())
+            logits.append(lg.cpu())
+            for _ in range(1, N):
+                self._decode_step(st, logits=buf)
+                toks.append(st.tok.tolist())
+                logits.append(buf.cpu())
+        self.check_device_errors(st)
+        return [list(r) for r in zip(*toks)], logits

@@ -1,0 +1,131 @@
+/* qd_decode.h - C ABI of the B200 (sm_100a) Qwen3 greedy-decode kernels.
+ *
+ * Every entry point takes raw device pointers, sizes and a CUDA stream; nothing here allocates,
+ * synchronises or reads device memory on the host, so every call can be captured in a CUDA graph.
+ * All buffers are caller-owned. Scratch buffers (split-K partial sums and tickets) are sized by the
+ * matching *_plan call, must be zero-filled once after allocation, and are left zero-ready by every
+ * successful launch. Two launches that share a scratch buffer must not overlap on the GPU.
+ *
+ * Return value: 0 (QD_OK) or a QD_ERR_* code; qd_last_error() describes the last failure of the
+ * calling thread. Device-side bounded waits report through the caller's `err` word (QD_DEVERR_*),
+ * which the host reads after a step; a wait never spins for more than about one second.
+ *
+ * The reference (Yokanater/htn-2026) has no C/C++ or CUDA code: its decode path is Python calling
+ * Triton kernels through small wrapper classes. Each entry point below names the wrapper and
+ * kernel it replaces, by file:line in that repository.
+ */
+#ifndef QD_DECODE_H
+#define QD_DECODE_H
+
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  QD_OK = 0,
+  QD_ERR_ARG = 1,         /* invalid pointer, size, stride or alignment */
+  QD_ERR_SCRATCH = 2,     /* scratch buffer smaller than the plan requires */
+  QD_ERR_CUDA = 3,        /* CUDA runtime error at launch */
+  QD_ERR_UNSUPPORTED = 4  /* shape outside what the kernels are built for */
+};
+
+enum { QD_EPI_STORE = 0, QD_EPI_RES = 1, QD_EPI_SWIGLU = 2 };
+
+enum {
+  QD_DEVERR_WAIT_FULL = 1,
+  QD_DEVERR_WAIT_EMPTY = 2,
+  QD_DEVERR_DRAIN = 4,
+  QD_DEVERR_TOKEN = 8,
+  QD_DEVERR_POS = 16
+};
+
+/* Library identification and the last error message of the calling thread. */
+const char* qd_version(void);
+const char* qd_last_error(void);
+/* Streaming multiprocessors of the current device. */
+int qd_sm_count(int* out);
+
+/* ---------------------------------------------------------------- weight packing
+ * Replaces the reference loader's layer-stacked packing copies (engine/engine.py:255-282).
+ * The packed layout is 16 KiB blocks of 128 rows x 64 columns, row-group-major, each 128-byte row
+ * with its 16-byte chunks swizzled (chunk c of row r at position c ^ (r & 7)).
+ * qd_pack_rows copies rows j = 0..n_src_rows-1 of a row-major BF16 source [n_src_rows, k] (row
+ * stride ld_src elements) into logical rows
+ *     (j / span) * group_stride + row_offset + (j % span)
+ * of a packed [n_dst_rows, k] destination. Plain stacking: span = n_src_rows, group_stride = 0,
+ * row_offset = first row. Gate/up interleave of the SwiGLU matrix: span = 64, group_stride = 128,
+ * row_offset = 0 (gate) or 64 (up). n_dst_rows % 128 == 0, k % 64 == 0. */
+int64_t qd_packed_bytes(int64_t n_rows, int64_t k);
+int qd_pack_rows(const void* src, int64_t ld_src, int64_t n_src_rows, int64_t k, void* dst, int64_t n_dst_rows,
+                 int64_t span, int64_t group_stride, int64_t row_offset, cudaStream_t stream);
+
+/* ---------------------------------------------------------------- embedding
+ * Replaces embed_ss (engine/kernels/fast.py:53-76) / F.embedding (engine/engine.py:338):
+ * x[i, :] = E[tok[i], :] for i < m, gathered from the packed embedding matrix (tied with the LM head).
+ * Out-of-range token ids are clamped and flagged with QD_DEVERR_TOKEN in *err. */
+int qd_embed(const int64_t* tok, const void* e_packed, int64_t vocab, int64_t k, int m, void* x, int64_t ldx,
+             int* err, int pdl, cudaStream_t stream);
+
+/* ---------------------------------------------------------------- streaming GEMV
+ * Replaces FastGemm (engine/kernels/fast.py:173-213, kernel :99-158) and Gemv + split-K reduce
+ * (engine/kernels/gemv.py:157-248, kernels :60-115):
+ *   y[i, :] = xn[i, :] . W^T,  xn = norm_w ? bf16(norm_w * bf16(x * rsqrt(mean(x^2) + eps))) : x
+ *   QD_EPI_STORE   out = bf16(y)
+ *   QD_EPI_RES     out = bf16(res + bf16(y))                   (out may alias res)
+ *   QD_EPI_SWIGLU  W is the gate/up matrix packed interleaved (64 gate rows, then the 64 up rows of
+ *                  the same outputs, per 128-row group); out[i, j] = bf16(bf16(silu(bf16 g)) * bf16 u),
+ *                  out has n / 2 columns
+ * x [m, k] BF16 (row stride ldx), W packed [n, k], 1 <= m <= 8, n % 128 == 0, k % 64 == 0.
+ * grid_hint <= 0 picks one CTA per SM. */
+int qd_gemv_plan(int64_t n, int64_t k, int m, int grid_hint, int* grid, int64_t* scratch_bytes);
+int qd_gemv(const void* x, int64_t ldx, const void* w_packed, int64_t n, int64_t k, int m, void* out, int64_t ldo,
+            const void* res, int64_t ldr, const void* norm_w, float eps, int epilogue, int grid, void* scratch,
+            int64_t scratch_bytes, int* err, int pdl, cudaStream_t stream);
+
+/* QKV projection with the attention prologue fused into its epilogue. Replaces FastGemm "qkv"
+ * (engine/engine.py:472) plus the q/k RMSNorm + RoPE + KV-cache append of FastAttention
+ * (engine/kernels/fast.py:240-293) / qk_norm_rope_cache (engine/kernels/fused.py:23-98, pos_mode 1).
+ * W packed [(nq + 2 nkv) * 128, k] rows q | k | v (head_dim 128). For every row i < m and position
+ * p = *pos: q_out[i, h, :] = rope(rmsnorm(q_h)), k_cache[i, kvh, p, :] = rope(rmsnorm(k_kvh)),
+ * v_cache[i, kvh, p, :] = v_kvh; caches are [m, nkv, cap, 128] with strides cs_b, cs_h (elements),
+ * cos/sin are [cap, 128] BF16 tables. raw_out (optional) receives the BF16 projection [m, n].
+ * A device position outside [0, cap) writes nothing and sets QD_DEVERR_POS in *err. */
+int qd_qkv_rope_append(const void* x, int64_t ldx, const void* w_packed, int64_t k, int m, const void* norm_w,
+                       float eps, const void* q_norm, const void* k_norm, const void* cos, const void* sin,
+                       const int64_t* pos, int64_t cap, int nq_heads, int nkv_heads, void* q_out, void* k_cache,
+                       void* v_cache, int64_t cs_b, int64_t cs_h, void* raw_out, int grid, void* scratch,
+                       int64_t scratch_bytes, int* err, int pdl, cudaStream_t stream);
+
+/* LM head with final RMSNorm prologue and argmax epilogue. Replaces FastLmHead
+ * (engine/kernels/fast.py:380-465) / LmHeadArgmax (engine/kernels/gemv.py:118-287):
+ * logits = bf16(xn . E^T), tok[i] = argmax (lowest index on exact ties), *pos += inc_pos.
+ * E packed [roundup(vocab, 128), k]; logits_out (optional) [m, vocab] BF16 with row stride ld_logits. */
+int qd_lm_head_plan(int64_t vocab, int64_t k, int m, int grid_hint, int* grid, int64_t* scratch_bytes);
+int qd_lm_head_argmax(const void* x, int64_t ldx, const void* e_packed, int64_t vocab, int64_t k, int m,
+                      const void* norm_w, float eps, int64_t* tok, int64_t* pos, int inc_pos, void* logits_out,
+                      int64_t ld_logits, int grid, void* scratch, int64_t scratch_bytes, int* err, int pdl,
+                      cudaStream_t stream);
+
+/* ---------------------------------------------------------------- decode attention
+ * Split-K GQA flash-decode with a log-sum-exp merge. Replaces DecodeAttention
+ * (engine/kernels/decode_attn.py:26-119) and the flash-decode + merge part of FastAttention
+ * (engine/kernels/fast.py:252-331, :345-376). One query per sequence at position p = *pos over keys
+ * [0, p] (the new token's K/V are already in the cache): out[b, h, :] = softmax(q k^T * scale) v with
+ * query head h reading KV head h / (nq / nkv). q, out [batch, nq, 128] BF16; caches
+ * [batch, nkv, cap, 128] with strides cs_b, cs_h. Scores and softmax in fp32, probabilities rounded
+ * to BF16 before P.V, fp32 accumulation; the last split to finish merges (fixed split order).
+ * A device position outside [0, cap) reads no key beyond the cache and sets QD_DEVERR_POS in *err. */
+int qd_attn_plan(int batch, int nkv_heads, int64_t cap, int grid_hint, int* splits, int64_t* chunk,
+                 int64_t* scratch_bytes);
+int qd_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, void* out, int batch,
+                   int nq_heads, int nkv_heads, int64_t cap, int64_t cs_b, int64_t cs_h, int splits, int64_t chunk,
+                   float scale, void* scratch, int64_t scratch_bytes, int* err, int pdl, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QD_DECODE_H */

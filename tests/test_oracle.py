@@ -1,0 +1,89 @@
+"""Pin the CPU oracle against the golden vectors recorded from the reference engine itself.
+
+tests/golden/*.json were produced by tests/golden/make_golden.py, which imports the reference
+engine (engine/engine.py) on CPU and records tier 0 (native Transformers loop) and tier 1 (the
+reference's eager torch restatement). The oracle must reproduce both bit-for-bit on CPU: it is the
+same torch arithmetic in the same order.
+"""
+
+import pytest
+import torch
+
+from conftest import load_golden, synth_state
+from oracle import qwen3_cpu as Q
+
+
+def _summ(logits, probes):
+    lf = logits.float()
+    vals, idx = torch.topk(lf, 8, dim=-1)
+    return vals, idx, torch.logsumexp(lf, -1), lf[:, probes]
+
+
+@pytest.mark.parametrize("case", ["config0", "b3_s17"])
+def test_oracle_matches_reference_golden(case):
+    g = load_golden(case)
+    state, cfg = synth_state(g["spec"]["layers"])
+    orc = Q.Qwen3Oracle(state, cfg)
+    toks, logits = orc.generate(g["prompt"], g["spec"]["new"])
+    assert toks == g["native"]["tokens"]
+    assert toks == g["tier1"]["tokens"]
+    probes = g["probe_ids"]
+    for t, step in enumerate(g["tier1"]["steps"]):
+        vals, idx, lse, pv = _summ(logits[t], probes)
+        assert vals.tolist() == step["top_vals"]
+        assert pv.tolist() == step["probe_vals"]
+        assert torch.allclose(lse, torch.tensor(step["lse"]), atol=1e-5, rtol=0)
+        # top-8 ids may permute only inside exact ties
+        for r in range(len(step["top_ids"])):
+            tv = step["top_vals"][r]
+            assert sorted(zip(tv, step["top_ids"][r])) == sorted(zip(vals[r].tolist(), idx[r].tolist())) or \
+                len(set(tv)) < len(tv)
+
+
+def test_teacher_forced_oracle_matches_free_run():
+    """Forcing the oracle's own tokens reproduces its own logits exactly (same prefix, same ops)."""
+    g = load_golden("b3_s17")
+    state, cfg = synth_state(g["spec"]["layers"])
+    orc = Q.Qwen3Oracle(state, cfg)
+    toks, logits = orc.generate(g["prompt"], g["spec"]["new"])
+    toks2, logits2 = orc.generate(g["prompt"], g["spec"]["new"], forced=toks)
+    assert toks2 == toks
+    for a, b in zip(logits, logits2):
+        assert torch.equal(a, b)
+
+
+def test_rope_tables_match_transformers_module():
+    from transformers import Qwen3Config
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding
+
+    conf = Qwen3Config(hidden_size=2560, num_attention_heads=32, num_key_value_heads=8, head_dim=128,
+                       rope_theta=5e6, max_position_embeddings=262144)
+    rot = Qwen3RotaryEmbedding(conf)
+    cap = 5000
+    cos, sin = rot(torch.empty(1, dtype=torch.bfloat16), torch.arange(cap)[None])
+    c2, s2 = Q.rope_tables(cap, 128, 5e6)
+    assert torch.equal(cos[0], c2) and torch.equal(sin[0], s2)
+
+
+def test_token_tie_rule():
+    lg = torch.tensor([0.0, 2.0, 1.99, -1.0])
+    assert Q.token_ok(1, lg, 0.05)
+    assert Q.token_ok(2, lg, 0.05)          # inside the tie margin
+    assert not Q.token_ok(2, lg, 0.005)
+    assert not Q.token_ok(0, lg, 0.05)
+    assert Q.argmax_lowest(torch.tensor([[1.0, 3.0, 3.0]])).item() == 1
+
+
+def test_native_loop_matches_golden():
+    """oracle.native (the reference's tier 0 restated over transformers) gives the golden tokens."""
+    from oracle import native
+
+    g = load_golden("b3_s17")
+    state, cfg = synth_state(g["spec"]["layers"])
+    model = native.build_model(state, cfg)
+    toks, logits, _ = native.greedy(model, g["prompt"], g["spec"]["new"])
+    assert toks == g["native"]["tokens"]
+    for t, step in enumerate(g["native"]["steps"]):
+        assert logits[t].float()[:, g["probe_ids"]].tolist() == step["probe_vals"]
+    m = native.teacher_forced_margin(model, g["prompt"], toks)
+    assert abs(m - g["teacher_forced"]["margin"]) < 1e-6
