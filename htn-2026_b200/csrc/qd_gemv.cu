@@ -26,6 +26,7 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <mutex>
 
 #include "qd_common.cuh"
 #include "qd_host.h"
@@ -764,4 +765,59 @@ extern "C" int qd_lm_head_argmax(const void* x, int64_t ldx, const void* e_packe
   a.ld_logits = ld_logits;
   a.err = err;
   return launch_any(a, MODE_LM, m, pdl, stream);
+}
+
+// ------------------------------------------------------------------ allocation-free entry point
+// Some callers cannot hand this library a scratch buffer: a host application whose device memory is
+// owned end to end by its own pool allocator and which passes only input and output buffers, a
+// plugin loaded into such a host with no allocator handle of its own, or a latency-critical loop
+// that must not call cudaMalloc (cudaMalloc can synchronize the device and stall other streams).
+// qd_gemv_noalloc serves them: its scratch (tickets and split-K partial sums) is this file-scope
+// device array, which every GPU that loads the library holds until the process exits.
+namespace qd {
+
+constexpr int64_t kNoAllocScratchBytes = 4ll << 20;  // 4 MiB: every decode projection at m <= 8
+static __device__ __align__(256) char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device. In host code the array's name is only a
+// host-side stand-in, so the address is looked up once per device with that device current (the
+// first call on each device) and cached.
+static int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* ptrs[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(QD_ERR_UNSUPPORTED, "device index %d", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(QD_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    ptrs[dev] = p;
+  }
+  *out = ptrs[dev];
+  return QD_OK;
+}
+
+}  // namespace qd
+
+extern "C" int qd_gemv_noalloc(const void* x, int64_t ldx, const void* w_packed, int64_t n, int64_t k, int m,
+                               void* out, int64_t ldo, const void* res, int64_t ldr, const void* norm_w, float eps,
+                               int epilogue, int* err, int pdl, cudaStream_t stream) {
+  Plan p;
+  if (!make_plan(n, k, m, 0, &p)) return qd_gemv_plan(n, k, m, 0, nullptr, nullptr);
+  if (p.bytes > kNoAllocScratchBytes)
+    return set_error(QD_ERR_UNSUPPORTED,
+                     "qd_gemv_noalloc: n=%lld k=%lld m=%d needs %lld B of scratch, above its fixed %lld B",
+                     (long long)n, (long long)k, m, (long long)p.bytes, (long long)kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  // The array keeps the previous call's contents (possibly of another shape): clear the tickets and
+  // the per-CTA argmax slots, everything in front of the partial sums, before this call uses them.
+  cudaError_t e = cudaMemsetAsync(scratch, 0, (size_t)p.off_partials, stream);
+  if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  return qd_gemv(x, ldx, w_packed, n, k, m, out, ldo, res, ldr, norm_w, eps, epilogue, p.grid, scratch,
+                 kNoAllocScratchBytes, err, pdl, stream);
 }

@@ -29,6 +29,8 @@ PROTOTYPES = {
     "qd_gemv_plan": (c_int, [c_int64, c_int64, c_int, c_int, P_INT, P_I64]),
     "qd_gemv": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_void_p, c_int64,
                         c_void_p, c_float, c_int, c_int, c_void_p, c_int64, c_void_p, c_int, c_void_p]),
+    "qd_gemv_noalloc": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_void_p,
+                                c_int64, c_void_p, c_float, c_int, c_void_p, c_int, c_void_p]),
     "qd_qkv_rope_append": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_float, c_void_p,
                                    c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p,
                                    c_void_p, c_int64, c_int64, c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int,

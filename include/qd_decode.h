@@ -85,6 +85,20 @@ int qd_gemv(const void* x, int64_t ldx, const void* w_packed, int64_t n, int64_t
             const void* res, int64_t ldr, const void* norm_w, float eps, int epilogue, int grid, void* scratch,
             int64_t scratch_bytes, int* err, int pdl, cudaStream_t stream);
 
+/* Allocation-free qd_gemv, for callers that cannot allocate device memory: a host whose device
+ * memory is owned end to end by its own pool allocator and which passes only input and output
+ * buffers, a plugin inside such a host with no allocator handle, or a latency-critical loop that must
+ * not call cudaMalloc (it can synchronize the device). Same arguments and results as qd_gemv with
+ * grid_hint 0, but no grid or scratch: scratch is a 4 MiB array compiled into the library, which every
+ * GPU that loads it holds until exit; shapes whose plan needs more return QD_ERR_UNSUPPORTED. The
+ * first call on each device looks up that array's device address (with that device current); make
+ * this first call before any stream capture begins. Every call clears the array's tickets (a memset
+ * on the stream) and reuses the array, so calls that may overlap on the GPU (other streams, other
+ * threads) race and must be serialized by the caller. It has no counterpart in the reference. */
+int qd_gemv_noalloc(const void* x, int64_t ldx, const void* w_packed, int64_t n, int64_t k, int m, void* out,
+                    int64_t ldo, const void* res, int64_t ldr, const void* norm_w, float eps, int epilogue, int* err,
+                    int pdl, cudaStream_t stream);
+
 /* QKV projection with the attention prologue fused into its epilogue. Replaces FastGemm "qkv"
  * (engine/engine.py:472) plus the q/k RMSNorm + RoPE + KV-cache append of FastAttention
  * (engine/kernels/fast.py:240-293) / qk_norm_rope_cache (engine/kernels/fused.py:23-98, pos_mode 1).
