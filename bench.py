@@ -45,9 +45,12 @@ def _args():
     p.add_argument("--batch", type=int, default=1, help="sequences per GPU")
     p.add_argument("--prompt", type=int, default=128)
     p.add_argument("--new", type=int, default=256)
-    p.add_argument("--cpu-steps", type=int, default=16, help="decode steps in the CPU baseline sample")
+    p.add_argument("--cpu-steps", type=int, default=96, help="decode steps in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--kernel", default=None, choices=["qkv", "o", "gu", "down", "lm", "attn"],
+                   help="time one decode kernel alone (small profiling case; random packed weights on the GPU)")
+    p.add_argument("--launches", type=int, default=8)
     return p.parse_args()
 
 
@@ -194,12 +197,15 @@ def gu_kernel_roofline(eng, st, launches_per_layer=3):
 
 
 def _traffic_from_profile():
-    path = os.path.join(REPO, "profiles", "gemv_gate_up_traffic.json")
+    """DRAM bytes per launch of the gate_up GEMV from the committed ncu summary (read + write)."""
+    path = os.path.join(REPO, "profiles", "gemv_gate_up_b1_full.md")
     try:
-        with open(path) as f:
-            return json.load(f)
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return {"traffic_bytes_per_launch": int(line.split(":")[1])}
     except Exception:
-        return None
+        pass
+    return None
 
 
 def run_ours(a):
@@ -240,11 +246,13 @@ def run_ours(a):
         stream = torch.cuda.current_stream()
         t_s, t_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with Clocks(local) as clk:
+            torch.cuda.nvtx.range_push("timed")
             t_s.record(stream)
             for _ in range(K):
                 st.decode_graph.replay()
             t_e.record(stream)
             torch.cuda.synchronize()
+            torch.cuda.nvtx.range_pop()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -323,9 +331,82 @@ def run_ours(a):
         dist.destroy_process_group()
 
 
+def run_kernel(a):
+    """One decode kernel alone, cycling over `--layers` copies of its weights (random, packed on the
+    GPU; > L2 from 2 copies for gate_up, down and the LM head), for profiling. Prints avg µs and GB/s."""
+    import torch
+
+    from decode_b200 import ops
+
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    H, I, V, nq, nkv, D, B, L = 2560, 9728, 151936, 32, 8, 128, a.batch, a.layers
+    g = torch.Generator(device=dev).manual_seed(0)
+    rnd = lambda *shape: (torch.randn(shape, generator=g, device=dev) * 0.02).to(torch.bfloat16)  # noqa: E731
+    x = torch.randn((B, I), generator=g, device=dev).to(torch.bfloat16)
+    xh = x[:, :H].contiguous()
+    nw = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    err = torch.zeros((1,), dtype=torch.int32, device=dev)
+    cap = a.prompt + a.new
+    pos = torch.tensor([cap - 1], dtype=torch.int64, device=dev)
+    if a.kernel == "attn":
+        kc = torch.randn((L, B, nkv, cap, D), generator=g, device=dev).to(torch.bfloat16)
+        vc = torch.randn((L, B, nkv, cap, D), generator=g, device=dev).to(torch.bfloat16)
+        q = torch.randn((B, nq, D), generator=g, device=dev).to(torch.bfloat16)
+        out = torch.empty((B, nq, D), dtype=torch.bfloat16, device=dev)
+        attn = ops.DecodeAttention(B, nq, nkv, cap, dev)
+        fn = lambda i: attn(q, kc[i], vc[i], pos, out, err=err, pdl=False)  # noqa: E731
+        nbytes = 2 * B * nkv * cap * D * 2 + 2 * B * nq * D * 2
+    else:
+        shapes = {"qkv": ((nq + 2 * nkv) * D, H), "o": (H, nq * D), "gu": (2 * I, H), "down": (H, I), "lm": (V, H)}
+        n, k = shapes[a.kernel]
+        ws = [ops.pack_matrix(rnd(n, k)) for _ in range(L)]
+        if a.kernel == "qkv":
+            from engine import rope_tables
+
+            cos, sin = (t.to(dev) for t in rope_tables(cap, D, 5e6))
+            kc = torch.zeros((B, nkv, cap, D), dtype=torch.bfloat16, device=dev)
+            vc = torch.zeros_like(kc)
+            q = torch.empty((B, nq, D), dtype=torch.bfloat16, device=dev)
+            plan = ops.QkvRopeAppend(B, H, nq, nkv, dev)
+            qn = torch.ones(D, dtype=torch.bfloat16, device=dev)
+            fn = lambda i: plan(xh, ws[i], nw, qn, qn, cos, sin, pos, q, kc, vc, err=err, pdl=False)  # noqa: E731
+        elif a.kernel == "lm":
+            plan = ops.LmHeadArgmax(B, V, H, dev)
+            tok = torch.zeros((B,), dtype=torch.int64, device=dev)
+            fn = lambda i: plan(xh, ws[i], nw, tok, err=err, pdl=False)  # noqa: E731
+        else:
+            epi = {"o": ops.Gemv.RES, "gu": ops.Gemv.SWIGLU, "down": ops.Gemv.RES}[a.kernel]
+            plan = ops.Gemv(B, n, k, epi, dev)
+            xin = x[:, :k].contiguous()
+            outb = torch.zeros((B, n), dtype=torch.bfloat16, device=dev)
+            if epi == ops.Gemv.RES:
+                fn = lambda i: plan(xin, ws[i], outb, res=outb, err=err, pdl=False)  # noqa: E731
+            else:
+                fn = lambda i: plan(xin, ws[i], outb[:, : n // 2], norm_w=nw, err=err, pdl=False)  # noqa: E731
+        nbytes = n * k * 2 + B * k * 2 + B * n * 2
+    for i in range(min(3, a.launches)):
+        fn(i % L)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(a.launches):
+        fn(i % L)
+    e.record()
+    e.synchronize()
+    us = s.elapsed_time(e) / a.launches * 1e3
+    assert int(err.item()) == 0
+    peak, kind = _peaks()
+    print(json.dumps({"kernel": a.kernel, "batch": B, "copies": L, "launches": a.launches, "avg_us": round(us, 2),
+                      "algorithmic_bytes": nbytes, "achieved_GBs": round(nbytes / us / 1e3, 1),
+                      "frac_of_peak": round(nbytes / us / 1e3 / peak, 4), "peak": peak, "peak_kind": kind}))
+
+
 def main():
     a = _args()
-    if a.impl == "reference":
+    if a.kernel:
+        run_kernel(a)
+    elif a.impl == "reference":
         run_reference(a)
     else:
         run_ours(a)
