@@ -24,6 +24,7 @@ constexpr uint64_t kWaitLimitNs = 1000000000ull;          // 1 s bound on every 
 constexpr int kErrWaitFull = 1;
 constexpr int kErrWaitEmpty = 2;
 constexpr int kErrDrain = 4;
+constexpr int kErrDep = 32;  // a wait for another CTA's results (persistent step kernel) timed out
 
 __host__ __device__ __forceinline__ int64_t packed_offset_elems(int64_t n, int64_t k, int64_t kblocks) {
   const int64_t g = n >> 7, r = n & 127, kb = k >> 6, c = (k & 63) >> 3, e = k & 7;
@@ -99,6 +100,15 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       ::"r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(policy)
       : "memory");
 }
+// Fire-and-forget prefetch of a global range into L2 (no completion tracking).
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -115,24 +125,35 @@ __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-__device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ uint2 ld_cg_v2(const void* p) {
-  uint2 v;
-  asm volatile("ld.global.cg.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ float ld_cg_f32(const float* p) {
-  float v;
-  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
-  return v;
-}
+// L2-only loads (bypass L1, which is not coherent across SMs) of data produced by other CTAs or
+// by the previous kernel. Compiler intrinsics rather than volatile asm, so independent loads are
+// issued back to back; they are never moved across a barrier or fence (those clobber memory).
+__device__ __forceinline__ uint4 ld_cg_v4(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
+__device__ __forceinline__ uint2 ld_cg_v2(const void* p) { return __ldcg(reinterpret_cast<const uint2*>(p)); }
+__device__ __forceinline__ float ld_cg_f32(const float* p) { return __ldcg(p); }
 __device__ __forceinline__ int64_t ld_cg_s64(const int64_t* p) {
-  int64_t v;
-  asm volatile("ld.global.cg.s64 %0, [%1];" : "=l"(v) : "l"(p));
+  return (int64_t)__ldcg(reinterpret_cast<const long long*>(p));
+}
+
+// gpu-scope release add / acquire load for the inter-CTA completion counters and tickets. The
+// pattern is: every thread writes, CTA barrier, one thread releases (release is cumulative over what
+// the barrier made visible to it); the reader acquires in one thread, then a CTA barrier.
+__device__ __forceinline__ void red_release_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int ld_volatile(const int* p) {
+  int v;
+  asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 

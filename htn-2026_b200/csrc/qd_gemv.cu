@@ -1,24 +1,6 @@
-// Streaming BF16 GEMV / skinny GEMM (m <= 8 rows) for the decode step, sm_100a.
-//
-// One persistent-style launch per projection. The packed weight matrix is a sequence of 16 KiB
-// blocks (128 rows x 64 columns, see qd_common.cuh); the T blocks are split stream-K style into G
-// contiguous ranges, one per CTA (G = one CTA per SM by default), so every CTA streams the same
-// number of bytes +-1 block whatever the matrix shape. Inside a CTA a producer warp keeps a ring of
-// NST blocks in flight with one-dimensional bulk copies (TMA, completion on an mbarrier); eight
-// consumer warps multiply each block by the activation rows held in shared memory with fp32 FMAs,
-// accumulating per (row, activation row) in registers while the block's row group stays the same.
-//
-// When a CTA leaves a row group it reduces its partial sums (warp shuffles) into shared memory.
-// If it covered the whole group it runs the epilogue directly; otherwise it stores the partial to
-// scratch and takes a ticket: the CTA whose blocks complete the group sums every partial of that
-// group in fixed order (deterministic) and runs the epilogue. No spin waits between CTAs.
-//
-// Epilogues (all BF16 rounding points of transformers' modeling_qwen3 kept):
-//   STORE, RES (residual add), SWIGLU (gate/up interleaved), QKV (per-head RMSNorm + RoPE + KV
-//   append / q store), LM (logits, argmax with lowest index on ties, global argmax by the last CTA,
-//   position advance).
-// Prologue: the activation rows are staged in shared memory, RMSNorm-ed when a norm weight is given
-// (each CTA computes the row statistics itself, so no statistics travel between kernels).
+// Streaming BF16 GEMV / skinny GEMM (m <= 8 rows) for the decode step, sm_100a: one launch per
+// projection. The device code (stream-K partition, TMA ring, split-K tickets, fused epilogues) is in
+// qd_gemv_dev.cuh, shared with the persistent decode-step kernel.
 //
 // Launched with programmatic dependent launch: the producer warp starts streaming weights (which no
 // kernel writes) before the preceding kernel has finished; consumers wait for it before touching
@@ -28,56 +10,13 @@
 #include <cstdlib>
 #include <mutex>
 
-#include "qd_common.cuh"
-#include "qd_host.h"
+#include "qd_gemv_dev.cuh"
+#include "qd_plan.h"
 
 namespace qd {
 
-enum { MODE_STORE = 0, MODE_RES = 1, MODE_SWIGLU = 2, MODE_QKV = 3, MODE_LM = 4 };
-
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kThreads = kConsumers + 32;
-
-struct GemvArgs {
-  const __nv_bfloat16* x;
-  int64_t ldx;
-  const char* w;
-  int64_t n, n_valid, k;
-  int kblocks;
-  int64_t total;
-  int grid, nst;
-  __nv_bfloat16* out;
-  int64_t ldo;
-  const __nv_bfloat16* res;
-  int64_t ldr;
-  const __nv_bfloat16* norm_w;
-  float eps;
-  float* partials;
-  int* tickets;
-  int smax;
-  int* err;
-  // QKV
-  const __nv_bfloat16 *q_norm, *k_norm, *cos, *sin;
-  const int64_t* pos;
-  int64_t cap;
-  int nq, nkv;
-  __nv_bfloat16 *q_out, *k_cache, *v_cache;
-  int64_t cs_b, cs_h;
-  __nv_bfloat16* raw_out;
-  // LM
-  int64_t* tok;
-  int64_t* pos_inc;
-  int inc_pos;
-  __nv_bfloat16* logits;
-  int64_t ld_logits;
-  float* cta_val;
-  int* cta_idx;
-  int* lm_ticket;
-};
-
 struct SmemLayout {
-  int ring, xs, red, wsum, lmv, lmi, flags, bars, total;
+  int ring, xs, red, wsum, lmv, lmi, flags, aux, bars, total;
 };
 
 __host__ __device__ inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
@@ -99,166 +38,32 @@ __host__ __device__ inline SmemLayout smem_layout(int M, int64_t k, int nst) {
   off += 8 * 4;
   L.flags = off;
   off += 16;
+  L.aux = off;
+  off += 256 * 4;
   L.bars = align_up(off, 8);
   off = L.bars + 2 * nst * 8;
   L.total = align_up(off, 128);
   return L;
 }
 
-// ------------------------------------------------------------------ epilogues (256 consumer threads)
-template <int M, int MODE>
-__device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum, float* lmv, int* lmi, int tid) {
-  if constexpr (MODE == MODE_STORE || MODE == MODE_RES) {
-    for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
-      const int m = idx >> 7, r = idx & 127;
-      const int64_t n = (int64_t)g * kBlockRows + r;
-      float v = bf16r(red[idx]);
-      if constexpr (MODE == MODE_RES) {
-        const uint16_t rb = __ldcg(reinterpret_cast<const unsigned short*>(a.res + m * a.ldr + n));
-        v = __uint_as_float((uint32_t)rb << 16) + v;
-      }
-      a.out[m * a.ldo + n] = __float2bfloat16_rn(v);
-    }
-  } else if constexpr (MODE == MODE_SWIGLU) {
-    for (int idx = tid; idx < M * 64; idx += kConsumers) {
-      const int m = idx >> 6, j = idx & 63;
-      const float gv = bf16r(red[m * kBlockRows + j]);
-      const float uv = bf16r(red[m * kBlockRows + 64 + j]);
-      const float s = bf16r(gv / (1.0f + expf(-gv)));
-      a.out[m * a.ldo + (int64_t)g * 64 + j] = __float2bfloat16_rn(s * uv);
-    }
-  } else if constexpr (MODE == MODE_QKV) {
-    const int64_t p = ld_cg_s64(a.pos);
-    const int warp = tid >> 5, lane = tid & 31;
-    if (p < 0 || p >= a.cap) {  // never write outside the cache or read outside the RoPE tables
-      if (tid == 0 && a.err) atomicOr(a.err, QD_DEVERR_POS);
-      return;
-    }
-    // BF16 projection output
-    for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
-      const float v = bf16r(red[idx]);
-      red[idx] = v;
-      if (a.raw_out) a.raw_out[(idx >> 7) * a.n + (int64_t)g * kBlockRows + (idx & 127)] = __float2bfloat16_rn(v);
-    }
-    if (g >= a.nq + a.nkv) {  // V head: append as is
-      const int kvh = g - a.nq - a.nkv;
-      for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
-        const int m = idx >> 7, r = idx & 127;
-        a.v_cache[m * a.cs_b + kvh * a.cs_h + p * 128 + r] = __float2bfloat16_rn(red[idx]);
-      }
-      return;
-    }
-    // per-head RMSNorm (Qwen3RMSNorm over 128): sum of squares per activation row
-    for (int base = 0; base < M * kBlockRows; base += kConsumers) {
-      const int idx = base + tid;
-      float sq = 0.f;
-      if (idx < M * kBlockRows) sq = red[idx] * red[idx];
-      sq = warp_sum(sq);
-      if (lane == 0 && idx < M * kBlockRows) wsum[idx >> 5] = sq;  // one slot per 32 rows
-    }
-    named_bar(1, kConsumers);
-    const __nv_bfloat16* nw = (g < a.nq) ? a.q_norm : a.k_norm;
-    for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
-      const int m = idx >> 7, r = idx & 127;
-      const float var = (wsum[m * 4 + 0] + wsum[m * 4 + 1] + wsum[m * 4 + 2] + wsum[m * 4 + 3]) / 128.0f;
-      const float rstd = 1.0f / sqrtf(var + a.eps);
-      const float y = bf16r(bf16_to_f(nw[r]) * bf16r(red[idx] * rstd));
-      red[idx] = y;  // each thread rewrites only its own entries; partners are read after the barrier
-    }
-    named_bar(1, kConsumers);
-    for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
-      const int m = idx >> 7, r = idx & 127;
-      const float y = red[idx];
-      const float yp = red[(idx & ~127) | (r ^ 64)];
-      const float c = bf16_to_f(a.cos[p * 128 + r]);
-      const float s = bf16_to_f(a.sin[p * 128 + r]);
-      // q*cos + rotate_half(q)*sin with every product a BF16 tensor (rotate_half = cat(-q2, q1))
-      const float rot = (r < 64) ? bf16r(-yp * s) : bf16r(yp * s);
-      const __nv_bfloat16 o = __float2bfloat16_rn(bf16r(y * c) + rot);
-      if (g < a.nq) {
-        a.q_out[((int64_t)m * a.nq + g) * 128 + r] = o;
-      } else {
-        a.k_cache[m * a.cs_b + (g - a.nq) * a.cs_h + p * 128 + r] = o;
-      }
-    }
-    (void)warp;
-  } else if constexpr (MODE == MODE_LM) {
-    const int warp = tid >> 5, lane = tid & 31;
-    for (int base = 0; base < M * kBlockRows; base += kConsumers) {
-      const int idx = base + tid;
-      float v = -INFINITY;
-      int n = 0x7fffffff;
-      if (idx < M * kBlockRows) {
-        const int m = idx >> 7, r = idx & 127;
-        const int64_t row = (int64_t)g * kBlockRows + r;
-        if (row < a.n_valid) {
-          v = bf16r(red[idx]);
-          n = (int)row;
-          if (a.logits) a.logits[m * a.ld_logits + row] = __float2bfloat16_rn(v);
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-        const int on = __shfl_xor_sync(0xffffffffu, n, o);
-        if (ov > v || (ov == v && on < n)) {
-          v = ov;
-          n = on;
-        }
-      }
-      if (lane == 0 && idx < M * kBlockRows) {
-        wsum[(idx >> 5) * 2] = v;
-        reinterpret_cast<int*>(wsum)[(idx >> 5) * 2 + 1] = n;
-      }
-    }
-    named_bar(1, kConsumers);
-    if (tid < M) {
-      float bv = lmv[tid];
-      int bi = lmi[tid];
-      for (int q = 0; q < 4; ++q) {
-        const float v = wsum[(tid * 4 + q) * 2];
-        const int n = reinterpret_cast<int*>(wsum)[(tid * 4 + q) * 2 + 1];
-        if (v > bv || (v == bv && n < bi)) {
-          bv = v;
-          bi = n;
-        }
-      }
-      lmv[tid] = bv;
-      lmi[tid] = bi;
-    }
-    (void)warp;
-  }
-}
-
 template <int M, int MODE>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvArgs a) {
   extern __shared__ __align__(1024) char smem[];
   const SmemLayout L = smem_layout(M, a.k, a.nst);
-  char* ring = smem + L.ring;
+  const Ring R{smem + L.ring, smem_u32(smem + L.bars), a.nst};
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem + L.xs);
   float* red = reinterpret_cast<float*>(smem + L.red);
   float* wsum = reinterpret_cast<float*>(smem + L.wsum);
   float* lmv = reinterpret_cast<float*>(smem + L.lmv);
   int* lmi = reinterpret_cast<int*>(smem + L.lmi);
   int* flags = reinterpret_cast<int*>(smem + L.flags);
-  const uint32_t bars = smem_u32(smem + L.bars);
-  const int nst = a.nst;
-  auto full_bar = [&](int s) { return bars + 8u * s; };
-  auto empty_bar = [&](int s) { return bars + 8u * (nst + s); };
+  float* aux = reinterpret_cast<float*>(smem + L.aux);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int cta = blockIdx.x;
-  const int64_t b_begin = part_begin(a.total, a.grid, cta);
-  const int64_t b_end = part_begin(a.total, a.grid, cta + 1);
-  const int nblk = (int)(b_end - b_begin);
-
   if (tid == 0) {
-    for (int s = 0; s < nst; ++s) {
-      mbar_init(full_bar(s), 1);
-      mbar_init(empty_bar(s), kConsumerWarps);
-    }
-    fence_mbar_init();
+    ring_init(R);
     flags[0] = 0;  // blocks issued by the producer
     flags[1] = 0;  // ticket result broadcast
   }
@@ -269,263 +74,29 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   __syncthreads();
 
   if (warp == kConsumerWarps) {
-    // ------------------------------------------------------------ producer warp
-    if (lane == 0) {
-      const uint64_t pol = policy_evict_first();
-      int issued = 0;
-      for (int it = 0; it < nblk; ++it) {
-        const int s = it % nst;
-        const int round = it / nst;
-        if (round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1, a.err, kErrWaitEmpty)) break;
-        mbar_arrive_expect_tx(full_bar(s), kBlockBytes);
-        bulk_g2s(smem_u32(ring + s * kBlockBytes), a.w + (b_begin + it) * (int64_t)kBlockBytes, kBlockBytes,
-                 full_bar(s), pol);
-        issued = it + 1;
-      }
+    if (lane == 0) {  // producer: this CTA's contiguous range of weight blocks
+      const int64_t b0 = part_begin(a.total, a.grid, cta), b1 = part_begin(a.total, a.grid, cta + 1);
+      int slot = 0, round = 0, issued = 0;
+      produce_range_prefetch(R, slot, round, issued, a.w + b0 * (int64_t)kBlockBytes, b1 - b0, a.prefetch,
+                             policy_evict_first(), a.err);
       flags[0] = issued;
     }
   } else {
-    // ------------------------------------------------------------ consumers
     grid_dep_wait();
     grid_dep_launch();
-    // stage activations (and RMSNorm them) in shared memory
-    const int kv8 = (int)(a.k >> 3);
-    for (int m = 0; m < M; ++m) {
-      float sq = 0.f;
-      for (int q = tid; q < kv8; q += kConsumers) {
-        const uint4 v = ld_cg_v4(a.x + m * a.ldx + q * 8);
-        *reinterpret_cast<uint4*>(xs + (int64_t)m * a.k + q * 8) = v;
-        if (a.norm_w) {
-          const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float lo = bf_lo(u[e]), hi = bf_hi(u[e]);
-            sq = fmaf(lo, lo, sq);
-            sq = fmaf(hi, hi, sq);
-          }
-        }
-      }
-      if (a.norm_w) {
-        sq = warp_sum(sq);
-        if (lane == 0) wsum[m * kConsumerWarps + warp] = sq;
-      }
-    }
-    named_bar(1, kConsumers);
-    if (a.norm_w) {
-      // Qwen3RMSNorm: w * bf16(x * rsqrt(mean(x^2) + eps)), rounded to BF16
-      for (int m = 0; m < M; ++m) {
-        float ss = 0.f;
-#pragma unroll
-        for (int w8 = 0; w8 < kConsumerWarps; ++w8) ss += wsum[m * kConsumerWarps + w8];
-        const float rstd = 1.0f / sqrtf(ss / (float)a.k + a.eps);
-        for (int q = tid; q < kv8; q += kConsumers) {
-          uint4* p = reinterpret_cast<uint4*>(xs + (int64_t)m * a.k + q * 8);
-          const uint4 xv = *p;
-          const uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + q * 8);
-          const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
-          const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
-          uint32_t o[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float lo = bf16r(bf_lo(wu[e]) * bf16r(bf_lo(xu[e]) * rstd));
-            const float hi = bf16r(bf_hi(wu[e]) * bf16r(bf_hi(xu[e]) * rstd));
-            o[e] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
-          }
-          *p = make_uint4(o[0], o[1], o[2], o[3]);
-        }
-      }
-      named_bar(1, kConsumers);
-    }
-
-    // per-lane geometry inside a 128x64 block
-    const int rsub = lane >> 3;  // 0..3
-    const int c = lane & 7;      // logical 16-byte chunk (8 columns)
-    int roff[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = 16 * warp + rsub + 4 * i;
-      roff[i] = r * 128 + ((c ^ (r & 7)) << 4);
-    }
-
-    float acc[4][M];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int m = 0; m < M; ++m) acc[i][m] = 0.f;
-
+    stage_x<M>(a, xs, wsum, tid);
+    int slot = 0, phase = 0;
     bool ok = true;
-    int64_t seg_first = b_begin;  // first block of the current segment
-    int g = (int)(b_begin / a.kblocks);
-    int kb = (int)(b_begin - (int64_t)g * a.kblocks) - 1;
-    int s = -1, phase = 0;
-    for (int it = 0; it < nblk; ++it) {
-      const int64_t b = b_begin + it;
-      if (++kb == a.kblocks) {
-        kb = 0;
-        ++g;
-      }
-      if (++s == nst) {
-        s = 0;
-        phase ^= 1;
-      }
-      if (ok) ok = mbar_wait(full_bar(s), phase, a.err, kErrWaitFull);
-      {
-        const char* blk = ring + s * kBlockBytes;
-        float xv[M][8];
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-          const uint4 u = *reinterpret_cast<const uint4*>(xs + (int64_t)m * a.k + kb * 64 + c * 8);
-          xv[m][0] = bf_lo(u.x);
-          xv[m][1] = bf_hi(u.x);
-          xv[m][2] = bf_lo(u.y);
-          xv[m][3] = bf_hi(u.y);
-          xv[m][4] = bf_lo(u.z);
-          xv[m][5] = bf_hi(u.z);
-          xv[m][6] = bf_lo(u.w);
-          xv[m][7] = bf_hi(u.w);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint4 u = *reinterpret_cast<const uint4*>(blk + roff[i]);
-          const float w8[8] = {bf_lo(u.x), bf_hi(u.x), bf_lo(u.y), bf_hi(u.y),
-                               bf_lo(u.z), bf_hi(u.z), bf_lo(u.w), bf_hi(u.w)};
-#pragma unroll
-          for (int m = 0; m < M; ++m)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[i][m] = fmaf(w8[e], xv[m][e], acc[i][m]);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty_bar(s));
-
-      const bool seg_end = (kb == a.kblocks - 1) || (it == nblk - 1);
-      if (!seg_end) continue;
-
-      // ---------------------------------------------------------- flush the segment of group g
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-          float v = acc[i][m];
-          v += __shfl_xor_sync(0xffffffffu, v, 4);
-          v += __shfl_xor_sync(0xffffffffu, v, 2);
-          v += __shfl_xor_sync(0xffffffffu, v, 1);
-          acc[i][m] = 0.f;
-          if (c == 0) red[m * kBlockRows + 16 * warp + rsub + 4 * i] = v;
-        }
-      named_bar(1, kConsumers);
-      const int64_t gb0 = (int64_t)g * a.kblocks;
-      const int nseg_blk = (int)(b + 1 - seg_first);
-      if (seg_first == gb0 && nseg_blk == a.kblocks) {
-        finalize_group<M, MODE>(a, g, red, wsum, lmv, lmi, tid);
-      } else {
-        const int c_lo = part_owner(a.total, a.grid, gb0);
-        float* dst = a.partials + ((int64_t)g * a.smax + (cta - c_lo)) * (M * kBlockRows);
-        for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) dst[idx] = red[idx];
-        __threadfence();
-        named_bar(1, kConsumers);
-        if (tid == 0) {
-          const int old = atomicAdd(a.tickets + g, nseg_blk);
-          flags[1] = (old + nseg_blk == a.kblocks) ? 1 : 0;
-        }
-        named_bar(1, kConsumers);
-        if (flags[1]) {
-          __threadfence();
-          const int c_hi = part_owner(a.total, a.grid, gb0 + a.kblocks - 1);
-          for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
-            float sum = 0.f;
-            for (int cc = c_lo; cc <= c_hi; ++cc) {
-              const int64_t s0 = part_begin(a.total, a.grid, cc), s1 = part_begin(a.total, a.grid, cc + 1);
-              if ((s1 < gb0 + a.kblocks ? s1 : gb0 + a.kblocks) <= (s0 > gb0 ? s0 : gb0)) continue;
-              sum += ld_cg_f32(a.partials + ((int64_t)g * a.smax + (cc - c_lo)) * (M * kBlockRows) + idx);
-            }
-            red[idx] = sum;
-          }
-          named_bar(1, kConsumers);
-          finalize_group<M, MODE>(a, g, red, wsum, lmv, lmi, tid);
-          if (tid == 0) atomicExch(a.tickets + g, 0);
-        }
-      }
-      named_bar(1, kConsumers);
-      seg_first = b + 1;
-    }
-
-    if constexpr (MODE == MODE_LM) {
-      // global argmax: every CTA posts its best per row; the last CTA reduces them in full
-      if (tid < M) {
-        a.cta_val[tid * a.grid + cta] = lmv[tid];
-        a.cta_idx[tid * a.grid + cta] = lmi[tid];
-      }
-      __threadfence();
-      named_bar(1, kConsumers);
-      if (tid == 0) flags[1] = (atomicAdd(a.lm_ticket, 1) == a.grid - 1) ? 1 : 0;
-      named_bar(1, kConsumers);
-      if (flags[1]) {
-        __threadfence();
-        for (int m = 0; m < M; ++m) {
-          float bv = -INFINITY;
-          int bi = 0x7fffffff;
-          for (int q = tid; q < a.grid; q += kConsumers) {
-            const float v = ld_cg_f32(a.cta_val + m * a.grid + q);
-            const int n = (int)__ldcg(a.cta_idx + m * a.grid + q);
-            if (v > bv || (v == bv && n < bi)) {
-              bv = v;
-              bi = n;
-            }
-          }
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int on = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && on < bi)) {
-              bv = ov;
-              bi = on;
-            }
-          }
-          if (lane == 0) {
-            wsum[warp * 2] = bv;
-            reinterpret_cast<int*>(wsum)[warp * 2 + 1] = bi;
-          }
-          named_bar(1, kConsumers);
-          if (tid == 0) {
-            for (int w8 = 1; w8 < kConsumerWarps; ++w8) {
-              const float v = wsum[w8 * 2];
-              const int n = reinterpret_cast<int*>(wsum)[w8 * 2 + 1];
-              if (v > bv || (v == bv && n < bi)) {
-                bv = v;
-                bi = n;
-              }
-            }
-            a.tok[m] = (int64_t)bi;
-          }
-          named_bar(1, kConsumers);
-        }
-        if (tid == 0) {
-          if (a.inc_pos && a.pos_inc) a.pos_inc[0] = a.pos_inc[0] + 1;
-          atomicExch(a.lm_ticket, 0);
-        }
-      }
-    }
-    (void)ok;
+    consume_blocks<M, MODE>(a, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
+    if constexpr (MODE == MODE_LM) lm_global_argmax<M>(a, cta, wsum, lmv, lmi, flags, tid);
   }
-
   __syncthreads();
-  // drain: never exit with a bulk copy still writing this CTA's shared memory
-  if (tid == 0) {
-    const int issued = flags[0];
-    for (int it = issued > nst ? issued - nst : 0; it < issued; ++it)
-      if (!mbar_wait(full_bar(it % nst), (it / nst) & 1, a.err, kErrDrain)) break;
-  }
+  if (tid == 0) ring_drain(R, flags[0], a.err);
 }
 
 // ------------------------------------------------------------------ host side
-struct Plan {
-  int grid, smax, nst;
-  int64_t groups, total;
-  int64_t off_tickets, off_lm_ticket, off_cta_val, off_cta_idx, off_partials, bytes;
-};
 
-static int env_int(const char* name, int dflt) {
+int env_int(const char* name, int dflt) {
   const char* v = getenv(name);
   return (v && *v) ? atoi(v) : dflt;
 }
@@ -537,6 +108,12 @@ static int ctas_per_sm() {
   return c < 1 ? 1 : (c > 4 ? 4 : c);
 }
 
+// QD_PREFETCH_BLOCKS: blocks each CTA keeps prefetched into L2 beyond its ring (default 8).
+int prefetch_blocks() {
+  const int v = env_int("QD_PREFETCH_BLOCKS", 8);
+  return v < 0 ? 0 : (v > 256 ? 256 : v);
+}
+
 static int default_nst(int M, int64_t k) {
   const int fixed = smem_layout(M, k, 0).total;
   const int budget = (ctas_per_sm() == 1 ? 227 * 1024 : 228 * 1024 / ctas_per_sm() - 1024);
@@ -546,7 +123,17 @@ static int default_nst(int M, int64_t k) {
   return nst < 2 ? 2 : nst;
 }
 
-static bool make_plan(int64_t n_rows, int64_t k, int M, int grid_hint, Plan* p) {
+int stream_k_smax(int64_t groups, int kblocks, int grid) {
+  const int64_t total = groups * kblocks;
+  int smax = 1;
+  for (int64_t gi = 0; gi < groups; ++gi) {
+    const int lo = part_owner(total, grid, gi * kblocks), hi = part_owner(total, grid, gi * kblocks + kblocks - 1);
+    if (hi - lo + 1 > smax) smax = hi - lo + 1;
+  }
+  return smax;
+}
+
+bool make_plan(int64_t n_rows, int64_t k, int M, int grid_hint, Plan* p) {
   if (n_rows <= 0 || k <= 0 || n_rows % kBlockRows || k % kBlockCols || M < 1 || M > 8) return false;
   const int kblocks = (int)(k / kBlockCols);
   p->groups = n_rows / kBlockRows;
@@ -555,11 +142,7 @@ static bool make_plan(int64_t n_rows, int64_t k, int M, int grid_hint, Plan* p) 
   if (g > p->total) g = (int)p->total;
   if (g < 1) g = 1;
   p->grid = g;
-  int smax = 1;
-  for (int64_t gi = 0; gi < p->groups; ++gi) {
-    const int lo = part_owner(p->total, g, gi * kblocks), hi = part_owner(p->total, g, gi * kblocks + kblocks - 1);
-    if (hi - lo + 1 > smax) smax = hi - lo + 1;
-  }
+  const int smax = stream_k_smax(p->groups, kblocks, g);
   p->smax = smax;
   p->nst = default_nst(M, k);
   int64_t off = 0;
@@ -631,6 +214,7 @@ static bool fill_common(GemvArgs& a, const Plan& p, const void* x, int64_t ldx, 
   a.total = p.total;
   a.grid = p.grid;
   a.nst = p.nst;
+  a.prefetch = prefetch_blocks();
   a.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
   a.eps = eps;
   char* sc = static_cast<char*>(scratch);

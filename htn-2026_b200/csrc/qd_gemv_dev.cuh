@@ -1,0 +1,531 @@
+// Device side of the streaming GEMV, shared by the per-projection kernel (qd_gemv.cu) and the
+// persistent decode-step kernel (qd_step.cu).
+//
+// A projection's packed weight matrix is a sequence of 16 KiB blocks (128 rows x 64 columns, see
+// qd_common.cuh). Its T blocks are split stream-K into G contiguous ranges, one per CTA, so every
+// CTA streams the same bytes +-1 block whatever the matrix shape. A producer warp keeps a ring of
+// blocks in flight with one-dimensional bulk copies (TMA, completion on an mbarrier); eight consumer
+// warps multiply each block by the activation rows staged in shared memory with fp32 FMAs and
+// accumulate per (row, activation row) in registers while the block's row group stays the same.
+//
+// Leaving a row group, a CTA reduces its partial sums (warp shuffles) into shared memory. If it
+// covered the whole group it runs the epilogue directly; otherwise it stores the partial to scratch
+// and takes a ticket: the CTA whose blocks complete the group sums every partial of that group in
+// fixed order (deterministic for a fixed grid) and runs the epilogue. No CTA waits on another here.
+//
+// Epilogues keep every BF16 rounding point of transformers' modeling_qwen3:
+//   STORE   out = bf16(y)
+//   RES     out = bf16(res + bf16(y))                      (residual add, may be in place)
+//   SWIGLU  out = bf16(bf16(silu(bf16 g)) * bf16 u)        (gate/up interleaved per 128-row group)
+//   QKV     per-head RMSNorm + RoPE (BF16 products), q store, K/V append at the device position
+//   LM      BF16 logits, argmax with the lowest index on ties, folded into a per-CTA best
+#pragma once
+
+#include "qd_common.cuh"
+#include "qd_host.h"
+
+namespace qd {
+
+enum { MODE_STORE = 0, MODE_RES = 1, MODE_SWIGLU = 2, MODE_QKV = 3, MODE_LM = 4 };
+
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kThreads = kConsumers + 32;  // + one producer warp
+constexpr int kBarConsumers = 1;           // named barrier of the 256 consumer threads
+constexpr int kStageBatch = 5;             // activation chunks per thread in flight (k <= 10240 in one pass)
+
+struct GemvArgs {
+  const __nv_bfloat16* x;
+  int64_t ldx;
+  const char* w;
+  int64_t n, n_valid, k;
+  int kblocks;
+  int64_t total;
+  int grid, nst, prefetch;
+  __nv_bfloat16* out;
+  int64_t ldo;
+  const __nv_bfloat16* res;
+  int64_t ldr;
+  const __nv_bfloat16* norm_w;
+  float eps;
+  float* partials;
+  int* tickets;
+  int smax;
+  int* err;
+  int* done;  // optional: +1 (release) per finalized row group
+  // QKV
+  const __nv_bfloat16 *q_norm, *k_norm, *cos, *sin;
+  const int64_t* pos;
+  int64_t cap;
+  int nq, nkv;
+  __nv_bfloat16 *q_out, *k_cache, *v_cache;
+  int64_t cs_b, cs_h;
+  __nv_bfloat16* raw_out;
+  // LM
+  int64_t* tok;
+  int64_t* pos_inc;
+  int inc_pos;
+  __nv_bfloat16* logits;
+  int64_t ld_logits;
+  float* cta_val;
+  int* cta_idx;
+  int* lm_ticket;
+};
+
+// Ring of 16 KiB blocks in shared memory with a full and an empty mbarrier per slot.
+struct Ring {
+  char* base;
+  uint32_t bars;
+  int nst;
+  __device__ __forceinline__ uint32_t full(int s) const { return bars + 8u * s; }
+  __device__ __forceinline__ uint32_t empty(int s) const { return bars + 8u * (nst + s); }
+};
+
+__device__ __forceinline__ void ring_init(const Ring& R) {
+  for (int s = 0; s < R.nst; ++s) {
+    mbar_init(R.full(s), 1);
+    mbar_init(R.empty(s), kConsumerWarps);
+  }
+  fence_mbar_init();
+}
+
+// Producer (one lane): issue `nblk` consecutive blocks starting at `src`. slot / round carry across
+// calls so several projections can share one ring. Returns false if a wait for a free slot expired.
+__device__ __forceinline__ bool produce_blocks(const Ring& R, int& slot, int& round, int& issued, const char* src,
+                                               int64_t nblk, uint64_t pol, int* err) {
+  for (int64_t i = 0; i < nblk; ++i) {
+    if (round > 0 && !mbar_wait(R.empty(slot), (round - 1) & 1, err, kErrWaitEmpty)) return false;
+    mbar_arrive_expect_tx(R.full(slot), kBlockBytes);
+    bulk_g2s(smem_u32(R.base + slot * kBlockBytes), src + i * (int64_t)kBlockBytes, kBlockBytes, R.full(slot), pol);
+    ++issued;
+    if (++slot == R.nst) {
+      slot = 0;
+      ++round;
+    }
+  }
+  return true;
+}
+
+// Producer over one contiguous range of blocks with an L2 lookahead: before waiting for a free ring
+// slot it keeps `ahead` blocks beyond the next issue prefetched into L2, so HBM keeps streaming while
+// the ring is full (the later bulk copies then hit L2).
+__device__ __forceinline__ bool produce_range_prefetch(const Ring& R, int& slot, int& round, int& issued,
+                                                       const char* src, int64_t nblk, int ahead, uint64_t pol,
+                                                       int* err) {
+  int64_t pf = 0;
+  for (int64_t i = 0; i < nblk; ++i) {
+    for (; pf < nblk && pf <= i + ahead; ++pf) prefetch_l2(src + pf * (int64_t)kBlockBytes, kBlockBytes);
+    if (round > 0 && !mbar_wait(R.empty(slot), (round - 1) & 1, err, kErrWaitEmpty)) return false;
+    mbar_arrive_expect_tx(R.full(slot), kBlockBytes);
+    bulk_g2s(smem_u32(R.base + slot * kBlockBytes), src + i * (int64_t)kBlockBytes, kBlockBytes, R.full(slot), pol);
+    ++issued;
+    if (++slot == R.nst) {
+      slot = 0;
+      ++round;
+    }
+  }
+  return true;
+}
+
+// Never leave with a bulk copy still writing shared memory: wait (bounded) for the last `nst`
+// issued blocks. Call from one thread after every consumer is done.
+__device__ __forceinline__ void ring_drain(const Ring& R, int issued, int* err) {
+  for (int it = issued > R.nst ? issued - R.nst : 0; it < issued; ++it)
+    if (!mbar_wait(R.full(it % R.nst), (it / R.nst) & 1, err, kErrDrain)) break;
+}
+
+__device__ __forceinline__ void signal_done(int* done, int tid) {
+  named_bar(kBarConsumers, kConsumers);
+  if (tid == 0) red_release_add(done, 1);
+}
+
+// Stage the activation rows x[0..M) in shared memory, RMSNorm-ed when a.norm_w is set:
+// xs = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))) (Qwen3RMSNorm's cast placement). 256 threads.
+template <int M>
+__device__ void stage_x(const GemvArgs& a, __nv_bfloat16* xs, float* wsum, int tid) {
+  const int warp = tid >> 5, lane = tid & 31;
+  const int kv8 = (int)(a.k >> 3);
+  for (int m = 0; m < M; ++m) {
+    float sq = 0.f;
+    for (int q0 = 0; q0 < kv8; q0 += kStageBatch * kConsumers) {
+      uint4 v[kStageBatch];  // all of this thread's loads in flight before the first is used
+#pragma unroll
+      for (int j = 0; j < kStageBatch; ++j) {
+        const int q = q0 + j * kConsumers + tid;
+        v[j] = q < kv8 ? ld_cg_v4(a.x + m * a.ldx + q * 8) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int j = 0; j < kStageBatch; ++j) {
+        const int q = q0 + j * kConsumers + tid;
+        if (q >= kv8) continue;
+        *reinterpret_cast<uint4*>(xs + (int64_t)m * a.k + q * 8) = v[j];
+        if (a.norm_w) {
+          const uint32_t u[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float lo = bf_lo(u[e]), hi = bf_hi(u[e]);
+            sq = fmaf(lo, lo, sq);
+            sq = fmaf(hi, hi, sq);
+          }
+        }
+      }
+    }
+    if (a.norm_w) {
+      sq = warp_sum(sq);
+      if (lane == 0) wsum[m * kConsumerWarps + warp] = sq;
+    }
+  }
+  named_bar(kBarConsumers, kConsumers);
+  if (a.norm_w) {
+    for (int m = 0; m < M; ++m) {
+      float ss = 0.f;
+#pragma unroll
+      for (int w8 = 0; w8 < kConsumerWarps; ++w8) ss += wsum[m * kConsumerWarps + w8];
+      const float rstd = 1.0f / sqrtf(ss / (float)a.k + a.eps);
+      for (int q = tid; q < kv8; q += kConsumers) {
+        uint4* p = reinterpret_cast<uint4*>(xs + (int64_t)m * a.k + q * 8);
+        const uint4 xv = *p;
+        const uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + q * 8);
+        const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
+        const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float lo = bf16r(bf_lo(wu[e]) * bf16r(bf_lo(xu[e]) * rstd));
+          const float hi = bf16r(bf_hi(wu[e]) * bf16r(bf_hi(xu[e]) * rstd));
+          o[e] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
+        }
+        *p = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    named_bar(kBarConsumers, kConsumers);
+  }
+}
+
+// ------------------------------------------------------------------ epilogues (256 consumer threads)
+template <int M, int MODE>
+__device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum, float* lmv, int* lmi,
+                               const float* aux, const int* flags, int tid) {
+  if constexpr (MODE == MODE_STORE || MODE == MODE_RES) {
+    for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
+      const int m = idx >> 7, r = idx & 127;
+      const int64_t n = (int64_t)g * kBlockRows + r;
+      float v = bf16r(red[idx]);
+      if constexpr (MODE == MODE_RES) {
+        const uint16_t rb = __ldcg(reinterpret_cast<const unsigned short*>(a.res + m * a.ldr + n));
+        v = __uint_as_float((uint32_t)rb << 16) + v;
+      }
+      a.out[m * a.ldo + n] = __float2bfloat16_rn(v);
+    }
+  } else if constexpr (MODE == MODE_SWIGLU) {
+    for (int idx = tid; idx < M * 64; idx += kConsumers) {
+      const int m = idx >> 6, j = idx & 63;
+      const float gv = bf16r(red[m * kBlockRows + j]);
+      const float uv = bf16r(red[m * kBlockRows + 64 + j]);
+      const float s = bf16r(gv / (1.0f + expf(-gv)));
+      a.out[m * a.ldo + (int64_t)g * 64 + j] = __float2bfloat16_rn(s * uv);
+    }
+  } else if constexpr (MODE == MODE_QKV) {
+    const int64_t p = flags[2];  // position and its RoPE row were loaded once per op (aux)
+    const int lane = tid & 31;
+    if (p < 0) return;           // out-of-range position: flagged, nothing written
+    // BF16 projection output
+    for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
+      const float v = bf16r(red[idx]);
+      red[idx] = v;
+      if (a.raw_out) a.raw_out[(idx >> 7) * a.n + (int64_t)g * kBlockRows + (idx & 127)] = __float2bfloat16_rn(v);
+    }
+    if (g >= a.nq + a.nkv) {  // V head: append as is
+      const int kvh = g - a.nq - a.nkv;
+      for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
+        const int m = idx >> 7, r = idx & 127;
+        a.v_cache[m * a.cs_b + kvh * a.cs_h + p * 128 + r] = __float2bfloat16_rn(red[idx]);
+      }
+      return;
+    }
+    // per-head RMSNorm (Qwen3RMSNorm over 128): sum of squares per activation row
+    for (int base = 0; base < M * kBlockRows; base += kConsumers) {
+      const int idx = base + tid;
+      float sq = 0.f;
+      if (idx < M * kBlockRows) sq = red[idx] * red[idx];
+      sq = warp_sum(sq);
+      if (lane == 0 && idx < M * kBlockRows) wsum[idx >> 5] = sq;  // one slot per 32 rows
+    }
+    named_bar(kBarConsumers, kConsumers);
+    const __nv_bfloat16* nw = (g < a.nq) ? a.q_norm : a.k_norm;
+    for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
+      const int m = idx >> 7, r = idx & 127;
+      const float var = (wsum[m * 4 + 0] + wsum[m * 4 + 1] + wsum[m * 4 + 2] + wsum[m * 4 + 3]) / 128.0f;
+      const float rstd = 1.0f / sqrtf(var + a.eps);
+      const float y = bf16r(bf16_to_f(nw[r]) * bf16r(red[idx] * rstd));
+      red[idx] = y;  // each thread rewrites only its own entries; partners are read after the barrier
+    }
+    named_bar(kBarConsumers, kConsumers);
+    for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
+      const int m = idx >> 7, r = idx & 127;
+      const float y = red[idx];
+      const float yp = red[(idx & ~127) | (r ^ 64)];
+      const float c = aux[r];
+      const float s = aux[128 + r];
+      // q*cos + rotate_half(q)*sin with every product a BF16 tensor (rotate_half = cat(-q2, q1))
+      const float rot = (r < 64) ? bf16r(-yp * s) : bf16r(yp * s);
+      const __nv_bfloat16 o = __float2bfloat16_rn(bf16r(y * c) + rot);
+      if (g < a.nq) {
+        a.q_out[((int64_t)m * a.nq + g) * 128 + r] = o;
+      } else {
+        a.k_cache[m * a.cs_b + (g - a.nq) * a.cs_h + p * 128 + r] = o;
+      }
+    }
+  } else if constexpr (MODE == MODE_LM) {
+    const int lane = tid & 31;
+    for (int base = 0; base < M * kBlockRows; base += kConsumers) {
+      const int idx = base + tid;
+      float v = -INFINITY;
+      int n = 0x7fffffff;
+      if (idx < M * kBlockRows) {
+        const int m = idx >> 7, r = idx & 127;
+        const int64_t row = (int64_t)g * kBlockRows + r;
+        if (row < a.n_valid) {
+          v = bf16r(red[idx]);
+          n = (int)row;
+          if (a.logits) a.logits[m * a.ld_logits + row] = __float2bfloat16_rn(v);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int on = __shfl_xor_sync(0xffffffffu, n, o);
+        if (ov > v || (ov == v && on < n)) {
+          v = ov;
+          n = on;
+        }
+      }
+      if (lane == 0 && idx < M * kBlockRows) {
+        wsum[(idx >> 5) * 2] = v;
+        reinterpret_cast<int*>(wsum)[(idx >> 5) * 2 + 1] = n;
+      }
+    }
+    named_bar(kBarConsumers, kConsumers);
+    if (tid < M) {
+      float bv = lmv[tid];
+      int bi = lmi[tid];
+      for (int q = 0; q < 4; ++q) {
+        const float v = wsum[(tid * 4 + q) * 2];
+        const int n = reinterpret_cast<int*>(wsum)[(tid * 4 + q) * 2 + 1];
+        if (v > bv || (v == bv && n < bi)) {
+          bv = v;
+          bi = n;
+        }
+      }
+      lmv[tid] = bv;
+      lmi[tid] = bi;
+    }
+  }
+}
+
+// Consume this CTA's blocks of one projection from the ring (in issue order), flushing a segment
+// at every row-group end; ring position (slot, phase) carries across projections.
+template <int M, int MODE>
+__device__ void consume_blocks(const GemvArgs& a, const Ring& R, int& slot, int& phase, int cta,
+                               const __nv_bfloat16* xs, float* red, float* wsum, float* lmv, int* lmi, int* flags,
+                               float* aux, int tid, bool& ok) {
+  const int warp = tid >> 5, lane = tid & 31;
+  if constexpr (MODE == MODE_QKV) {
+    // the decode position and its cos/sin rows, once per op (the epilogue of every head uses them)
+    const int64_t p = ld_cg_s64(a.pos);
+    const bool in = p >= 0 && p < a.cap;
+    if (tid < 128 && in) {
+      aux[tid] = bf16_to_f(a.cos[p * 128 + tid]);
+      aux[128 + tid] = bf16_to_f(a.sin[p * 128 + tid]);
+    }
+    if (tid == 0) {
+      flags[2] = in ? (int)p : -1;
+      if (!in && a.err) atomicOr(a.err, QD_DEVERR_POS);
+    }
+    named_bar(kBarConsumers, kConsumers);
+  }
+  const int64_t b_begin = part_begin(a.total, a.grid, cta);
+  const int64_t b_end = part_begin(a.total, a.grid, cta + 1);
+  const int rsub = lane >> 3;  // 0..3
+  const int c = lane & 7;      // logical 16-byte chunk (8 columns)
+  int roff[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = 16 * warp + rsub + 4 * i;
+    roff[i] = r * 128 + ((c ^ (r & 7)) << 4);
+  }
+  float acc[4][M];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[i][m] = 0.f;
+
+  int64_t seg_first = b_begin;
+  int g = (int)(b_begin / a.kblocks);
+  int kb = (int)(b_begin - (int64_t)g * a.kblocks) - 1;
+  for (int64_t b = b_begin; b < b_end; ++b) {
+    if (++kb == a.kblocks) {
+      kb = 0;
+      ++g;
+    }
+    if (ok) ok = mbar_wait(R.full(slot), phase, a.err, kErrWaitFull);
+    {
+      const char* blk = R.base + slot * kBlockBytes;
+      float xv[M][8];
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const uint4 u = *reinterpret_cast<const uint4*>(xs + (int64_t)m * a.k + kb * 64 + c * 8);
+        xv[m][0] = bf_lo(u.x);
+        xv[m][1] = bf_hi(u.x);
+        xv[m][2] = bf_lo(u.y);
+        xv[m][3] = bf_hi(u.y);
+        xv[m][4] = bf_lo(u.z);
+        xv[m][5] = bf_hi(u.z);
+        xv[m][6] = bf_lo(u.w);
+        xv[m][7] = bf_hi(u.w);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 u = *reinterpret_cast<const uint4*>(blk + roff[i]);
+        const float w8[8] = {bf_lo(u.x), bf_hi(u.x), bf_lo(u.y), bf_hi(u.y),
+                             bf_lo(u.z), bf_hi(u.z), bf_lo(u.w), bf_hi(u.w)};
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[i][m] = fmaf(w8[e], xv[m][e], acc[i][m]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(R.empty(slot));
+    if (++slot == R.nst) {
+      slot = 0;
+      phase ^= 1;
+    }
+
+    const bool seg_end = (kb == a.kblocks - 1) || (b == b_end - 1);
+    if (!seg_end) continue;
+
+    // ------------------------------------------------------------ flush the segment of group g
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        float v = acc[i][m];
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        acc[i][m] = 0.f;
+        if (c == 0) red[m * kBlockRows + 16 * warp + rsub + 4 * i] = v;
+      }
+    named_bar(kBarConsumers, kConsumers);
+    const int64_t gb0 = (int64_t)g * a.kblocks;
+    const int nseg_blk = (int)(b + 1 - seg_first);
+    bool finalized = false;
+    if (seg_first == gb0 && nseg_blk == a.kblocks) {
+      finalize_group<M, MODE>(a, g, red, wsum, lmv, lmi, aux, flags, tid);
+      finalized = true;
+    } else {
+      const int c_lo = part_owner(a.total, a.grid, gb0);
+      float* dst = a.partials + ((int64_t)g * a.smax + (cta - c_lo)) * (M * kBlockRows);
+      for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) dst[idx] = red[idx];
+      named_bar(kBarConsumers, kConsumers);
+      if (tid == 0) {  // release our partial, acquire the others' when we complete the group
+        const int old = atom_add_acq_rel(a.tickets + g, nseg_blk);
+        flags[1] = (old + nseg_blk == a.kblocks) ? 1 : 0;
+      }
+      named_bar(kBarConsumers, kConsumers);
+      if (flags[1]) {
+        // every CTA in [c_lo, c_hi] owns a non-empty part of the group (T >= G): sum their partials
+        // in CTA order, eight loads in flight at a time
+        const int nseg = part_owner(a.total, a.grid, gb0 + a.kblocks - 1) - c_lo + 1;
+        const float* pbase = a.partials + (int64_t)g * a.smax * (M * kBlockRows);
+        for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
+          float sum = 0.f;
+          int s = 0;
+          for (; s + 8 <= nseg; s += 8) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = ld_cg_f32(pbase + (int64_t)(s + j) * (M * kBlockRows) + idx);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) sum += v[j];
+          }
+          float v[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            v[j] = (s + j < nseg) ? ld_cg_f32(pbase + (int64_t)(s + j) * (M * kBlockRows) + idx) : 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (s + j < nseg) sum += v[j];
+          red[idx] = sum;
+        }
+        named_bar(kBarConsumers, kConsumers);
+        finalize_group<M, MODE>(a, g, red, wsum, lmv, lmi, aux, flags, tid);
+        if (tid == 0) atomicExch(a.tickets + g, 0);
+        finalized = true;
+      }
+    }
+    if (finalized && a.done) signal_done(a.done, tid);
+    named_bar(kBarConsumers, kConsumers);
+    seg_first = b + 1;
+  }
+}
+
+// Global argmax over the CTAs' per-row bests (LM head): each CTA posts its best, the last CTA to arrive
+// reduces all of them (lowest index on exact ties) and writes tok. Returns true in that last CTA.
+template <int M>
+__device__ bool lm_global_argmax(const GemvArgs& a, int cta, float* wsum, float* lmv, int* lmi, int* flags, int tid) {
+  const int warp = tid >> 5, lane = tid & 31;
+  if (tid < M) {
+    a.cta_val[tid * a.grid + cta] = lmv[tid];
+    a.cta_idx[tid * a.grid + cta] = lmi[tid];
+  }
+  named_bar(kBarConsumers, kConsumers);
+  if (tid == 0) flags[1] = (atom_add_acq_rel(a.lm_ticket, 1) == a.grid - 1) ? 1 : 0;
+  named_bar(kBarConsumers, kConsumers);
+  if (!flags[1]) return false;
+  for (int m = 0; m < M; ++m) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int q = tid; q < a.grid; q += kConsumers) {
+      const float v = ld_cg_f32(a.cta_val + m * a.grid + q);
+      const int n = (int)__ldcg(a.cta_idx + m * a.grid + q);
+      if (v > bv || (v == bv && n < bi)) {
+        bv = v;
+        bi = n;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int on = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && on < bi)) {
+        bv = ov;
+        bi = on;
+      }
+    }
+    if (lane == 0) {
+      wsum[warp * 2] = bv;
+      reinterpret_cast<int*>(wsum)[warp * 2 + 1] = bi;
+    }
+    named_bar(kBarConsumers, kConsumers);
+    if (tid == 0) {
+      for (int w8 = 1; w8 < kConsumerWarps; ++w8) {
+        const float v = wsum[w8 * 2];
+        const int n = reinterpret_cast<int*>(wsum)[w8 * 2 + 1];
+        if (v > bv || (v == bv && n < bi)) {
+          bv = v;
+          bi = n;
+        }
+      }
+      a.tok[m] = (int64_t)bi;
+    }
+    named_bar(kBarConsumers, kConsumers);
+  }
+  if (tid == 0) {
+    if (a.inc_pos && a.pos_inc) a.pos_inc[0] = ld_cg_s64(a.pos_inc) + 1;
+    atomicExch(a.lm_ticket, 0);
+  }
+  return true;
+}
+
+}  // namespace qd

@@ -17,6 +17,25 @@ c_void_p, c_int, c_int64, c_float = ctypes.c_void_p, ctypes.c_int, ctypes.c_int6
 P_I64 = ctypes.POINTER(ctypes.c_int64)
 P_INT = ctypes.POINTER(ctypes.c_int)
 
+class StepDesc(ctypes.Structure):
+    """qd_step_desc of include/qd_decode.h (every field 8 bytes wide, same order)."""
+
+    _fields_ = [
+        ("w_qkv", c_void_p), ("w_qkv_layer_bytes", c_int64), ("w_o", c_void_p), ("w_o_layer_bytes", c_int64),
+        ("w_gu", c_void_p), ("w_gu_layer_bytes", c_int64), ("w_down", c_void_p), ("w_down_layer_bytes", c_int64),
+        ("e_packed", c_void_p), ("ln1", c_void_p), ("ln2", c_void_p), ("q_norm", c_void_p), ("k_norm", c_void_p),
+        ("final_norm", c_void_p), ("layers", c_int64), ("hidden", c_int64), ("inter", c_int64),
+        ("nq_heads", c_int64), ("nkv_heads", c_int64), ("vocab", c_int64), ("batch", c_int64),
+        ("eps", ctypes.c_double), ("scale", ctypes.c_double), ("tok", c_void_p), ("pos", c_void_p),
+        ("x", c_void_p), ("q", c_void_p), ("attn", c_void_p), ("act", c_void_p), ("k_cache", c_void_p),
+        ("v_cache", c_void_p), ("cache_layer_stride", c_int64), ("cs_b", c_int64), ("cs_h", c_int64),
+        ("cap", c_int64), ("cos", c_void_p), ("sin", c_void_p), ("logits", c_void_p), ("ld_logits", c_int64),
+        ("err", c_void_p), ("trace", c_void_p),
+    ]
+
+
+P_DESC = ctypes.POINTER(StepDesc)
+
 # name -> (restype, argtypes); every function declared in include/qd_decode.h
 PROTOTYPES = {
     "qd_version": (ctypes.c_char_p, []),
@@ -40,6 +59,8 @@ PROTOTYPES = {
                                   c_void_p, c_int, c_void_p, c_int64, c_int, c_void_p, c_int64, c_void_p, c_int,
                                   c_void_p]),
     "qd_attn_plan": (c_int, [c_int, c_int, c_int64, c_int, P_INT, P_I64, P_I64]),
+    "qd_decode_step_plan": (c_int, [P_DESC, P_I64, P_INT]),
+    "qd_decode_step": (c_int, [P_DESC, c_void_p, c_int64, c_void_p]),
     "qd_attn_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64,
                                c_int64, c_int64, c_int, c_int64, c_float, c_void_p, c_int64, c_void_p, c_int,
                                c_void_p]),
@@ -49,7 +70,7 @@ QD_OK, QD_ERR_ARG, QD_ERR_SCRATCH, QD_ERR_CUDA, QD_ERR_UNSUPPORTED = 0, 1, 2, 3,
 QD_EPI_STORE, QD_EPI_RES, QD_EPI_SWIGLU = 0, 1, 2
 DEVERR = {1: "wait for a weight block timed out", 2: "wait for a free ring slot timed out",
           4: "drain of in-flight copies timed out", 8: "token id out of range",
-          16: "decode position outside the cache"}
+          16: "decode position outside the cache", 32: "a wait for another CTA's results timed out"}
 
 
 class QDError(RuntimeError):

@@ -6,6 +6,7 @@
   QkvRopeAppend                FastGemm "qkv" + the q/k-norm/RoPE/KV-append of FastAttention (fast.py:240-293)
   LmHeadArgmax                 engine/kernels/fast.py:439-465 (FastLmHead) / gemv.py:251-287
   DecodeAttention              engine/kernels/decode_attn.py:89-119 / FastAttention (fast.py:353-376)
+  DecodeStep                   the persistent whole-step kernel (engine/kernels/mega.py MegaStep, tier T6)
 
 Each object owns its scratch buffer (split-K partials and tickets, zero-filled once) and launches
 on the current torch CUDA stream, so calls are graph-capturable. Tensors must be CUDA tensors.
@@ -189,3 +190,45 @@ class DecodeAttention:
                self.nkv, self.capacity, k_cache.stride(0), k_cache.stride(1), self.splits, self.chunk, self.scale,
                _ptr(self.scratch), self.scratch.numel(), _ptr(err), int(pdl), _stream())
         return out
+
+
+class DecodeStep:
+    """One persistent launch per decode step (qd_decode_step): embedding, every layer and the LM head.
+    Holds the descriptor (pointers into the engine's weights and per-shape state) and the scratch."""
+
+    def __init__(self, eng, st, logits=None, trace=None):
+        d = L.StepDesc()
+        Lyr = eng.n_layers
+        d.w_qkv, d.w_qkv_layer_bytes = eng.w_qkv.data_ptr(), eng.w_qkv.stride(0) * 2
+        d.w_o, d.w_o_layer_bytes = eng.w_o.data_ptr(), eng.w_o.stride(0) * 2
+        d.w_gu, d.w_gu_layer_bytes = eng.w_gu.data_ptr(), eng.w_gu.stride(0) * 2
+        d.w_down, d.w_down_layer_bytes = eng.w_down.data_ptr(), eng.w_down.stride(0) * 2
+        d.e_packed = eng.e_packed.data_ptr()
+        d.ln1, d.ln2 = eng.ln1.data_ptr(), eng.ln2.data_ptr()
+        d.q_norm, d.k_norm, d.final_norm = eng.qn.data_ptr(), eng.kn.data_ptr(), eng.final_norm.data_ptr()
+        d.layers, d.hidden, d.inter = Lyr, eng.hidden, eng.inter
+        d.nq_heads, d.nkv_heads, d.vocab, d.batch = eng.nq, eng.nkv, eng.vocab, st.B
+        d.eps, d.scale = eng.eps, 1.0 / math.sqrt(eng.head_dim)
+        d.tok, d.pos = st.tok.data_ptr(), st.pos.data_ptr()
+        d.x, d.q, d.attn, d.act = st.x.data_ptr(), st.q.data_ptr(), st.attn_out.data_ptr(), st.act.data_ptr()
+        d.k_cache, d.v_cache = st.k_all.data_ptr(), st.v_all.data_ptr()
+        d.cache_layer_stride, d.cs_b, d.cs_h = st.k_all.stride(0), st.k_all.stride(1), st.k_all.stride(2)
+        d.cap = st.k_all.shape[3]
+        d.cos, d.sin = st.cos.data_ptr(), st.sin.data_ptr()
+        d.logits = logits.data_ptr() if logits is not None else None
+        d.ld_logits = logits.stride(0) if logits is not None else 0
+        d.err = st.err.data_ptr()
+        d.trace = trace.data_ptr() if trace is not None else None
+        self.desc = d
+        self._keep = (eng, st, logits, trace)
+        nbytes, splits = ctypes.c_int64(0), ctypes.c_int(0)
+        L.call("qd_decode_step_plan", ctypes.byref(d), ctypes.byref(nbytes), ctypes.byref(splits))
+        self.splits = splits.value
+        self.scratch = torch.zeros((max(1, nbytes.value),), dtype=torch.uint8, device=st.x.device)
+
+    def __call__(self):
+        L.call("qd_decode_step", ctypes.byref(self.desc), _ptr(self.scratch), self.scratch.numel(), _stream())
+
+    def reset(self):
+        """Clear counters / tickets after a device error (they are left mid-step)."""
+        self.scratch.zero_()

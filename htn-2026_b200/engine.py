@@ -6,8 +6,10 @@ QWEN_ENGINE_CONTRACT.md): it yields exactly `max_new_tokens` lists, one token id
 input order, ignores end-of-sequence ids, and yields nothing for max_new_tokens <= 0.
 
 Decode runs entirely in the hand-written CUDA library (decode_b200/libqd_decode.so, C ABI in
-include/qd_decode.h); there is no Triton, no tier fallback and no CPU path. One decode step is
-1 + 5 x layers + 1 launches, captured once per shape in a CUDA graph:
+include/qd_decode.h); there is no Triton, no tier fallback and no CPU path. By default a decode step
+is one persistent launch (qd_decode_step: one CTA per SM streams every weight block in op order while
+its consumers wait on completion counters); ENGINE_STEP=kernels runs the same arithmetic as
+1 + 5 x layers + 1 launches. Either way the step is captured once per shape in a CUDA graph:
 
   embed          x = E[tok]
   per layer      qkv   RMSNorm(x) @ Wqkv^T, per-head q/k RMSNorm + RoPE(pos), K/V appended at pos
@@ -45,6 +47,8 @@ MAX_BATCH = 8             # the streaming GEMV keeps up to 8 activation rows in 
 PREFILL_TOKENS = 16384    # prefill processes at most this many tokens per row chunk (engine/engine.py:79)
 USE_GRAPHS = os.environ.get("ENGINE_GRAPHS", "1") != "0"
 USE_PDL = os.environ.get("ENGINE_PDL", "1") != "0"
+# "persistent": one launch per decode step (qd_decode_step); "kernels": 1 + 5 x layers + 1 launches
+STEP_MODE = os.environ.get("ENGINE_STEP", "persistent")
 
 
 def log(msg):
@@ -102,6 +106,9 @@ class _State:
         self.gu = ops.Gemv(B, 2 * I, H, ops.Gemv.SWIGLU, dev, eps=eng.eps)
         self.down = ops.Gemv(B, H, I, ops.Gemv.RES, dev, eps=eng.eps)
         self.lm = ops.LmHeadArgmax(B, eng.vocab, H, dev, eps=eng.eps)
+        self.mode = STEP_MODE
+        self.step = ops.DecodeStep(eng, self) if self.mode == "persistent" else None
+        self.step_logits = None
         self.rows = max(1, min(B, PREFILL_TOKENS // S))
         pin = torch.cuda.is_available()
         self.host = torch.empty((max(N, 1), B), dtype=torch.int64, pin_memory=pin)
@@ -241,7 +248,16 @@ class Engine:
         return logits
 
     def _decode_step(self, st: _State, logits: torch.Tensor | None = None) -> None:
-        """One token per sequence at st.pos: 1 + 5 * layers + 1 kernel launches, all in libqd_decode."""
+        """One token per sequence at st.pos, all in libqd_decode: one persistent launch, or
+        1 + 5 * layers + 1 per-op launches."""
+        if st.mode == "persistent":
+            if logits is None:
+                st.step()
+            else:
+                if st.step_logits is None or st.step_logits._keep[2] is not logits:
+                    st.step_logits = ops.DecodeStep(self, st, logits)
+                st.step_logits()
+            return
         pdl, err = USE_PDL, st.err
         ops.embed(st.tok, self.e_packed, self.vocab, st.x, err, pdl)
         for i in range(self.n_layers):
@@ -257,6 +273,10 @@ class Engine:
     def check_device_errors(self, st: _State) -> None:
         code = int(st.err.item())
         if code:
+            # counters and tickets may be left mid-step: clear every scratch buffer before raising
+            for plan in (st.qkv, st.attn, st.o, st.gu, st.down, st.lm, st.step, st.step_logits):
+                if plan is not None:
+                    plan.scratch.zero_()
             st.err.zero_()
             raise RuntimeError(f"decode kernels reported a device error: {qdlib.describe_device_error(code)}")
 
@@ -362,7 +382,9 @@ class Engine:
         st = self.state
         if st is None or (st.B, st.S, st.N) != (B, S, N):
             st = self._build(B, S, N)
-        buf = torch.empty((B, self.vocab), dtype=BF16, device=self.device)
+        if st.logits is None:
+            st.logits = torch.empty((B, self.vocab), dtype=BF16, device=self.device)
+        buf = st.logits
         toks, logits = [], []
         with torch.inference_mode():
             st.ids.copy_(torch.tensor(input_ids, dtype=torch.int64))

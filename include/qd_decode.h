@@ -39,7 +39,8 @@ enum {
   QD_DEVERR_WAIT_EMPTY = 2,
   QD_DEVERR_DRAIN = 4,
   QD_DEVERR_TOKEN = 8,
-  QD_DEVERR_POS = 16
+  QD_DEVERR_POS = 16,
+  QD_DEVERR_DEP = 32
 };
 
 /* Library identification and the last error message of the calling thread. */
@@ -137,6 +138,60 @@ int qd_attn_plan(int batch, int nkv_heads, int64_t cap, int grid_hint, int* spli
 int qd_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, void* out, int batch,
                    int nq_heads, int nkv_heads, int64_t cap, int64_t cs_b, int64_t cs_h, int splits, int64_t chunk,
                    float scale, void* scratch, int64_t scratch_bytes, int* err, int pdl, cudaStream_t stream);
+
+/* ---------------------------------------------------------------- persistent decode step
+ * One launch = one whole decode step: embedding, every layer (the five ops above, same arithmetic,
+ * same stream-K partition and attention splits, so bit-identical results) and the LM head with
+ * argmax and position advance. Replaces the reference's persistent megakernel tier T6
+ * (engine/kernels/mega.py:48-223, MegaStep) and its per-op launch sequence T5
+ * (engine/engine.py:463-477). One CTA per SM, launched cooperatively: a producer warp streams every
+ * projection's weights in op order through a deep shared-memory ring, consumers wait (bounded, 1 s)
+ * on completion counters of the op that produces their input. All fields are 8 bytes wide.
+ * Weights are packed (qd_pack_rows) and layer-stacked with the given byte strides; norms are
+ * [layers, hidden] (ln1, ln2), [layers, 128] (q_norm, k_norm), [hidden] (final_norm); caches are
+ * [layers, batch, nkv, cap, 128] with element strides cache_layer_stride, cs_b, cs_h; x [batch,
+ * hidden], q and attn [batch, nq, 128], act [batch, inter]; logits (optional) [batch, ld_logits].
+ * `err` is required. 1 <= batch <= 8. qd_decode_step_plan gives the scratch size (zero-fill once;
+ * re-zero after any device error) and the attention split count. */
+typedef struct qd_step_desc {
+  const void* w_qkv;
+  int64_t w_qkv_layer_bytes;
+  const void* w_o;
+  int64_t w_o_layer_bytes;
+  const void* w_gu;
+  int64_t w_gu_layer_bytes;
+  const void* w_down;
+  int64_t w_down_layer_bytes;
+  const void* e_packed;
+  const void* ln1;
+  const void* ln2;
+  const void* q_norm;
+  const void* k_norm;
+  const void* final_norm;
+  int64_t layers, hidden, inter, nq_heads, nkv_heads, vocab, batch;
+  double eps, scale;
+  int64_t* tok;
+  int64_t* pos;
+  void* x;
+  void* q;
+  void* attn;
+  void* act;
+  void* k_cache;
+  void* v_cache;
+  int64_t cache_layer_stride, cs_b, cs_h, cap;
+  const void* cos;
+  const void* sin;
+  void* logits;
+  int64_t ld_logits;
+  int* err;
+  /* optional timeline (%globaltimer ns), [grid][ops][4] with ops = 2 + 5 layers in step order
+   * (embed, layers x {qkv, attn, o, gate_up, down}, lm): input ready, inputs staged, op done, and the
+   * time the producer issued the op's last block; null disables it */
+  uint64_t* trace;
+} qd_step_desc;
+
+int qd_decode_step_plan(const qd_step_desc* desc, int64_t* scratch_bytes, int* attn_splits);
+int qd_decode_step(const qd_step_desc* desc, void* scratch, int64_t scratch_bytes, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -14,6 +14,10 @@ Two bounds are checked per step, over all 151,936 entries:
     running the reference engine): BF16 logits near 4-8 have a 0.031 ulp, and one rounding flip
     at the LM head moves a logit by that much. 5e-2 on log-softmax is below the reference's own
     noise floor, so the bound is twice that floor.
+The tie rule for tokens uses the same calibrated bound: a token may differ from the reference argmax
+only where the reference's own top-2 gap is below it. The oracle runs on the test host's CPU, whose
+BF16 matmul kernels can round differently from the machine the golden vectors came from, so the
+reference side of the comparison carries that same ulp-level noise.
 """
 
 import pytest
@@ -41,13 +45,13 @@ def engines():
     return get
 
 
-def _golden_token_ok(tok, step, row):
+def _golden_token_ok(tok, step, row, tol):
     """Tie rule against the golden top-8 of the reference's native run."""
     vals, ids = step["top_vals"][row], step["top_ids"][row]
     best = vals[0]
     if tok in ids and vals[ids.index(tok)] == best:
         return True
-    return (best - vals[1]) < TOL and tok in ids and vals[ids.index(tok)] >= best - TOL
+    return (best - vals[1]) < tol and tok in ids and vals[ids.index(tok)] >= best - tol
 
 
 @pytest.mark.parametrize("case", ["config0", "b3_s17"])
@@ -62,7 +66,8 @@ def test_generate_matches_reference_golden(engines, case):
         for t in range(len(ref[b])):
             if toks[b][t] != ref[b][t]:
                 # allowed only at a reference near-tie; after a flip the prefixes differ, stop here
-                assert _golden_token_ok(toks[b][t], g["native"]["steps"][t], b), (case, b, t)
+                tol = max(TOL, 2 * g["self_drift"]["max_logsoftmax_diff"])
+                assert _golden_token_ok(toks[b][t], g["native"]["steps"][t], b, tol), (case, b, t)
                 break
 
 
@@ -80,7 +85,14 @@ def test_teacher_forced_logits_within_tolerance(engines, case):
         worst_lsm = max(worst_lsm, Q.log_softmax_maxdiff(logits[t], ref_logits[t]))
         worst_p = max(worst_p, Q.softmax_maxdiff(logits[t], ref_logits[t]))
         for b in range(len(toks)):
-            assert Q.token_ok(toks[b][t], ref_logits[t][b], TOL), (case, t, b)
+            if not Q.token_ok(toks[b][t], ref_logits[t][b], lsm_bound):
+                rv, ri = ref_logits[t][b].float().topk(3)
+                ours = logits[t][b].float()
+                raise AssertionError(
+                    f"{case} step {t} row {b}: token {toks[b][t]} (ref logit "
+                    f"{float(ref_logits[t][b][toks[b][t]]):.4f}, ours {float(ours[toks[b][t]]):.4f}); ref top3 "
+                    f"{list(zip(ri.tolist(), [round(v, 4) for v in rv.tolist()]))}, ours at those "
+                    f"{[round(float(ours[i]), 4) for i in ri.tolist()]}")
     print(f"{case}: max |softmax diff| {worst_p:.2e}, max |log-softmax diff| {worst_lsm:.4f} "
           f"(bound {lsm_bound:.4f}; reference self-drift {g['self_drift']['max_logsoftmax_diff']:.4f})")
     assert worst_p <= TOL
@@ -135,3 +147,56 @@ def test_contract_step_counts(engines):
     assert list(eng.generate(p, 0)) == []
     one = list(eng.generate(p, 1))
     assert len(one) == 1 and len(one[0]) == 1
+
+
+def test_persistent_step_matches_per_op_kernels_bit_exactly():
+    """The persistent step kernel runs the per-op kernels' arithmetic with the same partitions: same
+    tokens and bit-identical logits."""
+    import engine as E
+
+    g = load_golden("config0")
+    state, cfg = synth_state(4)
+    out = {}
+    for mode in ("persistent", "kernels"):
+        old = E.STEP_MODE
+        E.STEP_MODE = mode
+        try:
+            eng = E.Engine.from_state_dict(state, cfg, "cuda:0")
+            toks, logits = eng.generate_with_logits(g["prompt"], 12)
+            steps = list(eng.generate(g["prompt"], 12))
+        finally:
+            E.STEP_MODE = old
+        assert [list(r) for r in zip(*steps)] == toks
+        out[mode] = (toks, logits)
+        del eng
+    assert out["persistent"][0] == out["kernels"][0]
+    for a, b in zip(out["persistent"][1], out["kernels"][1]):
+        assert torch.equal(a, b)
+
+
+def test_persistent_step_long_cache_uses_both_attention_teams():
+    """A cache long enough that attention has more units than SMs, so the second 4-warp team of each
+    CTA runs units too (cap 740 -> 24 splits x 8 KV heads = 192 units): same tokens and logits as
+    the per-op kernels."""
+    import engine as E
+    from decode_b200 import synth
+
+    state, cfg = synth_state(2)
+    prompt = synth.random_prompt(1, 100, cfg["vocab_size"], seed=41)
+    out = {}
+    for mode in ("persistent", "kernels"):
+        old = E.STEP_MODE
+        E.STEP_MODE = mode
+        try:
+            eng = E.Engine.from_state_dict(state, cfg, "cuda:0")
+            st = eng._build(1, 100, 640)
+            if mode == "persistent":
+                assert st.step.splits * 8 > eng.sm_count
+            toks, logits = eng.generate_with_logits(prompt, 640)
+        finally:
+            E.STEP_MODE = old
+        out[mode] = (toks, logits[-8:])
+        del eng
+    assert out["persistent"][0] == out["kernels"][0]
+    for a, b in zip(out["persistent"][1], out["kernels"][1]):
+        assert torch.equal(a, b)
