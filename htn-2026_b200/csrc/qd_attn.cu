@@ -10,7 +10,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   __shared__ AttnSmem sm;
   grid_dep_wait();
   grid_dep_launch();
-  attn_unit(a, blockIdx.z, blockIdx.y, blockIdx.x, threadIdx.x, 1, sm);
+  const int64_t len = attn_len(a, ld_cg_s64(a.pos), threadIdx.x == 0 && blockIdx.x == 0);
+  attn_unit(a, blockIdx.z, blockIdx.y, blockIdx.x, threadIdx.x, 1, sm, len);
+}
+
+// QD_ATTN_KEYS_PER_SPLIT: keys per split at run time (default 32); the plan's split count is the cap.
+int attn_keys_per_split() {
+  const int v = env_int("QD_ATTN_KEYS_PER_SPLIT", 32);
+  return v < 32 ? 32 : v;
 }
 
 bool attn_plan(int batch, int nkv, int64_t cap, int grid_hint, AttnPlan* p) {
@@ -93,6 +100,7 @@ extern "C" int qd_attn_decode(const void* q, const void* k_cache, const void* v_
   a.tickets = reinterpret_cast<int*>(sc + need_acc + need_ml);
   a.err = err;
   a.done = nullptr;
+  a.keys_per_split = attn_keys_per_split();
   return launch_kernel((const void*)attn_decode_kernel, dim3(splits, nkv_heads, batch), dim3(kAttnWarps * 32), 0, pdl,
                        stream, &a);
 }

@@ -38,7 +38,31 @@ struct AttnArgs {
   int* tickets;
   int* err;
   int* done;  // optional: +1 (release) per merged (sequence, KV head)
+  int keys_per_split;  // splits in use at a given length: ~this many keys each, at most `splits`
 };
+
+// Valid length (pos + 1) clamped to the cache; flags QD_DEVERR_POS when the position is outside it.
+__device__ __forceinline__ int64_t attn_len(const AttnArgs& a, int64_t pos, bool flag) {
+  int64_t len = pos + 1;
+  if (len < 1 || len > a.cap) {
+    if (flag && a.err) atomicOr(a.err, QD_DEVERR_POS);
+    len = len < 1 ? 1 : a.cap;
+  }
+  return len;
+}
+
+// Splits in use at length len (every unit computes the same value): about keys_per_split keys each,
+// at most a.splits, chunk a multiple of 32 keys (one pass of the 4 warps).
+__device__ __forceinline__ int attn_active(const AttnArgs& a, int64_t len, int64_t* chunk) {
+  const int64_t kps = a.keys_per_split > 0 ? a.keys_per_split : a.chunk;
+  int64_t n = (len + kps - 1) / kps;
+  if (n > a.splits) n = a.splits;
+  if (n < 1) n = 1;
+  int64_t c = (len + n - 1) / n;
+  c = (c + 31) / 32 * 32;
+  *chunk = c;
+  return (int)((len + c - 1) / c);
+}
 
 // 16-byte aligned and sized (the q.k loop reads qs as float4; the step kernel places two of these
 // back to back).
@@ -49,16 +73,16 @@ struct __align__(16) AttnSmem {
   int last_flag;
 };
 
-// One unit on a team of 128 threads (team thread id `tid`, named barrier `bar_id`).
-static __device__ void attn_unit(const AttnArgs& a, int b, int kvh, int split, int tid, int bar_id, AttnSmem& sm) {
+// One unit on a team of 128 threads (team thread id `tid`, named barrier `bar_id`); `len` is the valid
+// length (attn_len). Units past the splits in use at this length return at once.
+static __device__ void attn_unit(const AttnArgs& a, int b, int kvh, int split, int tid, int bar_id, AttnSmem& sm,
+                                 int64_t len) {
   const int warp = tid >> 5, lane = tid & 31;
-  int64_t len = ld_cg_s64(a.pos) + 1;
-  if (len < 1 || len > a.cap) {  // a position outside the cache: read nothing beyond it, flag it
-    if (tid == 0 && split == 0 && a.err) atomicOr(a.err, QD_DEVERR_POS);
-    len = len < 1 ? 1 : a.cap;
-  }
-  const int64_t start = (int64_t)split * a.chunk;
-  int64_t end = start + a.chunk;
+  int64_t chunk;
+  const int n_use = attn_active(a, len, &chunk);
+  if (split >= n_use) return;
+  const int64_t start = (int64_t)split * chunk;
+  int64_t end = start + chunk;
   if (end > len) end = len;
 
   for (int h = 0; h < kGroup; ++h) {
@@ -119,10 +143,19 @@ static __device__ void attn_unit(const AttnArgs& a, int b, int kvh, int split, i
       s[h] += __shfl_xor_sync(0xffffffffu, s[h], 1);  // the 4 quarters of key kj
       s[h] += __shfl_xor_sync(0xffffffffu, s[h], 2);
       const float sc = valid ? s[h] * a.scale : -INFINITY;
-      const float m_new = fmaxf(m_run[h], warp_max(sc));
+      // the 4 lanes of a key now agree: reduce over the 8 keys (lane bits 2..4) only
+      float mt = sc;
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+      const float m_new = fmaxf(m_run[h], mt);
       const float alpha = expf(m_run[h] - m_new);  // exp(-inf) = 0 on the first pass
       const float p = valid ? expf(sc - m_new) : 0.f;
-      l_run[h] = l_run[h] * alpha + warp_sum(qd == 0 ? p : 0.f);  // each key counted once
+      float ps = p;  // each key counted once
+      ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+      l_run[h] = l_run[h] * alpha + ps;
 #pragma unroll
       for (int d = 0; d < 4; ++d) acc[h][d] *= alpha;
       m_run[h] = m_new;
@@ -152,6 +185,30 @@ static __device__ void attn_unit(const AttnArgs& a, int b, int kvh, int split, i
   }
   named_bar(bar_id, kAttnThreads);
   const int64_t row0 = ((int64_t)b * a.nq + kvh * kGroup) * a.splits;
+  if (n_use == 1) {  // one split covers every key: normalise and write, no partials or merge
+    for (int h = 0; h < kGroup; ++h) {
+      float mx = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, sm.wm[w][h]);
+      float num = 0.f, den = 0.f;
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) {
+        if (sm.wm[w][h] == -INFINITY) continue;
+        const float sc = expf(sm.wm[w][h] - mx);
+        num = fmaf(sm.wacc[w][h][tid], sc, num);
+        den = fmaf(sm.wl[w][h], sc, den);
+      }
+      // as the merge of one split computes it: weight exp(0) = 1
+      a.out[((int64_t)b * a.nq + kvh * kGroup + h) * kHeadDim + tid] =
+          __float2bfloat16_rn(fmaf(num, 1.0f, 0.f) / fmaf(den, 1.0f, 0.f));
+    }
+    if (a.done) {
+      named_bar(bar_id, kAttnThreads);
+      if (tid == 0) red_release_add(a.done, 1);
+    }
+    named_bar(bar_id, kAttnThreads);
+    return;
+  }
   for (int h = 0; h < kGroup; ++h) {
     float mx = -INFINITY;
 #pragma unroll
@@ -175,14 +232,14 @@ static __device__ void attn_unit(const AttnArgs& a, int b, int kvh, int split, i
   }
   named_bar(bar_id, kAttnThreads);
   if (tid == 0)
-    sm.last_flag = (atom_add_acq_rel(a.tickets + (int64_t)b * a.nkv + kvh, 1) == a.splits - 1) ? 1 : 0;
+    sm.last_flag = (atom_add_acq_rel(a.tickets + (int64_t)b * a.nkv + kvh, 1) == n_use - 1) ? 1 : 0;
   named_bar(bar_id, kAttnThreads);
   if (sm.last_flag) {
     // Merge the splits that hold keys (those past the valid length have max -inf and weight 0), in
     // split order. (max, sum) of every head and split go through shared memory (the warp-merge
     // buffer is free by now), then each thread combines its dimension for the 4 heads with all of
     // its accumulator loads in flight.
-    const int n_act = (int)((len + a.chunk - 1) / a.chunk < a.splits ? (len + a.chunk - 1) / a.chunk : a.splits);
+    const int n_act = n_use;  // every split in use holds at least one key
     float* mm = &sm.wacc[0][0][0];  // [kGroup][n_act] maxima, then sums, then weights
     float* ll = mm + kGroup * n_act;
     float* ww = ll + kGroup * n_act;

@@ -39,7 +39,7 @@ __host__ __device__ inline SmemLayout smem_layout(int M, int64_t k, int nst) {
   L.flags = off;
   off += 16;
   L.aux = off;
-  off += 256 * 4;
+  off += 512 * 4;
   L.bars = align_up(off, 8);
   off = L.bars + 2 * nst * 8;
   L.total = align_up(off, 128);

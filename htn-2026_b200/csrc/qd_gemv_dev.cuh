@@ -52,7 +52,8 @@ struct GemvArgs {
   int* tickets;
   int smax;
   int* err;
-  int* done;  // optional: +1 (release) per finalized row group
+  int* done;       // optional: +1 (release) per finalized row group
+  int pos_ready;   // QKV: flags[2] already holds the position and aux its cos/sin rows
   // QKV
   const __nv_bfloat16 *q_norm, *k_norm, *cos, *sin;
   const int64_t* pos;
@@ -145,6 +146,15 @@ template <int M>
 __device__ void stage_x(const GemvArgs& a, __nv_bfloat16* xs, float* wsum, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   const int kv8 = (int)(a.k >> 3);
+  // the norm weights this thread applies, loaded with its first activation row (k <= 10240)
+  uint4 nwv[kStageBatch];
+  if (a.norm_w) {
+#pragma unroll
+    for (int j = 0; j < kStageBatch; ++j) {
+      const int q = j * kConsumers + tid;
+      nwv[j] = q < kv8 ? *reinterpret_cast<const uint4*>(a.norm_w + q * 8) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
   for (int m = 0; m < M; ++m) {
     float sq = 0.f;
     for (int q0 = 0; q0 < kv8; q0 += kStageBatch * kConsumers) {
@@ -182,10 +192,13 @@ __device__ void stage_x(const GemvArgs& a, __nv_bfloat16* xs, float* wsum, int t
 #pragma unroll
       for (int w8 = 0; w8 < kConsumerWarps; ++w8) ss += wsum[m * kConsumerWarps + w8];
       const float rstd = 1.0f / sqrtf(ss / (float)a.k + a.eps);
-      for (int q = tid; q < kv8; q += kConsumers) {
+#pragma unroll
+      for (int j = 0; j < kStageBatch; ++j) {
+        const int q = j * kConsumers + tid;
+        if (q >= kv8) continue;
         uint4* p = reinterpret_cast<uint4*>(xs + (int64_t)m * a.k + q * 8);
         const uint4 xv = *p;
-        const uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + q * 8);
+        const uint4 wv = nwv[j];
         const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
         const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
         uint32_t o[4];
@@ -203,18 +216,43 @@ __device__ void stage_x(const GemvArgs& a, __nv_bfloat16* xs, float* wsum, int t
 }
 
 // ------------------------------------------------------------------ epilogues (256 consumer threads)
+constexpr int kResPer = (8 * kBlockRows + kConsumers - 1) / kConsumers;  // residual values per thread
+
+// Residual values of group g this thread's epilogue adds (one L2 round trip for all of them).
+template <int M>
+__device__ __forceinline__ void load_res(const GemvArgs& a, int g, int tid, float* rv) {
+#pragma unroll
+  for (int j = 0; j < kResPer; ++j) {
+    const int idx = tid + j * kConsumers;
+    if (idx < M * kBlockRows) {
+      const int m = idx >> 7, r = idx & 127;
+      const uint16_t rb = __ldcg(reinterpret_cast<const unsigned short*>(a.res + m * a.ldr + (int64_t)g * kBlockRows + r));
+      rv[j] = __uint_as_float((uint32_t)rb << 16);
+    }
+  }
+}
+
 template <int M, int MODE>
 __device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum, float* lmv, int* lmi,
-                               const float* aux, const int* flags, int tid) {
+                               const float* aux, const int* flags, int tid, const float* res_pre = nullptr) {
   if constexpr (MODE == MODE_STORE || MODE == MODE_RES) {
-    for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
+    float rv[kResPer];
+    if constexpr (MODE == MODE_RES) {
+      if (res_pre) {
+#pragma unroll
+        for (int j = 0; j < kResPer; ++j) rv[j] = res_pre[j];
+      } else {
+        load_res<M>(a, g, tid, rv);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kResPer; ++j) {
+      const int idx = tid + j * kConsumers;
+      if (idx >= M * kBlockRows) continue;
       const int m = idx >> 7, r = idx & 127;
       const int64_t n = (int64_t)g * kBlockRows + r;
       float v = bf16r(red[idx]);
-      if constexpr (MODE == MODE_RES) {
-        const uint16_t rb = __ldcg(reinterpret_cast<const unsigned short*>(a.res + m * a.ldr + n));
-        v = __uint_as_float((uint32_t)rb << 16) + v;
-      }
+      if constexpr (MODE == MODE_RES) v = rv[j] + v;
       a.out[m * a.ldo + n] = __float2bfloat16_rn(v);
     }
   } else if constexpr (MODE == MODE_SWIGLU) {
@@ -252,12 +290,12 @@ __device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum
       if (lane == 0 && idx < M * kBlockRows) wsum[idx >> 5] = sq;  // one slot per 32 rows
     }
     named_bar(kBarConsumers, kConsumers);
-    const __nv_bfloat16* nw = (g < a.nq) ? a.q_norm : a.k_norm;
+    const float* nw = aux + (g < a.nq ? 256 : 384);  // q_norm / k_norm, loaded once per op
     for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
       const int m = idx >> 7, r = idx & 127;
       const float var = (wsum[m * 4 + 0] + wsum[m * 4 + 1] + wsum[m * 4 + 2] + wsum[m * 4 + 3]) / 128.0f;
       const float rstd = 1.0f / sqrtf(var + a.eps);
-      const float y = bf16r(bf16_to_f(nw[r]) * bf16r(red[idx] * rstd));
+      const float y = bf16r(nw[r] * bf16r(red[idx] * rstd));
       red[idx] = y;  // each thread rewrites only its own entries; partners are read after the barrier
     }
     named_bar(kBarConsumers, kConsumers);
@@ -331,6 +369,8 @@ __device__ void consume_blocks(const GemvArgs& a, const Ring& R, int& slot, int&
                                float* aux, int tid, bool& ok) {
   const int warp = tid >> 5, lane = tid & 31;
   if constexpr (MODE == MODE_QKV) {
+    if (tid < 256) aux[256 + tid] = bf16_to_f(tid < 128 ? a.q_norm[tid] : a.k_norm[tid - 128]);
+    if (!a.pos_ready) {
     // the decode position and its cos/sin rows, once per op (the epilogue of every head uses them)
     const int64_t p = ld_cg_s64(a.pos);
     const bool in = p >= 0 && p < a.cap;
@@ -341,6 +381,7 @@ __device__ void consume_blocks(const GemvArgs& a, const Ring& R, int& slot, int&
     if (tid == 0) {
       flags[2] = in ? (int)p : -1;
       if (!in && a.err) atomicOr(a.err, QD_DEVERR_POS);
+    }
     }
     named_bar(kBarConsumers, kConsumers);
   }
@@ -439,6 +480,8 @@ __device__ void consume_blocks(const GemvArgs& a, const Ring& R, int& slot, int&
         // in CTA order, eight loads in flight at a time
         const int nseg = part_owner(a.total, a.grid, gb0 + a.kblocks - 1) - c_lo + 1;
         const float* pbase = a.partials + (int64_t)g * a.smax * (M * kBlockRows);
+        float res_pre[kResPer];
+        if constexpr (MODE == MODE_RES) load_res<M>(a, g, tid, res_pre);  // in flight with the partials
         for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
           float sum = 0.f;
           int s = 0;
@@ -459,7 +502,8 @@ __device__ void consume_blocks(const GemvArgs& a, const Ring& R, int& slot, int&
           red[idx] = sum;
         }
         named_bar(kBarConsumers, kConsumers);
-        finalize_group<M, MODE>(a, g, red, wsum, lmv, lmi, aux, flags, tid);
+        finalize_group<M, MODE>(a, g, red, wsum, lmv, lmi, aux, flags, tid,
+                                MODE == MODE_RES ? res_pre : nullptr);
         if (tid == 0) atomicExch(a.tickets + g, 0);
         finalized = true;
       }

@@ -23,6 +23,8 @@ struct AttnPlan {
 bool attn_plan(int batch, int nkv, int64_t cap, int grid_hint, AttnPlan* p);
 
 int env_int(const char* name, int dflt);
+// Keys per attention split at run time.
+int attn_keys_per_split();
 // Blocks each CTA keeps prefetched into L2 beyond its shared-memory ring.
 int prefetch_blocks();
 

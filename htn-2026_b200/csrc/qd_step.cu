@@ -40,7 +40,7 @@ struct StepArgs {
   __nv_bfloat16* logits;
   int64_t ld_logits;
   int* err;
-  int grid, nst, splits, kmax, prefetch, prefetch_max, evict_first;
+  int grid, nst, splits, kmax, prefetch, prefetch_max, evict_first, keys_per_split;
   int64_t chunk;
   int smax[K_KINDS];
   int64_t total[K_KINDS];
@@ -81,7 +81,7 @@ __host__ __device__ inline StepLayout step_layout(int M, int kmax, int nst) {
   L.flags = off;
   off += 16;
   L.aux = off;
-  off += 256 * 4;
+  off += 512 * 4;
   L.attn = sal(off, 16);
   static_assert(sizeof(AttnSmem) % 16 == 0, "attention team buffers must stay 16-byte aligned");
   off = L.attn + 2 * (int)sizeof(AttnSmem);
@@ -108,8 +108,7 @@ static __device__ void wait_dep(const StepArgs& A, const int* cnt, int target, i
     for (uint32_t i = 0;; ++i) {
       if (ld_acquire(cnt) >= target) break;
       if (ld_volatile(A.abort_flag)) break;
-      __nanosleep(32);
-      if ((i & 31u) == 31u && globaltimer() - t0 > kWaitLimitNs) {
+      if ((i & 255u) == 255u && globaltimer() - t0 > kWaitLimitNs) {
         atomicOr(A.err, kErrDep);
         atomicExch(A.abort_flag, 1);
         break;
@@ -150,6 +149,7 @@ static __device__ GemvArgs gemv_op(const StepArgs& A, int kind, int l) {
     a.cs_b = A.cs_b;
     a.cs_h = A.cs_h;
     a.done = ctr(A, l, 0);
+    a.pos_ready = 1;
   } else if (kind == K_O) {
     a.x = A.attn;
     a.ldx = (int64_t)A.nq * 128;
@@ -222,6 +222,19 @@ __device__ __forceinline__ StepSeg step_seg(const StepArgs& A, int cta, int s) {
                                      : A.w_down + l * A.down_lb;
   const int64_t b0 = part_begin(A.total[kind], A.grid, cta), b1 = part_begin(A.total[kind], A.grid, cta + 1);
   return StepSeg{base + b0 * (int64_t)kBlockBytes, b1 - b0};
+}
+
+__device__ __forceinline__ int64_t attn_len_of(const StepArgs& A, int64_t pos) {
+  AttnArgs t = {};
+  t.cap = A.cap;
+  return attn_len(t, pos, false);
+}
+__device__ __forceinline__ int attn_active_of(const StepArgs& A, int64_t len, int64_t* chunk) {
+  AttnArgs t = {};
+  t.splits = A.splits;
+  t.chunk = A.chunk;
+  t.keys_per_split = A.keys_per_split;
+  return attn_active(t, len, chunk);
 }
 
 template <int M>
@@ -310,6 +323,18 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
     grid_dep_wait();
     int slot = 0, phase = 0;
     bool ok = true;
+    // the decode position does not change during the step: read it and its RoPE rows once
+    const int64_t pos = ld_cg_s64(A.pos);
+    const bool pos_in = pos >= 0 && pos < A.cap;
+    if (tid < 128 && pos_in) {
+      aux[tid] = bf16_to_f(A.cos[pos * 128 + tid]);
+      aux[128 + tid] = bf16_to_f(A.sin[pos * 128 + tid]);
+    }
+    if (tid == 0) {
+      flags[2] = pos_in ? (int)pos : -1;
+      if (!pos_in && cta == 0) atomicOr(A.err, QD_DEVERR_POS);
+    }
+    named_bar(kBarConsumers, kConsumers);
     // embedding: CTA i < M gathers row i (tied, packed E)
     if (cta < M) {
       int64_t t = ld_cg_s64(A.tok + cta);
@@ -328,7 +353,36 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
     stamp(A, cta, 0, 2, tid);
     const int team = warp >> 2, team_tid = tid & (kAttnThreads - 1);
     const int units = M * A.nkv * A.splits;
+    const int64_t len = attn_len_of(A, pos);
+    int64_t achunk;
+    const int n_use = attn_active_of(A, len, &achunk);
     for (int l = 0; l < A.L; ++l) {
+      // Off the critical path, at the start of the layer: prefetch into L2 what this layer reads that
+      // does not depend on this step's activations - the cached keys / values of this CTA's attention
+      // units (every position but the new one) and the layer's small RMSNorm weights (the weight
+      // stream, with its evict-first policy, keeps them out of L2 otherwise).
+      {
+        const int per_b = A.nkv * A.splits;
+        for (int u = cta + team * G; u < units; u += 2 * G) {
+          const int b = u / per_b, rem = u - b * per_b, kvh = rem / A.splits, sp = rem % A.splits;
+          if (sp >= n_use) continue;
+          const int64_t k0 = sp * achunk, k1 = (k0 + achunk < len - 1) ? k0 + achunk : len - 1;
+          const int64_t off = l * A.c_ls + b * A.cs_b + kvh * A.cs_h;
+          for (int64_t kk = k0 + team_tid * 32; kk < k1; kk += kAttnThreads * 32) {
+            const uint32_t bytes = (uint32_t)((k1 - kk < 32 ? k1 - kk : 32) * kHeadDim * 2);
+            prefetch_l2(A.kc + off + kk * kHeadDim, bytes);
+            prefetch_l2(A.vc + off + kk * kHeadDim, bytes);
+          }
+        }
+        const int hb = A.H * 2;  // bytes of one norm weight row (multiple of 256)
+        if (tid == 0) {
+          prefetch_l2(A.ln1 + (int64_t)l * A.H, hb);
+          prefetch_l2(A.ln2 + (int64_t)l * A.H, hb);
+          prefetch_l2(A.qn + (int64_t)l * 128, 256);
+          prefetch_l2(A.kn + (int64_t)l * 128, 256);
+          if (l == A.L - 1) prefetch_l2(A.fnorm, hb);
+        }
+      }
       // QKV projection + q/k norm + RoPE + K/V append
       wait_dep(A, l == 0 ? A.counters : ctr(A, l - 1, 4), l == 0 ? M : A.H / kBlockRows, tid);
       stamp(A, cta, 1 + 5 * l, 0, tid);
@@ -339,9 +393,9 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
         consume_blocks<M, MODE_QKV>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
       }
       stamp(A, cta, 1 + 5 * l, 2, tid);
-      // attention: units (sequence, KV head, split) over CTAs, two teams of 4 warps per CTA
-      wait_dep(A, ctr(A, l, 0), A.nq + 2 * A.nkv, tid);
-      stamp(A, cta, 2 + 5 * l, 0, tid);
+      // attention: units (sequence, KV head, split) over CTAs, two teams of 4 warps per CTA. The cached
+      // keys / values (all but the new one the QKV epilogue appends) do not depend on this layer's
+      // projection, so each unit's range is prefetched into L2 before waiting for it.
       {
         AttnArgs at = {};
         at.q = A.q;
@@ -363,10 +417,13 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
         at.tickets = A.attn_tickets;
         at.err = A.err;
         at.done = ctr(A, l, 1);
+        at.keys_per_split = A.keys_per_split;
         const int per_b = A.nkv * A.splits;
+        wait_dep(A, ctr(A, l, 0), A.nq + 2 * A.nkv, tid);
+        stamp(A, cta, 2 + 5 * l, 0, tid);
         for (int u = cta + team * G; u < units; u += 2 * G) {
           const int b = u / per_b, rem = u - b * per_b;
-          attn_unit(at, b, rem / A.splits, rem % A.splits, team_tid, 2 + team, asm_team[team]);
+          attn_unit(at, b, rem / A.splits, rem % A.splits, team_tid, 2 + team, asm_team[team], len);
         }
       }
       stamp(A, cta, 2 + 5 * l, 2, tid);
@@ -601,6 +658,7 @@ extern "C" int qd_decode_step(const qd_step_desc* d, void* scratch, int64_t scra
   a.prefetch_max = env_int("QD_PREFETCH_MAX_BLOCKS", 8);
   if (a.prefetch_max < a.prefetch) a.prefetch_max = a.prefetch;
   a.evict_first = env_int("QD_EVICT_FIRST", 1) != 0;
+  a.keys_per_split = attn_keys_per_split();
   a.splits = p.splits;
   a.kmax = p.kmax;
   a.chunk = p.chunk;
