@@ -48,7 +48,7 @@ def _args():
     p.add_argument("--cpu-steps", type=int, default=96, help="decode steps in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--kernel", default=None, choices=["qkv", "o", "gu", "down", "lm", "attn"],
+    p.add_argument("--kernel", default=None, choices=["qkv", "o", "gu", "down", "lm", "attn", "step"],
                    help="time one decode kernel alone (small profiling case; random packed weights on the GPU)")
     p.add_argument("--launches", type=int, default=8)
     return p.parse_args()
@@ -196,16 +196,18 @@ def gu_kernel_roofline(eng, st, launches_per_layer=3):
     return ms, nbytes
 
 
-def _traffic_from_profile():
-    """DRAM bytes per launch of the gate_up GEMV from the committed ncu summary (read + write)."""
-    path = os.path.join(REPO, "profiles", "gemv_gate_up_b1_full.md")
+def _traffic_from_profile(name):
+    """`key: integer` lines (DRAM bytes per launch and the algorithmic bytes of the captured case) from a
+    committed ncu summary under profiles/."""
+    out = {}
     try:
-        for line in open(path):
-            if line.startswith("traffic_bytes_per_launch:"):
-                return {"traffic_bytes_per_launch": int(line.split(":")[1])}
+        for line in open(os.path.join(REPO, "profiles", name)):
+            for key in ("traffic_bytes_per_launch", "algorithmic_bytes_per_launch"):
+                if line.startswith(key + ":"):
+                    out[key] = int(line.split(":")[1])
     except Exception:
         pass
-    return None
+    return out or None
 
 
 def run_ours(a):
@@ -288,18 +290,30 @@ def run_ours(a):
                "note": "decode tokens/s between the first and last yield of Engine.generate (host prompt list in, "
                        "host token lists out); the prompt upload is amortised over the steps in h2d_bytes_per_step"}
 
-    # ---------------- roofline of the dominant kernel (gate_up GEMV) and of the whole step
+    # ---------------- roofline of the dominant kernel and of the whole step
     peak, peak_kind = _peaks()
-    gu_ms, gu_bytes = gu_kernel_roofline(eng, st)
-    achieved = gu_bytes / (gu_ms / 1e3) / 1e9
-    prof = _traffic_from_profile()
-    roofline = {"bound": "hbm", "kernel": "qd gemv gate_up+SwiGLU (99.6 MB weights/launch)",
-                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                "peak_kind": peak_kind, "avg_launch_us": round(gu_ms * 1e3, 2), "algorithmic_bytes": gu_bytes,
-                "traffic": (prof or {}).get("traffic_bytes_per_launch")}
     L_avg = S + W + K / 2
     step_bytes = weight_bytes(cfg) + B * kv_bytes_per_token(cfg) * (L_avg + 1)
     step_gbs = step_bytes / (ms_step / 1e3) / 1e9
+    gu_ms, gu_bytes = gu_kernel_roofline(eng, st)
+    gu_gbs = gu_bytes / (gu_ms / 1e3) / 1e9
+    persistent = st.mode == "persistent"
+    if persistent:
+        # the timed region is one launch of the persistent step kernel per step: it is the kernel
+        prof = _traffic_from_profile("decode_step_kernel_b1.md")
+        traffic = None
+        if prof:  # ncu capture of a smaller (fewer layers) step, scaled by algorithmic bytes
+            traffic = round(prof["traffic_bytes_per_launch"] * step_bytes / prof["algorithmic_bytes_per_launch"])
+        roofline = {"bound": "hbm", "kernel": "qd step_kernel<1> (persistent whole decode step, 1 launch/step)",
+                    "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(step_gbs / peak, 4),
+                    "peak_kind": peak_kind, "avg_launch_us": round(ms_step * 1e3, 2),
+                    "algorithmic_bytes": int(step_bytes), "traffic": traffic}
+    else:
+        prof = _traffic_from_profile("gemv_gate_up_b1_full.md")
+        roofline = {"bound": "hbm", "kernel": "qd gemv gate_up+SwiGLU (99.6 MB weights/launch)",
+                    "achieved": round(gu_gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(gu_gbs / peak, 4),
+                    "peak_kind": peak_kind, "avg_launch_us": round(gu_ms * 1e3, 2), "algorithmic_bytes": gu_bytes,
+                    "traffic": (prof or {}).get("traffic_bytes_per_launch")}
 
     cpu = None
     if rank == 0 and not a.no_cpu_baseline:
@@ -323,8 +337,12 @@ def run_ours(a):
                "step_roofline": {"bytes_per_step": step_bytes, "achieved": round(step_gbs, 1), "peak": peak,
                                  "unit": "GB/s", "frac": round(step_gbs / peak, 4),
                                  "roofline_tokens_per_s": round(world * B * peak * 1e9 / step_bytes, 1)},
+               "kernel_rooflines": {"gate_up_gemv_per_op_kernel": {
+                   "achieved": round(gu_gbs, 1), "avg_launch_us": round(gu_ms * 1e3, 2),
+                   "frac": round(gu_gbs / peak, 4), "algorithmic_bytes": gu_bytes}},
+               "step_mode": st.mode,
                "clocks": clk.summary(), "e2e": e2e, "cpu_baseline": cpu,
-               "gpu_launches": K * (2 + 5 * a.layers)}
+               "gpu_launches": K * (1 if persistent else 2 + 5 * a.layers)}
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.barrier()
@@ -340,6 +358,8 @@ def run_kernel(a):
 
     dev = torch.device("cuda:0")
     torch.cuda.set_device(dev)
+    if a.kernel == "step":
+        return run_step_kernel(a)
     H, I, V, nq, nkv, D, B, L = 2560, 9728, 151936, 32, 8, 128, a.batch, a.layers
     g = torch.Generator(device=dev).manual_seed(0)
     rnd = lambda *shape: (torch.randn(shape, generator=g, device=dev) * 0.02).to(torch.bfloat16)  # noqa: E731
@@ -400,6 +420,45 @@ def run_kernel(a):
     print(json.dumps({"kernel": a.kernel, "batch": B, "copies": L, "launches": a.launches, "avg_us": round(us, 2),
                       "algorithmic_bytes": nbytes, "achieved_GBs": round(nbytes / us / 1e3, 1),
                       "frac_of_peak": round(nbytes / us / 1e3 / peak, 4), "peak": peak, "peak_kind": kind}))
+
+
+def run_step_kernel(a):
+    """The persistent step kernel alone on a `--layers`-layer synthetic model (profiling case)."""
+    import torch
+
+    import engine as E
+
+    state, cfg = make_model(a.layers)
+    eng = E.Engine.from_state_dict(state, cfg, "cuda:0")
+    del state
+    B, S = a.batch, a.prompt
+    st = eng._build(B, S, a.launches + 8)
+    with torch.inference_mode():
+        st.ids.copy_(torch.tensor(synth_prompt(B, S), dtype=torch.int64))
+        st.pos.fill_(S)
+        st.prefill_graph.replay()
+        for _ in range(3):
+            st.step()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(a.launches):
+            st.step()
+        e.record()
+        e.synchronize()
+    eng.check_device_errors(st)
+    us = s.elapsed_time(e) / a.launches * 1e3
+    nbytes = weight_bytes(cfg) + B * kv_bytes_per_token(cfg) * (S + 3 + a.launches / 2 + 1)
+    peak, kind = _peaks()
+    print(json.dumps({"kernel": "step", "layers": a.layers, "batch": B, "launches": a.launches, "avg_us": round(us, 2),
+                      "algorithmic_bytes": int(nbytes), "achieved_GBs": round(nbytes / us / 1e3, 1),
+                      "frac_of_peak": round(nbytes / us / 1e3 / peak, 4), "peak": peak, "peak_kind": kind}))
+
+
+def synth_prompt(B, S):
+    from decode_b200 import synth
+
+    return synth.random_prompt(B, S, 151936, seed=0)
 
 
 def main():
