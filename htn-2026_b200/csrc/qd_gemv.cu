@@ -224,7 +224,7 @@ static bool fill_common(GemvArgs& a, const Plan& p, const void* x, int64_t ldx, 
   a.cta_idx = reinterpret_cast<int*>(sc + p.off_cta_idx);
   a.partials = reinterpret_cast<float*>(sc + p.off_partials);
   a.smax = p.smax;
-  (void)M;
+  a.m_act = M;
   return true;
 }
 

@@ -37,6 +37,7 @@ constexpr int kStageBatch = 5;             // activation chunks per thread in fl
 struct GemvArgs {
   const __nv_bfloat16* x;
   int64_t ldx;
+  const char* x_packed;  // tensor-core path: activations packed as [k/64][N][64] swizzled tiles
   const char* w;
   int64_t n, n_valid, k;
   int kblocks;
@@ -52,6 +53,7 @@ struct GemvArgs {
   int* tickets;
   int smax;
   int* err;
+  int m_act;       // activation rows that are real (<= M; the tensor-core path pads M to 16s)
   int* done;       // optional: +1 (release) per finalized row group
   int pos_ready;   // QKV: flags[2] already holds the position and aux its cos/sin rows
   // QKV
@@ -216,15 +218,19 @@ __device__ void stage_x(const GemvArgs& a, __nv_bfloat16* xs, float* wsum, int t
 }
 
 // ------------------------------------------------------------------ epilogues (256 consumer threads)
-constexpr int kResPer = (8 * kBlockRows + kConsumers - 1) / kConsumers;  // residual values per thread
+template <int M>
+constexpr int res_per() {  // residual values per thread
+  return (M * kBlockRows + kConsumers - 1) / kConsumers;
+}
 
 // Residual values of group g this thread's epilogue adds (one L2 round trip for all of them).
 template <int M>
 __device__ __forceinline__ void load_res(const GemvArgs& a, int g, int tid, float* rv) {
+  constexpr int kResPer = res_per<M>();
 #pragma unroll
   for (int j = 0; j < kResPer; ++j) {
     const int idx = tid + j * kConsumers;
-    if (idx < M * kBlockRows) {
+    if (idx < a.m_act * kBlockRows) {
       const int m = idx >> 7, r = idx & 127;
       const uint16_t rb = __ldcg(reinterpret_cast<const unsigned short*>(a.res + m * a.ldr + (int64_t)g * kBlockRows + r));
       rv[j] = __uint_as_float((uint32_t)rb << 16);
@@ -235,7 +241,9 @@ __device__ __forceinline__ void load_res(const GemvArgs& a, int g, int tid, floa
 template <int M, int MODE>
 __device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum, float* lmv, int* lmi,
                                const float* aux, const int* flags, int tid, const float* res_pre = nullptr) {
+  const int MA = a.m_act;  // rows to emit (the rest of the M are padding)
   if constexpr (MODE == MODE_STORE || MODE == MODE_RES) {
+    constexpr int kResPer = res_per<M>();
     float rv[kResPer];
     if constexpr (MODE == MODE_RES) {
       if (res_pre) {
@@ -248,7 +256,7 @@ __device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum
 #pragma unroll
     for (int j = 0; j < kResPer; ++j) {
       const int idx = tid + j * kConsumers;
-      if (idx >= M * kBlockRows) continue;
+      if (idx >= MA * kBlockRows) continue;
       const int m = idx >> 7, r = idx & 127;
       const int64_t n = (int64_t)g * kBlockRows + r;
       float v = bf16r(red[idx]);
@@ -256,7 +264,7 @@ __device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum
       a.out[m * a.ldo + n] = __float2bfloat16_rn(v);
     }
   } else if constexpr (MODE == MODE_SWIGLU) {
-    for (int idx = tid; idx < M * 64; idx += kConsumers) {
+    for (int idx = tid; idx < MA * 64; idx += kConsumers) {
       const int m = idx >> 6, j = idx & 63;
       const float gv = bf16r(red[m * kBlockRows + j]);
       const float uv = bf16r(red[m * kBlockRows + 64 + j]);
@@ -268,30 +276,30 @@ __device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum
     const int lane = tid & 31;
     if (p < 0) return;           // out-of-range position: flagged, nothing written
     // BF16 projection output
-    for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
+    for (int idx = tid; idx < MA * kBlockRows; idx += kConsumers) {
       const float v = bf16r(red[idx]);
       red[idx] = v;
       if (a.raw_out) a.raw_out[(idx >> 7) * a.n + (int64_t)g * kBlockRows + (idx & 127)] = __float2bfloat16_rn(v);
     }
     if (g >= a.nq + a.nkv) {  // V head: append as is
       const int kvh = g - a.nq - a.nkv;
-      for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
+      for (int idx = tid; idx < MA * kBlockRows; idx += kConsumers) {
         const int m = idx >> 7, r = idx & 127;
         a.v_cache[m * a.cs_b + kvh * a.cs_h + p * 128 + r] = __float2bfloat16_rn(red[idx]);
       }
       return;
     }
     // per-head RMSNorm (Qwen3RMSNorm over 128): sum of squares per activation row
-    for (int base = 0; base < M * kBlockRows; base += kConsumers) {
+    for (int base = 0; base < MA * kBlockRows; base += kConsumers) {
       const int idx = base + tid;
       float sq = 0.f;
-      if (idx < M * kBlockRows) sq = red[idx] * red[idx];
+      if (idx < MA * kBlockRows) sq = red[idx] * red[idx];
       sq = warp_sum(sq);
-      if (lane == 0 && idx < M * kBlockRows) wsum[idx >> 5] = sq;  // one slot per 32 rows
+      if (lane == 0 && idx < MA * kBlockRows) wsum[idx >> 5] = sq;  // one slot per 32 rows
     }
     named_bar(kBarConsumers, kConsumers);
     const float* nw = aux + (g < a.nq ? 256 : 384);  // q_norm / k_norm, loaded once per op
-    for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
+    for (int idx = tid; idx < MA * kBlockRows; idx += kConsumers) {
       const int m = idx >> 7, r = idx & 127;
       const float var = (wsum[m * 4 + 0] + wsum[m * 4 + 1] + wsum[m * 4 + 2] + wsum[m * 4 + 3]) / 128.0f;
       const float rstd = 1.0f / sqrtf(var + a.eps);
@@ -299,7 +307,7 @@ __device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum
       red[idx] = y;  // each thread rewrites only its own entries; partners are read after the barrier
     }
     named_bar(kBarConsumers, kConsumers);
-    for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
+    for (int idx = tid; idx < MA * kBlockRows; idx += kConsumers) {
       const int m = idx >> 7, r = idx & 127;
       const float y = red[idx];
       const float yp = red[(idx & ~127) | (r ^ 64)];
@@ -316,11 +324,11 @@ __device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum
     }
   } else if constexpr (MODE == MODE_LM) {
     const int lane = tid & 31;
-    for (int base = 0; base < M * kBlockRows; base += kConsumers) {
+    for (int base = 0; base < MA * kBlockRows; base += kConsumers) {
       const int idx = base + tid;
       float v = -INFINITY;
       int n = 0x7fffffff;
-      if (idx < M * kBlockRows) {
+      if (idx < MA * kBlockRows) {
         const int m = idx >> 7, r = idx & 127;
         const int64_t row = (int64_t)g * kBlockRows + r;
         if (row < a.n_valid) {
@@ -338,13 +346,13 @@ __device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum
           n = on;
         }
       }
-      if (lane == 0 && idx < M * kBlockRows) {
+      if (lane == 0 && idx < MA * kBlockRows) {
         wsum[(idx >> 5) * 2] = v;
         reinterpret_cast<int*>(wsum)[(idx >> 5) * 2 + 1] = n;
       }
     }
     named_bar(kBarConsumers, kConsumers);
-    if (tid < M) {
+    if (tid < MA) {
       float bv = lmv[tid];
       int bi = lmi[tid];
       for (int q = 0; q < 4; ++q) {
@@ -361,17 +369,70 @@ __device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum
   }
 }
 
-// Consume this CTA's blocks of one projection from the ring (in issue order), flushing a segment
-// at every row-group end; ring position (slot, phase) carries across projections.
+// A CTA's segment of row group g (blocks seg_first..b) is reduced into red[m * 128 + r]. If the segment is
+// the whole group, run the epilogue; otherwise store the partial, take the group's ticket, and the CTA
+// that completes the group sums all partials in CTA order and runs the epilogue. 256 consumer threads.
 template <int M, int MODE>
-__device__ void consume_blocks(const GemvArgs& a, const Ring& R, int& slot, int& phase, int cta,
-                               const __nv_bfloat16* xs, float* red, float* wsum, float* lmv, int* lmi, int* flags,
-                               float* aux, int tid, bool& ok) {
-  const int warp = tid >> 5, lane = tid & 31;
-  if constexpr (MODE == MODE_QKV) {
-    if (tid < 256) aux[256 + tid] = bf16_to_f(tid < 128 ? a.q_norm[tid] : a.k_norm[tid - 128]);
-    if (!a.pos_ready) {
-    // the decode position and its cos/sin rows, once per op (the epilogue of every head uses them)
+__device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64_t b, int cta, float* red,
+                              float* wsum, float* lmv, int* lmi, float* aux, int* flags, int tid) {
+  const int64_t gb0 = (int64_t)g * a.kblocks;
+  const int nseg_blk = (int)(b + 1 - seg_first);
+  bool finalized = false;
+  if (seg_first == gb0 && nseg_blk == a.kblocks) {
+    finalize_group<M, MODE>(a, g, red, wsum, lmv, lmi, aux, flags, tid);
+    finalized = true;
+  } else {
+    const int c_lo = part_owner(a.total, a.grid, gb0);
+    float* dst = a.partials + ((int64_t)g * a.smax + (cta - c_lo)) * (M * kBlockRows);
+    for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) dst[idx] = red[idx];
+    named_bar(kBarConsumers, kConsumers);
+    if (tid == 0) {  // release our partial, acquire the others' when we complete the group
+      const int old = atom_add_acq_rel(a.tickets + g, nseg_blk);
+      flags[1] = (old + nseg_blk == a.kblocks) ? 1 : 0;
+    }
+    named_bar(kBarConsumers, kConsumers);
+    if (flags[1]) {
+      // every CTA in [c_lo, c_hi] owns a non-empty part of the group (T >= G): sum their partials
+      // in CTA order, eight loads in flight at a time
+      const int nseg = part_owner(a.total, a.grid, gb0 + a.kblocks - 1) - c_lo + 1;
+      const float* pbase = a.partials + (int64_t)g * a.smax * (M * kBlockRows);
+      float res_pre[res_per<M>()];
+      if constexpr (MODE == MODE_RES) load_res<M>(a, g, tid, res_pre);  // in flight with the partials
+      for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
+        float sum = 0.f;
+        int s = 0;
+        for (; s + 8 <= nseg; s += 8) {
+          float v[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] = ld_cg_f32(pbase + (int64_t)(s + j) * (M * kBlockRows) + idx);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) sum += v[j];
+        }
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          v[j] = (s + j < nseg) ? ld_cg_f32(pbase + (int64_t)(s + j) * (M * kBlockRows) + idx) : 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (s + j < nseg) sum += v[j];
+        red[idx] = sum;
+      }
+      named_bar(kBarConsumers, kConsumers);
+      finalize_group<M, MODE>(a, g, red, wsum, lmv, lmi, aux, flags, tid, MODE == MODE_RES ? res_pre : nullptr);
+      if (tid == 0) atomicExch(a.tickets + g, 0);
+      finalized = true;
+    }
+  }
+  if (finalized && a.done) signal_done(a.done, tid);
+  named_bar(kBarConsumers, kConsumers);
+}
+
+// QKV epilogue inputs, loaded once per op into shared memory: q_norm / k_norm (aux[256..511]) and,
+// unless the caller preloaded them (pos_ready), the decode position (flags[2]) and its cos/sin rows
+// (aux[0..255]). 256 consumer threads; ends with a barrier.
+__device__ __forceinline__ void qkv_prologue(const GemvArgs& a, float* aux, int* flags, int tid) {
+  if (tid < 256) aux[256 + tid] = bf16_to_f(tid < 128 ? a.q_norm[tid] : a.k_norm[tid - 128]);
+  if (!a.pos_ready) {
     const int64_t p = ld_cg_s64(a.pos);
     const bool in = p >= 0 && p < a.cap;
     if (tid < 128 && in) {
@@ -382,9 +443,18 @@ __device__ void consume_blocks(const GemvArgs& a, const Ring& R, int& slot, int&
       flags[2] = in ? (int)p : -1;
       if (!in && a.err) atomicOr(a.err, QD_DEVERR_POS);
     }
-    }
-    named_bar(kBarConsumers, kConsumers);
   }
+  named_bar(kBarConsumers, kConsumers);
+}
+
+// Consume this CTA's blocks of one projection from the ring (in issue order), flushing a segment
+// at every row-group end; ring position (slot, phase) carries across projections.
+template <int M, int MODE>
+__device__ void consume_blocks(const GemvArgs& a, const Ring& R, int& slot, int& phase, int cta,
+                               const __nv_bfloat16* xs, float* red, float* wsum, float* lmv, int* lmi, int* flags,
+                               float* aux, int tid, bool& ok) {
+  const int warp = tid >> 5, lane = tid & 31;
+  if constexpr (MODE == MODE_QKV) qkv_prologue(a, aux, flags, tid);
   const int64_t b_begin = part_begin(a.total, a.grid, cta);
   const int64_t b_end = part_begin(a.total, a.grid, cta + 1);
   const int rsub = lane >> 3;  // 0..3
@@ -459,57 +529,7 @@ __device__ void consume_blocks(const GemvArgs& a, const Ring& R, int& slot, int&
         if (c == 0) red[m * kBlockRows + 16 * warp + rsub + 4 * i] = v;
       }
     named_bar(kBarConsumers, kConsumers);
-    const int64_t gb0 = (int64_t)g * a.kblocks;
-    const int nseg_blk = (int)(b + 1 - seg_first);
-    bool finalized = false;
-    if (seg_first == gb0 && nseg_blk == a.kblocks) {
-      finalize_group<M, MODE>(a, g, red, wsum, lmv, lmi, aux, flags, tid);
-      finalized = true;
-    } else {
-      const int c_lo = part_owner(a.total, a.grid, gb0);
-      float* dst = a.partials + ((int64_t)g * a.smax + (cta - c_lo)) * (M * kBlockRows);
-      for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) dst[idx] = red[idx];
-      named_bar(kBarConsumers, kConsumers);
-      if (tid == 0) {  // release our partial, acquire the others' when we complete the group
-        const int old = atom_add_acq_rel(a.tickets + g, nseg_blk);
-        flags[1] = (old + nseg_blk == a.kblocks) ? 1 : 0;
-      }
-      named_bar(kBarConsumers, kConsumers);
-      if (flags[1]) {
-        // every CTA in [c_lo, c_hi] owns a non-empty part of the group (T >= G): sum their partials
-        // in CTA order, eight loads in flight at a time
-        const int nseg = part_owner(a.total, a.grid, gb0 + a.kblocks - 1) - c_lo + 1;
-        const float* pbase = a.partials + (int64_t)g * a.smax * (M * kBlockRows);
-        float res_pre[kResPer];
-        if constexpr (MODE == MODE_RES) load_res<M>(a, g, tid, res_pre);  // in flight with the partials
-        for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
-          float sum = 0.f;
-          int s = 0;
-          for (; s + 8 <= nseg; s += 8) {
-            float v[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = ld_cg_f32(pbase + (int64_t)(s + j) * (M * kBlockRows) + idx);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) sum += v[j];
-          }
-          float v[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            v[j] = (s + j < nseg) ? ld_cg_f32(pbase + (int64_t)(s + j) * (M * kBlockRows) + idx) : 0.f;
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            if (s + j < nseg) sum += v[j];
-          red[idx] = sum;
-        }
-        named_bar(kBarConsumers, kConsumers);
-        finalize_group<M, MODE>(a, g, red, wsum, lmv, lmi, aux, flags, tid,
-                                MODE == MODE_RES ? res_pre : nullptr);
-        if (tid == 0) atomicExch(a.tickets + g, 0);
-        finalized = true;
-      }
-    }
-    if (finalized && a.done) signal_done(a.done, tid);
-    named_bar(kBarConsumers, kConsumers);
+    flush_segment<M, MODE>(a, g, seg_first, b, cta, red, wsum, lmv, lmi, aux, flags, tid);
     seg_first = b + 1;
   }
 }
@@ -519,7 +539,7 @@ __device__ void consume_blocks(const GemvArgs& a, const Ring& R, int& slot, int&
 template <int M>
 __device__ bool lm_global_argmax(const GemvArgs& a, int cta, float* wsum, float* lmv, int* lmi, int* flags, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
-  if (tid < M) {
+  if (tid < a.m_act) {
     a.cta_val[tid * a.grid + cta] = lmv[tid];
     a.cta_idx[tid * a.grid + cta] = lmi[tid];
   }
@@ -527,10 +547,12 @@ __device__ bool lm_global_argmax(const GemvArgs& a, int cta, float* wsum, float*
   if (tid == 0) flags[1] = (atom_add_acq_rel(a.lm_ticket, 1) == a.grid - 1) ? 1 : 0;
   named_bar(kBarConsumers, kConsumers);
   if (!flags[1]) return false;
-  for (int m = 0; m < M; ++m) {
+  // one warp per activation row: lanes stride over the CTAs' candidates, then a shuffle reduction
+  for (int m = warp; m < a.m_act; m += kConsumerWarps) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int q = tid; q < a.grid; q += kConsumers) {
+#pragma unroll 4
+    for (int q = lane; q < a.grid; q += 32) {
       const float v = ld_cg_f32(a.cta_val + m * a.grid + q);
       const int n = (int)__ldcg(a.cta_idx + m * a.grid + q);
       if (v > bv || (v == bv && n < bi)) {
@@ -547,23 +569,7 @@ __device__ bool lm_global_argmax(const GemvArgs& a, int cta, float* wsum, float*
         bi = on;
       }
     }
-    if (lane == 0) {
-      wsum[warp * 2] = bv;
-      reinterpret_cast<int*>(wsum)[warp * 2 + 1] = bi;
-    }
-    named_bar(kBarConsumers, kConsumers);
-    if (tid == 0) {
-      for (int w8 = 1; w8 < kConsumerWarps; ++w8) {
-        const float v = wsum[w8 * 2];
-        const int n = reinterpret_cast<int*>(wsum)[w8 * 2 + 1];
-        if (v > bv || (v == bv && n < bi)) {
-          bv = v;
-          bi = n;
-        }
-      }
-      a.tok[m] = (int64_t)bi;
-    }
-    named_bar(kBarConsumers, kConsumers);
+    if (lane == 0) a.tok[m] = (int64_t)bi;
   }
   if (tid == 0) {
     if (a.inc_pos && a.pos_inc) a.pos_inc[0] = ld_cg_s64(a.pos_inc) + 1;

@@ -118,8 +118,10 @@ static __device__ void wait_dep(const StepArgs& A, const int* cnt, int target, i
   named_bar(kBarConsumers, kConsumers);
 }
 
+template <int M>
 static __device__ GemvArgs gemv_op(const StepArgs& A, int kind, int l) {
   GemvArgs a = {};
+  a.m_act = M;
   a.grid = A.grid;
   a.nst = A.nst;
   a.partials = A.partials;
@@ -387,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       wait_dep(A, l == 0 ? A.counters : ctr(A, l - 1, 4), l == 0 ? M : A.H / kBlockRows, tid);
       stamp(A, cta, 1 + 5 * l, 0, tid);
       {
-        const GemvArgs op = gemv_op(A, K_QKV, l);
+        const GemvArgs op = gemv_op<M>(A, K_QKV, l);
         stage_x<M>(op, xs, wsum, tid);
         stamp(A, cta, 1 + 5 * l, 1, tid);
         consume_blocks<M, MODE_QKV>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
@@ -431,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       wait_dep(A, ctr(A, l, 1), M * A.nkv, tid);
       stamp(A, cta, 3 + 5 * l, 0, tid);
       {
-        const GemvArgs op = gemv_op(A, K_O, l);
+        const GemvArgs op = gemv_op<M>(A, K_O, l);
         stage_x<M>(op, xs, wsum, tid);
         stamp(A, cta, 3 + 5 * l, 1, tid);
         consume_blocks<M, MODE_RES>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
@@ -441,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       wait_dep(A, ctr(A, l, 2), A.H / kBlockRows, tid);
       stamp(A, cta, 4 + 5 * l, 0, tid);
       {
-        const GemvArgs op = gemv_op(A, K_GU, l);
+        const GemvArgs op = gemv_op<M>(A, K_GU, l);
         stage_x<M>(op, xs, wsum, tid);
         stamp(A, cta, 4 + 5 * l, 1, tid);
         consume_blocks<M, MODE_SWIGLU>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
@@ -451,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       wait_dep(A, ctr(A, l, 3), 2 * A.I / kBlockRows, tid);
       stamp(A, cta, 5 + 5 * l, 0, tid);
       {
-        const GemvArgs op = gemv_op(A, K_DOWN, l);
+        const GemvArgs op = gemv_op<M>(A, K_DOWN, l);
         stage_x<M>(op, xs, wsum, tid);
         stamp(A, cta, 5 + 5 * l, 1, tid);
         consume_blocks<M, MODE_RES>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
@@ -462,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
     wait_dep(A, ctr(A, A.L - 1, 4), A.H / kBlockRows, tid);
     stamp(A, cta, 1 + 5 * A.L, 0, tid);
     {
-      const GemvArgs op = gemv_op(A, K_LM, 0);
+      const GemvArgs op = gemv_op<M>(A, K_LM, 0);
       stage_x<M>(op, xs, wsum, tid);
       stamp(A, cta, 1 + 5 * A.L, 1, tid);
       consume_blocks<M, MODE_LM>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);

@@ -172,6 +172,95 @@ class LmHeadArgmax:
         return tok
 
 
+# ------------------------------------------------------------------ tensor-core batch path (16..64 rows)
+TC_MIN_BATCH, TC_MAX_BATCH = 9, 64
+
+
+def tc_n_pad(m: int) -> int:
+    """Batch padded to the MMA N dimension (a multiple of 16, at most 64)."""
+    assert 1 <= m <= TC_MAX_BATCH
+    return (m + 15) // 16 * 16
+
+
+class PackedActivations:
+    """The activation operand of the tensor-core kernels: [k/64][n_pad][64] swizzled BF16 tiles, with the
+    RMSNorm prologue applied while packing (qd_pack_act). Padding rows stay zero."""
+
+    def __init__(self, m: int, k: int, device):
+        self.m, self.k, self.n_pad = m, k, tc_n_pad(m)
+        self.t = torch.zeros((k * self.n_pad,), dtype=BF16, device=device)
+
+    def pack(self, x, norm_w=None, eps: float = 1e-6, pdl=True):
+        _check_bf16(x, norm_w)
+        assert x.shape == (self.m, self.k) and x.stride(1) == 1
+        L.call("qd_pack_act", _ptr(x), x.stride(0), self.m, self.n_pad, self.k, _ptr(norm_w), eps, _ptr(self.t),
+               int(pdl), _stream())
+        return self
+
+
+class _TcOp:
+    def __init__(self, n_pad: int, n: int, k: int, device, grid: int = 0):
+        g, nbytes = ctypes.c_int(0), ctypes.c_int64(0)
+        L.call("qd_tc_gemv_plan", n, k, n_pad, grid, ctypes.byref(g), ctypes.byref(nbytes))
+        self.grid = g.value
+        self.scratch = torch.zeros((max(1, nbytes.value),), dtype=torch.uint8, device=device)
+
+
+class TcGemv(_TcOp):
+    """Gemv for 9..64 rows on the tensor cores; x comes packed (PackedActivations)."""
+
+    STORE, RES, SWIGLU = L.QD_EPI_STORE, L.QD_EPI_RES, L.QD_EPI_SWIGLU
+
+    def __init__(self, m: int, n: int, k: int, epilogue: int, device, grid: int = 0):
+        self.m, self.n, self.k, self.epilogue, self.n_pad = m, n, k, epilogue, tc_n_pad(m)
+        super().__init__(self.n_pad, n, k, device, grid)
+
+    def __call__(self, xp: PackedActivations, w, out, res=None, err=None, pdl=True):
+        _check_bf16(w, out, res)
+        assert xp.m == self.m and xp.k == self.k and out.stride(1) == 1
+        L.call("qd_tc_gemv", _ptr(xp.t), self.n_pad, self.m, _ptr(w), self.n, self.k, _ptr(out), out.stride(0),
+               _ptr(res), res.stride(0) if res is not None else 0, self.epilogue, self.grid, _ptr(self.scratch),
+               self.scratch.numel(), _ptr(err), int(pdl), _stream())
+        return out
+
+
+class TcQkvRopeAppend(_TcOp):
+    """QkvRopeAppend for 9..64 rows on the tensor cores (the ln1 RMSNorm is applied when packing)."""
+
+    def __init__(self, m: int, k: int, nq: int, nkv: int, device, grid: int = 0):
+        self.m, self.k, self.nq, self.nkv, self.n_pad = m, k, nq, nkv, tc_n_pad(m)
+        self.n = (nq + 2 * nkv) * 128
+        super().__init__(self.n_pad, self.n, k, device, grid)
+
+    def __call__(self, xp: PackedActivations, w, q_norm, k_norm, cos, sin, pos, q_out, k_cache, v_cache,
+                 raw_out=None, err=None, pdl=True):
+        _check_bf16(w, q_norm, k_norm, cos, sin, q_out, k_cache, v_cache, raw_out)
+        assert xp.m == self.m and pos.dtype == torch.int64
+        assert k_cache.stride(2) == 128 and k_cache.stride() == v_cache.stride()
+        L.call("qd_tc_qkv_rope_append", _ptr(xp.t), self.n_pad, self.m, _ptr(w), self.k, _ptr(q_norm),
+               _ptr(k_norm), _ptr(cos), _ptr(sin), _ptr(pos), k_cache.shape[2], self.nq, self.nkv, _ptr(q_out),
+               _ptr(k_cache), _ptr(v_cache), k_cache.stride(0), k_cache.stride(1), _ptr(raw_out), self.grid,
+               _ptr(self.scratch), self.scratch.numel(), _ptr(err), int(pdl), _stream())
+        return q_out
+
+
+class TcLmHeadArgmax(_TcOp):
+    """LmHeadArgmax for 9..64 rows on the tensor cores (the final RMSNorm is applied when packing)."""
+
+    def __init__(self, m: int, vocab: int, k: int, device, grid: int = 0):
+        self.m, self.vocab, self.k, self.n_pad = m, vocab, k, tc_n_pad(m)
+        super().__init__(self.n_pad, packed_rows(vocab), k, device, grid)
+
+    def __call__(self, xp: PackedActivations, e_packed, tok, pos=None, inc_pos=False, logits=None, err=None,
+                 pdl=True):
+        _check_bf16(e_packed, logits)
+        assert xp.m == self.m and tok.dtype == torch.int64
+        L.call("qd_tc_lm_head_argmax", _ptr(xp.t), self.n_pad, self.m, _ptr(e_packed), self.vocab, self.k,
+               _ptr(tok), _ptr(pos), int(inc_pos), _ptr(logits), logits.stride(0) if logits is not None else 0,
+               self.grid, _ptr(self.scratch), self.scratch.numel(), _ptr(err), int(pdl), _stream())
+        return tok
+
+
 class DecodeAttention:
     """Split-K GQA flash-decode + LSE merge for a fixed (batch, capacity); see qd_attn_decode."""
 

@@ -124,6 +124,39 @@ int qd_lm_head_argmax(const void* x, int64_t ldx, const void* e_packed, int64_t 
                       int64_t ld_logits, int grid, void* scratch, int64_t scratch_bytes, int* err, int pdl,
                       cudaStream_t stream);
 
+/* ---------------------------------------------------------------- tensor-core batch path (16..64 rows)
+ * The same projections for batches of 16 to 64 sequences on the tcgen05 tensor cores (swap-AB: the
+ * 128 weight rows of a packed block are the MMA M dimension, the batch padded to n_pad in
+ * {16, 32, 48, 64} is N, fp32 accumulators in tensor memory). Replaces FastGemm at M > 8
+ * (engine/kernels/fast.py:173-213, whose Triton tl.dot tile covers up to GEMV_MAX_B = 64 rows,
+ * engine/engine.py:91) and FastLmHead at the same batch sizes (fast.py:439-465). Results equal
+ * qd_gemv / qd_qkv_rope_append / qd_lm_head_argmax up to the fp32 summation order of the dot
+ * products (rounded to BF16 at the same points).
+ *
+ * qd_pack_act writes the activation operand: xpk = [k / 64][n_pad][64] BF16 tiles in the
+ * 128-byte-swizzled K-major layout of the weight blocks (16-byte chunk c of row m at c ^ (m & 7)),
+ * from x [m_act, k] (row stride ldx), with the RMSNorm prologue applied when norm_w is given. Rows
+ * m_act..n_pad-1 are not written: zero them once (their products are computed and discarded).
+ * xpk needs k * n_pad * 2 bytes, 16-byte aligned. */
+int qd_pack_act(const void* x, int64_t ldx, int m_act, int n_pad, int64_t k, const void* norm_w, float eps, void* xpk,
+                int pdl, cudaStream_t stream);
+/* grid_hint <= 0 picks one CTA per SM. Scratch (zero-filled once, self-resetting) depends on n_pad. */
+int qd_tc_gemv_plan(int64_t n, int64_t k, int n_pad, int grid_hint, int* grid, int64_t* scratch_bytes);
+/* qd_gemv's STORE / RES / SWIGLU epilogues for rows 0..m_act-1 of the packed activations. */
+int qd_tc_gemv(const void* xpk, int n_pad, int m_act, const void* w_packed, int64_t n, int64_t k, void* out,
+               int64_t ldo, const void* res, int64_t ldr, int epilogue, int grid, void* scratch,
+               int64_t scratch_bytes, int* err, int pdl, cudaStream_t stream);
+/* qd_qkv_rope_append from packed activations (plan with n = (nq + 2 nkv) * 128). */
+int qd_tc_qkv_rope_append(const void* xpk, int n_pad, int m_act, const void* w_packed, int64_t k, const void* q_norm,
+                          const void* k_norm, const void* cos, const void* sin, const int64_t* pos, int64_t cap,
+                          int nq_heads, int nkv_heads, void* q_out, void* k_cache, void* v_cache, int64_t cs_b,
+                          int64_t cs_h, void* raw_out, int grid, void* scratch, int64_t scratch_bytes, int* err,
+                          int pdl, cudaStream_t stream);
+/* qd_lm_head_argmax from packed activations (plan with n = vocab rounded up to 128). */
+int qd_tc_lm_head_argmax(const void* xpk, int n_pad, int m_act, const void* e_packed, int64_t vocab, int64_t k,
+                         int64_t* tok, int64_t* pos, int inc_pos, void* logits_out, int64_t ld_logits, int grid,
+                         void* scratch, int64_t scratch_bytes, int* err, int pdl, cudaStream_t stream);
+
 /* ---------------------------------------------------------------- decode attention
  * Split-K GQA flash-decode with a log-sum-exp merge. Replaces DecodeAttention
  * (engine/kernels/decode_attn.py:26-119) and the flash-decode + merge part of FastAttention
