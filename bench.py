@@ -51,6 +51,10 @@ def _args():
     p.add_argument("--kernel", default=None, choices=["qkv", "o", "gu", "down", "lm", "attn", "step"],
                    help="time one decode kernel alone (small profiling case; random packed weights on the GPU)")
     p.add_argument("--launches", type=int, default=8)
+    p.add_argument("--tc", action="store_true", help="with --kernel: the tcgen05 kernel (activations pre-packed)")
+    p.add_argument("--sweep", default=None, choices=["linear", "attn"],
+                   help="BASELINE config 2 (decode linear shapes x batch x kernel path) or config 3 (GQA decode "
+                        "attention); one JSON line per case")
     return p.parse_args()
 
 
@@ -179,15 +183,20 @@ def gu_kernel_roofline(eng, st, launches_per_layer=3):
 
     L = eng.n_layers
     stream = torch.cuda.current_stream()
+    if st.mode == "tc":  # tensor-core kernel on the packed activations (packing is a separate launch)
+        st.xp_h.pack(st.x, eng.ln2[0], eng.eps, False)
+        gu = lambda i: st.gu(st.xp_h, eng.w_gu[i], st.act, pdl=False)  # noqa: E731
+    else:
+        gu = lambda i: st.gu(st.x, eng.w_gu[i], st.act, norm_w=eng.ln2[i], pdl=False)  # noqa: E731
     for i in range(min(L, 4)):
-        st.gu(st.x, eng.w_gu[i], st.act, norm_w=eng.ln2[i], pdl=False)
+        gu(i)
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n = 0
     s.record(stream)
     for _ in range(launches_per_layer):
         for i in range(L):
-            st.gu(st.x, eng.w_gu[i], st.act, norm_w=eng.ln2[i], pdl=False)
+            gu(i)
             n += 1
     e.record(stream)
     e.synchronize()
@@ -342,7 +351,7 @@ def run_ours(a):
                    "frac": round(gu_gbs / peak, 4), "algorithmic_bytes": gu_bytes}},
                "step_mode": st.mode,
                "clocks": clk.summary(), "e2e": e2e, "cpu_baseline": cpu,
-               "gpu_launches": K * (1 if persistent else 2 + 5 * a.layers)}
+               "gpu_launches": K * {"persistent": 1, "kernels": 2 + 5 * a.layers, "tc": 3 + 9 * a.layers}[st.mode]}
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.barrier()
@@ -381,7 +390,23 @@ def run_kernel(a):
         shapes = {"qkv": ((nq + 2 * nkv) * D, H), "o": (H, nq * D), "gu": (2 * I, H), "down": (H, I), "lm": (V, H)}
         n, k = shapes[a.kernel]
         ws = [ops.pack_matrix(rnd(n, k)) for _ in range(L)]
-        if a.kernel == "qkv":
+        if a.tc:
+            xp = ops.PackedActivations(B, k, dev).pack(x[:, :k].contiguous())
+            outb = torch.zeros((B, n), dtype=torch.bfloat16, device=dev)
+            if a.kernel == "lm":
+                plan = ops.TcLmHeadArgmax(B, V, H, dev)
+                tok = torch.zeros((B,), dtype=torch.int64, device=dev)
+                fn = lambda i: plan(xp, ws[i], tok, err=err, pdl=False)  # noqa: E731
+            else:
+                epi = {"o": ops.TcGemv.RES, "gu": ops.TcGemv.SWIGLU, "down": ops.TcGemv.RES,
+                       "qkv": ops.TcGemv.STORE}[a.kernel]
+                plan = ops.TcGemv(B, n, k, epi, dev)
+                if epi == ops.TcGemv.RES:
+                    fn = lambda i: plan(xp, ws[i], outb, res=outb, err=err, pdl=False)  # noqa: E731
+                else:
+                    o = outb[:, : n // 2] if epi == ops.TcGemv.SWIGLU else outb
+                    fn = lambda i: plan(xp, ws[i], o, err=err, pdl=False)  # noqa: E731
+        elif a.kernel == "qkv":
             from engine import rope_tables
 
             cos, sin = (t.to(dev) for t in rope_tables(cap, D, 5e6))
@@ -417,7 +442,8 @@ def run_kernel(a):
     us = s.elapsed_time(e) / a.launches * 1e3
     assert int(err.item()) == 0
     peak, kind = _peaks()
-    print(json.dumps({"kernel": a.kernel, "batch": B, "copies": L, "launches": a.launches, "avg_us": round(us, 2),
+    print(json.dumps({"kernel": a.kernel + ("_tc" if a.tc else ""), "batch": B, "copies": L,
+                      "launches": a.launches, "avg_us": round(us, 2),
                       "algorithmic_bytes": nbytes, "achieved_GBs": round(nbytes / us / 1e3, 1),
                       "frac_of_peak": round(nbytes / us / 1e3 / peak, 4), "peak": peak, "peak_kind": kind}))
 
@@ -455,6 +481,202 @@ def run_step_kernel(a):
                       "frac_of_peak": round(nbytes / us / 1e3 / peak, 4), "peak": peak, "peak_kind": kind}))
 
 
+def _time_cycle(fn, copies, launches):
+    """Average device time of fn(i) in ms, cycling over `copies` operand sets (CUDA events on the
+    launching stream, after warm-up)."""
+    import torch
+
+    for i in range(min(3, launches)):
+        fn(i % copies)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(launches):
+        fn(i % copies)
+    e.record()
+    e.synchronize()
+    return s.elapsed_time(e) / launches
+
+
+def run_sweep_linear(a):
+    """the five decode projections (K -> N) at M in {1, 4, 16, 64}, each with its plain
+    BF16 store and with its fused epilogue, on three paths:
+      cuda_core  the streaming GEMV (qd_gemv / qd_qkv_rope_append / qd_lm_head_argmax), M > 8 as
+                 ceil(M / 8) launches of 8 rows (each re-streams the weights)
+      tc         the tcgen05 kernels (qd_tc_*), timed alone and with the activation packing launch
+      cublas     torch F.linear on row-major weights (store only), the library baseline
+    Weights N(0, 0.02), activations N(0, 1), seed 1; every case cycles over enough weight copies to
+    exceed twice the L2. Bytes = 2NK + 2MK + 2MN (+ 2MN for a residual read); flops = 2MNK."""
+    import torch
+    import torch.nn.functional as F
+
+    from decode_b200 import ops
+    from engine import rope_tables
+
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    peak, kind = _peaks()
+    tpeak = _tensor_peak()
+    H, I, V, nq, nkv, D = 2560, 9728, 151936, 32, 8, 128
+    shapes = [("qkv", (nq + 2 * nkv) * D, H), ("o", H, nq * D), ("gu", 2 * I, H), ("down", H, I), ("lm", V, H)]
+    g = torch.Generator(device=dev).manual_seed(1)
+    err = torch.zeros((1,), dtype=torch.int32, device=dev)
+    cap = 64
+    cos, sin = (t.to(dev) for t in rope_tables(cap, D, 5e6))
+    pos = torch.tensor([cap - 1], dtype=torch.int64, device=dev)
+    ones_d = torch.ones(D, dtype=torch.bfloat16, device=dev)
+    launches = max(a.launches, 24)
+    for name, n, k in shapes:
+        copies = max(2, -(-(300 << 20) // (2 * n * k)))
+        wrm = [(torch.randn((n, k), generator=g, device=dev) * 0.02).to(torch.bfloat16) for _ in range(copies)]
+        wpk = [ops.pack_matrix(w) for w in wrm]
+        ones_k = torch.ones(k, dtype=torch.bfloat16, device=dev)
+        for M in (1, 4, 16, 64):
+            x = torch.randn((M, k), generator=g, device=dev).to(torch.bfloat16)
+            base = 2 * n * k + 2 * M * k + 2 * M * n
+            cases = []
+            # ---- cuda-core GEMV path (chunks of at most 8 rows)
+            chunks = [(r, min(M, r + 8)) for r in range(0, M, 8)]
+            for epi in ("store", "fused"):
+                outb = torch.zeros((M, n), dtype=torch.bfloat16, device=dev)
+                if name == "lm" and epi == "fused":
+                    plans = [ops.LmHeadArgmax(r1 - r0, V, k, dev) for r0, r1 in chunks]
+                    tok = torch.zeros((M,), dtype=torch.int64, device=dev)
+
+                    def fn(i, plans=plans, tok=tok, x=x):
+                        for (r0, r1), p in zip(chunks, plans):
+                            p(x[r0:r1], wpk[i], ones_k, tok[r0:r1], err=err, pdl=False)
+                elif name == "qkv" and epi == "fused":
+                    plans = [ops.QkvRopeAppend(r1 - r0, k, nq, nkv, dev) for r0, r1 in chunks]
+                    kc = torch.zeros((M, nkv, cap, D), dtype=torch.bfloat16, device=dev)
+                    vc, q = torch.zeros_like(kc), torch.empty((M, nq, D), dtype=torch.bfloat16, device=dev)
+
+                    def fn(i, plans=plans, kc=kc, vc=vc, q=q, x=x):
+                        for (r0, r1), p in zip(chunks, plans):
+                            p(x[r0:r1], wpk[i], ones_k, ones_d, ones_d, cos, sin, pos, q[r0:r1], kc[r0:r1],
+                              vc[r0:r1], err=err, pdl=False)
+                else:
+                    e = ops.Gemv.STORE
+                    if epi == "fused":
+                        e = {"o": ops.Gemv.RES, "down": ops.Gemv.RES, "gu": ops.Gemv.SWIGLU}[name]
+                    plans = [ops.Gemv(r1 - r0, n, k, e, dev) for r0, r1 in chunks]
+
+                    def fn(i, plans=plans, e=e, outb=outb, x=x):
+                        for (r0, r1), p in zip(chunks, plans):
+                            if e == ops.Gemv.RES:
+                                p(x[r0:r1], wpk[i], outb[r0:r1], res=outb[r0:r1], err=err, pdl=False)
+                            elif e == ops.Gemv.SWIGLU:
+                                p(x[r0:r1], wpk[i], outb[r0:r1, : n // 2], norm_w=ones_k, err=err, pdl=False)
+                            else:
+                                p(x[r0:r1], wpk[i], outb[r0:r1], err=err, pdl=False)
+                cases.append(("cuda_core", epi, fn, len(chunks)))
+            # ---- tensor-core path
+            xp = ops.PackedActivations(M, k, dev)
+            xp.pack(x)
+            for epi in ("store", "fused"):
+                outb = torch.zeros((M, n), dtype=torch.bfloat16, device=dev)
+                norm = None
+                if name == "lm" and epi == "fused":
+                    p = ops.TcLmHeadArgmax(M, V, k, dev)
+                    tok = torch.zeros((M,), dtype=torch.int64, device=dev)
+                    op = lambda i, p=p, tok=tok: p(xp, wpk[i], tok, err=err, pdl=False)  # noqa: E731
+                    norm = ones_k
+                elif name == "qkv" and epi == "fused":
+                    p = ops.TcQkvRopeAppend(M, k, nq, nkv, dev)
+                    kc = torch.zeros((M, nkv, cap, D), dtype=torch.bfloat16, device=dev)
+                    vc, q = torch.zeros_like(kc), torch.empty((M, nq, D), dtype=torch.bfloat16, device=dev)
+                    op = lambda i, p=p, kc=kc, vc=vc, q=q: p(xp, wpk[i], ones_d, ones_d, cos, sin, pos, q, kc,  # noqa: E731
+                                                             vc, err=err, pdl=False)
+                    norm = ones_k
+                else:
+                    e = ops.TcGemv.STORE
+                    if epi == "fused":
+                        e = {"o": ops.TcGemv.RES, "down": ops.TcGemv.RES, "gu": ops.TcGemv.SWIGLU}[name]
+                        norm = ones_k if name == "gu" else None
+                    p = ops.TcGemv(M, n, k, e, dev)
+                    if e == ops.TcGemv.RES:
+                        op = lambda i, p=p, o=outb: p(xp, wpk[i], o, res=o, err=err, pdl=False)  # noqa: E731
+                    elif e == ops.TcGemv.SWIGLU:
+                        op = lambda i, p=p, o=outb: p(xp, wpk[i], o[:, : n // 2], err=err, pdl=False)  # noqa: E731
+                    else:
+                        op = lambda i, p=p, o=outb: p(xp, wpk[i], o, err=err, pdl=False)  # noqa: E731
+                cases.append(("tc_kernel", epi, op, 1))
+                cases.append(("tc", epi, lambda i, op=op, norm=norm, x=x: (xp.pack(x, norm, 1e-6, False), op(i)), 2))
+            # ---- cuBLAS
+            outc = torch.empty((M, n), dtype=torch.bfloat16, device=dev)
+            cases.append(("cublas", "store", lambda i, x=x, o=outc: torch.matmul(x, wrm[i].t(), out=o), 1))
+            for path, epi, fn, nl in cases:
+                ms = _time_cycle(fn, copies, launches)
+                nbytes = base + (2 * M * n if epi == "fused" and name in ("o", "down") else 0)
+                if epi == "fused" and name == "gu":
+                    nbytes = 2 * n * k + 2 * M * k + M * n  # output is M x n/2
+                if epi == "fused" and name == "lm":
+                    nbytes = 2 * n * k + 2 * M * k + 8 * M  # argmax only, no logits written
+                flops = 2 * M * n * k
+                gbs = nbytes / (ms / 1e3) / 1e9
+                print(json.dumps({"sweep": "linear", "shape": name, "n": n, "k": k, "M": M, "path": path,
+                                  "epilogue": epi, "launches": nl, "us": round(ms * 1e3, 2), "GBs": round(gbs, 1),
+                                  "frac_hbm": round(gbs / peak, 4), "TFLOPs": round(flops / (ms / 1e3) / 1e12, 2),
+                                  "frac_tensor": round(flops / (ms / 1e3) / 1e12 / tpeak, 4),
+                                  "peak_hbm": peak, "peak_kind": kind}), flush=True)
+            assert int(err.item()) == 0
+        del wrm, wpk
+        torch.cuda.empty_cache()
+
+
+def run_sweep_attn(a):
+    """GQA decode attention (32 q / 8 KV heads, D 128) at B in {1, 8, 32} and cache
+    length L in {1024, 8192, 32768}, Q/K/V N(0, 1) seed 2: ours_stream (qd_attn_decode_stream, the
+    engine's kernel above 8 sequences), ours_team (qd_attn_decode, the per-unit kernel whose arithmetic
+    the persistent step kernel shares) and torch SDPA with enable_gqa (the library baseline).
+    Bytes = 4096 B L (K + V) + 2 x 8192 B (q, out)."""
+    import torch
+    import torch.nn.functional as F
+
+    from decode_b200 import ops
+
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    peak, kind = _peaks()
+    nq, nkv, D = 32, 8, 128
+    g = torch.Generator(device=dev).manual_seed(2)
+    err = torch.zeros((1,), dtype=torch.int32, device=dev)
+    launches = max(a.launches, 24)
+    for B in (1, 8, 32):
+        for L in (1024, 8192, 32768):
+            per = 2 * B * nkv * L * D * 2
+            copies = max(2, -(-(300 << 20) // per))
+            kc = [torch.randn((B, nkv, L, D), generator=g, device=dev).to(torch.bfloat16) for _ in range(copies)]
+            vc = [torch.randn((B, nkv, L, D), generator=g, device=dev).to(torch.bfloat16) for _ in range(copies)]
+            q = torch.randn((B, nq, D), generator=g, device=dev).to(torch.bfloat16)
+            out = torch.empty((B, nq, D), dtype=torch.bfloat16, device=dev)
+            attn = ops.DecodeAttention(B, nq, nkv, L, dev)
+            stream = ops.DecodeAttentionStream(B, nq, nkv, L, dev)
+            pos = torch.tensor([L - 1], dtype=torch.int64, device=dev)
+            q4 = q.view(B, nq, 1, D)
+            nbytes = 4096 * B * L + 2 * 8192 * B
+            for path, fn in (("ours_stream", lambda i: stream(q, kc[i], vc[i], pos, out, err=err, pdl=False)),
+                             ("ours_team", lambda i: attn(q, kc[i], vc[i], pos, out, err=err, pdl=False)),
+                             ("torch_sdpa", lambda i: F.scaled_dot_product_attention(
+                                 q4, kc[i], vc[i], scale=D ** -0.5, enable_gqa=True))):
+                ms = _time_cycle(fn, copies, launches)
+                gbs = nbytes / (ms / 1e3) / 1e9
+                print(json.dumps({"sweep": "attn", "B": B, "L": L, "path": path, "splits": attn.splits,
+                                  "us": round(ms * 1e3, 2), "GBs": round(gbs, 1), "frac_hbm": round(gbs / peak, 4),
+                                  "peak_hbm": peak, "peak_kind": kind}), flush=True)
+            assert int(err.item()) == 0
+            del kc, vc
+            torch.cuda.empty_cache()
+
+
+def _tensor_peak():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except Exception:
+        return 1590.0
+
+
 def synth_prompt(B, S):
     from decode_b200 import synth
 
@@ -463,7 +685,11 @@ def synth_prompt(B, S):
 
 def main():
     a = _args()
-    if a.kernel:
+    if a.sweep == "linear":
+        run_sweep_linear(a)
+    elif a.sweep == "attn":
+        run_sweep_attn(a)
+    elif a.kernel:
         run_kernel(a)
     elif a.impl == "reference":
         run_reference(a)

@@ -42,13 +42,16 @@ struct AttnArgs {
 };
 
 // Valid length (pos + 1) clamped to the cache; flags QD_DEVERR_POS when the position is outside it.
-__device__ __forceinline__ int64_t attn_len(const AttnArgs& a, int64_t pos, bool flag) {
+__device__ __forceinline__ int64_t attn_len_at(int64_t pos, int64_t cap, int* err, bool flag) {
   int64_t len = pos + 1;
-  if (len < 1 || len > a.cap) {
-    if (flag && a.err) atomicOr(a.err, QD_DEVERR_POS);
-    len = len < 1 ? 1 : a.cap;
+  if (len < 1 || len > cap) {
+    if (flag && err) atomicOr(err, QD_DEVERR_POS);
+    len = len < 1 ? 1 : cap;
   }
   return len;
+}
+__device__ __forceinline__ int64_t attn_len(const AttnArgs& a, int64_t pos, bool flag) {
+  return attn_len_at(pos, a.cap, a.err, flag);
 }
 
 // Splits in use at length len (every unit computes the same value): about keys_per_split keys each,

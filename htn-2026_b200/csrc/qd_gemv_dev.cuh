@@ -383,8 +383,17 @@ __device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64
     finalized = true;
   } else {
     const int c_lo = part_owner(a.total, a.grid, gb0);
-    float* dst = a.partials + ((int64_t)g * a.smax + (cta - c_lo)) * (M * kBlockRows);
-    for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) dst[idx] = red[idx];
+    // partials move as float4: kPer per thread, kSB segments' worth of loads in flight at a time
+    constexpr int kVec = M * kBlockRows / 4;
+    constexpr int kPer = (kVec + kConsumers - 1) / kConsumers;
+    constexpr int kSB = kPer >= 4 ? 2 : 8 / kPer;
+    float4* dst = reinterpret_cast<float4*>(a.partials + ((int64_t)g * a.smax + (cta - c_lo)) * (M * kBlockRows));
+    float4* red4 = reinterpret_cast<float4*>(red);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int q = tid + j * kConsumers;
+      if (q < kVec) __stcg(dst + q, red4[q]);
+    }
     named_bar(kBarConsumers, kConsumers);
     if (tid == 0) {  // release our partial, acquire the others' when we complete the group
       const int old = atom_add_acq_rel(a.tickets + g, nseg_blk);
@@ -393,29 +402,39 @@ __device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64
     named_bar(kBarConsumers, kConsumers);
     if (flags[1]) {
       // every CTA in [c_lo, c_hi] owns a non-empty part of the group (T >= G): sum their partials
-      // in CTA order, eight loads in flight at a time
+      // in CTA order
       const int nseg = part_owner(a.total, a.grid, gb0 + a.kblocks - 1) - c_lo + 1;
-      const float* pbase = a.partials + (int64_t)g * a.smax * (M * kBlockRows);
+      const float4* pbase = reinterpret_cast<const float4*>(a.partials + (int64_t)g * a.smax * (M * kBlockRows));
       float res_pre[res_per<M>()];
       if constexpr (MODE == MODE_RES) load_res<M>(a, g, tid, res_pre);  // in flight with the partials
-      for (int idx = tid; idx < M * kBlockRows; idx += kConsumers) {
-        float sum = 0.f;
-        int s = 0;
-        for (; s + 8 <= nseg; s += 8) {
-          float v[8];
+      float4 acc[kPer];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) v[j] = ld_cg_f32(pbase + (int64_t)(s + j) * (M * kBlockRows) + idx);
+      for (int j = 0; j < kPer; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int s0 = 0; s0 < nseg; s0 += kSB) {
+        float4 v[kSB][kPer];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) sum += v[j];
-        }
-        float v[8];
+        for (int b2 = 0; b2 < kSB; ++b2)
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          v[j] = (s + j < nseg) ? ld_cg_f32(pbase + (int64_t)(s + j) * (M * kBlockRows) + idx) : 0.f;
+          for (int j = 0; j < kPer; ++j) {
+            const int q = tid + j * kConsumers;
+            v[b2][j] = (s0 + b2 < nseg && q < kVec) ? __ldcg(pbase + (int64_t)(s0 + b2) * kVec + q)
+                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (s + j < nseg) sum += v[j];
-        red[idx] = sum;
+        for (int b2 = 0; b2 < kSB; ++b2)
+#pragma unroll
+          for (int j = 0; j < kPer; ++j)
+            if (s0 + b2 < nseg) {
+              acc[j].x += v[b2][j].x;
+              acc[j].y += v[b2][j].y;
+              acc[j].z += v[b2][j].z;
+              acc[j].w += v[b2][j].w;
+            }
+      }
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int q = tid + j * kConsumers;
+        if (q < kVec) red4[q] = acc[j];
       }
       named_bar(kBarConsumers, kConsumers);
       finalize_group<M, MODE>(a, g, red, wsum, lmv, lmi, aux, flags, tid, MODE == MODE_RES ? res_pre : nullptr);

@@ -150,32 +150,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemv_kernel(const __grid_con
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
-      const int64_t nblk = b_end - b_begin;
-      const int first = (int)(nblk < nst ? nblk : nst);
-      // weights never depend on the preceding kernel: the first ring's worth go out before waiting on it
+      const int nblk = (int)(b_end - b_begin);
+      const char* wsrc = a.w + b_begin * (int64_t)kBlockBytes;
+      const int first = nblk < nst ? nblk : nst;
+      const int ahead = a.prefetch;
+      int pf = 0;
+      // weights never depend on the preceding kernel: L2 prefetch and the first ring's worth of copies
+      // go out before waiting on it
+      for (; pf < nblk && pf < first + ahead; ++pf) prefetch_l2(wsrc + pf * (int64_t)kBlockBytes, kBlockBytes);
       for (int i = 0; i < first; ++i) {
         mbar_arrive_expect_tx(full_bar(i), (uint32_t)(kBlockBytes + xtile));
-        bulk_g2s(smem_u32(ring + i * Ly.stage), a.w + (b_begin + i) * (int64_t)kBlockBytes, kBlockBytes,
-                 full_bar(i), pol);
+        bulk_g2s(smem_u32(ring + i * Ly.stage), wsrc + i * (int64_t)kBlockBytes, kBlockBytes, full_bar(i), pol);
       }
       grid_dep_wait();
+      int kb = (int)(b_begin % a.kblocks);
       for (int i = 0; i < first; ++i) {
-        const int kb = (int)((b_begin + i) % a.kblocks);
         bulk_g2s(smem_u32(ring + i * Ly.stage + kBlockBytes), a.x_packed + kb * xtile, (uint32_t)xtile, full_bar(i),
                  pol);
+        if (++kb == a.kblocks) kb = 0;
       }
-      int issued = first;
-      for (int64_t i = first; i < nblk; ++i) {
-        const int s = (int)(i % nst);
-        const int round = (int)(i / nst);
-        if (!mbar_wait(empty_bar(s), (round - 1) & 1, a.err, kErrWaitEmpty)) break;
-        const int kb = (int)((b_begin + i) % a.kblocks);
-        mbar_arrive_expect_tx(full_bar(s), (uint32_t)(kBlockBytes + xtile));
-        bulk_g2s(smem_u32(ring + s * Ly.stage), a.w + (b_begin + i) * (int64_t)kBlockBytes, kBlockBytes, full_bar(s),
-                 pol);
-        bulk_g2s(smem_u32(ring + s * Ly.stage + kBlockBytes), a.x_packed + kb * xtile, (uint32_t)xtile,
-                 full_bar(s), pol);
+      int issued = first, slot = 0, round = 1;
+      for (int i = first; i < nblk; ++i) {
+        for (; pf < nblk && pf <= i + ahead; ++pf) prefetch_l2(wsrc + pf * (int64_t)kBlockBytes, kBlockBytes);
+        if (!mbar_wait(empty_bar(slot), (round - 1) & 1, a.err, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(full_bar(slot), (uint32_t)(kBlockBytes + xtile));
+        bulk_g2s(smem_u32(ring + slot * Ly.stage), wsrc + i * (int64_t)kBlockBytes, kBlockBytes, full_bar(slot), pol);
+        bulk_g2s(smem_u32(ring + slot * Ly.stage + kBlockBytes), a.x_packed + kb * xtile, (uint32_t)xtile,
+                 full_bar(slot), pol);
+        if (++kb == a.kblocks) kb = 0;
         ++issued;
+        if (++slot == nst) {
+          slot = 0;
+          ++round;
+        }
       }
       flags[0] = issued;
     }
@@ -183,30 +190,34 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemv_kernel(const __grid_con
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(N);
+      const int nblk = (int)(b_end - b_begin);
       bool ok = true;
-      int buf = 0, uses[2] = {0, 0};
-      int kb = (int)(b_begin % a.kblocks) - 1;
-      for (int64_t i = 0; i < b_end - b_begin; ++i) {
-        const int s = (int)(i % nst);
-        if (++kb == a.kblocks) kb = 0;
+      int buf = 0, uses[2] = {0, 0}, slot = 0, fph = 0;
+      int kb = (int)(b_begin % a.kblocks);
+      for (int i = 0; i < nblk; ++i) {
         const bool seg_start = (i == 0) || (kb == 0);
-        const bool seg_end = (kb == a.kblocks - 1) || (i == b_end - b_begin - 1);
+        const bool seg_end = (kb == a.kblocks - 1) || (i == nblk - 1);
         if (seg_start && uses[buf] > 0 && ok) ok = mbar_wait(acce_bar(buf), (uses[buf] - 1) & 1, a.err, kErrWaitFull);
-        if (ok) ok = mbar_wait(full_bar(s), (int)((i / nst) & 1), a.err, kErrWaitFull);
+        if (ok) ok = mbar_wait(full_bar(slot), fph, a.err, kErrWaitFull);
         tc_fence_after();
         if (ok) {
-          const uint32_t sa = smem_u32(ring + s * Ly.stage), sb = sa + kBlockBytes;
+          const uint32_t sa = smem_u32(ring + slot * Ly.stage), sb = sa + kBlockBytes;
 #pragma unroll
           for (int j = 0; j < 4; ++j)  // K = 64 per block, 16 per MMA: +32 bytes along the swizzled row
             umma_bf16(tmem + buf * N, umma_desc_sw128(sa + 32 * j), umma_desc_sw128(sb + 32 * j), idesc,
                       (seg_start && j == 0) ? 0u : 1u);
         }
-        umma_commit(empty_bar(s));  // frees the slot once these MMAs have read it
+        umma_commit(empty_bar(slot));  // frees the slot once these MMAs have read it
         if (seg_end) {
           umma_commit(accf_bar(buf));
           ++uses[buf];
           buf ^= 1;
         }
+        if (++slot == nst) {
+          slot = 0;
+          fph ^= 1;
+        }
+        if (++kb == a.kblocks) kb = 0;
       }
     }
   } else {
@@ -323,16 +334,29 @@ __global__ void __launch_bounds__(256) pack_act_kernel(const __grid_constant__ P
 }
 
 // ------------------------------------------------------------------ host side
+static int tc_ctas_per_sm() {
+  const int c = env_int("QD_TC_CTAS_PER_SM", 1);
+  return c < 1 ? 1 : (c > 4 ? 4 : c);
+}
+
+static int tc_prefetch_blocks() {  // L2 prefetch lookahead of the weight stream, in 16 KiB blocks
+  const int v = env_int("QD_TC_PREFETCH", 8);
+  return v < 0 ? 0 : (v > 64 ? 64 : v);
+}
+
 static int tc_nst(int N) {
-  int nst = 12;
-  while (nst > 1 && tc_layout(N, nst).total + 1024 > 227 * 1024) --nst;  // + base alignment slack
+  const int cps = tc_ctas_per_sm();
+  const int budget = cps == 1 ? 227 * 1024 : 228 * 1024 / cps - 1024;  // 1 KiB reserved per CTA
+  int nst = env_int("QD_TC_STAGES", 12);
+  if (nst > 12) nst = 12;
+  while (nst > 1 && tc_layout(N, nst).total + 1024 > budget) --nst;  // + base alignment slack
   return nst;
 }
 
 static bool tc_plan(int64_t n_rows, int64_t k, int n_pad, int grid_hint, Plan* p) {
   if (n_pad != 16 && n_pad != 32 && n_pad != 48 && n_pad != 64) return false;
   // one CTA per SM (the ring takes most of shared memory); the partition does not depend on the batch
-  if (!make_plan(n_rows, k, 8, grid_hint > 0 ? grid_hint : host_sm_count(), p)) return false;
+  if (!make_plan(n_rows, k, 8, grid_hint > 0 ? grid_hint : host_sm_count() * tc_ctas_per_sm(), p)) return false;
   const int smax = p->smax, g = p->grid;
   int64_t off = 0;
   auto take = [&](int64_t bytes) {
@@ -407,6 +431,7 @@ static int tc_common(GemvArgs& a, const void* xpk, int n_pad, int m_act, const v
   a.grid = p.grid;
   a.nst = p.nst;
   a.m_act = m_act;
+  a.prefetch = tc_prefetch_blocks();
   char* sc = static_cast<char*>(scratch);
   a.tickets = reinterpret_cast<int*>(sc + p.off_tickets);
   a.lm_ticket = reinterpret_cast<int*>(sc + p.off_lm_ticket);

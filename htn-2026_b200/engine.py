@@ -44,10 +44,12 @@ from decode_b200.loader import load_checkpoint  # noqa: E402
 DEVICE = os.environ.get("ENGINE_DEVICE", "cuda:0")
 BF16 = torch.bfloat16
 MAX_BATCH = 8             # the streaming GEMV keeps up to 8 activation rows in registers
+TC_MAX_BATCH = ops.TC_MAX_BATCH  # larger batches run the tcgen05 kernels (batch padded to 16/32/48/64)
 PREFILL_TOKENS = 16384    # prefill processes at most this many tokens per row chunk (engine/engine.py:79)
 USE_GRAPHS = os.environ.get("ENGINE_GRAPHS", "1") != "0"
 USE_PDL = os.environ.get("ENGINE_PDL", "1") != "0"
-# "persistent": one launch per decode step (qd_decode_step); "kernels": 1 + 5 x layers + 1 launches
+# "persistent": one launch per decode step (qd_decode_step); "kernels": 1 + 5 x layers + 1 launches;
+# "tc": the tensor-core kernels, 1 + 9 x layers + 2 launches (always used above MAX_BATCH)
 STEP_MODE = os.environ.get("ENGINE_STEP", "persistent")
 
 
@@ -100,13 +102,25 @@ class _State:
         self.attn_out = torch.zeros((B, nq, D), dtype=BF16, device=dev)
         self.act = torch.zeros((B, I), dtype=BF16, device=dev)
         self.logits = None
-        self.qkv = ops.QkvRopeAppend(B, H, nq, nkv, dev, eps=eng.eps)
-        self.attn = ops.DecodeAttention(B, nq, nkv, cap, dev)
-        self.o = ops.Gemv(B, H, nq * D, ops.Gemv.RES, dev, eps=eng.eps)
-        self.gu = ops.Gemv(B, 2 * I, H, ops.Gemv.SWIGLU, dev, eps=eng.eps)
-        self.down = ops.Gemv(B, H, I, ops.Gemv.RES, dev, eps=eng.eps)
-        self.lm = ops.LmHeadArgmax(B, eng.vocab, H, dev, eps=eng.eps)
-        self.mode = STEP_MODE
+        self.mode = "tc" if B > MAX_BATCH else STEP_MODE
+        if self.mode == "tc":
+            self.attn = ops.DecodeAttentionStream(B, nq, nkv, cap, dev)
+            # activation operands in the swizzled tile layout (RMSNorm applied while packing)
+            self.xp_h = ops.PackedActivations(B, H, dev)
+            self.xp_a = ops.PackedActivations(B, nq * D, dev)
+            self.xp_i = ops.PackedActivations(B, I, dev)
+            self.qkv = ops.TcQkvRopeAppend(B, H, nq, nkv, dev)
+            self.o = ops.TcGemv(B, H, nq * D, ops.TcGemv.RES, dev)
+            self.gu = ops.TcGemv(B, 2 * I, H, ops.TcGemv.SWIGLU, dev)
+            self.down = ops.TcGemv(B, H, I, ops.TcGemv.RES, dev)
+            self.lm = ops.TcLmHeadArgmax(B, eng.vocab, H, dev)
+        else:
+            self.attn = ops.DecodeAttention(B, nq, nkv, cap, dev)
+            self.qkv = ops.QkvRopeAppend(B, H, nq, nkv, dev, eps=eng.eps)
+            self.o = ops.Gemv(B, H, nq * D, ops.Gemv.RES, dev, eps=eng.eps)
+            self.gu = ops.Gemv(B, 2 * I, H, ops.Gemv.SWIGLU, dev, eps=eng.eps)
+            self.down = ops.Gemv(B, H, I, ops.Gemv.RES, dev, eps=eng.eps)
+            self.lm = ops.LmHeadArgmax(B, eng.vocab, H, dev, eps=eng.eps)
         self.step = ops.DecodeStep(eng, self) if self.mode == "persistent" else None
         self.step_logits = None
         self.rows = max(1, min(B, PREFILL_TOKENS // S))
@@ -260,6 +274,9 @@ class Engine:
             return
         pdl, err = USE_PDL, st.err
         ops.embed(st.tok, self.e_packed, self.vocab, st.x, err, pdl)
+        if st.mode == "tc":
+            self._decode_layers_tc(st, logits, pdl, err)
+            return
         for i in range(self.n_layers):
             kc, vc = st.k_all[i], st.v_all[i]
             st.qkv(st.x, self.w_qkv[i], self.ln1[i], self.qn[i], self.kn[i], st.cos, st.sin, st.pos, st.q, kc, vc,
@@ -269,6 +286,25 @@ class Engine:
             st.gu(st.x, self.w_gu[i], st.act, norm_w=self.ln2[i], err=err, pdl=pdl)
             st.down(st.act, self.w_down[i], st.x, res=st.x, err=err, pdl=pdl)
         st.lm(st.x, self.e_packed, self.final_norm, st.tok, st.pos, inc_pos=True, logits=logits, err=err, pdl=pdl)
+
+    def _decode_layers_tc(self, st: _State, logits, pdl, err) -> None:
+        """Layers and LM head on the tensor-core kernels: each projection reads its activations packed
+        into the MMA operand layout, with the preceding RMSNorm applied while packing."""
+        B, eps = st.B, self.eps
+        for i in range(self.n_layers):
+            kc, vc = st.k_all[i], st.v_all[i]
+            st.xp_h.pack(st.x, self.ln1[i], eps, pdl)
+            st.qkv(st.xp_h, self.w_qkv[i], self.qn[i], self.kn[i], st.cos, st.sin, st.pos, st.q, kc, vc, err=err,
+                   pdl=pdl)
+            st.attn(st.q, kc, vc, st.pos, st.attn_out, err=err, pdl=pdl)
+            st.xp_a.pack(st.attn_out.view(B, -1), None, eps, pdl)
+            st.o(st.xp_a, self.w_o[i], st.x, res=st.x, err=err, pdl=pdl)
+            st.xp_h.pack(st.x, self.ln2[i], eps, pdl)
+            st.gu(st.xp_h, self.w_gu[i], st.act, err=err, pdl=pdl)
+            st.xp_i.pack(st.act, None, eps, pdl)
+            st.down(st.xp_i, self.w_down[i], st.x, res=st.x, err=err, pdl=pdl)
+        st.xp_h.pack(st.x, self.final_norm, eps, pdl)
+        st.lm(st.xp_h, self.e_packed, st.tok, st.pos, inc_pos=True, logits=logits, err=err, pdl=pdl)
 
     def check_device_errors(self, st: _State) -> None:
         code = int(st.err.item())
@@ -282,8 +318,8 @@ class Engine:
 
     # ------------------------------------------------------------------ shapes, graphs
     def _build(self, B: int, S: int, N: int) -> _State:
-        if B > MAX_BATCH:
-            raise NotImplementedError(f"batch {B} > {MAX_BATCH}: the tensor-core skinny GEMM path is not built yet")
+        if B > TC_MAX_BATCH:
+            raise NotImplementedError(f"batch {B} > {TC_MAX_BATCH} per GPU: shard the batch across GPUs")
         self.state = None
         gc.collect()
         torch.cuda.empty_cache()

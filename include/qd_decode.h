@@ -172,6 +172,19 @@ int qd_attn_decode(const void* q, const void* k_cache, const void* v_cache, cons
                    int nq_heads, int nkv_heads, int64_t cap, int64_t cs_b, int64_t cs_h, int splits, int64_t chunk,
                    float scale, void* scratch, int64_t scratch_bytes, int* err, int pdl, cudaStream_t stream);
 
+/* Streaming variant of qd_attn_decode for large batch x length (same inputs, outputs and arithmetic
+ * up to fp32 summation order). The 32-key chunks of all (sequence, KV head) pairs are dealt out
+ * evenly over `grid` CTAs (stream-K), each moving K/V through a shared-memory ring with bulk copies;
+ * a pair split across CTAs is merged by its last CTA in CTA order. grid_hint <= 0 picks three CTAs
+ * per SM. Scratch (zero-filled once, self-resetting) comes from qd_attn_stream_plan, and grid / smax
+ * must be the plan's values. Replaces the same reference kernels as qd_attn_decode. */
+int qd_attn_stream_plan(int batch, int nkv_heads, int64_t cap, int grid_hint, int* grid, int* smax,
+                        int64_t* scratch_bytes);
+int qd_attn_decode_stream(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, void* out,
+                          int batch, int nq_heads, int nkv_heads, int64_t cap, int64_t cs_b, int64_t cs_h, int grid,
+                          int smax, float scale, void* scratch, int64_t scratch_bytes, int* err, int pdl,
+                          cudaStream_t stream);
+
 /* ---------------------------------------------------------------- persistent decode step
  * One launch = one whole decode step: embedding, every layer (the five ops above, same arithmetic,
  * same stream-K partition and attention splits, so bit-identical results) and the LM head with

@@ -1,0 +1,84 @@
+"""The engine's tensor-core path (batches of 9..64 per GPU, BASELINE config 4's shard sizes) against
+the oracle, on the GPU, with the parity rule of test_engine_gpu.py: teacher-forced logits within
+max-abs 5e-2 after softmax and within the calibrated log-softmax bound, tokens equal to the oracle's
+argmax up to reference near-ties."""
+
+import pytest
+import torch
+
+from conftest import load_golden, synth_state
+from oracle import qwen3_cpu as Q
+
+pytestmark = pytest.mark.gpu
+TOL = 5e-2
+
+
+def _lsm_bound():
+    drift = max(load_golden(c)["self_drift"]["max_logsoftmax_diff"] for c in ("config0", "b3_s17"))
+    return max(TOL, 2 * drift)
+
+
+@pytest.fixture(scope="module")
+def tc_engine():
+    import engine as E
+
+    state, cfg = synth_state(2)
+    return E.Engine.from_state_dict(state, cfg, "cuda:0"), state, cfg
+
+
+@pytest.mark.parametrize("B,S,N", [(16, 17, 5), (33, 9, 4), (64, 12, 3)])
+def test_tc_teacher_forced_logits_within_tolerance(tc_engine, B, S, N):
+    from decode_b200 import synth
+
+    eng, state, cfg = tc_engine
+    prompt = synth.random_prompt(B, S, cfg["vocab_size"], seed=B + S)
+    toks, logits = eng.generate_with_logits(prompt, N)
+    assert eng.state.mode == "tc"
+    orc = Q.Qwen3Oracle(state, cfg)
+    _, ref = orc.generate(prompt, N, forced=toks)
+    bound = _lsm_bound()
+    worst_lsm = worst_p = 0.0
+    for t in range(N):
+        worst_lsm = max(worst_lsm, Q.log_softmax_maxdiff(logits[t], ref[t]))
+        worst_p = max(worst_p, Q.softmax_maxdiff(logits[t], ref[t]))
+        for b in range(B):
+            assert Q.token_ok(toks[b][t], ref[t][b], bound), (B, t, b)
+    print(f"tc B={B}: max |softmax diff| {worst_p:.2e}, max |log-softmax diff| {worst_lsm:.4f} (bound {bound:.4f})")
+    assert worst_p <= TOL
+    assert worst_lsm <= bound
+
+
+def test_tc_graph_and_eager_agree_and_are_deterministic(tc_engine):
+    from decode_b200 import synth
+
+    eng, _, cfg = tc_engine
+    prompt = synth.random_prompt(24, 20, cfg["vocab_size"], seed=5)
+    a = list(eng.generate(prompt, 8))
+    b = list(eng.generate(prompt, 8))
+    toks, _ = eng.generate_with_logits(prompt, 8)
+    assert a == b
+    assert [list(r) for r in zip(*a)] == toks
+
+
+def test_tc_rows_are_independent_of_batch_neighbours(tc_engine):
+    """A sequence decodes to the same tokens whatever else shares its batch (rows never mix): same
+    batch shape, every other row replaced."""
+    from decode_b200 import synth
+
+    eng, _, cfg = tc_engine
+    p = synth.random_prompt(40, 16, cfg["vocab_size"], seed=9)
+    full = [list(r) for r in zip(*eng.generate(p, 6))]
+    q = synth.random_prompt(40, 16, cfg["vocab_size"], seed=10)
+    q[7] = p[7]
+    part = [list(r) for r in zip(*eng.generate(q, 6))]
+    assert part[7] == full[7]
+
+
+def test_tc_batch_limit_is_reported(tc_engine):
+    from decode_b200 import synth
+
+    eng, _, cfg = tc_engine
+    with pytest.raises(NotImplementedError):
+        list(eng.generate(synth.random_prompt(65, 4, cfg["vocab_size"], seed=1), 2))
+    eng.state = None
+    torch.cuda.synchronize()
