@@ -48,7 +48,7 @@ def _args():
     p.add_argument("--cpu-steps", type=int, default=96, help="decode steps in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--kernel", default=None, choices=["qkv", "o", "gu", "down", "lm", "attn", "step"],
+    p.add_argument("--kernel", default=None, choices=["qkv", "o", "gu", "down", "lm", "attn", "attn_stream", "step"],
                    help="time one decode kernel alone (small profiling case; random packed weights on the GPU)")
     p.add_argument("--launches", type=int, default=8)
     p.add_argument("--tc", action="store_true", help="with --kernel: the tcgen05 kernel (activations pre-packed)")
@@ -378,12 +378,12 @@ def run_kernel(a):
     err = torch.zeros((1,), dtype=torch.int32, device=dev)
     cap = a.prompt + a.new
     pos = torch.tensor([cap - 1], dtype=torch.int64, device=dev)
-    if a.kernel == "attn":
+    if a.kernel in ("attn", "attn_stream"):
         kc = torch.randn((L, B, nkv, cap, D), generator=g, device=dev).to(torch.bfloat16)
         vc = torch.randn((L, B, nkv, cap, D), generator=g, device=dev).to(torch.bfloat16)
         q = torch.randn((B, nq, D), generator=g, device=dev).to(torch.bfloat16)
         out = torch.empty((B, nq, D), dtype=torch.bfloat16, device=dev)
-        attn = ops.DecodeAttention(B, nq, nkv, cap, dev)
+        attn = (ops.DecodeAttentionStream if a.kernel == "attn_stream" else ops.DecodeAttention)(B, nq, nkv, cap, dev)
         fn = lambda i: attn(q, kc[i], vc[i], pos, out, err=err, pdl=False)  # noqa: E731
         nbytes = 2 * B * nkv * cap * D * 2 + 2 * B * nq * D * 2
     else:
@@ -626,8 +626,8 @@ def run_sweep_linear(a):
 
 def run_sweep_attn(a):
     """GQA decode attention (32 q / 8 KV heads, D 128) at B in {1, 8, 32} and cache
-    length L in {1024, 8192, 32768}, Q/K/V N(0, 1) seed 2: ours_stream (qd_attn_decode_stream, the
-    engine's kernel above 8 sequences), ours_team (qd_attn_decode, the per-unit kernel whose arithmetic
+    length L in {1024, 8192, 32768}, Q/K/V N(0, 1) seed 2: ours_tc (qd_attn_decode_tc, tcgen05),
+    ours_stream (qd_attn_decode_stream, CUDA cores), ours_team (qd_attn_decode, the per-unit kernel whose arithmetic
     the persistent step kernel shares) and torch SDPA with enable_gqa (the library baseline).
     Bytes = 4096 B L (K + V) + 2 x 8192 B (q, out)."""
     import torch
@@ -652,16 +652,18 @@ def run_sweep_attn(a):
             out = torch.empty((B, nq, D), dtype=torch.bfloat16, device=dev)
             attn = ops.DecodeAttention(B, nq, nkv, L, dev)
             stream = ops.DecodeAttentionStream(B, nq, nkv, L, dev)
+            tca = ops.DecodeAttentionTc(B, nq, nkv, L, dev)
             pos = torch.tensor([L - 1], dtype=torch.int64, device=dev)
             q4 = q.view(B, nq, 1, D)
             nbytes = 4096 * B * L + 2 * 8192 * B
-            for path, fn in (("ours_stream", lambda i: stream(q, kc[i], vc[i], pos, out, err=err, pdl=False)),
+            for path, fn in (("ours_tc", lambda i: tca(q, kc[i], vc[i], pos, out, err=err, pdl=False)),
+                             ("ours_stream", lambda i: stream(q, kc[i], vc[i], pos, out, err=err, pdl=False)),
                              ("ours_team", lambda i: attn(q, kc[i], vc[i], pos, out, err=err, pdl=False)),
                              ("torch_sdpa", lambda i: F.scaled_dot_product_attention(
                                  q4, kc[i], vc[i], scale=D ** -0.5, enable_gqa=True))):
                 ms = _time_cycle(fn, copies, launches)
                 gbs = nbytes / (ms / 1e3) / 1e9
-                print(json.dumps({"sweep": "attn", "B": B, "L": L, "path": path, "splits": attn.splits,
+                print(json.dumps({"sweep": "attn", "B": B, "L": L, "path": path,
                                   "us": round(ms * 1e3, 2), "GBs": round(gbs, 1), "frac_hbm": round(gbs / peak, 4),
                                   "peak_hbm": peak, "peak_kind": kind}), flush=True)
             assert int(err.item()) == 0

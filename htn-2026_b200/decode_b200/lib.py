@@ -72,6 +72,10 @@ PROTOTYPES = {
     "qd_attn_decode_stream": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                       c_int64, c_int64, c_int64, c_int, c_int, c_float, c_void_p, c_int64,
                                       c_void_p, c_int, c_void_p]),
+    "qd_attn_tc_plan": (c_int, [c_int, c_int, c_int64, c_int, P_INT, P_INT, P_I64]),
+    "qd_attn_decode_tc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                  c_int64, c_int64, c_int64, c_int, c_int, c_float, c_void_p, c_int64,
+                                  c_void_p, c_int, c_void_p]),
     "qd_attn_plan": (c_int, [c_int, c_int, c_int64, c_int, P_INT, P_I64, P_I64]),
     "qd_decode_step_plan": (c_int, [P_DESC, P_I64, P_INT]),
     "qd_decode_step": (c_int, [P_DESC, c_void_p, c_int64, c_void_p]),

@@ -7,6 +7,7 @@
   LmHeadArgmax                 engine/kernels/fast.py:439-465 (FastLmHead) / gemv.py:251-287
   DecodeAttention              engine/kernels/decode_attn.py:89-119 / FastAttention (fast.py:353-376)
   DecodeAttentionStream        the same, streamed stream-K over all (sequence, KV head) chunks (large batch)
+  DecodeAttentionTc            the same with q.k and P.V on tcgen05 tensor cores
   DecodeStep                   the persistent whole-step kernel (engine/kernels/mega.py MegaStep, tier T6)
   PackedActivations, TcGemv, TcQkvRopeAppend, TcLmHeadArgmax
                                FastGemm / FastLmHead at 9..64 rows (fast.py:173-213, :439-465) on tcgen05
@@ -288,11 +289,12 @@ class DecodeAttentionStream:
     """Streaming split-K GQA flash-decode (qd_attn_decode_stream): chunks of every (sequence, KV head)
     dealt out evenly over the CTAs; the large-batch / long-cache counterpart of DecodeAttention."""
 
+    PLAN, RUN = "qd_attn_stream_plan", "qd_attn_decode_stream"
+
     def __init__(self, batch: int, nq: int, nkv: int, capacity: int, device, grid: int = 0):
         self.batch, self.nq, self.nkv, self.capacity = batch, nq, nkv, capacity
         g, sm, nbytes = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int64(0)
-        L.call("qd_attn_stream_plan", batch, nkv, capacity, grid, ctypes.byref(g), ctypes.byref(sm),
-               ctypes.byref(nbytes))
+        L.call(self.PLAN, batch, nkv, capacity, grid, ctypes.byref(g), ctypes.byref(sm), ctypes.byref(nbytes))
         self.grid, self.smax = g.value, sm.value
         self.scratch = torch.zeros((max(1, nbytes.value),), dtype=torch.uint8, device=device)
         self.scale = 1.0 / math.sqrt(128)
@@ -300,10 +302,16 @@ class DecodeAttentionStream:
     def __call__(self, q, k_cache, v_cache, pos, out, err=None, pdl=True):
         _check_bf16(q, k_cache, v_cache, out)
         assert k_cache.shape[2] == self.capacity and k_cache.stride() == v_cache.stride()
-        L.call("qd_attn_decode_stream", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(pos), _ptr(out), self.batch,
+        L.call(self.RUN, _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(pos), _ptr(out), self.batch,
                self.nq, self.nkv, self.capacity, k_cache.stride(0), k_cache.stride(1), self.grid, self.smax,
                self.scale, _ptr(self.scratch), self.scratch.numel(), _ptr(err), int(pdl), _stream())
         return out
+
+
+class DecodeAttentionTc(DecodeAttentionStream):
+    """The same on the tensor cores (qd_attn_decode_tc): q.k and P.V as tcgen05 MMAs per 128-key chunk."""
+
+    PLAN, RUN = "qd_attn_tc_plan", "qd_attn_decode_tc"
 
 
 class DecodeStep:

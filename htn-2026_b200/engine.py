@@ -104,7 +104,7 @@ class _State:
         self.logits = None
         self.mode = "tc" if B > MAX_BATCH else STEP_MODE
         if self.mode == "tc":
-            self.attn = ops.DecodeAttentionStream(B, nq, nkv, cap, dev)
+            self.attn = ops.DecodeAttentionTc(B, nq, nkv, cap, dev)
             # activation operands in the swizzled tile layout (RMSNorm applied while packing)
             self.xp_h = ops.PackedActivations(B, H, dev)
             self.xp_a = ops.PackedActivations(B, nq * D, dev)

@@ -185,6 +185,17 @@ int qd_attn_decode_stream(const void* q, const void* k_cache, const void* v_cach
                           int smax, float scale, void* scratch, int64_t scratch_bytes, int* err, int pdl,
                           cudaStream_t stream);
 
+/* Tensor-core variant of qd_attn_decode_stream: 128-key chunks, q.k and P.V as tcgen05 MMAs (keys /
+ * dims x 16 columns holding the 4 query heads), K/V by TMA with 128-byte swizzle, softmax in fp32 on
+ * the CUDA cores between the two MMAs, probabilities rounded to BF16. Same inputs, outputs, merge and
+ * error behaviour; grid_hint <= 0 picks one CTA per SM; grid / smax must be qd_attn_tc_plan's values. */
+int qd_attn_tc_plan(int batch, int nkv_heads, int64_t cap, int grid_hint, int* grid, int* smax,
+                    int64_t* scratch_bytes);
+int qd_attn_decode_tc(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, void* out,
+                      int batch, int nq_heads, int nkv_heads, int64_t cap, int64_t cs_b, int64_t cs_h, int grid,
+                      int smax, float scale, void* scratch, int64_t scratch_bytes, int* err, int pdl,
+                      cudaStream_t stream);
+
 /* ---------------------------------------------------------------- persistent decode step
  * One launch = one whole decode step: embedding, every layer (the five ops above, same arithmetic,
  * same stream-K partition and attention splits, so bit-identical results) and the LM head with

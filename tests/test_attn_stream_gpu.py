@@ -1,6 +1,7 @@
-"""Streaming split-K GQA flash-decode (qd_attn_decode_stream) on the GPU against the oracle's SDPA
-restatement and an fp32 math reference, through the C ABI. Grids are varied so that CTAs end one
-(sequence, KV head) pair and start the next, and pairs are merged from up to dozens of segments."""
+"""Streaming split-K GQA flash-decode (qd_attn_decode_stream, CUDA cores, and qd_attn_decode_tc, tcgen05
+tensor cores) on the GPU against the oracle's SDPA restatement and an fp32 math reference, through the
+C ABI. Grids are varied so that CTAs end one (sequence, KV head) pair and start the next, and pairs are
+merged from up to dozens of segments."""
 
 import math
 
@@ -14,6 +15,12 @@ BF16 = torch.bfloat16
 DEV = "cuda:0"
 
 
+def _cls(kind):
+    from decode_b200 import ops
+
+    return ops.DecodeAttentionTc if kind == "tc" else ops.DecodeAttentionStream
+
+
 def _rand(shape, std, gen):
     return (torch.randn(shape, generator=gen) * std).to(BF16)
 
@@ -22,7 +29,8 @@ def _rand(shape, std, gen):
                                           (8, 1000, 1024, 0), (2, 64, 65, 0), (1, 4096, 8192, 0),
                                           (64, 1280, 1536, 0), (5, 777, 800, 7), (5, 777, 800, 37),
                                           (16, 300, 320, 1000), (32, 1024, 1024, 0)])
-def test_stream_attention_matches_oracle(B, L, cap, grid):
+@pytest.mark.parametrize("kind", ["stream", "tc"])
+def test_stream_attention_matches_oracle(B, L, cap, grid, kind):
     from decode_b200 import ops
 
     nq, nkv, D = 32, 8, 128
@@ -32,7 +40,7 @@ def test_stream_attention_matches_oracle(B, L, cap, grid):
     vc = torch.full((B, nkv, cap, D), float("nan"), dtype=BF16)
     kc[:, :, :L] = _rand((B, nkv, L, D), 1.0, g)
     vc[:, :, :L] = _rand((B, nkv, L, D), 1.0, g)
-    attn = ops.DecodeAttentionStream(B, nq, nkv, cap, DEV, grid=grid)
+    attn = _cls(kind)(B, nq, nkv, cap, DEV, grid=grid)
     out = torch.empty((B, nq, D), dtype=BF16, device=DEV)
     err = torch.zeros((1,), dtype=torch.int32, device=DEV)
     pos = torch.tensor([L - 1], dtype=torch.int64, device=DEV)
@@ -47,7 +55,8 @@ def test_stream_attention_matches_oracle(B, L, cap, grid):
     assert (o - ref32).abs().max().item() < 2e-2
 
 
-def test_stream_attention_deterministic_across_calls_and_lengths():
+@pytest.mark.parametrize("kind", ["stream", "tc"])
+def test_stream_attention_deterministic_across_calls_and_lengths(kind):
     """Fixed grid: bit-identical results on repeated calls (tickets reset themselves), and a shorter
     valid length on the same plan reads only its keys."""
     from decode_b200 import ops
@@ -57,7 +66,7 @@ def test_stream_attention_deterministic_across_calls_and_lengths():
     q = _rand((B, nq, D), 1.0, g).to(DEV)
     kc = _rand((B, nkv, cap, D), 1.0, g).to(DEV)
     vc = _rand((B, nkv, cap, D), 1.0, g).to(DEV)
-    attn = ops.DecodeAttentionStream(B, nq, nkv, cap, DEV)
+    attn = _cls(kind)(B, nq, nkv, cap, DEV)
     outs = []
     for L in (2000, 2000, 2000, 150, 2000):
         out = torch.empty((B, nq, D), dtype=BF16, device=DEV)
@@ -68,7 +77,8 @@ def test_stream_attention_deterministic_across_calls_and_lengths():
     assert (outs[3].float().cpu() - ref.float()).abs().max().item() < 2e-2
 
 
-def test_stream_attention_flags_position_outside_cache():
+@pytest.mark.parametrize("kind", ["stream", "tc"])
+def test_stream_attention_flags_position_outside_cache(kind):
     from decode_b200 import ops
 
     B, nq, nkv, D, cap = 1, 32, 8, 128, 64
@@ -76,7 +86,7 @@ def test_stream_attention_flags_position_outside_cache():
     q = _rand((B, nq, D), 1.0, g).to(DEV)
     kc = _rand((B, nkv, cap, D), 1.0, g).to(DEV)
     vc = _rand((B, nkv, cap, D), 1.0, g).to(DEV)
-    attn = ops.DecodeAttentionStream(B, nq, nkv, cap, DEV)
+    attn = _cls(kind)(B, nq, nkv, cap, DEV)
     out = torch.empty((B, nq, D), dtype=BF16, device=DEV)
     err = torch.zeros((1,), dtype=torch.int32, device=DEV)
     attn(q, kc, vc, torch.tensor([cap + 5], dtype=torch.int64, device=DEV), out, err=err)  # clamped, flagged
