@@ -185,7 +185,7 @@ def gu_kernel_roofline(eng, st, launches_per_layer=3):
     stream = torch.cuda.current_stream()
     if st.mode == "tc":  # tensor-core kernel on the packed activations (packing is a separate launch)
         st.xp_h.pack(st.x, eng.ln2[0], eng.eps, False)
-        gu = lambda i: st.gu(st.xp_h, eng.w_gu[i], st.act, pdl=False)  # noqa: E731
+        gu = lambda i: st.gu(st.xp_h, eng.w_gu[i], st.xp_i, pdl=False)  # noqa: E731
     else:
         gu = lambda i: st.gu(st.x, eng.w_gu[i], st.act, norm_w=eng.ln2[i], pdl=False)  # noqa: E731
     for i in range(min(L, 4)):
@@ -351,7 +351,7 @@ def run_ours(a):
                    "frac": round(gu_gbs / peak, 4), "algorithmic_bytes": gu_bytes}},
                "step_mode": st.mode,
                "clocks": clk.summary(), "e2e": e2e, "cpu_baseline": cpu,
-               "gpu_launches": K * {"persistent": 1, "kernels": 2 + 5 * a.layers, "tc": 3 + 9 * a.layers}[st.mode]}
+               "gpu_launches": K * {"persistent": 1, "kernels": 2 + 5 * a.layers, "tc": 3 + 7 * a.layers}[st.mode]}
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.barrier()

@@ -39,6 +39,7 @@ struct alignas(64) TcAttnArgs {
   const __nv_bfloat16* q;
   const int64_t* pos;
   __nv_bfloat16* out;
+  int out_npad;  // 0: out [B, nq, 128]; else the O projection's packed operand [nq * 2][out_npad][64]
   int batch, nq, nkv, grid, smax;
   int64_t cap;
   float scale;
@@ -67,6 +68,13 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar), "l"(policy)
       : "memory");
+}
+
+// element index of output (sequence b, query head hq, dim d) in either output layout
+__device__ __forceinline__ int64_t attn_out_index(const TcAttnArgs& a, int b, int hq, int d) {
+  if (!a.out_npad) return ((int64_t)b * a.nq + hq) * kHeadDim + d;
+  const int k = hq * kHeadDim + d, kb = k >> 6, c = k & 63;
+  return ((int64_t)kb * a.out_npad + b) * 64 + (((c >> 3) ^ (b & 7)) << 3) + (c & 7);
 }
 
 // byte offset of element (row, col) in a [rows][64] BF16 128-byte-swizzled tile (1 KiB-aligned base)
@@ -305,10 +313,10 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
 #pragma unroll
         for (int h = 0; h < kGroup; ++h) l[h] = ((lb[h] + lb[4 + h]) + lb[8 + h]) + lb[12 + h];
         const int bb = pair / a.nkv, kvh = pair - bb * a.nkv;
-        const int64_t orow = ((int64_t)bb * a.nq + kvh * kGroup) * kHeadDim;
         if (seg_first == 0 && ci == nch - 1) {
 #pragma unroll
-          for (int h = 0; h < kGroup; ++h) a.out[orow + h * kHeadDim + tid] = __float2bfloat16_rn(acc[h] / l[h]);
+          for (int h = 0; h < kGroup; ++h)
+            a.out[attn_out_index(a, bb, kvh * kGroup + h, tid)] = __float2bfloat16_rn(acc[h] / l[h]);
         } else {
           const int64_t gc0 = (int64_t)pair * nch;
           const int c_lo = part_owner(T, G, gc0);
@@ -362,7 +370,7 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
                 }
                 float den = 0.f;
                 for (int sg = 0; sg < nseg; ++sg) den = fmaf(ll[h * nseg + sg], ww[h * nseg + sg], den);
-                a.out[orow + h * kHeadDim + tid] = __float2bfloat16_rn(nm / den);
+                a.out[attn_out_index(a, bb, kvh * kGroup + h, tid)] = __float2bfloat16_rn(nm / den);
               }
               if (tid == 0) atomicExch(a.tickets + pair, 0);
             }
@@ -459,13 +467,15 @@ extern "C" int qd_attn_tc_plan(int batch, int nkv_heads, int64_t cap, int grid_h
 }
 
 extern "C" int qd_attn_decode_tc(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos,
-                                 void* out, int batch, int nq_heads, int nkv_heads, int64_t cap, int64_t cs_b,
+                                 void* out, int out_npad, int batch, int nq_heads, int nkv_heads, int64_t cap, int64_t cs_b,
                                  int64_t cs_h, int grid, int smax, float scale, void* scratch, int64_t scratch_bytes,
                                  int* err, int pdl, cudaStream_t stream) {
   if (!q || !k_cache || !v_cache || !pos || !out || !scratch) return set_error(QD_ERR_ARG, "null pointer");
   if (nkv_heads < 1 || nq_heads != nkv_heads * kGroup)
     return set_error(QD_ERR_UNSUPPORTED, "attention is built for %d query heads per KV head", kGroup);
   if (batch < 1 || cap < 1 || (int64_t)batch * nkv_heads > (1 << 24)) return set_error(QD_ERR_ARG, "bad sizes");
+  if (out_npad && (out_npad < batch || out_npad % 16 || out_npad > 64 || !aligned16(out)))
+    return set_error(QD_ERR_ARG, "out_npad must be 0 or a multiple of 16 in [batch, 64], out 16-byte aligned");
   int want_smax = 0;
   const int want_grid = tc_attn_grid(batch * nkv_heads, cap, grid, &want_smax);
   if (grid != want_grid || smax != want_smax)
@@ -484,6 +494,7 @@ extern "C" int qd_attn_decode_tc(const void* q, const void* k_cache, const void*
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.pos = pos;
   a.out = static_cast<__nv_bfloat16*>(out);
+  a.out_npad = out_npad;
   a.batch = batch;
   a.nq = nq_heads;
   a.nkv = nkv_heads;

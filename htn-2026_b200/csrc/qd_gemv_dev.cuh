@@ -54,6 +54,7 @@ struct GemvArgs {
   int smax;
   int* err;
   int m_act;       // activation rows that are real (<= M; the tensor-core path pads M to 16s)
+  int out_npad;    // SWIGLU: 0 = row-major out; else out is the next projection's packed operand
   int* done;       // optional: +1 (release) per finalized row group
   int pos_ready;   // QKV: flags[2] already holds the position and aux its cos/sin rows
   // QKV
@@ -269,7 +270,11 @@ __device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum
       const float gv = bf16r(red[m * kBlockRows + j]);
       const float uv = bf16r(red[m * kBlockRows + 64 + j]);
       const float s = bf16r(gv / (1.0f + expf(-gv)));
-      a.out[m * a.ldo + (int64_t)g * 64 + j] = __float2bfloat16_rn(s * uv);
+      if (a.out_npad)  // output column g * 64 + j is column j of K-block g of the next projection
+        a.out[((int64_t)g * a.out_npad + m) * 64 + (((j >> 3) ^ (m & 7)) << 3) + (j & 7)] =
+            __float2bfloat16_rn(s * uv);
+      else
+        a.out[m * a.ldo + (int64_t)g * 64 + j] = __float2bfloat16_rn(s * uv);
     }
   } else if constexpr (MODE == MODE_QKV) {
     const int64_t p = flags[2];  // position and its RoPE row were loaded once per op (aux)

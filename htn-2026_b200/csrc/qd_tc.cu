@@ -304,8 +304,10 @@ static int tc_ctas_per_sm() {
   return c < 1 ? 1 : (c > 4 ? 4 : c);
 }
 
-static int tc_prefetch_blocks() {  // L2 prefetch lookahead of the weight stream, in 16 KiB blocks
-  const int v = env_int("QD_TC_PREFETCH", 8);
+// L2 prefetch lookahead of the weight stream, in 16 KiB blocks. Off by default: on B200 the ring of
+// bulk copies alone keeps this kernel at the same rate (measured 0 / 8 / 16 / 32 blocks).
+static int tc_prefetch_blocks() {
+  const int v = env_int("QD_TC_PREFETCH", 0);
   return v < 0 ? 0 : (v > 64 ? 64 : v);
 }
 
@@ -454,6 +456,10 @@ extern "C" int qd_tc_gemv(const void* xpk, int n_pad, int m_act, const void* w_p
   } else if (epilogue == QD_EPI_SWIGLU) {
     mode = MODE_SWIGLU;
     if (ldo < n / 2) return set_error(QD_ERR_ARG, "ldo < n/2");
+  } else if (epilogue == QD_EPI_SWIGLU_PACKED) {
+    mode = MODE_SWIGLU;
+    if (!aligned16(out)) return set_error(QD_ERR_ARG, "packed out must be 16-byte aligned");
+    a.out_npad = n_pad;
   } else {
     return set_error(QD_ERR_ARG, "unknown epilogue %d", epilogue);
   }

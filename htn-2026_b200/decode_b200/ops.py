@@ -211,18 +211,23 @@ class _TcOp:
 
 
 class TcGemv(_TcOp):
-    """Gemv for 9..64 rows on the tensor cores; x comes packed (PackedActivations)."""
+    """Gemv for 9..64 rows on the tensor cores; x comes packed (PackedActivations). With SWIGLU_PACKED
+    `out` is the next projection's PackedActivations, written directly by the epilogue."""
 
-    STORE, RES, SWIGLU = L.QD_EPI_STORE, L.QD_EPI_RES, L.QD_EPI_SWIGLU
+    STORE, RES, SWIGLU, SWIGLU_PACKED = L.QD_EPI_STORE, L.QD_EPI_RES, L.QD_EPI_SWIGLU, L.QD_EPI_SWIGLU_PACKED
 
     def __init__(self, m: int, n: int, k: int, epilogue: int, device, grid: int = 0):
         self.m, self.n, self.k, self.epilogue, self.n_pad = m, n, k, epilogue, tc_n_pad(m)
         super().__init__(self.n_pad, n, k, device, grid)
 
     def __call__(self, xp: PackedActivations, w, out, res=None, err=None, pdl=True):
+        if self.epilogue == self.SWIGLU_PACKED:
+            assert isinstance(out, PackedActivations) and out.m == self.m and out.k == self.n // 2
+            out = out.t
         _check_bf16(w, out, res)
-        assert xp.m == self.m and xp.k == self.k and out.stride(1) == 1
-        L.call("qd_tc_gemv", _ptr(xp.t), self.n_pad, self.m, _ptr(w), self.n, self.k, _ptr(out), out.stride(0),
+        assert xp.m == self.m and xp.k == self.k and out.stride(-1) == 1
+        ldo = out.stride(0) if out.dim() > 1 else 0
+        L.call("qd_tc_gemv", _ptr(xp.t), self.n_pad, self.m, _ptr(w), self.n, self.k, _ptr(out), ldo,
                _ptr(res), res.stride(0) if res is not None else 0, self.epilogue, self.grid, _ptr(self.scratch),
                self.scratch.numel(), _ptr(err), int(pdl), _stream())
         return out
@@ -309,9 +314,22 @@ class DecodeAttentionStream:
 
 
 class DecodeAttentionTc(DecodeAttentionStream):
-    """The same on the tensor cores (qd_attn_decode_tc): q.k and P.V as tcgen05 MMAs per 128-key chunk."""
+    """The same on the tensor cores (qd_attn_decode_tc): q.k and P.V as tcgen05 MMAs per 128-key chunk.
+    `out` is a [B, nq, 128] tensor or a PackedActivations (the O projection's operand, written directly)."""
 
     PLAN, RUN = "qd_attn_tc_plan", "qd_attn_decode_tc"
+
+    def __call__(self, q, k_cache, v_cache, pos, out, err=None, pdl=True):
+        packed = isinstance(out, PackedActivations)
+        _check_bf16(q, k_cache, v_cache, out.t if packed else out)
+        assert k_cache.shape[2] == self.capacity and k_cache.stride() == v_cache.stride()
+        if packed:
+            assert out.m == self.batch and out.k == self.nq * 128
+        L.call(self.RUN, _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(pos), _ptr(out.t if packed else out),
+               out.n_pad if packed else 0, self.batch, self.nq, self.nkv, self.capacity, k_cache.stride(0),
+               k_cache.stride(1), self.grid, self.smax, self.scale, _ptr(self.scratch), self.scratch.numel(),
+               _ptr(err), int(pdl), _stream())
+        return out
 
 
 class DecodeStep:

@@ -49,7 +49,7 @@ PREFILL_TOKENS = 16384    # prefill processes at most this many tokens per row c
 USE_GRAPHS = os.environ.get("ENGINE_GRAPHS", "1") != "0"
 USE_PDL = os.environ.get("ENGINE_PDL", "1") != "0"
 # "persistent": one launch per decode step (qd_decode_step); "kernels": 1 + 5 x layers + 1 launches;
-# "tc": the tensor-core kernels, 1 + 9 x layers + 2 launches (always used above MAX_BATCH)
+# "tc": the tensor-core kernels, 1 + 7 x layers + 2 launches (always used above MAX_BATCH)
 STEP_MODE = os.environ.get("ENGINE_STEP", "persistent")
 
 
@@ -111,7 +111,7 @@ class _State:
             self.xp_i = ops.PackedActivations(B, I, dev)
             self.qkv = ops.TcQkvRopeAppend(B, H, nq, nkv, dev)
             self.o = ops.TcGemv(B, H, nq * D, ops.TcGemv.RES, dev)
-            self.gu = ops.TcGemv(B, 2 * I, H, ops.TcGemv.SWIGLU, dev)
+            self.gu = ops.TcGemv(B, 2 * I, H, ops.TcGemv.SWIGLU_PACKED, dev)
             self.down = ops.TcGemv(B, H, I, ops.TcGemv.RES, dev)
             self.lm = ops.TcLmHeadArgmax(B, eng.vocab, H, dev)
         else:
@@ -289,19 +289,18 @@ class Engine:
 
     def _decode_layers_tc(self, st: _State, logits, pdl, err) -> None:
         """Layers and LM head on the tensor-core kernels: each projection reads its activations packed
-        into the MMA operand layout, with the preceding RMSNorm applied while packing."""
+        into the MMA operand layout - RMSNorm-ed by a packing kernel before QKV, gate/up and the LM head,
+        written packed directly by the attention and SwiGLU epilogues before O and down."""
         B, eps = st.B, self.eps
         for i in range(self.n_layers):
             kc, vc = st.k_all[i], st.v_all[i]
             st.xp_h.pack(st.x, self.ln1[i], eps, pdl)
             st.qkv(st.xp_h, self.w_qkv[i], self.qn[i], self.kn[i], st.cos, st.sin, st.pos, st.q, kc, vc, err=err,
                    pdl=pdl)
-            st.attn(st.q, kc, vc, st.pos, st.attn_out, err=err, pdl=pdl)
-            st.xp_a.pack(st.attn_out.view(B, -1), None, eps, pdl)
+            st.attn(st.q, kc, vc, st.pos, st.xp_a, err=err, pdl=pdl)       # written packed for O
             st.o(st.xp_a, self.w_o[i], st.x, res=st.x, err=err, pdl=pdl)
             st.xp_h.pack(st.x, self.ln2[i], eps, pdl)
-            st.gu(st.xp_h, self.w_gu[i], st.act, err=err, pdl=pdl)
-            st.xp_i.pack(st.act, None, eps, pdl)
+            st.gu(st.xp_h, self.w_gu[i], st.xp_i, err=err, pdl=pdl)        # SwiGLU written packed for down
             st.down(st.xp_i, self.w_down[i], st.x, res=st.x, err=err, pdl=pdl)
         st.xp_h.pack(st.x, self.final_norm, eps, pdl)
         st.lm(st.xp_h, self.e_packed, st.tok, st.pos, inc_pos=True, logits=logits, err=err, pdl=pdl)

@@ -32,7 +32,7 @@ enum {
   QD_ERR_UNSUPPORTED = 4  /* shape outside what the kernels are built for */
 };
 
-enum { QD_EPI_STORE = 0, QD_EPI_RES = 1, QD_EPI_SWIGLU = 2 };
+enum { QD_EPI_STORE = 0, QD_EPI_RES = 1, QD_EPI_SWIGLU = 2, QD_EPI_SWIGLU_PACKED = 3 };
 
 enum {
   QD_DEVERR_WAIT_FULL = 1,
@@ -142,7 +142,9 @@ int qd_pack_act(const void* x, int64_t ldx, int m_act, int n_pad, int64_t k, con
                 int pdl, cudaStream_t stream);
 /* grid_hint <= 0 picks one CTA per SM. Scratch (zero-filled once, self-resetting) depends on n_pad. */
 int qd_tc_gemv_plan(int64_t n, int64_t k, int n_pad, int grid_hint, int* grid, int64_t* scratch_bytes);
-/* qd_gemv's STORE / RES / SWIGLU epilogues for rows 0..m_act-1 of the packed activations. */
+/* qd_gemv's STORE / RES / SWIGLU epilogues for rows 0..m_act-1 of the packed activations.
+ * QD_EPI_SWIGLU_PACKED: the SwiGLU output goes straight into the packed activation layout of the next
+ * projection (`out` = [n/128][n_pad][64] tiles, as qd_pack_act would write it; ldo unused). */
 int qd_tc_gemv(const void* xpk, int n_pad, int m_act, const void* w_packed, int64_t n, int64_t k, void* out,
                int64_t ldo, const void* res, int64_t ldr, int epilogue, int grid, void* scratch,
                int64_t scratch_bytes, int* err, int pdl, cudaStream_t stream);
@@ -188,11 +190,13 @@ int qd_attn_decode_stream(const void* q, const void* k_cache, const void* v_cach
 /* Tensor-core variant of qd_attn_decode_stream: 128-key chunks, q.k and P.V as tcgen05 MMAs (keys /
  * dims x 16 columns holding the 4 query heads), K/V by TMA with 128-byte swizzle, softmax in fp32 on
  * the CUDA cores between the two MMAs, probabilities rounded to BF16. Same inputs, outputs, merge and
- * error behaviour; grid_hint <= 0 picks one CTA per SM; grid / smax must be qd_attn_tc_plan's values. */
+ * error behaviour; grid_hint <= 0 picks one CTA per SM; grid / smax must be qd_attn_tc_plan's values.
+ * out_npad = 0: out is [batch, nq, 128]; out_npad = 16..64 (>= batch, multiple of 16): out is the packed
+ * activation operand of the O projection, [nq * 2][out_npad][64] tiles (qd_pack_act's layout). */
 int qd_attn_tc_plan(int batch, int nkv_heads, int64_t cap, int grid_hint, int* grid, int* smax,
                     int64_t* scratch_bytes);
 int qd_attn_decode_tc(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, void* out,
-                      int batch, int nq_heads, int nkv_heads, int64_t cap, int64_t cs_b, int64_t cs_h, int grid,
+                      int out_npad, int batch, int nq_heads, int nkv_heads, int64_t cap, int64_t cs_b, int64_t cs_h, int grid,
                       int smax, float scale, void* scratch, int64_t scratch_bytes, int* err, int pdl,
                       cudaStream_t stream);
 

@@ -93,3 +93,23 @@ def test_stream_attention_flags_position_outside_cache(kind):
     assert int(err.item()) == 16
     ref = Q.attention_decode(q.cpu(), kc.cpu(), vc.cpu(), cap)
     assert (out.float().cpu() - ref.float()).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("B", [9, 33, 64])
+def test_tc_attention_packed_output_is_packed_rowmajor(B):
+    """out_npad > 0 writes the O projection's packed operand: bit-equal to packing the [B, 32, 128] output."""
+    from decode_b200 import ops
+
+    nq, nkv, D, cap, L = 32, 8, 128, 640, 600
+    g = torch.Generator().manual_seed(B)
+    q = _rand((B, nq, D), 1.0, g).to(DEV)
+    kc = _rand((B, nkv, cap, D), 1.0, g).to(DEV)
+    vc = _rand((B, nkv, cap, D), 1.0, g).to(DEV)
+    attn = ops.DecodeAttentionTc(B, nq, nkv, cap, DEV)
+    pos = torch.tensor([L - 1], dtype=torch.int64, device=DEV)
+    row = torch.empty((B, nq, D), dtype=BF16, device=DEV)
+    attn(q, kc, vc, pos, row)
+    packed = ops.PackedActivations(B, nq * D, DEV)
+    attn(q, kc, vc, pos, packed)
+    ref = ops.PackedActivations(B, nq * D, DEV).pack(row.view(B, -1))
+    assert torch.equal(packed.t.view(torch.int16), ref.t.view(torch.int16))

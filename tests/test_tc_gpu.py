@@ -233,3 +233,20 @@ def test_tc_lm_head_ties_pick_lowest_index():
     tok = torch.empty((m,), dtype=torch.int64, device=DEV)
     lm(xp, ops.pack_matrix(E.to(DEV)), tok)
     assert (tok.cpu() == 300).all()
+
+
+@pytest.mark.parametrize("m", [16, 40])
+def test_tc_swiglu_packed_output_is_packed_rowmajor(m):
+    """SWIGLU_PACKED writes exactly what packing the row-major SwiGLU output would."""
+    ops = _ops()
+    inter, k = 9728, 2560
+    g = torch.Generator().manual_seed(77 + m)
+    x, gate, up = _rand((m, k), 1.0, g), _rand((inter, k), 0.02, g), _rand((inter, k), 0.02, g)
+    xp = ops.PackedActivations(m, k, DEV).pack(x.to(DEV))
+    w = ops.pack_gate_up(gate.to(DEV), up.to(DEV))
+    row = torch.empty((m, inter), dtype=BF16, device=DEV)
+    ops.TcGemv(m, 2 * inter, k, ops.TcGemv.SWIGLU, DEV)(xp, w, row)
+    packed = ops.PackedActivations(m, inter, DEV)
+    ops.TcGemv(m, 2 * inter, k, ops.TcGemv.SWIGLU_PACKED, DEV)(xp, w, packed)
+    ref = ops.PackedActivations(m, inter, DEV).pack(row)
+    assert torch.equal(packed.t.view(torch.int16), ref.t.view(torch.int16))
