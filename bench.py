@@ -48,7 +48,7 @@ def _args():
     p.add_argument("--cpu-steps", type=int, default=96, help="decode steps in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--kernel", default=None, choices=["qkv", "o", "gu", "down", "lm", "attn", "attn_stream", "step"],
+    p.add_argument("--kernel", default=None, choices=["qkv", "o", "gu", "down", "lm", "attn", "attn_stream", "attn_tc", "step"],
                    help="time one decode kernel alone (small profiling case; random packed weights on the GPU)")
     p.add_argument("--launches", type=int, default=8)
     p.add_argument("--tc", action="store_true", help="with --kernel: the tcgen05 kernel (activations pre-packed)")
@@ -378,12 +378,13 @@ def run_kernel(a):
     err = torch.zeros((1,), dtype=torch.int32, device=dev)
     cap = a.prompt + a.new
     pos = torch.tensor([cap - 1], dtype=torch.int64, device=dev)
-    if a.kernel in ("attn", "attn_stream"):
+    if a.kernel in ("attn", "attn_stream", "attn_tc"):
         kc = torch.randn((L, B, nkv, cap, D), generator=g, device=dev).to(torch.bfloat16)
         vc = torch.randn((L, B, nkv, cap, D), generator=g, device=dev).to(torch.bfloat16)
         q = torch.randn((B, nq, D), generator=g, device=dev).to(torch.bfloat16)
         out = torch.empty((B, nq, D), dtype=torch.bfloat16, device=dev)
-        attn = (ops.DecodeAttentionStream if a.kernel == "attn_stream" else ops.DecodeAttention)(B, nq, nkv, cap, dev)
+        attn = {"attn": ops.DecodeAttention, "attn_stream": ops.DecodeAttentionStream,
+                "attn_tc": ops.DecodeAttentionTc}[a.kernel](B, nq, nkv, cap, dev)
         fn = lambda i: attn(q, kc[i], vc[i], pos, out, err=err, pdl=False)  # noqa: E731
         nbytes = 2 * B * nkv * cap * D * 2 + 2 * B * nq * D * 2
     else:

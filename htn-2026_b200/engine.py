@@ -45,11 +45,14 @@ DEVICE = os.environ.get("ENGINE_DEVICE", "cuda:0")
 BF16 = torch.bfloat16
 MAX_BATCH = 8             # the streaming GEMV keeps up to 8 activation rows in registers
 TC_MAX_BATCH = ops.TC_MAX_BATCH  # larger batches run the tcgen05 kernels (batch padded to 16/32/48/64)
+# From this batch up the tcgen05 kernel chain beats the CUDA-core persistent step on B200 (measured:
+# tie at batch 4 with a 128-token prompt, tc ahead at 4 with 1024 and at 8 by 1.5-1.7x).
+TC_MIN_BATCH = int(os.environ.get("ENGINE_TC_MIN_BATCH", "4"))
 PREFILL_TOKENS = 16384    # prefill processes at most this many tokens per row chunk (engine/engine.py:79)
 USE_GRAPHS = os.environ.get("ENGINE_GRAPHS", "1") != "0"
 USE_PDL = os.environ.get("ENGINE_PDL", "1") != "0"
 # "persistent": one launch per decode step (qd_decode_step); "kernels": 1 + 5 x layers + 1 launches;
-# "tc": the tensor-core kernels, 1 + 7 x layers + 2 launches (always used above MAX_BATCH)
+# "tc": the tensor-core kernels, 1 + 7 x layers + 2 launches (used from TC_MIN_BATCH up)
 STEP_MODE = os.environ.get("ENGINE_STEP", "persistent")
 
 
@@ -102,7 +105,7 @@ class _State:
         self.attn_out = torch.zeros((B, nq, D), dtype=BF16, device=dev)
         self.act = torch.zeros((B, I), dtype=BF16, device=dev)
         self.logits = None
-        self.mode = "tc" if B > MAX_BATCH else STEP_MODE
+        self.mode = "tc" if (B > MAX_BATCH or B >= TC_MIN_BATCH) else STEP_MODE
         if self.mode == "tc":
             self.attn = ops.DecodeAttentionTc(B, nq, nkv, cap, dev)
             # activation operands in the swizzled tile layout (RMSNorm applied while packing)
