@@ -79,7 +79,7 @@ extern "C" int qd_attn_decode(const void* q, const void* k_cache, const void* v_
   const int64_t need = need_acc + need_ml + ((int64_t)batch * nkv_heads * 4 + 255) / 256 * 256;
   if (scratch_bytes < need)
     return set_error(QD_ERR_SCRATCH, "scratch %lld B < %lld B", (long long)scratch_bytes, (long long)need);
-  AttnArgs a;
+  AttnArgs a = {};
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.k = static_cast<const __nv_bfloat16*>(k_cache);
   a.v = static_cast<const __nv_bfloat16*>(v_cache);

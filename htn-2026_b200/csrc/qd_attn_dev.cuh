@@ -37,8 +37,9 @@ struct AttnArgs {
   float* part_ml;
   int* tickets;
   int* err;
-  int* done;  // optional: +1 (release) per merged (sequence, KV head)
+  int* done;  // optional: +1 (release) per merged (sequence, KV head), or per unit with partials_only
   int keys_per_split;  // splits in use at a given length: ~this many keys each, at most `splits`
+  int partials_only;   // every unit leaves its (acc, max, sum) and signals; the reader merges them
 };
 
 // Valid length (pos + 1) clamped to the cache; flags QD_DEVERR_POS when the position is outside it.
@@ -188,7 +189,7 @@ static __device__ void attn_unit(const AttnArgs& a, int b, int kvh, int split, i
   }
   named_bar(bar_id, kAttnThreads);
   const int64_t row0 = ((int64_t)b * a.nq + kvh * kGroup) * a.splits;
-  if (n_use == 1) {  // one split covers every key: normalise and write, no partials or merge
+  if (!a.partials_only && n_use == 1) {  // one split covers every key: normalise and write, no merge
     for (int h = 0; h < kGroup; ++h) {
       float mx = -INFINITY;
 #pragma unroll
@@ -234,6 +235,11 @@ static __device__ void attn_unit(const AttnArgs& a, int b, int kvh, int split, i
     }
   }
   named_bar(bar_id, kAttnThreads);
+  if (a.partials_only) {  // the consumer merges (attn_merge_partials); release this unit's partial
+    if (tid == 0 && a.done) red_release_add(a.done, 1);
+    named_bar(bar_id, kAttnThreads);
+    return;
+  }
   if (tid == 0)
     sm.last_flag = (atom_add_acq_rel(a.tickets + (int64_t)b * a.nkv + kvh, 1) == n_use - 1) ? 1 : 0;
   named_bar(bar_id, kAttnThreads);

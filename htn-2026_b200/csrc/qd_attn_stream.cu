@@ -406,7 +406,7 @@ extern "C" int qd_attn_decode_stream(const void* q, const void* k_cache, const v
   const int64_t need = stream_scratch(batch * nkv_heads, smax, &om, &ot);
   if (scratch_bytes < need)
     return set_error(QD_ERR_SCRATCH, "scratch %lld B < %lld B", (long long)scratch_bytes, (long long)need);
-  StreamArgs a;
+  StreamArgs a = {};
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.k = static_cast<const __nv_bfloat16*>(k_cache);
   a.v = static_cast<const __nv_bfloat16*>(v_cache);

@@ -487,7 +487,7 @@ extern "C" int qd_attn_decode_tc(const void* q, const void* k_cache, const void*
   const int64_t need = tc_attn_scratch(batch * nkv_heads, smax, &om, &ot);
   if (scratch_bytes < need)
     return set_error(QD_ERR_SCRATCH, "scratch %lld B < %lld B", (long long)scratch_bytes, (long long)need);
-  TcAttnArgs a;
+  TcAttnArgs a = {};
   if (!encode_cache_map(&a.tk, k_cache, batch, nkv_heads, cap, cs_b, cs_h) ||
       !encode_cache_map(&a.tv, v_cache, batch, nkv_heads, cap, cs_b, cs_h))
     return set_error(QD_ERR_CUDA, "cuTensorMapEncodeTiled failed for the KV cache");

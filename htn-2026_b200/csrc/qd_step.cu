@@ -44,6 +44,7 @@ struct StepArgs {
   int64_t chunk;
   int smax[K_KINDS];
   int64_t total[K_KINDS];
+  int o_merge;       // 1: attention leaves split partials, the O projection's CTAs merge them
   int* counters;
   int* abort_flag;
   int* tickets;
@@ -114,6 +115,63 @@ static __device__ void wait_dep(const StepArgs& A, const int* cnt, int target, i
         break;
       }
     }
+  }
+  named_bar(kBarConsumers, kConsumers);
+}
+
+// The O projection's input at batch 1..8: attention units leave their split partials (acc, max, sum)
+// and each O CTA merges, for the query heads its K-range reads (K-block kb = dims 64kb.. = head kb/2),
+// exactly what the attention kernel's last split computes (same order, same operations), into xs.
+// Saves the split ticket, the merge's round trips and the output write + reload on the critical path.
+template <int M>
+static __device__ void stage_attn_merge(const StepArgs& A, const GemvArgs& op, int n_use, int cta,
+                                        __nv_bfloat16* xs, float* scr, int tid) {
+  const int64_t b0 = part_begin(op.total, op.grid, cta), b1 = part_begin(op.total, op.grid, cta + 1);
+  uint32_t mask = 0;
+  int kb = (int)(b0 % op.kblocks);
+  for (int64_t b = b0; b < b1; ++b) {
+    mask |= 1u << (kb >> 1);
+    if (++kb == op.kblocks) kb = 0;
+  }
+  const int nh = __popc(mask), P = M * nh, E = P * n_use;
+  float* mm = scr;  // [P][n_use] maxima, sums, weights; [P] denominators
+  float* ll = mm + E;
+  float* ww = ll + E;
+  float* den = ww + E;
+  for (int t = tid; t < E; t += kConsumers) {
+    const int p = t / n_use, sp = t - p * n_use, m = p / nh, hq = __fns(mask, 0, p - m * nh + 1);
+    const int64_t part = ((int64_t)m * A.nq + hq) * A.splits + sp;
+    mm[t] = ld_cg_f32(A.attn_ml + part * 2);
+    ll[t] = ld_cg_f32(A.attn_ml + part * 2 + 1);
+  }
+  named_bar(kBarConsumers, kConsumers);
+  for (int t = tid; t < E; t += kConsumers) {
+    const int p = t / n_use;
+    float mx = -INFINITY;
+    for (int sp = 0; sp < n_use; ++sp) mx = fmaxf(mx, mm[p * n_use + sp]);
+    ww[t] = (mm[t] == -INFINITY) ? 0.f : expf(mm[t] - mx);
+  }
+  named_bar(kBarConsumers, kConsumers);
+  for (int p = tid; p < P; p += kConsumers) {
+    float d = 0.f;
+    for (int sp = 0; sp < n_use; ++sp) d = fmaf(ll[p * n_use + sp], ww[p * n_use + sp], d);
+    den[p] = d;
+  }
+  named_bar(kBarConsumers, kConsumers);
+  // out = bf16(sum_s acc_s w_s / sum_s l_s w_s) in split order, eight loads in flight at a time
+  for (int idx = tid; idx < P * kHeadDim; idx += kConsumers) {
+    const int p = idx >> 7, d = idx & 127, m = p / nh, hq = __fns(mask, 0, p - m * nh + 1);
+    const int64_t row = ((int64_t)m * A.nq + hq) * A.splits;
+    float num = 0.f;
+    for (int s0 = 0; s0 < n_use; s0 += 8) {
+      float av[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) av[j] = (s0 + j < n_use) ? ld_cg_f32(A.attn_acc + (row + s0 + j) * kHeadDim + d) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (s0 + j < n_use) num = fmaf(av[j], ww[p * n_use + s0 + j], num);
+    }
+    xs[(int64_t)m * op.k + hq * kHeadDim + d] = __float2bfloat16_rn(num / den[p]);
   }
   named_bar(kBarConsumers, kConsumers);
 }
@@ -420,6 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
         at.err = A.err;
         at.done = ctr(A, l, 1);
         at.keys_per_split = A.keys_per_split;
+        at.partials_only = A.o_merge;
         const int per_b = A.nkv * A.splits;
         wait_dep(A, ctr(A, l, 0), A.nq + 2 * A.nkv, tid);
         stamp(A, cta, 2 + 5 * l, 0, tid);
@@ -430,11 +489,14 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       }
       stamp(A, cta, 2 + 5 * l, 2, tid);
       // O projection + residual
-      wait_dep(A, ctr(A, l, 1), M * A.nkv, tid);
+      wait_dep(A, ctr(A, l, 1), A.o_merge ? M * A.nkv * n_use : M * A.nkv, tid);
       stamp(A, cta, 3 + 5 * l, 0, tid);
       {
         const GemvArgs op = gemv_op<M>(A, K_O, l);
-        stage_x<M>(op, xs, wsum, tid);
+        if (A.o_merge)
+          stage_attn_merge<M>(A, op, n_use, cta, xs, reinterpret_cast<float*>(asm_team), tid);
+        else
+          stage_x<M>(op, xs, wsum, tid);
         stamp(A, cta, 3 + 5 * l, 1, tid);
         consume_blocks<M, MODE_RES>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
       }
@@ -479,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
 }
 
 struct StepPlan {
-  int grid, nst, splits, kmax, smem;
+  int grid, nst, splits, kmax, smem, o_merge;
   int64_t chunk;
   int smax[K_KINDS];
   int64_t total[K_KINDS];
@@ -543,6 +605,21 @@ static int step_plan(const qd_step_desc* d, StepPlan* p) {
   p->off_attn_ml = take(B * nq * ap.splits * 2 * 4);
   p->off_attn_tickets = take(B * nkv * 4);
   p->bytes = off;
+  // O-side attention merge: the most query heads one O CTA reads, times the splits, must fit the
+  // attention shared memory (free while O stages its input); heads as bits of a 32-bit mask
+  {
+    const int64_t T = p->total[K_O], kbl = nq * 128 / kBlockCols;
+    int nh_max = 0;
+    for (int c = 0; c < G; ++c) {
+      uint32_t mask = 0;
+      for (int64_t b = part_begin(T, G, c); b < part_begin(T, G, c + 1); ++b) mask |= 1u << ((b % kbl) >> 1);
+      const int nh = __builtin_popcount(mask);
+      if (nh > nh_max) nh_max = nh;
+    }
+    const int64_t need = (3 * (int64_t)ap.splits + 1) * B * nh_max;
+    const int64_t cap_f = 2 * (int64_t)sizeof(AttnSmem) / 4;
+    p->o_merge = (nq <= 32 && need <= cap_f && env_int("QD_STEP_O_MERGE", 1) != 0) ? 1 : 0;
+  }
   return QD_OK;
 }
 
@@ -636,6 +713,7 @@ extern "C" int qd_decode_step(const qd_step_desc* d, void* scratch, int64_t scra
   a.vocab = d->vocab;
   a.vocab_rows = (d->vocab + kBlockRows - 1) / kBlockRows * kBlockRows;
   a.eps = (float)d->eps;
+  a.o_merge = p.o_merge;
   a.scale = (float)d->scale;
   a.tok = d->tok;
   a.pos = d->pos;

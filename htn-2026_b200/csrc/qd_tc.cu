@@ -314,7 +314,9 @@ static int tc_prefetch_blocks() {
 static int tc_nst(int N) {
   const int cps = tc_ctas_per_sm();
   const int budget = cps == 1 ? 227 * 1024 : 228 * 1024 / cps - 1024;  // 1 KiB reserved per CTA
-  int nst = env_int("QD_TC_STAGES", 12);
+  // 4 stages: the same rate as 12 (the ring is not the limit) in about half the shared memory, so
+  // the next kernel's CTA can be resident beside this one and start its prologue under PDL
+  int nst = env_int("QD_TC_STAGES", 4);
   if (nst > 12) nst = 12;
   while (nst > 1 && tc_layout(N, nst).total + 1024 > budget) --nst;  // + base alignment slack
   return nst;
@@ -420,7 +422,7 @@ extern "C" int qd_pack_act(const void* x, int64_t ldx, int m_act, int n_pad, int
     return set_error(QD_ERR_ARG, "pack_act: null or unaligned pointer");
   if (m_act < 1 || m_act > n_pad || k % kBlockCols || ldx < k || ldx % 8)
     return set_error(QD_ERR_ARG, "pack_act: bad sizes");
-  PackActArgs a;
+  PackActArgs a = {};
   a.x = static_cast<const __nv_bfloat16*>(x);
   a.ldx = ldx;
   a.k = k;
