@@ -91,6 +91,28 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
   }
 }
 
+// mbar_wait that also gives up at once when another CTA has raised `abort` (polled every 64 tries), and
+// raises it itself when its own limit expires, so one expired wait ends the whole grid quickly.
+__device__ __forceinline__ bool mbar_wait_abort(uint32_t bar, uint32_t parity, int* err, int code, int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (*reinterpret_cast<volatile int*>(abort)) return false;
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        if (err) atomicOr(err, code);
+        atomicExch(abort, 1);
+        return false;
+      }
+    }
+  }
+}
+
+// Orders this thread's generic-proxy global accesses with async-proxy (TMA / bulk copy) accesses: a
+// writer issues it before publishing data a bulk copy will read, the reader after acquiring the flag.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 // One-dimensional bulk copy global -> this CTA's shared memory, completing on `bar`. No multicast.
 // `policy` is an L2 cache policy (createpolicy) for the source lines.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,

@@ -139,6 +139,7 @@ __device__ __forceinline__ void ring_drain(const Ring& R, int issued, int* err) 
 }
 
 __device__ __forceinline__ void signal_done(int* done, int tid) {
+  fence_proxy_async_global();  // results this CTA wrote may be read next by another CTA's bulk copies
   named_bar(kBarConsumers, kConsumers);
   if (tid == 0) red_release_add(done, 1);
 }

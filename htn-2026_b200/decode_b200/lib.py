@@ -79,6 +79,8 @@ PROTOTYPES = {
     "qd_attn_plan": (c_int, [c_int, c_int, c_int64, c_int, P_INT, P_I64, P_I64]),
     "qd_decode_step_plan": (c_int, [P_DESC, P_I64, P_INT]),
     "qd_decode_step": (c_int, [P_DESC, c_void_p, c_int64, c_void_p]),
+    "qd_tc_decode_step_plan": (c_int, [P_DESC, P_I64, P_INT]),
+    "qd_tc_decode_step": (c_int, [P_DESC, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "qd_attn_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64,
                                c_int64, c_int64, c_int, c_int64, c_float, c_void_p, c_int64, c_void_p, c_int,
                                c_void_p]),

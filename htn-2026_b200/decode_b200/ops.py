@@ -290,6 +290,27 @@ class DecodeAttention:
         return out
 
 
+class TcDecodeStep:
+    """Persistent tcgen05 decode step (qd_tc_decode_step) for batches of 4..64: one launch per step over
+    the engine's packed weights, with the state's packed activation operands (xp_h, xp_a, xp_i)."""
+
+    def __init__(self, eng, st, logits=None, trace=None):
+        self.desc = _step_desc(eng, st, logits, trace)
+        self._keep = (eng, st, logits, trace)
+        nbytes, npad = ctypes.c_int64(0), ctypes.c_int(0)
+        L.call("qd_tc_decode_step_plan", ctypes.byref(self.desc), ctypes.byref(nbytes), ctypes.byref(npad))
+        assert npad.value == st.xp_h.n_pad
+        self.ptrs = (_ptr(st.xp_h.t), _ptr(st.xp_a.t), _ptr(st.xp_i.t))
+        self.scratch = torch.zeros((max(1, nbytes.value),), dtype=torch.uint8, device=st.x.device)
+
+    def __call__(self):
+        L.call("qd_tc_decode_step", ctypes.byref(self.desc), *self.ptrs, _ptr(self.scratch), self.scratch.numel(),
+               _stream())
+
+    def reset(self):
+        self.scratch.zero_()
+
+
 class DecodeAttentionStream:
     """Streaming split-K GQA flash-decode (qd_attn_decode_stream): chunks of every (sequence, KV head)
     dealt out evenly over the CTAs; the large-batch / long-cache counterpart of DecodeAttention."""
@@ -332,34 +353,39 @@ class DecodeAttentionTc(DecodeAttentionStream):
         return out
 
 
+def _step_desc(eng, st, logits=None, trace=None):
+    """qd_step_desc over the engine's packed weights and one shape state."""
+    d = L.StepDesc()
+    Lyr = eng.n_layers
+    d.w_qkv, d.w_qkv_layer_bytes = eng.w_qkv.data_ptr(), eng.w_qkv.stride(0) * 2
+    d.w_o, d.w_o_layer_bytes = eng.w_o.data_ptr(), eng.w_o.stride(0) * 2
+    d.w_gu, d.w_gu_layer_bytes = eng.w_gu.data_ptr(), eng.w_gu.stride(0) * 2
+    d.w_down, d.w_down_layer_bytes = eng.w_down.data_ptr(), eng.w_down.stride(0) * 2
+    d.e_packed = eng.e_packed.data_ptr()
+    d.ln1, d.ln2 = eng.ln1.data_ptr(), eng.ln2.data_ptr()
+    d.q_norm, d.k_norm, d.final_norm = eng.qn.data_ptr(), eng.kn.data_ptr(), eng.final_norm.data_ptr()
+    d.layers, d.hidden, d.inter = Lyr, eng.hidden, eng.inter
+    d.nq_heads, d.nkv_heads, d.vocab, d.batch = eng.nq, eng.nkv, eng.vocab, st.B
+    d.eps, d.scale = eng.eps, 1.0 / math.sqrt(eng.head_dim)
+    d.tok, d.pos = st.tok.data_ptr(), st.pos.data_ptr()
+    d.x, d.q, d.attn, d.act = st.x.data_ptr(), st.q.data_ptr(), st.attn_out.data_ptr(), st.act.data_ptr()
+    d.k_cache, d.v_cache = st.k_all.data_ptr(), st.v_all.data_ptr()
+    d.cache_layer_stride, d.cs_b, d.cs_h = st.k_all.stride(0), st.k_all.stride(1), st.k_all.stride(2)
+    d.cap = st.k_all.shape[3]
+    d.cos, d.sin = st.cos.data_ptr(), st.sin.data_ptr()
+    d.logits = logits.data_ptr() if logits is not None else None
+    d.ld_logits = logits.stride(0) if logits is not None else 0
+    d.err = st.err.data_ptr()
+    d.trace = trace.data_ptr() if trace is not None else None
+    return d
+
+
 class DecodeStep:
     """One persistent launch per decode step (qd_decode_step): embedding, every layer and the LM head.
     Holds the descriptor (pointers into the engine's weights and per-shape state) and the scratch."""
 
     def __init__(self, eng, st, logits=None, trace=None):
-        d = L.StepDesc()
-        Lyr = eng.n_layers
-        d.w_qkv, d.w_qkv_layer_bytes = eng.w_qkv.data_ptr(), eng.w_qkv.stride(0) * 2
-        d.w_o, d.w_o_layer_bytes = eng.w_o.data_ptr(), eng.w_o.stride(0) * 2
-        d.w_gu, d.w_gu_layer_bytes = eng.w_gu.data_ptr(), eng.w_gu.stride(0) * 2
-        d.w_down, d.w_down_layer_bytes = eng.w_down.data_ptr(), eng.w_down.stride(0) * 2
-        d.e_packed = eng.e_packed.data_ptr()
-        d.ln1, d.ln2 = eng.ln1.data_ptr(), eng.ln2.data_ptr()
-        d.q_norm, d.k_norm, d.final_norm = eng.qn.data_ptr(), eng.kn.data_ptr(), eng.final_norm.data_ptr()
-        d.layers, d.hidden, d.inter = Lyr, eng.hidden, eng.inter
-        d.nq_heads, d.nkv_heads, d.vocab, d.batch = eng.nq, eng.nkv, eng.vocab, st.B
-        d.eps, d.scale = eng.eps, 1.0 / math.sqrt(eng.head_dim)
-        d.tok, d.pos = st.tok.data_ptr(), st.pos.data_ptr()
-        d.x, d.q, d.attn, d.act = st.x.data_ptr(), st.q.data_ptr(), st.attn_out.data_ptr(), st.act.data_ptr()
-        d.k_cache, d.v_cache = st.k_all.data_ptr(), st.v_all.data_ptr()
-        d.cache_layer_stride, d.cs_b, d.cs_h = st.k_all.stride(0), st.k_all.stride(1), st.k_all.stride(2)
-        d.cap = st.k_all.shape[3]
-        d.cos, d.sin = st.cos.data_ptr(), st.sin.data_ptr()
-        d.logits = logits.data_ptr() if logits is not None else None
-        d.ld_logits = logits.stride(0) if logits is not None else 0
-        d.err = st.err.data_ptr()
-        d.trace = trace.data_ptr() if trace is not None else None
-        self.desc = d
+        d = self.desc = _step_desc(eng, st, logits, trace)
         self._keep = (eng, st, logits, trace)
         nbytes, splits = ctypes.c_int64(0), ctypes.c_int(0)
         L.call("qd_decode_step_plan", ctypes.byref(d), ctypes.byref(nbytes), ctypes.byref(splits))

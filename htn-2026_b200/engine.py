@@ -48,11 +48,17 @@ TC_MAX_BATCH = ops.TC_MAX_BATCH  # larger batches run the tcgen05 kernels (batch
 # From this batch up the tcgen05 kernel chain beats the CUDA-core persistent step on B200 (measured:
 # tie at batch 4 with a 128-token prompt, tc ahead at 4 with 1024 and at 8 by 1.5-1.7x).
 TC_MIN_BATCH = int(os.environ.get("ENGINE_TC_MIN_BATCH", "4"))
+# tensor-core path: "persistent" = one qd_tc_decode_step launch per step; "chain" = the per-op kernels;
+# "auto" = persistent up to TC_PERSISTENT_MAX_BATCH (measured: 9 % faster at batch 8, 2 % slower at 16 and
+# 17 % slower at 64, where its attention has two K/V stages to the chain kernel's three)
+TC_STEP = os.environ.get("ENGINE_TC_STEP", "auto")
+TC_PERSISTENT_MAX_BATCH = int(os.environ.get("ENGINE_TC_PERSISTENT_MAX_BATCH", "12"))
 PREFILL_TOKENS = 16384    # prefill processes at most this many tokens per row chunk (engine/engine.py:79)
 USE_GRAPHS = os.environ.get("ENGINE_GRAPHS", "1") != "0"
 USE_PDL = os.environ.get("ENGINE_PDL", "1") != "0"
 # "persistent": one launch per decode step (qd_decode_step); "kernels": 1 + 5 x layers + 1 launches;
-# "tc": the tensor-core kernels, 1 + 7 x layers + 2 launches (used from TC_MIN_BATCH up)
+# "tc": the tensor-core kernels (used from TC_MIN_BATCH up): one persistent launch per step, or the
+# chain of 1 + 7 x layers + 2 launches (TC_STEP)
 STEP_MODE = os.environ.get("ENGINE_STEP", "persistent")
 
 
@@ -125,6 +131,9 @@ class _State:
             self.down = ops.Gemv(B, H, I, ops.Gemv.RES, dev, eps=eng.eps)
             self.lm = ops.LmHeadArgmax(B, eng.vocab, H, dev, eps=eng.eps)
         self.step = ops.DecodeStep(eng, self) if self.mode == "persistent" else None
+        persistent_tc = TC_STEP == "persistent" or (TC_STEP == "auto" and B <= TC_PERSISTENT_MAX_BATCH)
+        self.tstep = ops.TcDecodeStep(eng, self) if (self.mode == "tc" and persistent_tc) else None
+        self.tstep_logits = None
         self.step_logits = None
         self.rows = max(1, min(B, PREFILL_TOKENS // S))
         pin = torch.cuda.is_available()
@@ -275,6 +284,14 @@ class Engine:
                     st.step_logits = ops.DecodeStep(self, st, logits)
                 st.step_logits()
             return
+        if st.tstep is not None:
+            if logits is None:
+                st.tstep()
+            else:
+                if st.tstep_logits is None or st.tstep_logits._keep[2] is not logits:
+                    st.tstep_logits = ops.TcDecodeStep(self, st, logits)
+                st.tstep_logits()
+            return
         pdl, err = USE_PDL, st.err
         ops.embed(st.tok, self.e_packed, self.vocab, st.x, err, pdl)
         if st.mode == "tc":
@@ -312,7 +329,8 @@ class Engine:
         code = int(st.err.item())
         if code:
             # counters and tickets may be left mid-step: clear every scratch buffer before raising
-            for plan in (st.qkv, st.attn, st.o, st.gu, st.down, st.lm, st.step, st.step_logits):
+            for plan in (st.qkv, st.attn, st.o, st.gu, st.down, st.lm, st.step, st.step_logits, st.tstep,
+                         st.tstep_logits):
                 if plan is not None:
                     plan.scratch.zero_()
             st.err.zero_()

@@ -254,6 +254,17 @@ typedef struct qd_step_desc {
 int qd_decode_step_plan(const qd_step_desc* desc, int64_t* scratch_bytes, int* attn_splits);
 int qd_decode_step(const qd_step_desc* desc, void* scratch, int64_t scratch_bytes, cudaStream_t stream);
 
+/* Persistent tcgen05 decode step for batches of 4..64 (one cooperative launch per step): the tensor-core
+ * kernel chain (qd_pack_act, qd_tc_qkv_rope_append, qd_attn_decode_tc, qd_tc_gemv, qd_tc_lm_head_argmax)
+ * inside one launch with the same partitions and arithmetic, so its tokens and logits are
+ * bit-identical to the chain's. Same descriptor as qd_decode_step (its `attn` and `act` buffers are
+ * not used) plus the three packed activation operands, each [k/64][n_pad][64] BF16 zero-filled once:
+ * xh (k = hidden), xa (k = nq * 128), xi (k = inter); n_pad = batch rounded up to 16 (the plan's).
+ * Replaces the reference's per-op FastGemm / FastAttention launches at batch > 8 (engine/engine.py:463-477). */
+int qd_tc_decode_step_plan(const qd_step_desc* desc, int64_t* scratch_bytes, int* n_pad);
+int qd_tc_decode_step(const qd_step_desc* desc, void* xh, void* xa, void* xi, void* scratch, int64_t scratch_bytes,
+                      cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
