@@ -349,9 +349,10 @@ def run_ours(a):
                "kernel_rooflines": {"gate_up_gemv_per_op_kernel": {
                    "achieved": round(gu_gbs, 1), "avg_launch_us": round(gu_ms * 1e3, 2),
                    "frac": round(gu_gbs / peak, 4), "algorithmic_bytes": gu_bytes}},
-               "step_mode": st.mode,
+               "step_mode": st.mode + ("+persistent" if st.tstep is not None else ""),
                "clocks": clk.summary(), "e2e": e2e, "cpu_baseline": cpu,
-               "gpu_launches": K * {"persistent": 1, "kernels": 2 + 5 * a.layers, "tc": 3 + 7 * a.layers}[st.mode]}
+               "gpu_launches": K * (1 if st.tstep is not None else
+                                    {"persistent": 1, "kernels": 2 + 5 * a.layers, "tc": 3 + 7 * a.layers}[st.mode])}
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.barrier()

@@ -121,3 +121,19 @@ def test_tc_persistent_step_matches_kernel_chain(B):
         del eng
     for a, b in zip(out["persistent"][1], out["chain"][1]):
         assert float((a.float() - b.float()).abs().max()) <= 0.0625
+
+
+@pytest.mark.parametrize("B", [8, 24])
+def test_tc_poisoned_cache_slots_are_never_read(tc_engine, B):
+    """NaN in every cache slot past the valid length leaves the tokens unchanged (tensor-core paths:
+    the persistent step at 8, the chain at 24)."""
+    from decode_b200 import synth
+
+    eng, _, cfg = tc_engine
+    p = synth.random_prompt(B, 40, cfg["vocab_size"], seed=77)
+    ref = list(eng.generate(p, 6))
+    st = eng.state
+    st.k_all.fill_(float("nan"))
+    st.v_all.fill_(float("nan"))
+    again = list(eng.generate(p, 6))
+    assert again == ref
