@@ -195,7 +195,10 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
       };
       if (n > 0) issue_qk(0);
       for (int i = 0; i < n; ++i) {
-        if (i + 1 < n) issue_qk(i + 1);
+        // the next chunk's q.k goes first unless it starts a new pair: then it waits for that pair's q,
+        // and this chunk's P.V must not wait with it
+        const bool next_new_pair = (i + 1 < n) && ci_next == 0;
+        if (i + 1 < n && !next_new_pair) issue_qk(i + 1);
         const int slot = i % kTStages, b = i & 1;
         if (ok) ok = mbar_wait(pfull_bar(b), (i >> 1) & 1, a.err, kErrWaitFull);
         tc_fence_after();
@@ -209,6 +212,7 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
         }
         umma_commit(ofull_bar(b));
         umma_commit(empty_bar(slot));
+        if (next_new_pair) issue_qk(i + 1);
       }
     }
   } else {
@@ -217,17 +221,27 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
     int pair = (int)(c_begin / nch), ci = (int)(c_begin - (int64_t)pair * nch);
     int seg_first = ci;
     float m_run[kGroup], l_thr[kGroup], acc[kGroup];
-    auto put_q = [&](int pr) {  // q of pair pr into the operand tile (the previous pair's q.k is done)
+    // q of a pair: loaded into registers one pair ahead (its latency hides behind the current pair),
+    // stored into the operand tile when the previous pair's last q.k is done
+    const int pair_last = (int)((c_end - 1) / nch);
+    unsigned short qn[kGroup];
+    auto load_q = [&](int pr) {
       const int b = pr / a.nkv, kvh = pr - b * a.nkv;
 #pragma unroll
-      for (int h = 0; h < kGroup; ++h) {
-        const __nv_bfloat16 qv = a.q[((int64_t)b * a.nq + kvh * kGroup + h) * kHeadDim + tid];
-        *reinterpret_cast<__nv_bfloat16*>(smem + Ly::qb + (tid >> 6) * (kTN * 128) + sw128_off(h, tid & 63)) = qv;
-      }
+      for (int h = 0; h < kGroup; ++h)
+        qn[h] = __ldcg(reinterpret_cast<const unsigned short*>(a.q) + ((int64_t)b * a.nq + kvh * kGroup + h) * kHeadDim +
+                       tid);
+    };
+    auto put_q = [&](int pr) {  // store the loaded q of pair pr, then load the following pair's
+#pragma unroll
+      for (int h = 0; h < kGroup; ++h)
+        *reinterpret_cast<unsigned short*>(smem + Ly::qb + (tid >> 6) * (kTN * 128) + sw128_off(h, tid & 63)) = qn[h];
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(qready_bar);
+      if (pr + 1 <= pair_last) load_q(pr + 1);
     };
+    load_q(pair);
     auto reset_state = [&]() {
 #pragma unroll
       for (int h = 0; h < kGroup; ++h) {

@@ -487,7 +487,8 @@ __device__ void mma_attn(const TcStepArgs& A, const AttnWork& w, const TcStepLay
   };
   if (w.n > 0) issue_qk(0);
   for (int i = 0; i < w.n; ++i) {
-    if (i + 1 < w.n) issue_qk(i + 1);
+    const bool next_new_pair = (i + 1 < w.n) && ci_next == 0;  // its q.k waits for the pair's q: after P.V
+    if (i + 1 < w.n && !next_new_pair) issue_qk(i + 1);
     const int gi = ms.agi + i, slot = gi % kAStages, b = gi & 1;
     if (ok) ok = mbar_wait_abort(pfull(b), (gi >> 1) & 1, A.err, kErrWaitFull, A.abort_flag);
     tc_fence_after();
@@ -501,6 +502,7 @@ __device__ void mma_attn(const TcStepArgs& A, const AttnWork& w, const TcStepLay
     }
     umma_commit(ofull(b));
     umma_commit(aempty(slot));
+    if (next_new_pair) issue_qk(i + 1);
   }
   ms.agi += w.n;
 }
@@ -519,18 +521,24 @@ __device__ void softmax_attn(const TcStepArgs& A, const AttnWork& w, int l, int 
   const int N = (A.m_act + 15) / 16 * 16;
   int pair = w.pair0, ci = w.ci0, seg_first = ci;
   float m_run[kGroup], l_thr[kGroup], acc[kGroup];
-  auto put_q = [&](int pr) {
+  // q of a pair (written every layer by other CTAs: read through L2) is loaded one pair ahead
+  const int pair_last = w.n > 0 ? w.pair0 + (w.ci0 + w.n - 1) / w.nch : 0;
+  unsigned short qn[kGroup];
+  auto load_q = [&](int pr) {
     const int b = pr / A.nkv, kvh = pr - b * A.nkv;
 #pragma unroll
-    for (int h = 0; h < kGroup; ++h) {
-      // written every layer by other CTAs: read through L2, never a stale L1 line
-      const unsigned short qv = __ldcg(reinterpret_cast<const unsigned short*>(A.q) +
-                                       ((int64_t)b * A.nq + kvh * kGroup + h) * kHeadDim + tid);
-      *reinterpret_cast<unsigned short*>(smem + Ly.qb + (tid >> 6) * (kAN * 128) + sw128(h, tid & 63)) = qv;
-    }
+    for (int h = 0; h < kGroup; ++h)
+      qn[h] = __ldcg(reinterpret_cast<const unsigned short*>(A.q) + ((int64_t)b * A.nq + kvh * kGroup + h) * kHeadDim +
+                     tid);
+  };
+  auto put_q = [&](int pr) {
+#pragma unroll
+    for (int h = 0; h < kGroup; ++h)
+      *reinterpret_cast<unsigned short*>(smem + Ly.qb + (tid >> 6) * (kAN * 128) + sw128(h, tid & 63)) = qn[h];
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(qready);
+    if (pr + 1 <= pair_last) load_q(pr + 1);
   };
   auto reset = [&]() {
 #pragma unroll
@@ -544,7 +552,10 @@ __device__ void softmax_attn(const TcStepArgs& A, const AttnWork& w, int l, int 
     const int k = hq * kHeadDim + d, kb = k >> 6, c = k & 63;
     return ((int64_t)kb * N + b) * 64 + (((c >> 3) ^ (b & 7)) << 3) + (c & 7);
   };
-  if (w.n > 0) put_q(pair);
+  if (w.n > 0) {
+    load_q(pair);
+    put_q(pair);
+  }
   reset();
   bool ok = true;
   for (int i = 0; i < w.n; ++i) {
