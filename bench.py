@@ -52,7 +52,7 @@ def _args():
                    help="time one decode kernel alone (small profiling case; random packed weights on the GPU)")
     p.add_argument("--launches", type=int, default=8)
     p.add_argument("--tc", action="store_true", help="with --kernel: the tcgen05 kernel (activations pre-packed)")
-    p.add_argument("--sweep", default=None, choices=["linear", "attn"],
+    p.add_argument("--sweep", default=None, choices=["linear", "attn", "prefill"],
                    help="BASELINE config 2 (decode linear shapes x batch x kernel path) or config 3 (GQA decode "
                         "attention); one JSON line per case")
     return p.parse_args()
@@ -673,6 +673,80 @@ def run_sweep_attn(a):
             torch.cuda.empty_cache()
 
 
+def run_sweep_prefill(a):
+    """Prompt projections (prefill, engine/engine.py:550-592) at M tokens in {128, 1024, 16384} (the
+    prompt of config 1, one config-4 sequence, a full 16384-token prefill chunk): qd_tc_gemm over the
+    packed weights (plain store and fused epilogue) against cuBLAS (torch.matmul on row-major
+    weights, store only). Flops = 2MNK, against the measured dense BF16 peak. Then the engine's whole
+    prompt forward for configs 1 and 4 (one GPU's shard: 8 x 1024), timed by CUDA events around the
+    prefill graph."""
+    import torch
+
+    from decode_b200 import ops
+
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    tpeak = _tensor_peak()
+    H, I, nq, nkv, D = 2560, 9728, 32, 8, 128
+    shapes = [("qkv", (nq + 2 * nkv) * D, H), ("o", H, nq * D), ("gu", 2 * I, H), ("down", H, I)]
+    g = torch.Generator(device=dev).manual_seed(1)
+    err = torch.zeros((1,), dtype=torch.int32, device=dev)
+    launches = max(a.launches, 12)
+    for name, n, k in shapes:
+        w = (torch.randn((n, k), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        wp = ops.pack_matrix(w)
+        for M in (128, 1024, 16384):
+            x = torch.randn((M, k), generator=g, device=dev).to(torch.bfloat16)
+            out = torch.empty((M, n), dtype=torch.bfloat16, device=dev)
+            epi = {"o": ops.Gemv.RES, "down": ops.Gemv.RES, "gu": ops.Gemv.SWIGLU}.get(name, ops.Gemv.STORE)
+            cases = [("tc_gemm", "store", lambda i: ops.tc_gemm(x, wp, n, out, err=err))]
+            if epi == ops.Gemv.RES:
+                cases.append(("tc_gemm", "fused", lambda i: ops.tc_gemm(x, wp, n, out, res=out, epilogue=epi, err=err)))
+            elif epi == ops.Gemv.SWIGLU:
+                cases.append(("tc_gemm", "fused", lambda i: ops.tc_gemm(x, wp, n, out[:, : n // 2], epilogue=epi,
+                                                                       err=err)))
+            cases.append(("cublas", "store", lambda i: torch.matmul(x, w.t(), out=out)))
+            grid, bn = ops.tc_gemm_plan(M, n, k)
+            for path, ep, fn in cases:
+                ms = _time_cycle(fn, 1, launches)
+                tf = 2 * M * n * k / (ms / 1e3) / 1e12
+                print(json.dumps({"sweep": "prefill", "shape": name, "n": n, "k": k, "M": M, "path": path,
+                                  "epilogue": ep, "tile_n": bn if path == "tc_gemm" else None,
+                                  "grid": grid if path == "tc_gemm" else None, "us": round(ms * 1e3, 2),
+                                  "TFLOPs": round(tf, 1), "frac_tensor": round(tf / tpeak, 4),
+                                  "peak_tflops": tpeak}), flush=True)
+            assert int(err.item()) == 0
+            del x, out
+        del w, wp
+        torch.cuda.empty_cache()
+    # whole prompt forward through the engine (random-init weights)
+    import engine as E
+
+    state, cfg = make_model(a.layers)
+    eng = E.Engine.from_state_dict(state, cfg, "cuda:0")
+    del state
+    for B, S in ((1, 128), (8, 1024)):
+        st = eng._build(B, S, 2)
+        with torch.inference_mode():
+            st.ids.copy_(torch.tensor(synth_prompt(B, S), dtype=torch.int64))
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.prefill_graph.replay()
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(3):
+            st.prefill_graph.replay()
+        e.record()
+        e.synchronize()
+        ms = s.elapsed_time(e) / 3
+        # the last layer continues only the last position (o, gate/up, down, LM head on B rows)
+        rest = 4096 * 2560 + 2560 * 19456 + 9728 * 2560
+        flops = 2 * B * S * (a.layers * 2560 * 6144 + (a.layers - 1) * rest) + 2 * B * (rest + 151936 * 2560)
+        eng.check_device_errors(st)
+        print(json.dumps({"sweep": "prefill_forward", "layers": a.layers, "batch": B, "prompt": S, "ms": round(ms, 3),
+                          "tokens_per_s": round(B * S / (ms / 1e3), 1),
+                          "projection_TFLOPs": round(flops / (ms / 1e3) / 1e12, 1)}), flush=True)
+
+
 def _tensor_peak():
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
@@ -693,6 +767,8 @@ def main():
         run_sweep_linear(a)
     elif a.sweep == "attn":
         run_sweep_attn(a)
+    elif a.sweep == "prefill":
+        run_sweep_prefill(a)
     elif a.kernel:
         run_kernel(a)
     elif a.impl == "reference":

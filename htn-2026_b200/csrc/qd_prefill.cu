@@ -1,0 +1,547 @@
+// Prompt (prefill) kernels for sm_100a: a tcgen05 GEMM over the packed weights, the row RMSNorm and the
+// per-head q/k RMSNorm + RoPE + KV-cache write of the prompt positions.
+//
+// The prefill forward (engine/engine.py:550-592) runs every prompt token through the layers at once,
+// so its projections are real GEMMs (rows = tokens). qd_tc_gemm computes
+//     out[t, :] = epilogue(x[t, :] . W^T)
+// with x [m, k] row-major BF16 and W in the packed 16 KiB-block layout the decode kernels stream, so one
+// copy of the weights serves both phases. Tiles are 128 tokens x BN weight rows (BN = 128 or 256):
+// A = the token tile, loaded by a 2-D TMA tensor map with the 128-byte swizzle (box 64 columns x 128
+// rows, rows past m read as zero); B = BN/128 packed blocks, one bulk copy each - the packed block
+// already is a K-major 128-byte-swizzled operand, and two consecutive blocks form one 256-row operand
+// (8-row atoms 1 KiB apart). Per 64-column K step: 4 tcgen05.mma (M = 128, N = BN, K = 16) into an
+// fp32 accumulator in tensor memory, two accumulators alternating so the epilogue of one tile
+// overlaps the MMAs of the next.
+//
+// Warp roles (192 threads): warps 0-3 epilogue (warp w reads TMEM lanes 32w.., i.e. tokens 32w..),
+// warp 4 producer, warp 5 MMA issuer. The CTAs are persistent over the tiles; tiles run in groups of
+// kGroupM token tiles x all weight tiles so a group's activations stay in L2 while the weights stream.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "qd_common.cuh"
+#include "qd_host.h"
+#include "qd_plan.h"
+#include "qd_umma.cuh"
+
+namespace qd {
+
+constexpr int kGemmThreads = 192;
+constexpr int kGemmEpiWarps = 4;
+constexpr int kGroupM = 8;  // token tiles per raster group
+
+enum { GEMM_STORE = 0, GEMM_RES = 1, GEMM_SWIGLU = 2 };
+
+struct alignas(64) GemmArgs {
+  CUtensorMap tx;  // x [m, k] BF16, box {64, 128}, 128-byte swizzle
+  const char* w;   // packed [ngroups * 128, k]
+  __nv_bfloat16* out;
+  const __nv_bfloat16* res;
+  int64_t ldo, ldr, m, n;
+  int kblocks, ngroups, m_tiles, n_tiles, tiles, nst;
+  int* err;
+};
+
+template <int BN>
+struct GemmLayout {
+  static constexpr int stage = kBlockBytes + BN * 128;  // token tile + BN/128 weight blocks
+  static __host__ __device__ int bars(int nst) { return nst * stage; }
+  static __host__ __device__ int total(int nst) { return bars(nst) + (2 * nst + 4) * 8 + 16; }
+};
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+// tile index -> (token tile, weight tile): groups of kGroupM token tiles, weight tiles outer within
+// a group
+__device__ __forceinline__ void gemm_tile(const GemmArgs& a, int t, int* mt, int* nt) {
+  const int per_group = kGroupM * a.n_tiles;
+  const int grp = t / per_group, rem = t - grp * per_group;
+  const int m0 = grp * kGroupM;
+  const int gm = (a.m_tiles - m0) < kGroupM ? (a.m_tiles - m0) : kGroupM;
+  *mt = m0 + rem % gm;
+  *nt = rem / gm;
+}
+
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_constant__ GemmArgs a) {
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  using Ly = GemmLayout<BN>;
+  const int nst = a.nst;
+  const uint32_t ring = smem_u32(smem);
+  const uint32_t bars = smem_u32(smem + Ly::bars(nst));
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (nst + s); };
+  auto accf_bar = [&](int i) { return bars + 8u * (2 * nst + i); };
+  auto acce_bar = [&](int i) { return bars + 8u * (2 * nst + 2 + i); };
+  int* misc = reinterpret_cast<int*>(smem + Ly::bars(nst) + (2 * nst + 4) * 8);  // tmem slot, abort, issued
+  constexpr uint32_t kCols = 2 * BN;  // two accumulators
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int cta = blockIdx.x, G = gridDim.x;
+  if (tid == 0) {
+    for (int s = 0; s < nst; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(accf_bar(i), 1);
+      mbar_init(acce_bar(i), kGemmEpiWarps);
+    }
+    fence_mbar_init();
+    misc[1] = 0;
+    misc[2] = 0;
+  }
+  if (warp == 5) tmem_alloc(smem_u32(misc), kCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = (uint32_t)misc[0];
+  int* abort = misc + 1;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_normal();
+      int slot = 0, round = 0, issued = 0;
+      bool ok = true;
+      for (int t = cta; t < a.tiles && ok; t += G) {
+        int mt, nt;
+        gemm_tile(a, t, &mt, &nt);
+        const int g0 = nt * (BN / 128);
+        for (int kb = 0; kb < a.kblocks; ++kb) {
+          if (round > 0 && !mbar_wait_abort(empty_bar(slot), (round - 1) & 1, a.err, kErrWaitEmpty, abort)) {
+            ok = false;
+            break;
+          }
+          const uint32_t st = ring + slot * Ly::stage;
+          mbar_arrive_expect_tx(full_bar(slot), (uint32_t)Ly::stage);
+          tma_load_2d(st, &a.tx, kb * 64, mt * 128, full_bar(slot), pol);
+#pragma unroll
+          for (int h = 0; h < BN / 128; ++h) {
+            // a missing last group (odd group count) repeats the previous one: computed, never stored
+            const int g = (g0 + h < a.ngroups) ? g0 + h : a.ngroups - 1;
+            bulk_g2s(st + kBlockBytes * (1 + h), a.w + ((int64_t)g * a.kblocks + kb) * kBlockBytes, kBlockBytes,
+                     full_bar(slot), pol);
+          }
+          ++issued;
+          if (++slot == nst) {
+            slot = 0;
+            ++round;
+          }
+        }
+      }
+      misc[2] = issued;
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(BN);
+      int slot = 0, fph = 0, i = 0;
+      bool ok = true;
+      for (int t = cta; t < a.tiles && ok; t += G, ++i) {
+        const int buf = i & 1;
+        if (i >= 2 && !mbar_wait_abort(acce_bar(buf), ((i >> 1) - 1) & 1, a.err, kErrWaitFull, abort)) break;
+        tc_fence_after();
+        for (int kb = 0; kb < a.kblocks; ++kb) {
+          if (!mbar_wait_abort(full_bar(slot), fph, a.err, kErrWaitFull, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = ring + slot * Ly::stage, sb = sa + kBlockBytes;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            umma_bf16(tmem + buf * BN, umma_desc_sw128(sa + 32 * j), umma_desc_sw128(sb + 32 * j), idesc,
+                      (kb | j) ? 1u : 0u);
+          umma_commit(empty_bar(slot));
+          if (++slot == nst) {
+            slot = 0;
+            fph ^= 1;
+          }
+        }
+        if (ok) umma_commit(accf_bar(buf));
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue: thread = token row
+    int i = 0;
+    for (int t = cta; t < a.tiles; t += G, ++i) {
+      const int buf = i & 1;
+      if (!mbar_wait_abort(accf_bar(buf), (i >> 1) & 1, a.err, kErrWaitFull, abort)) break;
+      tc_fence_after();
+      int mt, nt;
+      gemm_tile(a, t, &mt, &nt);
+      const int64_t row = (int64_t)mt * 128 + 32 * warp + lane;
+      const bool live = row < a.m;
+      const uint32_t tb = tmem + ((uint32_t)(32 * warp) << 16) + buf * BN;
+      if constexpr (EPI == GEMM_SWIGLU) {
+        // group g of the interleaved gate/up matrix: 64 gate rows, then the 64 up rows of the same
+        // outputs 64g..64g+63
+#pragma unroll 1
+        for (int h = 0; h < BN / 128; ++h) {
+          const int g = nt * (BN / 128) + h;
+          if (g >= a.ngroups) break;
+#pragma unroll 1
+          for (int j0 = 0; j0 < 64; j0 += 16) {
+            uint32_t gr[16], ur[16];
+            tmem_ld16_raw(tb + h * 128 + j0, gr);
+            tmem_ld16_raw(tb + h * 128 + 64 + j0, ur);
+            tmem_wait_ld16(gr);
+            tmem_wait_ld16(ur);
+            uint32_t o[8];
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              float r2[2];
+#pragma unroll
+              for (int d = 0; d < 2; ++d) {
+                const float gv = bf16r(__uint_as_float(gr[e + d]));
+                const float uv = bf16r(__uint_as_float(ur[e + d]));
+                const float s = bf16r(gv / (1.0f + expf(-gv)));
+                r2[d] = s * uv;
+              }
+              o[e >> 1] = pack_bf2(r2[0], r2[1]);
+            }
+            if (live) {
+              uint4* dst = reinterpret_cast<uint4*>(a.out + row * a.ldo + (int64_t)g * 64 + j0);
+              dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+              dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          const int64_t col = (int64_t)nt * BN + c;  // n % 128 == 0: a 32-column chunk is all in or all out
+          uint32_t r0[16], r1[16];
+          tmem_ld16_raw(tb + c, r0);
+          tmem_ld16_raw(tb + c + 16, r1);
+          tmem_wait_ld16(r0);
+          tmem_wait_ld16(r1);
+          if (!live || col >= a.n) continue;
+          float v[32];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            v[e] = bf16r(__uint_as_float(r0[e]));
+            v[16 + e] = bf16r(__uint_as_float(r1[e]));
+          }
+          if constexpr (EPI == GEMM_RES) {
+            const uint4* rp = reinterpret_cast<const uint4*>(a.res + row * a.ldr + col);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 u = rp[q];
+              const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                v[8 * q + 2 * e] += bf_lo(w4[e]);
+                v[8 * q + 2 * e + 1] += bf_hi(w4[e]);
+              }
+            }
+          }
+          uint4* dst = reinterpret_cast<uint4*>(a.out + row * a.ldo + col);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(pack_bf2(v[8 * q], v[8 * q + 1]), pack_bf2(v[8 * q + 2], v[8 * q + 3]),
+                                pack_bf2(v[8 * q + 4], v[8 * q + 5]), pack_bf2(v[8 * q + 6], v[8 * q + 7]));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce_bar(buf));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 5) tmem_dealloc(tmem, kCols);
+  if (tid == 0) {  // no bulk copy may still be writing shared memory when the CTA exits
+    const int issued = misc[2];
+    for (int it = issued > nst ? issued - nst : 0; it < issued; ++it)
+      if (!mbar_wait(full_bar(it % nst), (it / nst) & 1, a.err, kErrDrain)) break;
+  }
+}
+
+// ------------------------------------------------------------------ row RMSNorm
+struct RmsArgs {
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* w;
+  __nv_bfloat16* out;
+  int64_t ldx, ldo, k;
+  float eps;
+};
+
+// One CTA of 256 threads per row: out = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))) (Qwen3RMSNorm's
+// cast placement, engine/engine.py:505-509).
+__global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const __grid_constant__ RmsArgs a) {
+  __shared__ float wsum[8];
+  const int64_t m = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int k8 = (int)(a.k >> 3);
+  const __nv_bfloat16* xr = a.x + m * a.ldx;
+  float sq = 0.f;
+  for (int q = tid; q < k8; q += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + q * 8);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float lo = bf_lo(u[e]), hi = bf_hi(u[e]);
+      sq = fmaf(lo, lo, sq);
+      sq = fmaf(hi, hi, sq);
+    }
+  }
+  sq = warp_sum(sq);
+  if (lane == 0) wsum[warp] = sq;
+  __syncthreads();
+  float ss = 0.f;
+#pragma unroll
+  for (int w8 = 0; w8 < 8; ++w8) ss += wsum[w8];
+  const float rstd = 1.0f / sqrtf(ss / (float)a.k + a.eps);
+  for (int q = tid; q < k8; q += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + q * 8);
+    const uint4 wv = *reinterpret_cast<const uint4*>(a.w + q * 8);
+    const uint32_t xu[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float lo = bf16r(bf_lo(wu[e]) * bf16r(bf_lo(xu[e]) * rstd));
+      const float hi = bf16r(bf_hi(wu[e]) * bf16r(bf_hi(xu[e]) * rstd));
+      o[e] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
+    }
+    *reinterpret_cast<uint4*>(a.out + m * a.ldo + q * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ------------------------------------------------------------------ prompt q/k norm + RoPE + cache write
+struct QkRopeArgs {
+  const __nv_bfloat16* qkv;  // [b * S, (nq + 2 nkv) * 128], token t = i * S + s
+  const __nv_bfloat16 *qn, *kn, *cos, *sin;
+  __nv_bfloat16* q_out;  // [b * S, nq * 128]
+  __nv_bfloat16 *k_cache, *v_cache;
+  int64_t ldqkv, ldq, S, cs_b, cs_h, tokens;
+  int nq, nkv;
+  float eps;
+};
+
+// One warp per (token, head); lane l holds elements 4l..4l+3, so the RoPE partner of element r
+// (r ^ 64) sits in lane l ^ 16. Same arithmetic and rounding points as the decode QKV epilogue
+// (engine/kernels/fused.py:23-81 with pos_mode 0: position = prompt index).
+__global__ void __launch_bounds__(256) prefill_qk_rope_kernel(const __grid_constant__ QkRopeArgs a) {
+  const int heads = a.nq + 2 * a.nkv;
+  const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (wid >= a.tokens * heads) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t t = wid / heads;
+  const int h = (int)(wid - t * heads);
+  const int64_t i = t / a.S, s = t - i * a.S;
+  const uint2 u = *reinterpret_cast<const uint2*>(a.qkv + t * a.ldqkv + (int64_t)h * 128 + 4 * lane);
+  float x[4] = {bf_lo(u.x), bf_hi(u.x), bf_lo(u.y), bf_hi(u.y)};
+  if (h >= a.nq + a.nkv) {  // V head: into the cache as is
+    const int kvh = h - a.nq - a.nkv;
+    *reinterpret_cast<uint2*>(a.v_cache + i * a.cs_b + kvh * a.cs_h + s * 128 + 4 * lane) = u;
+    return;
+  }
+  float sq = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+  sq = warp_sum(sq);
+  const float rstd = 1.0f / sqrtf(sq / 128.0f + a.eps);
+  const __nv_bfloat16* nw = h < a.nq ? a.qn : a.kn;
+  float y[4], yp[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) y[e] = bf16r(bf16_to_f(nw[4 * lane + e]) * bf16r(x[e] * rstd));
+#pragma unroll
+  for (int e = 0; e < 4; ++e) yp[e] = __shfl_xor_sync(0xffffffffu, y[e], 16);
+  uint32_t o[2];
+#pragma unroll
+  for (int e = 0; e < 4; e += 2) {
+    float r2[2];
+#pragma unroll
+    for (int d = 0; d < 2; ++d) {
+      const int r = 4 * lane + e + d;
+      const float c = bf16_to_f(a.cos[s * 128 + r]);
+      const float sn = bf16_to_f(a.sin[s * 128 + r]);
+      const float rot = (r < 64) ? bf16r(-yp[e + d] * sn) : bf16r(yp[e + d] * sn);
+      r2[d] = bf16r(y[e + d] * c) + rot;
+    }
+    o[e >> 1] = pack_bf2(r2[0], r2[1]);
+  }
+  const uint2 ov = make_uint2(o[0], o[1]);
+  if (h < a.nq)
+    *reinterpret_cast<uint2*>(a.q_out + t * a.ldq + (int64_t)h * 128 + 4 * lane) = ov;
+  else
+    *reinterpret_cast<uint2*>(a.k_cache + i * a.cs_b + (h - a.nq) * a.cs_h + s * 128 + 4 * lane) = ov;
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 gemm_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+template <int BN>
+static int gemm_nst() {
+  int nst = env_int("QD_GEMM_STAGES", 8);
+  if (nst > 8) nst = 8;
+  while (nst > 2 && GemmLayout<BN>::total(nst) + 1024 > 227 * 1024) --nst;
+  return nst;
+}
+
+// BN = 256 when the 256-wide tiles alone give every SM at least one tile, else 128
+static int gemm_bn(int64_t m, int64_t n) {
+  const int64_t mt = (m + 127) / 128;
+  const int forced = env_int("QD_GEMM_BN", 0);
+  if (forced == 128 || forced == 256) return forced;
+  return mt * ((n + 255) / 256) >= host_sm_count() ? 256 : 128;
+}
+
+template <int BN, int EPI>
+static int launch_gemm(const GemmArgs& a, int grid, cudaStream_t stream) {
+  auto kern = tc_gemm_kernel<BN, EPI>;
+  const int smem = GemmLayout<BN>::total(a.nst) + 1024;
+  static int configured = 0;
+  if (smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured = smem;
+  }
+  return launch_kernel((const void*)kern, dim3(grid), dim3(kGemmThreads), smem, 0, stream, (void*)&a);
+}
+
+}  // namespace qd
+
+using namespace qd;
+
+extern "C" int qd_tc_gemm_plan(int64_t m, int64_t n, int64_t k, int* grid, int* bn) {
+  if (m < 1 || n < 128 || n % 128 || k < 64 || k % 64) return set_error(QD_ERR_ARG, "tc gemm plan: bad sizes");
+  const int b = gemm_bn(m, n);
+  const int64_t tiles = ((m + 127) / 128) * ((n + b - 1) / b);
+  const int64_t g = tiles < host_sm_count() ? tiles : host_sm_count();
+  if (grid) *grid = (int)g;
+  if (bn) *bn = b;
+  return QD_OK;
+}
+
+extern "C" int qd_tc_gemm(const void* x, int64_t ldx, int64_t m, const void* w_packed, int64_t n, int64_t k, void* out,
+                          int64_t ldo, const void* res, int64_t ldr, int epilogue, int* err, cudaStream_t stream) {
+  if (!x || !w_packed || !out) return set_error(QD_ERR_ARG, "null pointer");
+  if (m < 1 || n < 128 || n % 128 || k < 64 || k % 64 || ldx < k || ldx % 8 || ldo % 8)
+    return set_error(QD_ERR_ARG, "tc gemm: m >= 1, n %% 128 == 0, k %% 64 == 0, ldx >= k, ldx/ldo %% 8 == 0");
+  if (epilogue != GEMM_STORE && epilogue != GEMM_RES && epilogue != GEMM_SWIGLU)
+    return set_error(QD_ERR_ARG, "tc gemm: epilogue must be QD_EPI_STORE, QD_EPI_RES or QD_EPI_SWIGLU");
+  if (ldo < (epilogue == GEMM_SWIGLU ? n / 2 : n)) return set_error(QD_ERR_ARG, "tc gemm: ldo too small");
+  if (epilogue == GEMM_RES && (!res || ldr < n || ldr % 8 || !aligned16(res)))
+    return set_error(QD_ERR_ARG, "tc gemm: residual needs ldr >= n, ldr %% 8 == 0, 16-byte alignment");
+  if (!aligned16(x) || !aligned16(w_packed) || !aligned16(out)) return set_error(QD_ERR_ARG, "tc gemm: alignment");
+  if (m > (int64_t)INT32_MAX - 128 || k > (1 << 24)) return set_error(QD_ERR_UNSUPPORTED, "tc gemm: too large");
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = gemm_encode_fn();
+  if (!encode) return set_error(QD_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  GemmArgs a = {};
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
+    const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(&a.tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(QD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  }
+  const int bn = gemm_bn(m, n);
+  a.w = static_cast<const char*>(w_packed);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.res = static_cast<const __nv_bfloat16*>(res);
+  a.ldo = ldo;
+  a.ldr = ldr;
+  a.m = m;
+  a.n = n;
+  a.kblocks = (int)(k / 64);
+  a.ngroups = (int)(n / 128);
+  a.m_tiles = (int)((m + 127) / 128);
+  a.n_tiles = (int)((n + bn - 1) / bn);
+  const int64_t tiles = (int64_t)a.m_tiles * a.n_tiles;
+  if (tiles > INT32_MAX) return set_error(QD_ERR_UNSUPPORTED, "tc gemm: too many tiles");
+  a.tiles = (int)tiles;
+  a.err = err;
+  const int grid = a.tiles < host_sm_count() ? a.tiles : host_sm_count();
+  if (bn == 256) {
+    a.nst = gemm_nst<256>();
+    if (epilogue == GEMM_STORE) return launch_gemm<256, GEMM_STORE>(a, grid, stream);
+    if (epilogue == GEMM_RES) return launch_gemm<256, GEMM_RES>(a, grid, stream);
+    return launch_gemm<256, GEMM_SWIGLU>(a, grid, stream);
+  }
+  a.nst = gemm_nst<128>();
+  if (epilogue == GEMM_STORE) return launch_gemm<128, GEMM_STORE>(a, grid, stream);
+  if (epilogue == GEMM_RES) return launch_gemm<128, GEMM_RES>(a, grid, stream);
+  return launch_gemm<128, GEMM_SWIGLU>(a, grid, stream);
+}
+
+extern "C" int qd_rmsnorm_rows(const void* x, int64_t ldx, int64_t m, int64_t k, const void* norm_w, float eps,
+                               void* out, int64_t ldo, cudaStream_t stream) {
+  if (!x || !norm_w || !out) return set_error(QD_ERR_ARG, "null pointer");
+  if (m < 1 || k < 8 || k % 8 || ldx < k || ldo < k || ldx % 8 || ldo % 8 || m > INT32_MAX)
+    return set_error(QD_ERR_ARG, "rmsnorm: bad sizes");
+  if (!aligned16(x) || !aligned16(norm_w) || !aligned16(out)) return set_error(QD_ERR_ARG, "rmsnorm: alignment");
+  RmsArgs a = {};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.w = static_cast<const __nv_bfloat16*>(norm_w);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.ldx = ldx;
+  a.ldo = ldo;
+  a.k = k;
+  a.eps = eps;
+  return launch_kernel((const void*)rmsnorm_rows_kernel, dim3((unsigned)m), dim3(256), 0, 0, stream, &a);
+}
+
+extern "C" int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int64_t S, int nq_heads, int nkv_heads,
+                                  const void* q_norm, const void* k_norm, float eps, const void* cos, const void* sin,
+                                  void* q_out, int64_t ldq, void* k_cache, void* v_cache, int64_t cap, int64_t cs_b,
+                                  int64_t cs_h, cudaStream_t stream) {
+  if (!qkv || !q_norm || !k_norm || !cos || !sin || !q_out || !k_cache || !v_cache)
+    return set_error(QD_ERR_ARG, "null pointer");
+  if (batch < 1 || S < 1 || S > cap || nq_heads < 1 || nkv_heads < 1 ||
+      ldqkv < (int64_t)(nq_heads + 2 * nkv_heads) * 128 || ldq < (int64_t)nq_heads * 128 || ldqkv % 4 || ldq % 4 ||
+      cs_h < cap * 128 || cs_b < (int64_t)nkv_heads * cs_h || cs_h % 4 || cs_b % 4)
+    return set_error(QD_ERR_ARG, "prefill q/k rope: bad sizes");
+  if (((uintptr_t)qkv | (uintptr_t)q_out | (uintptr_t)k_cache | (uintptr_t)v_cache) & 7)
+    return set_error(QD_ERR_ARG, "prefill q/k rope: 8-byte alignment");
+  QkRopeArgs a = {};
+  a.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  a.qn = static_cast<const __nv_bfloat16*>(q_norm);
+  a.kn = static_cast<const __nv_bfloat16*>(k_norm);
+  a.cos = static_cast<const __nv_bfloat16*>(cos);
+  a.sin = static_cast<const __nv_bfloat16*>(sin);
+  a.q_out = static_cast<__nv_bfloat16*>(q_out);
+  a.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  a.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  a.ldqkv = ldqkv;
+  a.ldq = ldq;
+  a.S = S;
+  a.cs_b = cs_b;
+  a.cs_h = cs_h;
+  a.tokens = (int64_t)batch * S;
+  a.nq = nq_heads;
+  a.nkv = nkv_heads;
+  a.eps = eps;
+  const int64_t warps = a.tokens * (nq_heads + 2 * nkv_heads);
+  const int64_t blocks = (warps + 7) / 8;
+  if (blocks > INT32_MAX) return set_error(QD_ERR_UNSUPPORTED, "prefill q/k rope: too many tokens");
+  return launch_kernel((const void*)prefill_qk_rope_kernel, dim3((unsigned)blocks), dim3(256), 0, 0, stream, &a);
+}

@@ -270,6 +270,45 @@ class TcLmHeadArgmax(_TcOp):
         return tok
 
 
+# ------------------------------------------------------------------------------------ prompt (prefill)
+def tc_gemm(x, w, n: int, out, res=None, epilogue: int = L.QD_EPI_STORE, err=None):
+    """out = epilogue(x @ W^T) on the tensor cores for any number of token rows (qd_tc_gemm): x [m, k]
+    BF16 (unit column stride), W packed [n, k]; SWIGLU writes n / 2 columns."""
+    _check_bf16(x, w, out, res)
+    m, k = x.shape
+    assert x.stride(1) == 1 and out.stride(1) == 1 and out.shape[0] == m
+    L.call("qd_tc_gemm", _ptr(x), x.stride(0), m, _ptr(w), n, k, _ptr(out), out.stride(0), _ptr(res),
+           res.stride(0) if res is not None else 0, epilogue, _ptr(err), _stream())
+    return out
+
+
+def tc_gemm_plan(m: int, n: int, k: int) -> tuple[int, int]:
+    g, bn = ctypes.c_int(0), ctypes.c_int(0)
+    L.call("qd_tc_gemm_plan", m, n, k, ctypes.byref(g), ctypes.byref(bn))
+    return g.value, bn.value
+
+
+def rmsnorm_rows(x, w, eps: float, out):
+    """out = Qwen3RMSNorm(x) row by row (qd_rmsnorm_rows)."""
+    _check_bf16(x, w, out)
+    m, k = x.shape
+    assert x.stride(1) == 1 and out.stride(1) == 1
+    L.call("qd_rmsnorm_rows", _ptr(x), x.stride(0), m, k, _ptr(w), eps, _ptr(out), out.stride(0), _stream())
+    return out
+
+
+def prefill_qk_rope(qkv, batch: int, S: int, nq: int, nkv: int, q_norm, k_norm, eps: float, cos, sin, q_out,
+                    k_cache, v_cache):
+    """q/k RMSNorm + RoPE of the prompt positions 0..S-1, K/V into the caches (qd_prefill_qk_rope).
+    qkv [batch * S, (nq + 2 nkv) * 128]; q_out [batch * S, nq * 128]; caches [batch, nkv, cap, 128]."""
+    _check_bf16(qkv, q_norm, k_norm, cos, sin, q_out, k_cache, v_cache)
+    assert k_cache.stride() == v_cache.stride() and qkv.stride(1) == 1 and q_out.stride(1) == 1
+    L.call("qd_prefill_qk_rope", _ptr(qkv), qkv.stride(0), batch, S, nq, nkv, _ptr(q_norm), _ptr(k_norm), eps,
+           _ptr(cos), _ptr(sin), _ptr(q_out), q_out.stride(0), _ptr(k_cache), _ptr(v_cache), k_cache.shape[2],
+           k_cache.stride(0), k_cache.stride(1), _stream())
+    return q_out
+
+
 class DecodeAttention:
     """Split-K GQA flash-decode + LSE merge for a fixed (batch, capacity); see qd_attn_decode."""
 

@@ -19,10 +19,12 @@ its consumers wait on completion counters); ENGINE_STEP=kernels runs the same ar
                  down  x = bf16(x + bf16(act @ Wd^T))
   lm head        tok = argmax(bf16(RMSNorm(x) @ E^T)), pos += 1
 
-Weights are packed once at load into the kernels' blocked layout (decode_b200/ops.py). The prompt
-forward (prefill, engine/engine.py:550-592) still uses PyTorch (cuBLAS GEMMs + SDPA) on row-major
-copies of the weights and writes the same KV cache; it is captured in a CUDA graph too. The stream
-loop keeps the GPU one step ahead of the host like engine/engine.py:719-757.
+Weights are packed once at load into the kernels' blocked layout (decode_b200/ops.py), the only copy
+kept. The prompt forward (prefill, engine/engine.py:550-592) runs on the same packed weights through
+the library's tcgen05 GEMM (qd_tc_gemm, fused residual / SwiGLU epilogues), row RMSNorm and prompt
+q/k-norm + RoPE + KV-cache kernels; its causal attention is PyTorch's flash SDPA, as in the
+reference. It is captured in a CUDA graph too. The stream loop keeps the GPU one step ahead of the
+host like engine/engine.py:719-757.
 """
 
 from __future__ import annotations
@@ -187,89 +189,87 @@ class Engine:
         Lyr = self.n_layers
         nq_rows, nkv_rows = self.nq * D, self.nkv * D
         n_qkv = nq_rows + 2 * nkv_rows
-        # row-major copies for the PyTorch prefill; packed copies for the decode kernels
-        self.embed_rm = get("model.embed_tokens.weight")
-        self.lm_rm = get("lm_head.weight") if ("lm_head.weight" in state and not cfg.get("tie_word_embeddings", True)) \
-            else self.embed_rm
+        # one packed copy of every matrix serves prefill and decode; row-major checkpoint tensors are
+        # staged one at a time and dropped after packing
+        if "lm_head.weight" in state and not cfg.get("tie_word_embeddings", True):
+            raise NotImplementedError("untied LM head: the embedding gather reads the packed LM matrix")
         self.final_norm = get("model.norm.weight")
         self.ln1 = torch.empty((Lyr, H), dtype=BF16, device=dev)
         self.ln2 = torch.empty((Lyr, H), dtype=BF16, device=dev)
         self.qn = torch.empty((Lyr, D), dtype=BF16, device=dev)
         self.kn = torch.empty((Lyr, D), dtype=BF16, device=dev)
-        self.w_qkv_rm = torch.empty((Lyr, n_qkv, H), dtype=BF16, device=dev)
-        self.w_o_rm = torch.empty((Lyr, H, nq_rows), dtype=BF16, device=dev)
-        self.w_gu_rm = torch.empty((Lyr, 2 * I, H), dtype=BF16, device=dev)
-        self.w_down_rm = torch.empty((Lyr, H, I), dtype=BF16, device=dev)
         self.w_qkv = ops.new_packed(n_qkv, H, dev, Lyr)
         self.w_o = ops.new_packed(H, nq_rows, dev, Lyr)
         self.w_gu = ops.new_packed(2 * I, H, dev, Lyr)
         self.w_down = ops.new_packed(H, I, dev, Lyr)
         with torch.no_grad():
+            qkv_rm = torch.empty((n_qkv, H), dtype=BF16, device=dev)
             for i in range(Lyr):
                 p = f"model.layers.{i}."
                 self.ln1[i].copy_(state[p + "input_layernorm.weight"])
                 self.ln2[i].copy_(state[p + "post_attention_layernorm.weight"])
                 self.qn[i].copy_(state[p + "self_attn.q_norm.weight"])
                 self.kn[i].copy_(state[p + "self_attn.k_norm.weight"])
-                self.w_qkv_rm[i, :nq_rows].copy_(state[p + "self_attn.q_proj.weight"])
-                self.w_qkv_rm[i, nq_rows:nq_rows + nkv_rows].copy_(state[p + "self_attn.k_proj.weight"])
-                self.w_qkv_rm[i, nq_rows + nkv_rows:].copy_(state[p + "self_attn.v_proj.weight"])
-                self.w_o_rm[i].copy_(state[p + "self_attn.o_proj.weight"])
-                self.w_gu_rm[i, :I].copy_(state[p + "mlp.gate_proj.weight"])
-                self.w_gu_rm[i, I:].copy_(state[p + "mlp.up_proj.weight"])
-                self.w_down_rm[i].copy_(state[p + "mlp.down_proj.weight"])
-                ops.pack_rows(self.w_qkv_rm[i], self.w_qkv[i], n_qkv)
-                ops.pack_rows(self.w_o_rm[i], self.w_o[i], H)
-                ops.pack_gate_up(self.w_gu_rm[i, :I], self.w_gu_rm[i, I:], self.w_gu[i])
-                ops.pack_rows(self.w_down_rm[i], self.w_down[i], H)
-            self.e_packed = ops.pack_matrix(self.lm_rm)
-            if self.lm_rm is not self.embed_rm:
-                raise NotImplementedError("untied LM head: the embedding gather reads the packed LM matrix")
+                qkv_rm[:nq_rows].copy_(state[p + "self_attn.q_proj.weight"])
+                qkv_rm[nq_rows:nq_rows + nkv_rows].copy_(state[p + "self_attn.k_proj.weight"])
+                qkv_rm[nq_rows + nkv_rows:].copy_(state[p + "self_attn.v_proj.weight"])
+                ops.pack_rows(qkv_rm, self.w_qkv[i], n_qkv)
+                ops.pack_rows(get(p + "self_attn.o_proj.weight"), self.w_o[i], H)
+                ops.pack_gate_up(get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight"), self.w_gu[i])
+                ops.pack_rows(get(p + "mlp.down_proj.weight"), self.w_down[i], H)
+            self.e_packed = ops.pack_matrix(get("model.embed_tokens.weight"))
+            del qkv_rm
         torch.cuda.synchronize()
         self.state = None
         self.sm_count = ops.sm_count()
 
     # ------------------------------------------------------------------ model step
     def _prefill(self, st: _State) -> torch.Tensor:
-        """Prompt forward in row chunks (engine/engine.py:550-592): K/V [0, S) into the cache, first
-        token into st.tok; returns the last position's logits [B, V]."""
+        """Prompt forward in row chunks (engine/engine.py:550-592) on the library's prompt kernels
+        (qd_tc_gemm over the packed weights, qd_rmsnorm_rows, qd_prefill_qk_rope); causal attention is
+        PyTorch's flash SDPA with GQA, as in the reference (engine/engine.py:517-531). K/V [0, S) go
+        into the cache, the first token into st.tok; returns the last position's logits [B, V]."""
         B, S = st.B, st.S
-        H, D, nq, nkv = self.hidden, self.head_dim, self.nq, self.nkv
-        cos = st.cos[:S][None, None]
-        sin = st.sin[:S][None, None]
+        H, D, nq, nkv, I, eps = self.hidden, self.head_dim, self.nq, self.nkv, self.inter, self.eps
+        n_qkv = (nq + 2 * nkv) * D
+        vrows = ops.packed_rows(self.vocab)
+        dev, err = self.device, st.err
+        RES, SWIGLU = ops.Gemv.RES, ops.Gemv.SWIGLU
         last_layer = self.n_layers - 1
-        outs = []
+        logits = torch.empty((B, vrows), dtype=BF16, device=dev)
         for r0 in range(0, B, st.rows):
             r1 = min(B, r0 + st.rows)
             b, M = r1 - r0, (r1 - r0) * S
-            x = F.embedding(st.ids[r0:r1], self.embed_rm).view(M, H)
+            x = torch.empty((M, H), dtype=BF16, device=dev)
+            h = torch.empty((M, H), dtype=BF16, device=dev)
+            qkv = torch.empty((M, n_qkv), dtype=BF16, device=dev)
+            q = torch.empty((M, nq * D), dtype=BF16, device=dev)
+            act = torch.empty((M, I), dtype=BF16, device=dev)
+            ops.embed(st.ids[r0:r1].reshape(M), self.e_packed, self.vocab, x, err, pdl=False)
+            xl, hl = x.view(b, S, H)[:, -1], h[:b]  # the last position of every sequence
             for i in range(self.n_layers):
                 kc, vc = st.k_all[i, r0:r1], st.v_all[i, r0:r1]
-                h = _rms(x, self.ln1[i], self.eps).view(M, H)
-                qkv = F.linear(h, self.w_qkv_rm[i])
-                q = _rms(qkv, self.qn[i], self.eps, nq).view(b, S, nq, D).transpose(1, 2)
-                k = _rms(qkv[:, nq * D:], self.kn[i], self.eps, nkv).view(b, S, nkv, D).transpose(1, 2)
-                v = qkv[:, (nq + nkv) * D:].view(b, S, nkv, D).transpose(1, 2)
-                q = (q * cos) + (_rotate_half(q) * sin)
-                k = (k * cos) + (_rotate_half(k) * sin)
-                kc[:, :, :S].copy_(k)
-                vc[:, :, :S].copy_(v)
-                if i == last_layer:
-                    a = F.scaled_dot_product_attention(q[:, :, -1:].contiguous(), kc[:, :, :S], vc[:, :, :S],
+                ops.rmsnorm_rows(x, self.ln1[i], eps, h)
+                ops.tc_gemm(h, self.w_qkv[i], n_qkv, qkv, err=err)
+                ops.prefill_qk_rope(qkv, b, S, nq, nkv, self.qn[i], self.kn[i], eps, st.cos, st.sin, q, kc, vc)
+                q4 = q.view(b, S, nq, D).transpose(1, 2)
+                if i == last_layer:  # only the last position continues (engine/engine.py:577-583)
+                    a = F.scaled_dot_product_attention(q4[:, :, -1:].contiguous(), kc[:, :, :S], vc[:, :, :S],
                                                        scale=D ** -0.5, enable_gqa=True)
-                    x = x.view(b, S, H)[:, -1] + F.linear(a.reshape(b, nq * D), self.w_o_rm[i])
-                    h = _rms(x, self.ln2[i], self.eps).view(b, H)
-                    gu = F.linear(h, self.w_gu_rm[i])
-                    x = x + F.linear(F.silu(gu[:, :self.inter]) * gu[:, self.inter:], self.w_down_rm[i])
+                    ops.tc_gemm(a.reshape(b, nq * D), self.w_o[i], H, xl, res=xl, epilogue=RES, err=err)
+                    ops.rmsnorm_rows(xl, self.ln2[i], eps, hl)
+                    ops.tc_gemm(hl, self.w_gu[i], 2 * I, act[:b], epilogue=SWIGLU, err=err)
+                    ops.tc_gemm(act[:b], self.w_down[i], H, xl, res=xl, epilogue=RES, err=err)
                     break
-                a = F.scaled_dot_product_attention(q.contiguous(), kc[:, :, :S], vc[:, :, :S], is_causal=True,
+                a = F.scaled_dot_product_attention(q4, kc[:, :, :S], vc[:, :, :S], is_causal=True,
                                                    scale=D ** -0.5, enable_gqa=True)
-                x = x + F.linear(a.transpose(1, 2).reshape(M, nq * D), self.w_o_rm[i])
-                h = _rms(x, self.ln2[i], self.eps).view(M, H)
-                gu = F.linear(h, self.w_gu_rm[i])
-                x = x + F.linear(F.silu(gu[:, :self.inter]) * gu[:, self.inter:], self.w_down_rm[i])
-            outs.append(F.linear(_rms(x, self.final_norm, self.eps).view(b, H), self.lm_rm))
-        logits = outs[0] if len(outs) == 1 else torch.cat(outs, 0)
+                ops.tc_gemm(a.transpose(1, 2).reshape(M, nq * D), self.w_o[i], H, x, res=x, epilogue=RES, err=err)
+                ops.rmsnorm_rows(x, self.ln2[i], eps, h)
+                ops.tc_gemm(h, self.w_gu[i], 2 * I, act, epilogue=SWIGLU, err=err)
+                ops.tc_gemm(act, self.w_down[i], H, x, res=x, epilogue=RES, err=err)
+            ops.rmsnorm_rows(xl, self.final_norm, eps, hl)
+            ops.tc_gemm(hl, self.e_packed, vrows, logits[r0:r1], err=err)
+        logits = logits[:, :self.vocab]
         st.tok.copy_(torch.argmax(logits, dim=-1))
         return logits
 

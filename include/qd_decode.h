@@ -265,6 +265,36 @@ int qd_tc_decode_step_plan(const qd_step_desc* desc, int64_t* scratch_bytes, int
 int qd_tc_decode_step(const qd_step_desc* desc, void* xh, void* xa, void* xi, void* scratch, int64_t scratch_bytes,
                       cudaStream_t stream);
 
+/* ---------------------------------------------------------------- prompt (prefill) path
+ * The prefill forward (engine/engine.py:550-592) on the same packed weights as decode.
+ *
+ * qd_tc_gemm replaces its F.linear calls (engine/engine.py:564, :580-589) and the fused epilogues that
+ * follow them: out[t, :] = epilogue(x[t, :] . W^T) for t < m, on the tcgen05 tensor cores (tiles of
+ * 128 tokens x 128 or 256 weight rows, fp32 accumulation in tensor memory). x [m, k] BF16 row-major
+ * (row stride ldx, 16-byte aligned, ldx % 8 == 0), W packed [n, k] (n % 128 == 0, k % 64 == 0).
+ * Epilogues as qd_gemv: QD_EPI_STORE out = bf16(y); QD_EPI_RES out = bf16(res + bf16(y)) (out may
+ * alias res); QD_EPI_SWIGLU (W = the interleaved gate/up matrix) out [m, n / 2] =
+ * bf16(bf16(silu(bf16 g)) * bf16 u). No scratch; one launch. qd_tc_gemm_plan reports the grid and tile
+ * width it will use. */
+int qd_tc_gemm_plan(int64_t m, int64_t n, int64_t k, int* grid, int* bn);
+int qd_tc_gemm(const void* x, int64_t ldx, int64_t m, const void* w_packed, int64_t n, int64_t k, void* out,
+               int64_t ldo, const void* res, int64_t ldr, int epilogue, int* err, cudaStream_t stream);
+
+/* Row RMSNorm, out[i] = bf16(w * bf16(x[i] * rsqrt(mean(x[i]^2) + eps))): replaces the torch / Triton
+ * norm of the prefill (engine/engine.py:505-509, engine/kernels/rmsnorm.py:14-32). k % 8 == 0,
+ * 16-byte aligned rows. */
+int qd_rmsnorm_rows(const void* x, int64_t ldx, int64_t m, int64_t k, const void* norm_w, float eps, void* out,
+                    int64_t ldo, cudaStream_t stream);
+
+/* Prompt q/k RMSNorm + RoPE + KV-cache write: replaces qk_norm_rope_cache with pos_mode 0
+ * (engine/kernels/fused.py:23-98, called from engine/engine.py:566-572). qkv [batch * S, (nq + 2 nkv) * 128]
+ * (token i * S + s at position s); q_out [batch * S, nq * 128] receives rope(rmsnorm(q)); k_cache /
+ * v_cache [batch, nkv, cap, 128] (strides cs_b, cs_h) receive positions 0..S-1. */
+int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int64_t S, int nq_heads, int nkv_heads,
+                       const void* q_norm, const void* k_norm, float eps, const void* cos, const void* sin, void* q_out,
+                       int64_t ldq, void* k_cache, void* v_cache, int64_t cap, int64_t cs_b, int64_t cs_h,
+                       cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

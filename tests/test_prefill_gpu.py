@@ -1,0 +1,191 @@
+"""Prompt (prefill) kernels on the GPU, through the C ABI, against CPU / fp64 references.
+
+qd_tc_gemm (tcgen05, tiles of 128 tokens x 128 or 256 weight rows) is checked against an fp64 product
+of the same BF16 operands with the same BF16 rounding points, for both tile widths, ragged token
+counts (rows past m must stay untouched), an odd number of 128-row weight groups, strided rows, the
+residual epilogue in place and the SwiGLU epilogue on the interleaved gate/up matrix. The tensor
+cores accumulate in fp32 in their own order, so an output may sit one BF16 ulp away at a rounding
+tie. qd_rmsnorm_rows and qd_prefill_qk_rope are checked against the oracle's op restatements
+(oracle/qwen3_cpu.py, engine/engine.py:505-509 and :550-592).
+"""
+
+import pytest
+import torch
+
+from oracle import qwen3_cpu as Q
+
+pytestmark = pytest.mark.gpu
+BF16 = torch.bfloat16
+DEV = "cuda:0"
+RTOL = 2.0 ** -7
+
+
+def _ops():
+    from decode_b200 import ops
+
+    return ops
+
+
+def _rand(shape, std, gen):
+    return (torch.randn(shape, generator=gen) * std).to(BF16)
+
+
+def _ref(x, w):
+    """fp64 product of the BF16 operands, on the GPU (exact enough to be the rounding reference)."""
+    return x.to(DEV).double() @ w.to(DEV).double().T
+
+
+def _assert_close(ours, ref, extra=None, rtol=RTOL):
+    ours, ref = ours.float(), ref.float().to(ours.device)
+    tol = rtol * (ref.abs() + (extra.abs().to(ours.device) if extra is not None else 0)) + 1e-3
+    bad = (ours - ref).abs() > tol
+    assert not bad.any(), f"{int(bad.sum())} mismatches, max diff {float((ours - ref).abs().max()):.4g}"
+
+
+# (m, n, k): ragged token tiles, an odd group count (n = 384), the model's projection shapes
+SHAPES = [(1, 256, 128), (7, 384, 640), (128, 2560, 2560), (129, 6144, 2560), (300, 2560, 4096),
+          (2048, 2560, 640), (517, 2560, 9728)]
+
+
+@pytest.mark.parametrize("bn", ["128", "256"])
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_tc_gemm_store(m, n, k, bn, monkeypatch):
+    monkeypatch.setenv("QD_GEMM_BN", bn)
+    ops = _ops()
+    g = torch.Generator().manual_seed(m * 7 + n + k)
+    x, w = _rand((m, k), 1.0, g), _rand((n, k), 0.02, g)
+    out = torch.full((m + 5, n), float("nan"), dtype=BF16, device=DEV)  # rows m.. must stay untouched
+    ops.tc_gemm(x.to(DEV), ops.pack_matrix(w.to(DEV)), n, out[:m])
+    _assert_close(out[:m], _ref(x, w).to(BF16))
+    assert torch.isnan(out[m:].float()).all()
+
+
+def test_tc_gemm_plan_picks_wide_tiles_for_large_prompts():
+    ops = _ops()
+    sms = ops.sm_count()
+    grid, bn = ops.tc_gemm_plan(16384, 19456, 2560)
+    assert bn == 256 and grid == sms
+    grid, bn = ops.tc_gemm_plan(128, 2560, 4096)
+    assert bn == 128 and grid == 20
+
+
+@pytest.mark.parametrize("bn", ["128", "256"])
+@pytest.mark.parametrize("m,n,k", [(300, 2560, 4096), (1100, 2560, 9728), (5, 2560, 4096)])
+def test_tc_gemm_residual_in_place_strided(m, n, k, bn, monkeypatch):
+    """out = bf16(res + bf16(x W^T)) written over res, with x and res rows strided (every third row of
+    a larger buffer, as the last-position rows of a prompt are)."""
+    monkeypatch.setenv("QD_GEMM_BN", bn)
+    ops = _ops()
+    g = torch.Generator().manual_seed(m + 3 * n + k)
+    x, w, res = _rand((m, k), 1.0, g), _rand((n, k), 0.02, g), _rand((m, n), 1.0, g)
+    xb = torch.zeros((3 * m, k), dtype=BF16, device=DEV)
+    xb[::3] = x.to(DEV)
+    rb = torch.full((3 * m, n), float("nan"), dtype=BF16, device=DEV)
+    rb[::3] = res.to(DEV)
+    xr = rb[::3]
+    ops.tc_gemm(xb[::3], ops.pack_matrix(w.to(DEV)), n, xr, res=xr, epilogue=ops.Gemv.RES)
+    y = _ref(x, w).to(BF16).float()
+    ref = (res.to(DEV).float() + y).to(BF16)
+    # bf16(y) may round one ulp apart at a tie, and that ulp can carry into the rounded sum
+    _assert_close(xr, ref, extra=y)
+    assert torch.isnan(rb[1::3].float()).all() and torch.isnan(rb[2::3].float()).all()
+
+
+@pytest.mark.parametrize("bn", ["128", "256"])
+@pytest.mark.parametrize("m", [3, 300, 1500])
+def test_tc_gemm_swiglu_gate_up(m, bn, monkeypatch):
+    monkeypatch.setenv("QD_GEMM_BN", bn)
+    ops = _ops()
+    inter, k = 9728, 2560
+    g = torch.Generator().manual_seed(inter + m)
+    x, gate, up = _rand((m, k), 1.0, g), _rand((inter, k), 0.02, g), _rand((inter, k), 0.02, g)
+    out = torch.empty((m, inter), dtype=BF16, device=DEV)
+    ops.tc_gemm(x.to(DEV), ops.pack_gate_up(gate.to(DEV), up.to(DEV)), 2 * inter, out, epilogue=ops.Gemv.SWIGLU)
+    gu = _ref(x, torch.cat([gate, up])).to(BF16)
+    ref = Q.swiglu(gu.cpu(), inter)
+    # a one-ulp difference in bf16(g) or bf16(u) at a rounding tie moves the output by up to
+    # |u| |silu'(g)| ulp(g) + |silu(g)| ulp(u), with |silu'| < 1.1
+    gv, uv = gu[:, :inter].float().cpu(), gu[:, inter:].float().cpu()
+    sv = torch.nn.functional.silu(gv)
+    _assert_close(out, ref, extra=(1.1 * gv.abs() * uv.abs() + sv.abs() * uv.abs()).to(DEV), rtol=2.0 ** -6)
+
+
+def test_tc_gemm_deterministic_and_tile_width_independent(monkeypatch):
+    """Each output is one tile's fp32 accumulation in K order: the same bits for either tile width and
+    on every run."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(5)
+    m, n, k = 2000, 6144, 2560
+    x, w = _rand((m, k), 1.0, g).to(DEV), ops.pack_matrix(_rand((n, k), 0.02, g).to(DEV))
+    outs = []
+    for bn in ("256", "128", "256"):
+        monkeypatch.setenv("QD_GEMM_BN", bn)
+        o = torch.empty((m, n), dtype=BF16, device=DEV)
+        ops.tc_gemm(x, w, n, o)
+        outs.append(o)
+    assert torch.equal(outs[0], outs[2]) and torch.equal(outs[0], outs[1])
+
+
+def test_tc_gemm_lm_head_shape():
+    """The prompt's LM head: 151936 vocabulary rows (1187 groups, odd) for a few last positions."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(11)
+    m, n, k = 4, 151936, 2560
+    x, e = _rand((m, k), 1.0, g), _rand((n, k), 0.02, g)
+    out = torch.empty((m, n), dtype=BF16, device=DEV)
+    ops.tc_gemm(x.to(DEV), ops.pack_matrix(e.to(DEV)), n, out)
+    ref = _ref(x, e).to(BF16).float()
+    _assert_close(out, ref)
+    # our argmax is the reference's, or a reference near-tie within one BF16 ulp of the best
+    idx = out.float().argmax(-1)
+    best = ref.max(-1).values
+    at = ref.gather(1, idx[:, None])[:, 0]
+    assert ((best - at) <= RTOL * best.abs() + 1e-3).all()
+
+
+@pytest.mark.parametrize("m,k", [(1, 2560), (77, 2560), (3000, 2560), (5, 4096)])
+def test_rmsnorm_rows(m, k):
+    ops = _ops()
+    g = torch.Generator().manual_seed(m + k)
+    x = _rand((m, k), 1.0, g)
+    w = (1.0 + 0.1 * torch.randn(k, generator=g)).to(BF16)
+    out = torch.empty((m, k), dtype=BF16, device=DEV)
+    ops.rmsnorm_rows(x.to(DEV), w.to(DEV), 1e-6, out)
+    # two roundings (bf16(x * rstd), then bf16(w * that)): an fp32-level difference in rstd (sum order,
+    # rsqrt vs 1/sqrt) that flips the inner rounding can leave the output two ulps apart
+    _assert_close(out, Q.rms_norm(x, w, 1e-6).view(m, k), rtol=2.0 ** -6)
+
+
+@pytest.mark.parametrize("b,S", [(1, 1), (1, 128), (3, 17), (2, 1024)])
+def test_prefill_qk_rope_and_cache(b, S):
+    ops = _ops()
+    nq, nkv, D, eps = 32, 8, 128, 1e-6
+    cap = S + 9
+    g = torch.Generator().manual_seed(b * 100 + S)
+    qkv = _rand((b * S, (nq + 2 * nkv) * D), 1.0, g)
+    qn = (1.0 + 0.1 * torch.randn(D, generator=g)).to(BF16)
+    kn = (1.0 + 0.1 * torch.randn(D, generator=g)).to(BF16)
+    cos, sin = Q.rope_tables(cap, D, 5e6)
+    q = torch.empty((b * S, nq * D), dtype=BF16, device=DEV)
+    kc = torch.full((b, nkv, cap, D), float("nan"), dtype=BF16, device=DEV)
+    vc = torch.full((b, nkv, cap, D), float("nan"), dtype=BF16, device=DEV)
+    ops.prefill_qk_rope(qkv.to(DEV), b, S, nq, nkv, qn.to(DEV), kn.to(DEV), eps, cos.to(DEV), sin.to(DEV), q, kc, vc)
+    # oracle: per-head norm, then RoPE at each token's own position s (engine/engine.py:566-572)
+    c = cos[:S].repeat(b, 1)[:, None]
+    s = sin[:S].repeat(b, 1)[:, None]
+    qh = Q.rms_norm(qkv, qn, eps, nq)
+    kh = Q.rms_norm(qkv[:, nq * D:], kn, eps, nkv)
+    qr = (qh * c) + (Q.rotate_half(qh) * s)
+    kr = (kh * c) + (Q.rotate_half(kh) * s)
+    vr = qkv[:, (nq + nkv) * D:].view(b * S, nkv, D)
+
+    def rope_tol(y):
+        y = y.float()
+        return (y * c.float()).abs() + (Q.rotate_half(y) * s.float()).abs()
+
+    _assert_close(q.view(b * S, nq, D), qr, extra=rope_tol(qh))
+    kcs = kc[:, :, :S].permute(0, 2, 1, 3).reshape(b * S, nkv, D)
+    vcs = vc[:, :, :S].permute(0, 2, 1, 3).reshape(b * S, nkv, D)
+    _assert_close(kcs, kr, extra=rope_tol(kh))
+    assert torch.equal(vcs.cpu(), vr)
+    assert torch.isnan(kc[:, :, S:].float()).all() and torch.isnan(vc[:, :, S:].float()).all()
