@@ -719,6 +719,24 @@ def run_sweep_prefill(a):
             del x, out
         del w, wp
         torch.cuda.empty_cache()
+    # causal prompt attention: qd_prefill_attn against PyTorch's flash SDPA (the reference's call)
+    nq, nkv, D = 32, 8, 128
+    for b, S in ((1, 128), (8, 1024), (16, 1024), (1, 8192)):
+        q = torch.randn((b * S, nq * D), generator=g, device=dev).to(torch.bfloat16)
+        kc = torch.randn((b, nkv, S, D), generator=g, device=dev).to(torch.bfloat16)
+        vc = torch.randn((b, nkv, S, D), generator=g, device=dev).to(torch.bfloat16)
+        out = torch.empty((b * S, nq * D), dtype=torch.bfloat16, device=dev)
+        q4 = q.view(b, S, nq, D).transpose(1, 2)
+        flops = 4 * b * nq * (S * (S + 1) // 2) * D
+        for path, fn in (("qd_prefill_attn", lambda i: ops.prefill_attn(q, b, S, nq, nkv, kc, vc, out, err=err)),
+                         ("torch_flash_sdpa", lambda i: torch.nn.functional.scaled_dot_product_attention(
+                             q4, kc, vc, is_causal=True, scale=D ** -0.5, enable_gqa=True))):
+            ms = _time_cycle(fn, 1, launches)
+            tf = flops / (ms / 1e3) / 1e12
+            print(json.dumps({"sweep": "prefill_attn", "batch": b, "prompt": S, "path": path, "us": round(ms * 1e3, 2),
+                              "TFLOPs": round(tf, 1), "frac_tensor": round(tf / tpeak, 4)}), flush=True)
+        assert int(err.item()) == 0
+        del q, kc, vc, out
     # whole prompt forward through the engine (random-init weights)
     import engine as E
 

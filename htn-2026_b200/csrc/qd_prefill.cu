@@ -383,6 +383,302 @@ __global__ void __launch_bounds__(256) prefill_qk_rope_kernel(const __grid_const
     *reinterpret_cast<uint2*>(a.k_cache + i * a.cs_b + (h - a.nq) * a.cs_h + s * 128 + 4 * lane) = ov;
 }
 
+// ------------------------------------------------------------------ prompt causal attention
+// Flash attention over the prompt (engine/engine.py:579, F.scaled_dot_product_attention with
+// is_causal and enable_gqa) on the tensor cores, for the query positions q0..S-1 of every sequence
+// (q0 = 0: the whole prompt; q0 = S - 1: the last layer, where only the last position continues,
+// engine/engine.py:577-583). Work unit = (sequence, query head, tile of 128 queries); the units of the
+// most key tiles go first. Per key tile of 128 keys:
+//   S = Q K^T      tcgen05.mma M = 128 queries, N = 128 keys, K = 128 dims (8 MMAs), fp32 in TMEM,
+//                  two S buffers so the next tile's S overlaps this tile's softmax
+//   softmax        warps 0-3, thread = query row: row max over the tile (causal mask on the diagonal
+//                  tile), P = exp2((s - m) * scale * log2 e) rounded to BF16 into a 128-byte-swizzled
+//                  K-major operand tile, row sums in fp32
+//   O += P V       M = 128 queries, N = 128 dims (V read as an MN-major operand), K = 128 keys
+// The running max only moves when it grows by more than 2^8 in the exp2 domain; then the thread's O
+// row is rescaled in TMEM (tcgen05.ld / st) and its sum with it - the quotient O / l is unchanged by
+// which max is used. Q, K and V arrive by TMA from tensor maps whose key (query) extent is the prompt
+// length, so rows past it read as zero. Warp 4 loads, warp 5 issues the MMAs.
+constexpr int kPaThreads = 192;
+constexpr int kPaTile = 128;
+constexpr int kPaBox = kPaTile * 128;  // [128 rows][64 dims] BF16: 16 KiB
+
+struct alignas(64) PrefillAttnArgs {
+  CUtensorMap tq, tk, tv;
+  __nv_bfloat16* out;  // [b * (S - q0), nq * 128]: row i * (S - q0) + s - q0
+  int64_t ldo, S, q0;
+  int batch, nq, nkv, n_qt, qt0, units;
+  float scale_log2;
+  int* err;
+};
+
+struct PaLayout {
+  static constexpr int q = 0;                      // Q: 2 dim halves
+  static constexpr int kv = q + 2 * kPaBox;        // 2 stages x (K half 0, K half 1, V half 0, V half 1)
+  static constexpr int p = kv + 2 * 4 * kPaBox;    // P: 2 key halves
+  static constexpr int bars = p + 2 * kPaBox;      // 13 barriers
+  static constexpr int misc = bars + 13 * 8;       // tmem slot, abort, K/V tiles issued, Q tiles issued
+  static constexpr int total = misc + 16;
+};
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d_pf(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                               uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void pa_unit(const PrefillAttnArgs& a, int u, int* i, int* h, int* qt) {
+  const int per = a.batch * a.nq;
+  *qt = a.n_qt - 1 - u / per;  // >= qt0
+  const int rem = u % per;
+  *i = rem / a.nq;
+  *h = rem - *i * a.nq;
+}
+
+__global__ void __launch_bounds__(kPaThreads, 1) prefill_attn_kernel(const __grid_constant__ PrefillAttnArgs a) {
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const uint32_t sb = smem_u32(smem);
+  const uint32_t bars = sb + PaLayout::bars;
+  const uint32_t qfull = bars, qempty = bars + 8, pfull = bars + 48, odone = bars + 56, ofree = bars + 64;
+  auto kvfull = [&](int s) { return bars + 16 + 8u * s; };
+  auto kvempty = [&](int s) { return bars + 32 + 8u * s; };
+  auto sfull = [&](int s) { return bars + 72 + 8u * s; };
+  auto sfree = [&](int s) { return bars + 88 + 8u * s; };
+  int* misc = reinterpret_cast<int*>(smem + PaLayout::misc);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = gridDim.x;
+  if (tid == 0) {
+    mbar_init(qfull, 1);
+    mbar_init(qempty, 1);
+    mbar_init(pfull, 4);
+    mbar_init(odone, 1);
+    mbar_init(ofree, 4);
+    for (int s2 = 0; s2 < 2; ++s2) {
+      mbar_init(kvfull(s2), 1);
+      mbar_init(kvempty(s2), 1);
+      mbar_init(sfull(s2), 1);
+      mbar_init(sfree(s2), 4);
+    }
+    fence_mbar_init();
+    misc[1] = 0;
+    misc[2] = 0;
+    misc[3] = 0;
+  }
+  if (warp == 5) tmem_alloc(smem_u32(misc), 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = (uint32_t)misc[0];
+  const uint32_t tS = tmem, tO = tmem + 256;  // S[2] in columns 0-255, O in 256-383
+  int* abort = misc + 1;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_normal();
+      int t = 0, k = 0, kv_issued = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < a.units && ok; u += G, ++k) {
+        int i, h, qt;
+        pa_unit(a, u, &i, &h, &qt);
+        if (k >= 1 && !mbar_wait_abort(qempty, (k - 1) & 1, a.err, kErrWaitEmpty, abort)) break;
+        misc[3] = k + 1;
+        mbar_arrive_expect_tx(qfull, 2 * kPaBox);
+        tma_load_3d(sb + PaLayout::q, &a.tq, h * 128, qt * kPaTile, i, qfull, pol);
+        tma_load_3d(sb + PaLayout::q + kPaBox, &a.tq, h * 128 + 64, qt * kPaTile, i, qfull, pol);
+        const int kvh = h / (a.nq / a.nkv);
+        for (int j = 0; j <= qt; ++j, ++t) {
+          const int st = t & 1;
+          if (t >= 2 && !mbar_wait_abort(kvempty(st), ((t >> 1) - 1) & 1, a.err, kErrWaitEmpty, abort)) {
+            ok = false;
+            break;
+          }
+          const uint32_t d = sb + PaLayout::kv + st * 4 * kPaBox;
+          mbar_arrive_expect_tx(kvfull(st), 4 * kPaBox);
+          tma_load_4d_pf(d, &a.tk, 0, j * kPaTile, kvh, i, kvfull(st), pol);
+          tma_load_4d_pf(d + kPaBox, &a.tk, 64, j * kPaTile, kvh, i, kvfull(st), pol);
+          tma_load_4d_pf(d + 2 * kPaBox, &a.tv, 0, j * kPaTile, kvh, i, kvfull(st), pol);
+          tma_load_4d_pf(d + 3 * kPaBox, &a.tv, 64, j * kPaTile, kvh, i, kvfull(st), pol);
+          ++kv_issued;
+        }
+      }
+      misc[2] = kv_issued;
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_s = umma_idesc_bf16(128), id_o = umma_idesc_bf16(128, false, true);
+      int t = 0, k = 0;
+      bool ok = true;
+      auto issue_pv = [&](int tt, bool first) {
+        if (ok && first && k >= 1) ok = mbar_wait_abort(ofree, (k - 1) & 1, a.err, kErrWaitFull, abort);
+        if (ok) ok = mbar_wait_abort(pfull, tt & 1, a.err, kErrWaitFull, abort);
+        tc_fence_after();
+        if (ok) {
+          const uint32_t v = sb + PaLayout::kv + (tt & 1) * 4 * kPaBox + 2 * kPaBox;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)  // 16 keys per MMA: P +32 B inside a 64-key half; V two 8-key atoms
+            umma_bf16(tO, umma_desc_sw128(sb + PaLayout::p + (j >> 2) * kPaBox + (j & 3) * 32),
+                      umma_desc_sw128(v + j * 2048, kPaBox, 1024), id_o, (first && j == 0) ? 0u : 1u);
+        }
+        umma_commit(odone);
+        umma_commit(kvempty(tt & 1));
+      };
+      for (int u = blockIdx.x; u < a.units && ok; u += G, ++k) {
+        int i, h, qt;
+        pa_unit(a, u, &i, &h, &qt);
+        if (!mbar_wait_abort(qfull, k & 1, a.err, kErrWaitFull, abort)) break;
+        for (int j = 0; j <= qt; ++j) {
+          const int tt = t + j;
+          if (ok) ok = mbar_wait_abort(kvfull(tt & 1), (tt >> 1) & 1, a.err, kErrWaitFull, abort);
+          if (ok && tt >= 2) ok = mbar_wait_abort(sfree(tt & 1), ((tt >> 1) - 1) & 1, a.err, kErrWaitFull, abort);
+          tc_fence_after();
+          if (ok) {
+            const uint32_t kt = sb + PaLayout::kv + (tt & 1) * 4 * kPaBox;
+#pragma unroll
+            for (int d = 0; d < 8; ++d)  // 16 dims per MMA: +32 B inside a 64-dim half, the next half after 4
+              umma_bf16(tS + (tt & 1) * 128, umma_desc_sw128(sb + PaLayout::q + (d >> 2) * kPaBox + (d & 3) * 32),
+                        umma_desc_sw128(kt + (d >> 2) * kPaBox + (d & 3) * 32), id_s, d > 0 ? 1u : 0u);
+          }
+          umma_commit(sfull(tt & 1));
+          if (j == qt) umma_commit(qempty);
+          if (j >= 1) issue_pv(tt - 1, j == 1);
+        }
+        issue_pv(t + qt, qt == 0);
+        t += qt + 1;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue (thread = query row)
+    const int r = 32 * warp + lane;
+    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+    char* pt = smem + PaLayout::p;
+    int t = 0, k = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < a.units && ok; u += G, ++k) {
+      int i, h, qt;
+      pa_unit(a, u, &i, &h, &qt);
+      const int q = qt * kPaTile + r;  // query position within the sequence
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j <= qt; ++j) {
+        const int tt = t + j;
+        const uint32_t ts = tS + (tt & 1) * 128 + lane_off;
+        if (ok) ok = mbar_wait_abort(sfull(tt & 1), (tt >> 1) & 1, a.err, kErrWaitFull, abort);
+        tc_fence_after();
+        const bool diag = (j == qt);
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t v[32];
+          tmem_ld32(ts + 32 * c4, v);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const bool masked = diag && (32 * c4 + e > r);  // key j*128 + c > query qt*128 + r
+            if (!masked) mx = fmaxf(mx, __uint_as_float(v[e]));
+          }
+        }
+        const float m_new = mx * a.scale_log2;
+        // the P buffer and O are free once the previous tile's P.V is done
+        if (ok && tt >= 1) ok = mbar_wait_abort(odone, (tt - 1) & 1, a.err, kErrWaitFull, abort);
+        tc_fence_after();
+        if (m_new > m_used + 8.f) {
+          const float alpha = exp2f(m_used - m_new);  // 0 on the first tile
+          if (j > 0) {
+#pragma unroll 1
+            for (int c4 = 0; c4 < 4; ++c4) {
+              uint32_t o[32];
+              tmem_ld32(tO + lane_off + 32 * c4, o);
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+              tmem_st32(tO + lane_off + 32 * c4, o);
+            }
+          }
+          l *= alpha;
+          m_used = m_new;
+        }
+#pragma unroll 1
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t v[32];
+          tmem_ld32(ts + 32 * c4, v);
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float p2[2];
+#pragma unroll
+            for (int d = 0; d < 2; ++d) {
+              const bool masked = diag && (32 * c4 + e + d > r);
+              p2[d] = masked ? 0.f : exp2f(fmaf(__uint_as_float(v[e + d]), a.scale_log2, -m_used));
+              l += p2[d];
+            }
+            pk[e >> 1] = pack_bf2(p2[0], p2[1]);
+          }
+          // keys 32 c4 .. +31: half c4 / 2, 16-byte chunks 4 (c4 & 1) .. +3 of row r, swizzled
+          char* row = pt + (c4 >> 1) * kPaBox + r * 128;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int chunk = 4 * (c4 & 1) + c;
+            *reinterpret_cast<uint4*>(row + ((chunk ^ (r & 7)) << 4)) =
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          }
+        }
+        tc_fence_before();
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(sfree(tt & 1));
+          mbar_arrive(pfull);
+        }
+      }
+      // ---- unit end: O / l for this row
+      const int tl = t + qt;
+      if (ok) ok = mbar_wait_abort(odone, tl & 1, a.err, kErrWaitFull, abort);
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      __nv_bfloat16* dst = a.out + ((int64_t)i * (a.S - a.q0) + (q - a.q0)) * a.ldo + (int64_t)h * 128;
+#pragma unroll 1
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t o[32];
+        tmem_ld32(tO + lane_off + 32 * c4, o);
+        if (q < a.S && q >= a.q0) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c4);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            d4[c] = make_uint4(pack_bf2(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
+                               pack_bf2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv),
+                               pack_bf2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv),
+                               pack_bf2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ofree);
+      t += qt + 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 5) tmem_dealloc(tmem, 512);
+  if (tid == 0) {  // no bulk copy may still be writing shared memory when the CTA exits
+    const int issued = misc[2], q_issued = misc[3];
+    for (int it = issued > 2 ? issued - 2 : 0; it < issued; ++it)
+      if (!mbar_wait(kvfull(it & 1), (it >> 1) & 1, a.err, kErrDrain)) break;
+    if (q_issued > 0) mbar_wait(qfull, (q_issued - 1) & 1, a.err, kErrDrain);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 static PFN_cuTensorMapEncodeTiled_v12000 gemm_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -544,4 +840,66 @@ extern "C" int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int
   const int64_t blocks = (warps + 7) / 8;
   if (blocks > INT32_MAX) return set_error(QD_ERR_UNSUPPORTED, "prefill q/k rope: too many tokens");
   return launch_kernel((const void*)prefill_qk_rope_kernel, dim3((unsigned)blocks), dim3(256), 0, 0, stream, &a);
+}
+
+extern "C" int qd_prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, int nq_heads,
+                               int nkv_heads, const void* k_cache, const void* v_cache, int64_t cap, int64_t cs_b,
+                               int64_t cs_h, float scale, void* out, int64_t ldo, int* err, cudaStream_t stream) {
+  if (!q || !k_cache || !v_cache || !out) return set_error(QD_ERR_ARG, "null pointer");
+  if (batch < 1 || S < 1 || S > cap || q_begin < 0 || q_begin >= S || nq_heads < 1 || nkv_heads < 1 ||
+      nq_heads % nkv_heads || ldq < (int64_t)nq_heads * 128 || ldo < (int64_t)nq_heads * 128 || ldq % 8 ||
+      ldo % 8 || cs_h < cap * 128 || cs_b < (int64_t)nkv_heads * cs_h || cs_h % 8 || cs_b % 8)
+    return set_error(QD_ERR_ARG, "prefill attention: bad sizes or strides");
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out))
+    return set_error(QD_ERR_ARG, "prefill attention: alignment");
+  const int64_t n_qt = (S + kPaTile - 1) / kPaTile, qt0 = q_begin / kPaTile;
+  const int64_t units = (int64_t)batch * nq_heads * (n_qt - qt0);
+  if (units > INT32_MAX || S > INT32_MAX - kPaTile) return set_error(QD_ERR_UNSUPPORTED, "prefill attention: too large");
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = gemm_encode_fn();
+  if (!encode) return set_error(QD_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  PrefillAttnArgs a = {};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  {
+    const cuuint64_t dims[3] = {(cuuint64_t)nq_heads * 128, (cuuint64_t)S, (cuuint64_t)batch};
+    const cuuint64_t strides[2] = {(cuuint64_t)ldq * 2, (cuuint64_t)(S * ldq * 2)};
+    const cuuint32_t box[3] = {64, (cuuint32_t)kPaTile, 1};
+    if (encode(&a.tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return set_error(QD_ERR_CUDA, "cuTensorMapEncodeTiled failed for q");
+  }
+  {
+    // key extent = the prompt length: keys past it read as zero
+    const cuuint64_t dims[4] = {128, (cuuint64_t)S, (cuuint64_t)nkv_heads, (cuuint64_t)batch};
+    const cuuint64_t strides[3] = {256, (cuuint64_t)cs_h * 2, (cuuint64_t)cs_b * 2};
+    const cuuint32_t box[4] = {64, (cuuint32_t)kPaTile, 1, 1};
+    if (encode(&a.tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(k_cache), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+        encode(&a.tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(v_cache), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return set_error(QD_ERR_CUDA, "cuTensorMapEncodeTiled failed for the KV cache");
+  }
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.ldo = ldo;
+  a.S = S;
+  a.q0 = q_begin;
+  a.qt0 = (int)qt0;
+  a.batch = batch;
+  a.nq = nq_heads;
+  a.nkv = nkv_heads;
+  a.n_qt = (int)n_qt;
+  a.units = (int)units;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.err = err;
+  const int smem = PaLayout::total + 1024;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured = true;
+  }
+  const int grid = units < host_sm_count() ? (int)units : host_sm_count();
+  return launch_kernel((const void*)prefill_attn_kernel, dim3(grid), dim3(kPaThreads), smem, 0, stream, &a);
 }

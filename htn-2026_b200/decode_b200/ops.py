@@ -309,6 +309,17 @@ def prefill_qk_rope(qkv, batch: int, S: int, nq: int, nkv: int, q_norm, k_norm, 
     return q_out
 
 
+def prefill_attn(q, batch: int, S: int, nq: int, nkv: int, k_cache, v_cache, out, q_begin: int = 0, err=None):
+    """Causal GQA attention of the prompt positions q_begin..S-1 over the cached keys 0..s
+    (qd_prefill_attn): q [batch * S, nq * 128] token-major; out [batch * (S - q_begin), nq * 128]."""
+    _check_bf16(q, k_cache, v_cache, out)
+    assert k_cache.stride() == v_cache.stride() and q.stride(1) == 1 and out.stride(1) == 1
+    L.call("qd_prefill_attn", _ptr(q), q.stride(0), batch, S, q_begin, nq, nkv, _ptr(k_cache), _ptr(v_cache),
+           k_cache.shape[2], k_cache.stride(0), k_cache.stride(1), 1.0 / math.sqrt(128), _ptr(out), out.stride(0),
+           _ptr(err), _stream())
+    return out
+
+
 class DecodeAttention:
     """Split-K GQA flash-decode + LSE merge for a fixed (batch, capacity); see qd_attn_decode."""
 

@@ -21,9 +21,9 @@ its consumers wait on completion counters); ENGINE_STEP=kernels runs the same ar
 
 Weights are packed once at load into the kernels' blocked layout (decode_b200/ops.py), the only copy
 kept. The prompt forward (prefill, engine/engine.py:550-592) runs on the same packed weights through
-the library's tcgen05 GEMM (qd_tc_gemm, fused residual / SwiGLU epilogues), row RMSNorm and prompt
-q/k-norm + RoPE + KV-cache kernels; its causal attention is PyTorch's flash SDPA, as in the
-reference. It is captured in a CUDA graph too. The stream loop keeps the GPU one step ahead of the
+the library's tcgen05 GEMM (qd_tc_gemm, fused residual / SwiGLU epilogues), row RMSNorm, prompt
+q/k-norm + RoPE + KV-cache kernel and tcgen05 causal flash attention (qd_prefill_attn). It is
+captured in a CUDA graph too. The stream loop keeps the GPU one step ahead of the
 host like engine/engine.py:719-757.
 """
 
@@ -35,7 +35,6 @@ import sys
 import time
 
 import torch
-import torch.nn.functional as F
 
 sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
@@ -76,19 +75,6 @@ def rope_tables(cap: int, head_dim: int, theta: float):
     freqs = (inv_freq[None, :, None].float() @ pos[:, None, :].float()).transpose(1, 2)
     emb = torch.cat((freqs, freqs), dim=-1)
     return emb.cos()[0].to(BF16).contiguous(), emb.sin()[0].to(BF16).contiguous()
-
-
-def _rms(x, w, eps, heads=1):
-    """Qwen3RMSNorm with the reference's cast placement (engine/engine.py:505-509)."""
-    n = w.numel()
-    xf = x[:, : heads * n].reshape(x.shape[0], heads, n).to(torch.float32)
-    xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
-    return w * xf.to(BF16)
-
-
-def _rotate_half(x):
-    half = x.shape[-1] // 2
-    return torch.cat((-x[..., half:], x[..., :half]), dim=-1)
 
 
 class _State:
@@ -225,10 +211,10 @@ class Engine:
 
     # ------------------------------------------------------------------ model step
     def _prefill(self, st: _State) -> torch.Tensor:
-        """Prompt forward in row chunks (engine/engine.py:550-592) on the library's prompt kernels
-        (qd_tc_gemm over the packed weights, qd_rmsnorm_rows, qd_prefill_qk_rope); causal attention is
-        PyTorch's flash SDPA with GQA, as in the reference (engine/engine.py:517-531). K/V [0, S) go
-        into the cache, the first token into st.tok; returns the last position's logits [B, V]."""
+        """Prompt forward in row chunks (engine/engine.py:550-592) on the library's prompt kernels:
+        qd_tc_gemm over the packed weights, qd_rmsnorm_rows, qd_prefill_qk_rope (K/V [0, S) into the
+        cache) and qd_prefill_attn (causal GQA flash attention on the tensor cores). The first token goes
+        into st.tok; returns the last position's logits [B, V]."""
         B, S = st.B, st.S
         H, D, nq, nkv, I, eps = self.hidden, self.head_dim, self.nq, self.nkv, self.inter, self.eps
         n_qkv = (nq + 2 * nkv) * D
@@ -244,6 +230,7 @@ class Engine:
             h = torch.empty((M, H), dtype=BF16, device=dev)
             qkv = torch.empty((M, n_qkv), dtype=BF16, device=dev)
             q = torch.empty((M, nq * D), dtype=BF16, device=dev)
+            att = torch.empty((M, nq * D), dtype=BF16, device=dev)
             act = torch.empty((M, I), dtype=BF16, device=dev)
             ops.embed(st.ids[r0:r1].reshape(M), self.e_packed, self.vocab, x, err, pdl=False)
             xl, hl = x.view(b, S, H)[:, -1], h[:b]  # the last position of every sequence
@@ -252,18 +239,15 @@ class Engine:
                 ops.rmsnorm_rows(x, self.ln1[i], eps, h)
                 ops.tc_gemm(h, self.w_qkv[i], n_qkv, qkv, err=err)
                 ops.prefill_qk_rope(qkv, b, S, nq, nkv, self.qn[i], self.kn[i], eps, st.cos, st.sin, q, kc, vc)
-                q4 = q.view(b, S, nq, D).transpose(1, 2)
                 if i == last_layer:  # only the last position continues (engine/engine.py:577-583)
-                    a = F.scaled_dot_product_attention(q4[:, :, -1:].contiguous(), kc[:, :, :S], vc[:, :, :S],
-                                                       scale=D ** -0.5, enable_gqa=True)
-                    ops.tc_gemm(a.reshape(b, nq * D), self.w_o[i], H, xl, res=xl, epilogue=RES, err=err)
+                    ops.prefill_attn(q, b, S, nq, nkv, kc, vc, att[:b], q_begin=S - 1, err=err)
+                    ops.tc_gemm(att[:b], self.w_o[i], H, xl, res=xl, epilogue=RES, err=err)
                     ops.rmsnorm_rows(xl, self.ln2[i], eps, hl)
                     ops.tc_gemm(hl, self.w_gu[i], 2 * I, act[:b], epilogue=SWIGLU, err=err)
                     ops.tc_gemm(act[:b], self.w_down[i], H, xl, res=xl, epilogue=RES, err=err)
                     break
-                a = F.scaled_dot_product_attention(q4, kc[:, :, :S], vc[:, :, :S], is_causal=True,
-                                                   scale=D ** -0.5, enable_gqa=True)
-                ops.tc_gemm(a.transpose(1, 2).reshape(M, nq * D), self.w_o[i], H, x, res=x, epilogue=RES, err=err)
+                ops.prefill_attn(q, b, S, nq, nkv, kc, vc, att, err=err)
+                ops.tc_gemm(att, self.w_o[i], H, x, res=x, epilogue=RES, err=err)
                 ops.rmsnorm_rows(x, self.ln2[i], eps, h)
                 ops.tc_gemm(h, self.w_gu[i], 2 * I, act, epilogue=SWIGLU, err=err)
                 ops.tc_gemm(act, self.w_down[i], H, x, res=x, epilogue=RES, err=err)

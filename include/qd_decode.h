@@ -295,6 +295,19 @@ int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int64_t S, int
                        int64_t ldq, void* k_cache, void* v_cache, int64_t cap, int64_t cs_b, int64_t cs_h,
                        cudaStream_t stream);
 
+/* Prompt causal attention (flash attention on the tensor cores): replaces the prefill's
+ * F.scaled_dot_product_attention(q, K, V, is_causal=True, enable_gqa=True) (engine/engine.py:579,
+ * :584, :517-531). For every sequence i < batch, query head h and prompt position s in
+ * [q_begin, S): out[i * (S - q_begin) + s - q_begin, h * 128 ..] = softmax(q k^T * scale) v over keys
+ * 0..s of KV head h / (nq / nkv). q [batch * S, nq * 128] (row stride ldq, token i * S + s, as
+ * qd_prefill_qk_rope writes it); k_cache / v_cache [batch, nkv, cap, 128] hold positions 0..S-1
+ * (strides cs_b, cs_h). q_begin = 0 is the whole prompt; q_begin = S - 1 gives the last position
+ * only (the reference's last layer, engine/engine.py:577-583). Rows are 16-byte aligned, ldq and
+ * ldo multiples of 8. */
+int qd_prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, int nq_heads, int nkv_heads,
+                    const void* k_cache, const void* v_cache, int64_t cap, int64_t cs_b, int64_t cs_h, float scale,
+                    void* out, int64_t ldo, int* err, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

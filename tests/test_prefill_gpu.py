@@ -6,7 +6,8 @@ counts (rows past m must stay untouched), an odd number of 128-row weight groups
 residual epilogue in place and the SwiGLU epilogue on the interleaved gate/up matrix. The tensor
 cores accumulate in fp32 in their own order, so an output may sit one BF16 ulp away at a rounding
 tie. qd_rmsnorm_rows and qd_prefill_qk_rope are checked against the oracle's op restatements
-(oracle/qwen3_cpu.py, engine/engine.py:505-509 and :550-592).
+(oracle/qwen3_cpu.py, engine/engine.py:505-509 and :550-592), qd_prefill_attn against the exact
+softmax in fp64 and against PyTorch's flash SDPA (the reference's prompt attention).
 """
 
 import pytest
@@ -189,3 +190,71 @@ def test_prefill_qk_rope_and_cache(b, S):
     _assert_close(kcs, kr, extra=rope_tol(kh))
     assert torch.equal(vcs.cpu(), vr)
     assert torch.isnan(kc[:, :, S:].float()).all() and torch.isnan(vc[:, :, S:].float()).all()
+
+
+def _attn_ref(q, kc, vc, b, S, nq, nkv, q_begin):
+    """fp64 causal GQA attention of positions q_begin..S-1 (exact softmax), rows i * (S - q_begin) + s."""
+    D = 128
+    qd = q.to(DEV).double().view(b, S, nq, D).transpose(1, 2)                     # [b, nq, S, D]
+    k = kc[:, :, :S].to(DEV).double().repeat_interleave(nq // nkv, dim=1)        # [b, nq, S, D]
+    v = vc[:, :, :S].to(DEV).double().repeat_interleave(nq // nkv, dim=1)
+    s = (qd @ k.transpose(-1, -2)) / (D ** 0.5)
+    mask = torch.ones((S, S), dtype=torch.bool, device=DEV).tril()
+    s = s.masked_fill(~mask, float("-inf"))
+    o = torch.softmax(s, -1) @ v                                                   # [b, nq, S, D]
+    return o[:, :, q_begin:].transpose(1, 2).reshape(b * (S - q_begin), nq * D)
+
+
+@pytest.mark.parametrize("b,S", [(1, 1), (1, 127), (1, 128), (3, 17), (2, 300), (1, 1024)])
+@pytest.mark.parametrize("last_only", [False, True])
+def test_prefill_attn_causal_gqa(b, S, last_only):
+    """Against the exact softmax, with NaN in every cache slot past the prompt (never read): P is
+    rounded to BF16 before P.V (as flash attention does), so an output may differ by a few ulp of the
+    values it averages (|v| <= ~5 here), hence the absolute term."""
+    ops = _ops()
+    nq, nkv, D = 32, 8, 128
+    cap = S + 40
+    g = torch.Generator().manual_seed(b * 1000 + S)
+    q = _rand((b * S, nq * D), 1.0, g)
+    kc = torch.full((b, nkv, cap, D), float("nan"), dtype=BF16)
+    vc = torch.full((b, nkv, cap, D), float("nan"), dtype=BF16)
+    kc[:, :, :S] = _rand((b, nkv, S, D), 1.0, g)
+    vc[:, :, :S] = _rand((b, nkv, S, D), 1.0, g)
+    q0 = S - 1 if last_only else 0
+    rows = b * (S - q0)
+    out = torch.full((rows + 2, nq * D), float("nan"), dtype=BF16, device=DEV)
+    ops.prefill_attn(q.to(DEV), b, S, nq, nkv, kc.to(DEV), vc.to(DEV), out[:rows], q_begin=q0)
+    ref = _attn_ref(q, kc, vc, b, S, nq, nkv, q0).float()
+    _assert_close(out[:rows], ref, extra=torch.ones_like(ref), rtol=2.0 ** -6)
+    assert torch.isnan(out[rows:].float()).all()
+
+
+def test_prefill_attn_matches_torch_flash_sdpa():
+    """The same computation as the reference's prompt attention (flash SDPA, enable_gqa), to within
+    the BF16 rounding of the probabilities and of the output."""
+    ops = _ops()
+    b, S, nq, nkv, D = 2, 700, 32, 8, 128
+    g = torch.Generator().manual_seed(77)
+    q = _rand((b * S, nq * D), 1.0, g).to(DEV)
+    kc = _rand((b, nkv, S, D), 1.0, g).to(DEV)
+    vc = _rand((b, nkv, S, D), 1.0, g).to(DEV)
+    out = torch.empty((b * S, nq * D), dtype=BF16, device=DEV)
+    ops.prefill_attn(q, b, S, nq, nkv, kc, vc, out)
+    ref = torch.nn.functional.scaled_dot_product_attention(q.view(b, S, nq, D).transpose(1, 2), kc, vc, is_causal=True,
+                                                           scale=D ** -0.5, enable_gqa=True)
+    ref = ref.transpose(1, 2).reshape(b * S, nq * D).float()
+    _assert_close(out, ref, extra=torch.ones_like(ref), rtol=2.0 ** -6)
+
+
+def test_prefill_attn_deterministic():
+    ops = _ops()
+    b, S, nq, nkv, D = 2, 513, 32, 8, 128
+    g = torch.Generator().manual_seed(3)
+    q = _rand((b * S, nq * D), 1.0, g).to(DEV)
+    kc = _rand((b, nkv, S, D), 1.0, g).to(DEV)
+    vc = _rand((b, nkv, S, D), 1.0, g).to(DEV)
+    o1 = torch.empty((b * S, nq * D), dtype=BF16, device=DEV)
+    o2 = torch.empty_like(o1)
+    ops.prefill_attn(q, b, S, nq, nkv, kc, vc, o1)
+    ops.prefill_attn(q, b, S, nq, nkv, kc, vc, o2)
+    assert torch.equal(o1, o2)
