@@ -25,6 +25,7 @@ constexpr int kErrWaitFull = 1;
 constexpr int kErrWaitEmpty = 2;
 constexpr int kErrDrain = 4;
 constexpr int kErrDep = 32;  // a wait for another CTA's results (persistent step kernel) timed out
+constexpr int kErrSmem = 64;  // dynamic shared memory not aligned as the kernel's layout requires
 
 __host__ __device__ __forceinline__ int64_t packed_offset_elems(int64_t n, int64_t k, int64_t kblocks) {
   const int64_t g = n >> 7, r = n & 127, kb = k >> 6, c = (k & 63) >> 3, e = k & 7;

@@ -391,15 +391,19 @@ __global__ void __launch_bounds__(256) prefill_qk_rope_kernel(const __grid_const
 // most key tiles go first. Per key tile of 128 keys:
 //   S = Q K^T      tcgen05.mma M = 128 queries, N = 128 keys, K = 128 dims (8 MMAs), fp32 in TMEM,
 //                  two S buffers so the next tile's S overlaps this tile's softmax
-//   softmax        warps 0-3, thread = query row: row max over the tile (causal mask on the diagonal
-//                  tile), P = exp2((s - m) * scale * log2 e) rounded to BF16 into a 128-byte-swizzled
-//                  K-major operand tile, row sums in fp32
+//   softmax        warps 0-7, two per query row (TMEM lane), each with 64 of the keys: row max
+//                  (causal mask on the diagonal tile) from both halves' maxima exchanged through
+//                  shared memory, then each turns its 64 keys into
+//                  P = exp2((s - m) * scale * log2 e) (ex2.approx), rounded to BF16 into a
+//                  128-byte-swizzled K-major operand tile (two P buffers), and sums them in fp32
 //   O += P V       M = 128 queries, N = 128 dims (V read as an MN-major operand), K = 128 keys
-// The running max only moves when it grows by more than 2^8 in the exp2 domain; then the thread's O
-// row is rescaled in TMEM (tcgen05.ld / st) and its sum with it - the quotient O / l is unchanged by
-// which max is used. Q, K and V arrive by TMA from tensor maps whose key (query) extent is the prompt
-// length, so rows past it read as zero. Warp 4 loads, warp 5 issues the MMAs.
-constexpr int kPaThreads = 192;
+// The running max only moves when some row of a warp grows by more than 2^8 in the exp2 domain; then
+// the warp rescales its O columns in TMEM (tcgen05.ld / st) and its sums with them - the quotient
+// O / l does not depend on which max is used. K and V have separate two-stage rings: a K tile is free
+// once its S is computed, a V tile once its P.V is. Q, K and V arrive by TMA from tensor maps whose
+// query / key extent is the prompt length, so rows past it read as zero. Warp 8 loads, warp 9 issues
+// the MMAs.
+constexpr int kPaThreads = 320;
 constexpr int kPaTile = 128;
 constexpr int kPaBox = kPaTile * 128;  // [128 rows][64 dims] BF16: 16 KiB
 
@@ -414,11 +418,13 @@ struct alignas(64) PrefillAttnArgs {
 
 struct PaLayout {
   static constexpr int q = 0;                      // Q: 2 dim halves
-  static constexpr int kv = q + 2 * kPaBox;        // 2 stages x (K half 0, K half 1, V half 0, V half 1)
-  static constexpr int p = kv + 2 * 4 * kPaBox;    // P: 2 key halves
-  static constexpr int bars = p + 2 * kPaBox;      // 13 barriers
-  static constexpr int misc = bars + 13 * 8;       // tmem slot, abort, K/V tiles issued, Q tiles issued
-  static constexpr int total = misc + 16;
+  static constexpr int k = q + 2 * kPaBox;         // K: 2 stages x 2 dim halves
+  static constexpr int v = k + 2 * 2 * kPaBox;     // V: 2 stages x 2 dim halves
+  static constexpr int p = v + 2 * 2 * kPaBox;     // P: 2 buffers x 2 key halves
+  static constexpr int red = p + 2 * 2 * kPaBox;   // row max / sum exchange [2 tiles][2 halves][128] fp32
+  static constexpr int bars = red + 2 * 2 * 128 * 4;  // 19 barriers
+  static constexpr int misc = bars + 19 * 8;       // tmem slot, abort, K tiles, V tiles, Q tiles issued
+  static constexpr int total = misc + 32;
 };
 
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar,
@@ -438,6 +444,18 @@ __device__ __forceinline__ void tma_load_4d_pf(uint32_t dst, const CUtensorMap* 
       : "memory");
 }
 
+// three-input max (sm_100) and the hardware base-2 exponential (flush-to-zero; exp2(-inf) = 0)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 __device__ __forceinline__ void pa_unit(const PrefillAttnArgs& a, int u, int* i, int* h, int* qt) {
   const int per = a.batch * a.nq;
   *qt = a.n_qt - 1 - u / per;  // >= qt0
@@ -447,36 +465,46 @@ __device__ __forceinline__ void pa_unit(const PrefillAttnArgs& a, int u, int* i,
 }
 
 __global__ void __launch_bounds__(kPaThreads, 1) prefill_attn_kernel(const __grid_constant__ PrefillAttnArgs a) {
+  // the layout needs all but a few hundred bytes of the 227 KiB, so there is no room to realign: dynamic
+  // shared memory starts 1 KiB-aligned on sm_100 (nothing static precedes it); if not, flag and do nothing
   extern __shared__ __align__(1024) char smem_raw[];
-  char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  if (smem_u32(smem_raw) & 1023u) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.err, kErrSmem);
+    return;
+  }
+  char* smem = smem_raw;
   const uint32_t sb = smem_u32(smem);
   const uint32_t bars = sb + PaLayout::bars;
-  const uint32_t qfull = bars, qempty = bars + 8, pfull = bars + 48, odone = bars + 56, ofree = bars + 64;
-  auto kvfull = [&](int s) { return bars + 16 + 8u * s; };
-  auto kvempty = [&](int s) { return bars + 32 + 8u * s; };
-  auto sfull = [&](int s) { return bars + 72 + 8u * s; };
-  auto sfree = [&](int s) { return bars + 88 + 8u * s; };
+  const uint32_t qfull = bars, qempty = bars + 8, ofree = bars + 144;
+  auto kfull = [&](int s) { return bars + 16 + 8u * s; };
+  auto kempty = [&](int s) { return bars + 32 + 8u * s; };
+  auto vfull = [&](int s) { return bars + 48 + 8u * s; };
+  auto vempty = [&](int s) { return bars + 64 + 8u * s; };
+  auto sfull = [&](int s) { return bars + 80 + 8u * s; };
+  auto sfree = [&](int s) { return bars + 96 + 8u * s; };
+  auto pfull = [&](int s) { return bars + 112 + 8u * s; };
+  auto odone = [&](int s) { return bars + 128 + 8u * s; };
   int* misc = reinterpret_cast<int*>(smem + PaLayout::misc);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x;
   if (tid == 0) {
     mbar_init(qfull, 1);
     mbar_init(qempty, 1);
-    mbar_init(pfull, 4);
-    mbar_init(odone, 1);
-    mbar_init(ofree, 4);
+    mbar_init(ofree, 8);
     for (int s2 = 0; s2 < 2; ++s2) {
-      mbar_init(kvfull(s2), 1);
-      mbar_init(kvempty(s2), 1);
+      mbar_init(kfull(s2), 1);
+      mbar_init(kempty(s2), 1);
+      mbar_init(vfull(s2), 1);
+      mbar_init(vempty(s2), 1);
       mbar_init(sfull(s2), 1);
-      mbar_init(sfree(s2), 4);
+      mbar_init(sfree(s2), 8);
+      mbar_init(pfull(s2), 8);
+      mbar_init(odone(s2), 1);
     }
     fence_mbar_init();
-    misc[1] = 0;
-    misc[2] = 0;
-    misc[3] = 0;
+    for (int m = 1; m < 8; ++m) misc[m] = 0;
   }
-  if (warp == 5) tmem_alloc(smem_u32(misc), 512);
+  if (warp == 9) tmem_alloc(smem_u32(misc), 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -484,75 +512,84 @@ __global__ void __launch_bounds__(kPaThreads, 1) prefill_attn_kernel(const __gri
   const uint32_t tS = tmem, tO = tmem + 256;  // S[2] in columns 0-255, O in 256-383
   int* abort = misc + 1;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol = policy_evict_normal();
-      int t = 0, k = 0, kv_issued = 0;
+      int t = 0, k = 0, kn = 0, vn = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < a.units && ok; u += G, ++k) {
         int i, h, qt;
         pa_unit(a, u, &i, &h, &qt);
         if (k >= 1 && !mbar_wait_abort(qempty, (k - 1) & 1, a.err, kErrWaitEmpty, abort)) break;
-        misc[3] = k + 1;
+        misc[4] = k + 1;
         mbar_arrive_expect_tx(qfull, 2 * kPaBox);
         tma_load_3d(sb + PaLayout::q, &a.tq, h * 128, qt * kPaTile, i, qfull, pol);
         tma_load_3d(sb + PaLayout::q + kPaBox, &a.tq, h * 128 + 64, qt * kPaTile, i, qfull, pol);
         const int kvh = h / (a.nq / a.nkv);
         for (int j = 0; j <= qt; ++j, ++t) {
           const int st = t & 1;
-          if (t >= 2 && !mbar_wait_abort(kvempty(st), ((t >> 1) - 1) & 1, a.err, kErrWaitEmpty, abort)) {
+          if (t >= 2 && !mbar_wait_abort(kempty(st), ((t >> 1) - 1) & 1, a.err, kErrWaitEmpty, abort)) {
             ok = false;
             break;
           }
-          const uint32_t d = sb + PaLayout::kv + st * 4 * kPaBox;
-          mbar_arrive_expect_tx(kvfull(st), 4 * kPaBox);
-          tma_load_4d_pf(d, &a.tk, 0, j * kPaTile, kvh, i, kvfull(st), pol);
-          tma_load_4d_pf(d + kPaBox, &a.tk, 64, j * kPaTile, kvh, i, kvfull(st), pol);
-          tma_load_4d_pf(d + 2 * kPaBox, &a.tv, 0, j * kPaTile, kvh, i, kvfull(st), pol);
-          tma_load_4d_pf(d + 3 * kPaBox, &a.tv, 64, j * kPaTile, kvh, i, kvfull(st), pol);
-          ++kv_issued;
+          const uint32_t dk = sb + PaLayout::k + st * 2 * kPaBox;
+          mbar_arrive_expect_tx(kfull(st), 2 * kPaBox);
+          tma_load_4d_pf(dk, &a.tk, 0, j * kPaTile, kvh, i, kfull(st), pol);
+          tma_load_4d_pf(dk + kPaBox, &a.tk, 64, j * kPaTile, kvh, i, kfull(st), pol);
+          misc[2] = ++kn;
+          if (t >= 2 && !mbar_wait_abort(vempty(st), ((t >> 1) - 1) & 1, a.err, kErrWaitEmpty, abort)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dv = sb + PaLayout::v + st * 2 * kPaBox;
+          mbar_arrive_expect_tx(vfull(st), 2 * kPaBox);
+          tma_load_4d_pf(dv, &a.tv, 0, j * kPaTile, kvh, i, vfull(st), pol);
+          tma_load_4d_pf(dv + kPaBox, &a.tv, 64, j * kPaTile, kvh, i, vfull(st), pol);
+          misc[3] = ++vn;
         }
       }
-      misc[2] = kv_issued;
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t id_s = umma_idesc_bf16(128), id_o = umma_idesc_bf16(128, false, true);
       int t = 0, k = 0;
       bool ok = true;
       auto issue_pv = [&](int tt, bool first) {
+        const int b = tt & 1;
         if (ok && first && k >= 1) ok = mbar_wait_abort(ofree, (k - 1) & 1, a.err, kErrWaitFull, abort);
-        if (ok) ok = mbar_wait_abort(pfull, tt & 1, a.err, kErrWaitFull, abort);
+        if (ok) ok = mbar_wait_abort(pfull(b), (tt >> 1) & 1, a.err, kErrWaitFull, abort);
+        if (ok) ok = mbar_wait_abort(vfull(b), (tt >> 1) & 1, a.err, kErrWaitFull, abort);
         tc_fence_after();
         if (ok) {
-          const uint32_t v = sb + PaLayout::kv + (tt & 1) * 4 * kPaBox + 2 * kPaBox;
+          const uint32_t v = sb + PaLayout::v + b * 2 * kPaBox, pp = sb + PaLayout::p + b * 2 * kPaBox;
 #pragma unroll
           for (int j = 0; j < 8; ++j)  // 16 keys per MMA: P +32 B inside a 64-key half; V two 8-key atoms
-            umma_bf16(tO, umma_desc_sw128(sb + PaLayout::p + (j >> 2) * kPaBox + (j & 3) * 32),
+            umma_bf16(tO, umma_desc_sw128(pp + (j >> 2) * kPaBox + (j & 3) * 32),
                       umma_desc_sw128(v + j * 2048, kPaBox, 1024), id_o, (first && j == 0) ? 0u : 1u);
         }
-        umma_commit(odone);
-        umma_commit(kvempty(tt & 1));
+        umma_commit(odone(b));
+        umma_commit(vempty(b));
       };
       for (int u = blockIdx.x; u < a.units && ok; u += G, ++k) {
         int i, h, qt;
         pa_unit(a, u, &i, &h, &qt);
         if (!mbar_wait_abort(qfull, k & 1, a.err, kErrWaitFull, abort)) break;
         for (int j = 0; j <= qt; ++j) {
-          const int tt = t + j;
-          if (ok) ok = mbar_wait_abort(kvfull(tt & 1), (tt >> 1) & 1, a.err, kErrWaitFull, abort);
-          if (ok && tt >= 2) ok = mbar_wait_abort(sfree(tt & 1), ((tt >> 1) - 1) & 1, a.err, kErrWaitFull, abort);
+          const int tt = t + j, b = tt & 1;
+          if (ok) ok = mbar_wait_abort(kfull(b), (tt >> 1) & 1, a.err, kErrWaitFull, abort);
+          if (ok && tt >= 2) ok = mbar_wait_abort(sfree(b), ((tt >> 1) - 1) & 1, a.err, kErrWaitFull, abort);
           tc_fence_after();
           if (ok) {
-            const uint32_t kt = sb + PaLayout::kv + (tt & 1) * 4 * kPaBox;
+            const uint32_t kt = sb + PaLayout::k + b * 2 * kPaBox;
 #pragma unroll
             for (int d = 0; d < 8; ++d)  // 16 dims per MMA: +32 B inside a 64-dim half, the next half after 4
-              umma_bf16(tS + (tt & 1) * 128, umma_desc_sw128(sb + PaLayout::q + (d >> 2) * kPaBox + (d & 3) * 32),
+              umma_bf16(tS + b * 128, umma_desc_sw128(sb + PaLayout::q + (d >> 2) * kPaBox + (d & 3) * 32),
                         umma_desc_sw128(kt + (d >> 2) * kPaBox + (d & 3) * 32), id_s, d > 0 ? 1u : 0u);
           }
-          umma_commit(sfull(tt & 1));
+          umma_commit(sfull(b));
+          umma_commit(kempty(b));
           if (j == qt) umma_commit(qempty);
           if (j >= 1) issue_pv(tt - 1, j == 1);
         }
@@ -561,98 +598,119 @@ __global__ void __launch_bounds__(kPaThreads, 1) prefill_attn_kernel(const __gri
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax + epilogue (thread = query row)
-    const int r = 32 * warp + lane;
-    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
-    char* pt = smem + PaLayout::p;
+    // ------------------------------------------------------------ softmax + epilogue: two warps per row
+    const int grp = warp >> 2, wq = warp & 3;  // grp: which 64 keys / dims of the row
+    const int r = 32 * wq + lane;
+    const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
+    float* red = reinterpret_cast<float*>(smem + PaLayout::red);
     int t = 0, k = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < a.units && ok; u += G, ++k) {
+    // every softmax warp runs all its units and tiles even after a failed wait (the waits are then
+    // skipped): the two warps of a row meet at named barriers, so neither may leave early
+    for (int u = blockIdx.x; u < a.units; u += G, ++k) {
       int i, h, qt;
       pa_unit(a, u, &i, &h, &qt);
       const int q = qt * kPaTile + r;  // query position within the sequence
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; j <= qt; ++j) {
-        const int tt = t + j;
-        const uint32_t ts = tS + (tt & 1) * 128 + lane_off;
-        if (ok) ok = mbar_wait_abort(sfull(tt & 1), (tt >> 1) & 1, a.err, kErrWaitFull, abort);
+        const int tt = t + j, b = tt & 1;
+        const uint32_t ts = tS + b * 128 + lane_off;
+        if (ok) ok = mbar_wait_abort(sfull(b), (tt >> 1) & 1, a.err, kErrWaitFull, abort);
         tc_fence_after();
         const bool diag = (j == qt);
-        float mx = -INFINITY;
-#pragma unroll 1
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint32_t v[32];
-          tmem_ld32(ts + 32 * c4, v);
+        // this half's 64 scores stay in registers for the exp pass; on the diagonal tile the keys past
+        // the row's query (column > r) become -inf, whose exp2 is 0
+        uint32_t own[64];
+        tmem_ld64(ts + 64 * grp, own);
+        if (diag) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const bool masked = diag && (32 * c4 + e > r);  // key j*128 + c > query qt*128 + r
-            if (!masked) mx = fmaxf(mx, __uint_as_float(v[e]));
-          }
+          for (int e = 0; e < 64; ++e)
+            if (64 * grp + e > r) own[e] = __float_as_uint(-INFINITY);
+        }
+        float mx;
+        {  // four independent max chains
+          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+          for (int e = 0; e < 64; e += 8)
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              m4[c] = fmax3(m4[c], __uint_as_float(own[e + 2 * c]), __uint_as_float(own[e + 2 * c + 1]));
+          mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        }
+        {  // row max = max of the two halves' maxima (exchange slots alternate by tile)
+          float* rx = red + b * 256;
+          rx[grp * 128 + r] = mx;
+          named_bar(1 + wq, 64);
+          mx = fmaxf(rx[r], rx[128 + r]);
         }
         const float m_new = mx * a.scale_log2;
-        // the P buffer and O are free once the previous tile's P.V is done
-        if (ok && tt >= 1) ok = mbar_wait_abort(odone, (tt - 1) & 1, a.err, kErrWaitFull, abort);
-        tc_fence_after();
-        if (m_new > m_used + 8.f) {
-          const float alpha = exp2f(m_used - m_new);  // 0 on the first tile
+        // warp-uniform: the TMEM loads / stores of the rescale are warp-collective, and warps w and
+        // w + 4 (the two halves of the same rows) take the same decision
+        if (__any_sync(0xffffffffu, m_new > m_used + 8.f)) {
+          const float m_to = fmaxf(m_used, m_new);
+          const float alpha = exp2f(m_used - m_to);  // 0 on the first tile, 1 where the max did not grow
           if (j > 0) {
+            // O must hold the previous tile's P.V before it is rescaled
+            if (ok) ok = mbar_wait_abort(odone((tt - 1) & 1), ((tt - 1) >> 1) & 1, a.err, kErrWaitFull, abort);
+            tc_fence_after();
 #pragma unroll 1
-            for (int c4 = 0; c4 < 4; ++c4) {
+            for (int c2 = 0; c2 < 2; ++c2) {
+              const uint32_t ta = tO + lane_off + 64 * grp + 32 * c2;
               uint32_t o[32];
-              tmem_ld32(tO + lane_off + 32 * c4, o);
+              tmem_ld32(ta, o);
 #pragma unroll
               for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-              tmem_st32(tO + lane_off + 32 * c4, o);
+              tmem_st32(ta, o);
             }
           }
           l *= alpha;
-          m_used = m_new;
+          m_used = m_to;
         }
-#pragma unroll 1
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint32_t v[32];
-          tmem_ld32(ts + 32 * c4, v);
-          uint32_t pk[16];
+        // P buffer b was last read by the P.V two tiles back
+        if (ok && tt >= 2) ok = mbar_wait_abort(odone(b), ((tt >> 1) - 1) & 1, a.err, kErrWaitFull, abort);
+        char* pt = smem + PaLayout::p + b * 2 * kPaBox + grp * kPaBox + r * 128;  // keys 64 grp.. of row r
+        const float nm = -m_used;
+        float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // eight independent sum chains
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float p2[2];
+        for (int c = 0; c < 8; ++c) {  // 16-byte chunk c of the row (8 keys), stored swizzled by row
+          uint32_t pk[4];
 #pragma unroll
-            for (int d = 0; d < 2; ++d) {
-              const bool masked = diag && (32 * c4 + e + d > r);
-              p2[d] = masked ? 0.f : exp2f(fmaf(__uint_as_float(v[e + d]), a.scale_log2, -m_used));
-              l += p2[d];
-            }
-            pk[e >> 1] = pack_bf2(p2[0], p2[1]);
+          for (int e = 0; e < 8; e += 2) {
+            const float p0 = ex2_approx(fmaf(__uint_as_float(own[8 * c + e]), a.scale_log2, nm));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(own[8 * c + e + 1]), a.scale_log2, nm));
+            ls[e] += p0;
+            ls[e + 1] += p1;
+            pk[e >> 1] = pack_bf2(p0, p1);
           }
-          // keys 32 c4 .. +31: half c4 / 2, 16-byte chunks 4 (c4 & 1) .. +3 of row r, swizzled
-          char* row = pt + (c4 >> 1) * kPaBox + r * 128;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int chunk = 4 * (c4 & 1) + c;
-            *reinterpret_cast<uint4*>(row + ((chunk ^ (r & 7)) << 4)) =
-                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-          }
+          *reinterpret_cast<uint4*>(pt + ((c ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
+        l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
         tc_fence_before();
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(sfree(tt & 1));
-          mbar_arrive(pfull);
+          mbar_arrive(sfree(b));
+          mbar_arrive(pfull(b));
         }
       }
-      // ---- unit end: O / l for this row
+      // ---- unit end: O / l for this row's 64 dims; l is the sum of both halves
       const int tl = t + qt;
-      if (ok) ok = mbar_wait_abort(odone, tl & 1, a.err, kErrWaitFull, abort);
+      if (ok) ok = mbar_wait_abort(odone(tl & 1), (tl >> 1) & 1, a.err, kErrWaitFull, abort);
       tc_fence_after();
-      const float inv = 1.0f / l;
-      __nv_bfloat16* dst = a.out + ((int64_t)i * (a.S - a.q0) + (q - a.q0)) * a.ldo + (int64_t)h * 128;
+      // the exchange slots of the tile after tl: both halves read them last before tile tl's barrier,
+      // and the second barrier keeps the next tile's max from overwriting them before both have read
+      float* lx = red + ((tl + 1) & 1) * 256;
+      lx[grp * 128 + r] = l;
+      named_bar(1 + wq, 64);
+      const float inv = 1.0f / (lx[r] + lx[128 + r]);
+      named_bar(1 + wq, 64);
+      __nv_bfloat16* dst = a.out + ((int64_t)i * (a.S - a.q0) + (q - a.q0)) * a.ldo + (int64_t)h * 128 + 64 * grp;
 #pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int c2 = 0; c2 < 2; ++c2) {
         uint32_t o[32];
-        tmem_ld32(tO + lane_off + 32 * c4, o);
+        tmem_ld32(tO + lane_off + 64 * grp + 32 * c2, o);
         if (q < a.S && q >= a.q0) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c4);
+          uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c2);
 #pragma unroll
           for (int c = 0; c < 4; ++c)
             d4[c] = make_uint4(pack_bf2(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
@@ -670,12 +728,14 @@ __global__ void __launch_bounds__(kPaThreads, 1) prefill_attn_kernel(const __gri
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 5) tmem_dealloc(tmem, 512);
+  if (warp == 9) tmem_dealloc(tmem, 512);
   if (tid == 0) {  // no bulk copy may still be writing shared memory when the CTA exits
-    const int issued = misc[2], q_issued = misc[3];
-    for (int it = issued > 2 ? issued - 2 : 0; it < issued; ++it)
-      if (!mbar_wait(kvfull(it & 1), (it >> 1) & 1, a.err, kErrDrain)) break;
-    if (q_issued > 0) mbar_wait(qfull, (q_issued - 1) & 1, a.err, kErrDrain);
+    const int kn = misc[2], vn = misc[3], qn = misc[4];
+    for (int it = kn > 2 ? kn - 2 : 0; it < kn; ++it)
+      if (!mbar_wait(kfull(it & 1), (it >> 1) & 1, a.err, kErrDrain)) break;
+    for (int it = vn > 2 ? vn - 2 : 0; it < vn; ++it)
+      if (!mbar_wait(vfull(it & 1), (it >> 1) & 1, a.err, kErrDrain)) break;
+    if (qn > 0) mbar_wait(qfull, (qn - 1) & 1, a.err, kErrDrain);
   }
 }
 
@@ -893,7 +953,7 @@ extern "C" int qd_prefill_attn(const void* q, int64_t ldq, int batch, int64_t S,
   a.units = (int)units;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.err = err;
-  const int smem = PaLayout::total + 1024;
+  const int smem = PaLayout::total;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

@@ -99,7 +99,8 @@ QD_OK, QD_ERR_ARG, QD_ERR_SCRATCH, QD_ERR_CUDA, QD_ERR_UNSUPPORTED = 0, 1, 2, 3,
 QD_EPI_STORE, QD_EPI_RES, QD_EPI_SWIGLU, QD_EPI_SWIGLU_PACKED = 0, 1, 2, 3
 DEVERR = {1: "wait for a weight block timed out", 2: "wait for a free ring slot timed out",
           4: "drain of in-flight copies timed out", 8: "token id out of range",
-          16: "decode position outside the cache", 32: "a wait for another CTA's results timed out"}
+          16: "decode position outside the cache", 32: "a wait for another CTA's results timed out",
+          64: "dynamic shared memory misaligned (kernel did nothing)"}
 
 
 class QDError(RuntimeError):

@@ -40,7 +40,8 @@ enum {
   QD_DEVERR_DRAIN = 4,
   QD_DEVERR_TOKEN = 8,
   QD_DEVERR_POS = 16,
-  QD_DEVERR_DEP = 32
+  QD_DEVERR_DEP = 32,
+  QD_DEVERR_SMEM = 64 /* a kernel found its dynamic shared memory misaligned and did nothing */
 };
 
 /* Library identification and the last error message of the calling thread. */
