@@ -48,7 +48,8 @@ def _args():
     p.add_argument("--cpu-steps", type=int, default=96, help="decode steps in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--kernel", default=None, choices=["qkv", "o", "gu", "down", "lm", "attn", "attn_stream", "attn_tc", "step"],
+    p.add_argument("--kernel", default=None, choices=["qkv", "o", "gu", "down", "lm", "attn", "attn_stream", "attn_tc", "step",
+                                                      "prefill_gu", "prefill_attn"],
                    help="time one decode kernel alone (small profiling case; random packed weights on the GPU)")
     p.add_argument("--launches", type=int, default=8)
     p.add_argument("--tc", action="store_true", help="with --kernel: the tcgen05 kernel (activations pre-packed)")
@@ -359,6 +360,41 @@ def run_ours(a):
         dist.destroy_process_group()
 
 
+def run_prefill_kernel(a):
+    """One prompt kernel alone on `--prompt` tokens of one sequence (profiling case): prefill_gu is
+    qd_tc_gemm with the SwiGLU epilogue on the gate/up shape (x [S, 2560] N(0, 1), packed weights
+    N(0, 0.02)); prefill_attn is qd_prefill_attn over the whole prompt (q, K, V N(0, 1), 32 q / 8 KV
+    heads). Prints avg us and TFLOP/s over `--launches` launches after three warm-up launches."""
+    import torch
+
+    from decode_b200 import ops
+
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    S, H, I, nq, nkv, D = a.prompt, 2560, 9728, 32, 8, 128
+    g = torch.Generator(device=dev).manual_seed(0)
+    err = torch.zeros((1,), dtype=torch.int32, device=dev)
+    if a.kernel == "prefill_gu":
+        x = torch.randn((S, H), generator=g, device=dev).to(torch.bfloat16)
+        w = ops.pack_matrix((torch.randn((2 * I, H), generator=g, device=dev) * 0.02).to(torch.bfloat16))
+        out = torch.empty((S, I), dtype=torch.bfloat16, device=dev)
+        fn = lambda i: ops.tc_gemm(x, w, 2 * I, out, epilogue=ops.Gemv.SWIGLU, err=err)  # noqa: E731
+        flops = 2 * S * 2 * I * H
+    else:
+        q = torch.randn((S, nq * D), generator=g, device=dev).to(torch.bfloat16)
+        kc = torch.randn((1, nkv, S, D), generator=g, device=dev).to(torch.bfloat16)
+        vc = torch.randn((1, nkv, S, D), generator=g, device=dev).to(torch.bfloat16)
+        out = torch.empty((S, nq * D), dtype=torch.bfloat16, device=dev)
+        fn = lambda i: ops.prefill_attn(q, 1, S, nq, nkv, kc, vc, out, err=err)  # noqa: E731
+        flops = 4 * nq * (S * (S + 1) // 2) * D
+    ms = _time_cycle(fn, 1, a.launches)
+    assert int(err.item()) == 0
+    tf = flops / (ms / 1e3) / 1e12
+    print(json.dumps({"kernel": a.kernel, "prompt": S, "launches": a.launches, "avg_us": round(ms * 1e3, 2),
+                      "TFLOPs": round(tf, 1), "frac_of_peak": round(tf / _tensor_peak(), 4),
+                      "peak_tflops": _tensor_peak()}))
+
+
 def run_kernel(a):
     """One decode kernel alone, cycling over `--layers` copies of its weights (random, packed on the
     GPU; > L2 from 2 copies for gate_up, down and the LM head), for profiling. Prints avg µs and GB/s."""
@@ -370,6 +406,8 @@ def run_kernel(a):
     torch.cuda.set_device(dev)
     if a.kernel == "step":
         return run_step_kernel(a)
+    if a.kernel in ("prefill_gu", "prefill_attn"):
+        return run_prefill_kernel(a)
     H, I, V, nq, nkv, D, B, L = 2560, 9728, 151936, 32, 8, 128, a.batch, a.layers
     g = torch.Generator(device=dev).manual_seed(0)
     rnd = lambda *shape: (torch.randn(shape, generator=g, device=dev) * 0.02).to(torch.bfloat16)  # noqa: E731
