@@ -30,7 +30,8 @@ constexpr int kTStage = 4 * kTBox;         // K dims 0-63, K dims 64-127, V dims
 constexpr int kTStages = 3;
 constexpr int kTN = 16;                    // MMA N: the 4 query heads of the KV head + 12 zero rows
 constexpr int kTThreads = 192;
-constexpr int kTCols = 64;                 // tensor memory: S[2] and O[2], 16 columns each
+constexpr int kTSO = 3;                    // S / O accumulator sets in tensor memory
+constexpr int kTCols = 128;                // tensor memory: S[3] and O[3], 16 columns each (allocated as 128)
 constexpr int kTSoftBar = 1;               // named barrier of warps 0-3
 constexpr int kTStageMax = 160;            // merge staging: 3 x 4 x smax floats
 
@@ -56,7 +57,8 @@ struct TcAttnLayout {
   static constexpr int stg = pb + 2 * 2 * kTN * 128;     // merge staging
   static constexpr int red = stg + 3 * kGroup * kTStageMax * 4;  // [2][4 warps][4 heads] maxima, [4][4] sums
   static constexpr int bars = red + 3 * 4 * kGroup * 4;
-  static constexpr int nbars = 2 * kTStages + 2 * 4 + 1;  // full, empty, s_full, p_full, o_full, d_free, q_ready
+  static constexpr int nbars = 2 * kTStages + 3 * kTSO + 2 + 1;  // full, empty, s_full[3], o_full[3], d_free[3],
+                                                                 // p_full[2], q_ready
   static constexpr int misc = bars + nbars * 8;           // tmem slot, flag, issued
   static constexpr int total = misc + 16;
 };
@@ -104,11 +106,11 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
   const uint32_t bars = sbase + Ly::bars;
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (kTStages + s); };
-  auto sfull_bar = [&](int b) { return bars + 8u * (2 * kTStages + b); };
-  auto pfull_bar = [&](int b) { return bars + 8u * (2 * kTStages + 2 + b); };
-  auto ofull_bar = [&](int b) { return bars + 8u * (2 * kTStages + 4 + b); };
-  auto dfree_bar = [&](int b) { return bars + 8u * (2 * kTStages + 6 + b); };
-  const uint32_t qready_bar = bars + 8u * (2 * kTStages + 8);
+  auto sfull_bar = [&](int b) { return bars + 8u * (2 * kTStages + b); };              // b < kTSO
+  auto ofull_bar = [&](int b) { return bars + 8u * (2 * kTStages + kTSO + b); };       // b < kTSO
+  auto dfree_bar = [&](int b) { return bars + 8u * (2 * kTStages + 2 * kTSO + b); };   // b < kTSO
+  auto pfull_bar = [&](int b) { return bars + 8u * (2 * kTStages + 3 * kTSO + b); };   // b < 2
+  const uint32_t qready_bar = bars + 8u * (2 * kTStages + 3 * kTSO + 2);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + Ly::misc);
   int* issued_s = reinterpret_cast<int*>(smem + Ly::misc + 8);
 
@@ -117,12 +119,12 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kTSO; ++b) {
       mbar_init(sfull_bar(b), 1);
-      mbar_init(pfull_bar(b), 4);
       mbar_init(ofull_bar(b), 1);
       mbar_init(dfree_bar(b), 4);
     }
+    for (int b = 0; b < 2; ++b) mbar_init(pfull_bar(b), 4);
     mbar_init(qready_bar, 4);
     fence_mbar_init();
     *issued_s = 0;
@@ -137,7 +139,7 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t tS0 = tmem, tO0 = tmem + 2 * kTN;
+  const uint32_t tS0 = tmem, tO0 = tmem + kTSO * kTN;
 
   if (warp == 4) {
     // ---------------------------------------------------------------- producer
@@ -174,9 +176,9 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
       int qph = 1;
       int ci_next = (int)(c_begin % nch);  // chunk-in-pair of the next q.k to issue
       auto issue_qk = [&](int i) {
-        const int slot = i % kTStages, b = i & 1;
+        const int slot = i % kTStages, b = i % kTSO;
         if (ok) ok = mbar_wait(full_bar(slot), (i / kTStages) & 1, a.err, kErrWaitFull);
-        if (ok && i >= 2) ok = mbar_wait(dfree_bar(b), ((i >> 1) - 1) & 1, a.err, kErrWaitFull);
+        if (ok && i >= kTSO) ok = mbar_wait(dfree_bar(b), ((i / kTSO) - 1) & 1, a.err, kErrWaitFull);
         if (ok && i > 0 && ci_next == 0) {  // first chunk of a new pair: its q must be in place
           ok = mbar_wait(qready_bar, qph & 1, a.err, kErrWaitFull);
           ++qph;
@@ -199,18 +201,18 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
         // and this chunk's P.V must not wait with it
         const bool next_new_pair = (i + 1 < n) && ci_next == 0;
         if (i + 1 < n && !next_new_pair) issue_qk(i + 1);
-        const int slot = i % kTStages, b = i & 1;
+        const int slot = i % kTStages, b = i & 1, bo = i % kTSO;
         if (ok) ok = mbar_wait(pfull_bar(b), (i >> 1) & 1, a.err, kErrWaitFull);
         tc_fence_after();
         if (ok) {
           const uint32_t vst = sbase + Ly::stages + slot * kTStage + 2 * kTBox;
 #pragma unroll
           for (int j = 0; j < 8; ++j)  // 16 keys per MMA: two 8-key atoms of 1 KiB; dims 64-127 one box on
-            umma_bf16(tO0 + b * kTN, umma_desc_sw128(vst + j * 2048, kTBox, 1024),
+            umma_bf16(tO0 + bo * kTN, umma_desc_sw128(vst + j * 2048, kTBox, 1024),
                       umma_desc_sw128(sbase + Ly::pb + b * (2 * kTN * 128) + (j >> 2) * (kTN * 128) + (j & 3) * 32),
                       id_pv, j > 0 ? 1u : 0u);
         }
-        umma_commit(ofull_bar(b));
+        umma_commit(ofull_bar(bo));
         umma_commit(empty_bar(slot));
         if (next_new_pair) issue_qk(i + 1);
       }
@@ -253,14 +255,30 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
     put_q(pair);
     reset_state();
     bool ok = true;
+    // O of chunk j: thread tid holds dim tid of the 4 heads; acc = acc * alpha_j + O_j
+    auto consume_o = [&](int j, const float* al) {
+      const int bo = j % kTSO;
+      if (ok) ok = mbar_wait(ofull_bar(bo), (j / kTSO) & 1, a.err, kErrWaitFull);
+      tc_fence_after();
+      float o[4];
+      tmem_ld4(tO0 + bo * kTN + ((uint32_t)(32 * warp) << 16), o);
+      tmem_wait_ld();
+#pragma unroll
+      for (int h = 0; h < kGroup; ++h) acc[h] = fmaf(acc[h], al[h], o[h]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dfree_bar(bo));
+    };
+    bool have_pend = false;
+    float pend_alpha[kGroup];
     for (int i = 0; i < n; ++i) {
-      const int slot = i % kTStages, b = i & 1;
+      const int slot = i % kTStages, b = i & 1, bs = i % kTSO;
       const int k0 = ci * kTKeys;
       const int nk = (int)((len - k0) < kTKeys ? (len - k0) : kTKeys);
-      if (ok) ok = mbar_wait(sfull_bar(b), (i >> 1) & 1, a.err, kErrWaitFull);
+      if (ok) ok = mbar_wait(sfull_bar(bs), (i / kTSO) & 1, a.err, kErrWaitFull);
       tc_fence_after();
       float s[4];
-      tmem_ld4(tS0 + b * kTN + ((uint32_t)(32 * warp) << 16), s);
+      tmem_ld4(tS0 + bs * kTN + ((uint32_t)(32 * warp) << 16), s);
       tmem_wait_ld();
       const bool valid = tid < nk;
       float mx[kGroup];
@@ -302,18 +320,19 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
       const bool pair_end = (ci == nch - 1) || (i == n - 1);
       // the next chunk starts a new pair: its q goes in now, so its q.k can run during this P.V
       if (pair_end && i + 1 < n) put_q(pair + 1);
-      // O of this chunk: thread tid holds dim tid of the 4 heads
-      if (ok) ok = mbar_wait(ofull_bar(b), (i >> 1) & 1, a.err, kErrWaitFull);
-      tc_fence_after();
-      float o[4];
-      tmem_ld4(tO0 + b * kTN + ((uint32_t)(32 * warp) << 16), o);
-      tmem_wait_ld();
+      // O of the previous chunk of this segment (deferred by one chunk, so its P.V runs during this
+      // chunk's softmax), then this chunk's own O only where the segment ends
+      if (have_pend) {
+        consume_o(i - 1, pend_alpha);
+        have_pend = false;
+      }
+      if (!pair_end) {
 #pragma unroll
-      for (int h = 0; h < kGroup; ++h) acc[h] = fmaf(acc[h], alpha[h], o[h]);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dfree_bar(b));
-      if (pair_end) {
+        for (int h = 0; h < kGroup; ++h) pend_alpha[h] = alpha[h];
+        have_pend = true;
+        ++ci;
+      } else {
+        consume_o(i, alpha);
         // ---- flush the pair segment [seg_first, ci]: sums over the 128 key threads, then out or partial
         float l[kGroup];
 #pragma unroll
@@ -397,8 +416,6 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
         }
         seg_first = ci;
         reset_state();
-      } else {
-        ++ci;
       }
     }
   }

@@ -375,6 +375,14 @@ __device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum
   }
 }
 
+// Optional timeline hook of the segment flush (a kernel that defines it before including this header
+// records its phases); a no-op otherwise.
+#ifndef QD_FLUSH_HOOK
+#define QD_FLUSH_HOOK(k, flags, tid) \
+  do {                                \
+  } while (0)
+#endif
+
 // A CTA's segment of row group g (blocks seg_first..b) is reduced into red[m * 128 + r]. If the segment is
 // the whole group, run the epilogue; otherwise store the partial, take the group's ticket, and the CTA
 // that completes the group sums all partials in CTA order and runs the epilogue. 256 consumer threads.
@@ -406,6 +414,7 @@ __device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64
       flags[1] = (old + nseg_blk == a.kblocks) ? 1 : 0;
     }
     named_bar(kBarConsumers, kConsumers);
+    QD_FLUSH_HOOK(2, flags, tid);
     if (flags[1]) {
       // every CTA in [c_lo, c_hi] owns a non-empty part of the group (T >= G): sum their partials
       // in CTA order
@@ -443,7 +452,9 @@ __device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64
         if (q < kVec) red4[q] = acc[j];
       }
       named_bar(kBarConsumers, kConsumers);
+      QD_FLUSH_HOOK(3, flags, tid);
       finalize_group<M, MODE>(a, g, red, wsum, lmv, lmi, aux, flags, tid, MODE == MODE_RES ? res_pre : nullptr);
+      QD_FLUSH_HOOK(4, flags, tid);
       if (tid == 0) atomicExch(a.tickets + g, 0);
       finalized = true;
     }

@@ -13,6 +13,25 @@
 // read the accumulator (tcgen05.ld 32x32b, warp w reads TMEM lanes 32(w % 4).. and half of the
 // columns), then run the same split-K flush and fused epilogues as the CUDA-core kernel
 // (qd_gemv_dev.cuh). The work partition (stream-K over blocks) is the CUDA-core kernel's.
+// Development timeline (built only with -DQD_TC_TRACE): %globaltimer stamps per CTA into a buffer set
+// with qd_tc_trace_set; slot layout in tc_gemv_kernel.
+#ifdef QD_TC_TRACE
+namespace qd {
+static __device__ unsigned long long* g_tc_trace;
+}
+#define QD_FLUSH_HOOK(k, flags, tid)                                                                   \
+  do {                                                                                               \
+    if (g_tc_trace && (tid) == 0) g_tc_trace[blockIdx.x * 64 + (flags)[3] + (k)] = globaltimer();     \
+  } while (0)
+#define TC_STAMP(k)                                                            \
+  do {                                                                         \
+    if (g_tc_trace) g_tc_trace[blockIdx.x * 64 + (k)] = globaltimer();         \
+  } while (0)
+#else
+#define TC_STAMP(k) \
+  do {              \
+  } while (0)
+#endif
 #include "qd_gemv_dev.cuh"
 #include "qd_plan.h"
 #include "qd_umma.cuh"
@@ -110,6 +129,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemv_kernel(const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  if (tid == 0) TC_STAMP(0);
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------ producer
@@ -127,7 +147,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemv_kernel(const __grid_con
         mbar_arrive_expect_tx(full_bar(i), (uint32_t)(kBlockBytes + xtile));
         bulk_g2s(smem_u32(ring + i * Ly.stage), wsrc + i * (int64_t)kBlockBytes, kBlockBytes, full_bar(i), pol);
       }
+      TC_STAMP(1);
       grid_dep_wait();
+      TC_STAMP(2);
       int kb = (int)(b_begin % a.kblocks);
       for (int i = 0; i < first; ++i) {
         bulk_g2s(smem_u32(ring + i * Ly.stage + kBlockBytes), a.x_packed + kb * xtile, (uint32_t)xtile, full_bar(i),
@@ -150,6 +172,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemv_kernel(const __grid_con
         }
       }
       flags[0] = issued;
+      TC_STAMP(3);
     }
   } else if (warp == kConsumerWarps + 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -190,6 +213,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemv_kernel(const __grid_con
     grid_dep_wait();
     grid_dep_launch();
     if constexpr (MODE == MODE_QKV) qkv_prologue(a, aux, flags, tid);
+    if (tid == 0) TC_STAMP(6);
+    int n_seg = 0;
     bool ok = true;
     int buf = 0, fph[2] = {0, 0};
     const int q = warp & 3, half = warp >> 2;
@@ -206,6 +231,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemv_kernel(const __grid_con
       if (ok) ok = mbar_wait(accf_bar(buf), fph[buf], a.err, kErrWaitFull);
       fph[buf] ^= 1;
       tc_fence_after();
+      if (tid == 0 && n_seg < 7) TC_STAMP(8 + 8 * n_seg);
       // row r = 32q + lane of the group; this warp's half of the N batch columns
 #pragma unroll
       for (int c8 = 0; c8 < N / 16; ++c8) {
@@ -220,8 +246,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemv_kernel(const __grid_con
       __syncwarp();
       if (lane == 0) mbar_arrive(acce_bar(buf));
       buf ^= 1;
+      if (tid == 0) {
+        if (n_seg < 7) TC_STAMP(9 + 8 * n_seg);
+        flags[3] = 8 + 8 * (n_seg < 7 ? n_seg : 6);  // trace slot base of this segment's flush phases
+      }
       named_bar(kBarConsumers, kConsumers);
       flush_segment<N, MODE>(a, g, seg_first, b, cta, red, wsum, lmv, lmi, aux, flags, tid);
+      if (tid == 0 && n_seg < 7) TC_STAMP(13 + 8 * n_seg);
+      ++n_seg;
       seg_first = b + 1;
     }
     if constexpr (MODE == MODE_LM) lm_global_argmax<N>(a, cta, wsum, lmv, lmi, flags, tid);
@@ -520,3 +552,9 @@ extern "C" int qd_tc_lm_head_argmax(const void* xpk, int n_pad, int m_act, const
   a.ld_logits = ld_logits;
   return tc_launch(a, MODE_LM, n_pad, pdl, stream);
 }
+
+#ifdef QD_TC_TRACE
+extern "C" int qd_tc_trace_set(void* p) {
+  return cudaMemcpyToSymbol(qd::g_tc_trace, &p, sizeof(p)) == cudaSuccess ? 0 : 3;
+}
+#endif
