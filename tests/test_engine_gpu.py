@@ -139,6 +139,29 @@ def test_poisoned_cache_slots_are_never_read(engines):
     assert again == ref
 
 
+def test_prefill_row_chunks_are_bit_identical(engines, monkeypatch):
+    """A prompt batch over one prefill chunk (at most 16384 tokens per chunk, engine/engine.py:79, :189)
+    runs as several chunks of whole sequences. Every prompt kernel is row-independent and deterministic,
+    so the first-token logits, the cache and the decoded logits equal the one-chunk run's bit for bit."""
+    import engine as E
+    from decode_b200 import synth
+
+    eng, _, cfg = engines(2)
+    p = synth.random_prompt(5, 40, cfg["vocab_size"], seed=41)
+    eng.state = None
+    toks1, lg1 = eng.generate_with_logits(p, 3)
+    assert eng.state.rows == 5
+    k1, v1 = eng.state.k_all[:, :, :, :40].clone(), eng.state.v_all[:, :, :, :40].clone()
+    monkeypatch.setattr(E, "PREFILL_TOKENS", 100)  # 2 sequences of 40 tokens per chunk: 3 chunks
+    eng.state = None
+    toks2, lg2 = eng.generate_with_logits(p, 3)
+    assert eng.state.rows == 2
+    assert toks1 == toks2
+    assert all(torch.equal(a, b) for a, b in zip(lg1, lg2))
+    assert torch.equal(k1, eng.state.k_all[:, :, :, :40]) and torch.equal(v1, eng.state.v_all[:, :, :, :40])
+    eng.state = None
+
+
 def test_contract_step_counts(engines):
     from decode_b200 import synth
 
