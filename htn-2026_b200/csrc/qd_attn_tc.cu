@@ -451,23 +451,9 @@ static int64_t tc_attn_scratch(int pairs, int smax, int64_t* off_ml, int64_t* of
   return acc + ml + ((int64_t)pairs * 4 + 255) / 256 * 256;
 }
 
-// cuTensorMapEncodeTiled through the runtime's driver entry point: the library needs no link-time
-// dependency on the driver library (it loads on hosts without a GPU).
-static PFN_cuTensorMapEncodeTiled_v12000 encode_tiled_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
 static bool encode_cache_map(CUtensorMap* m, const void* base, int batch, int nkv, int64_t cap, int64_t cs_b,
                              int64_t cs_h) {
-  const PFN_cuTensorMapEncodeTiled_v12000 encode = encode_tiled_fn();
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (!encode) return false;
   const cuuint64_t dims[4] = {(cuuint64_t)kHeadDim, (cuuint64_t)cap, (cuuint64_t)nkv, (cuuint64_t)batch};
   const cuuint64_t strides[3] = {(cuuint64_t)kHeadDim * 2, (cuuint64_t)cs_h * 2, (cuuint64_t)cs_b * 2};

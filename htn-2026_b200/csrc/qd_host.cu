@@ -27,6 +27,18 @@ int host_sm_count() {
   return n;
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
 int launch_kernel(const void* func, dim3 grid, dim3 block, int smem, int pdl, cudaStream_t stream, void* arg) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;

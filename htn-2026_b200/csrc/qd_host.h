@@ -1,6 +1,8 @@
 // Host-side helpers shared by the C-ABI translation units.
 #pragma once
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -17,5 +19,9 @@ int host_sm_count();
 int launch_kernel(const void* func, dim3 grid, dim3 block, int smem, int pdl, cudaStream_t stream, void* arg);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (looked up once): the library needs no
+// link-time dependency on the driver library, so it loads on hosts without a GPU. Null if unavailable.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 }  // namespace qd

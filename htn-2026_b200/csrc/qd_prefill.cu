@@ -740,18 +740,6 @@ __global__ void __launch_bounds__(kPaThreads, 1) prefill_attn_kernel(const __gri
 }
 
 // ------------------------------------------------------------------ host side
-static PFN_cuTensorMapEncodeTiled_v12000 gemm_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
 template <int BN>
 static int gemm_nst() {
   int nst = env_int("QD_GEMM_STAGES", 8);
@@ -807,7 +795,7 @@ extern "C" int qd_tc_gemm(const void* x, int64_t ldx, int64_t m, const void* w_p
     return set_error(QD_ERR_ARG, "tc gemm: residual needs ldr >= n, ldr %% 8 == 0, 16-byte alignment");
   if (!aligned16(x) || !aligned16(w_packed) || !aligned16(out)) return set_error(QD_ERR_ARG, "tc gemm: alignment");
   if (m > (int64_t)INT32_MAX - 128 || k > (1 << 24)) return set_error(QD_ERR_UNSUPPORTED, "tc gemm: too large");
-  const PFN_cuTensorMapEncodeTiled_v12000 encode = gemm_encode_fn();
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (!encode) return set_error(QD_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   GemmArgs a = {};
   {
@@ -915,7 +903,7 @@ extern "C" int qd_prefill_attn(const void* q, int64_t ldq, int batch, int64_t S,
   const int64_t n_qt = (S + kPaTile - 1) / kPaTile, qt0 = q_begin / kPaTile;
   const int64_t units = (int64_t)batch * nq_heads * (n_qt - qt0);
   if (units > INT32_MAX || S > INT32_MAX - kPaTile) return set_error(QD_ERR_UNSUPPORTED, "prefill attention: too large");
-  const PFN_cuTensorMapEncodeTiled_v12000 encode = gemm_encode_fn();
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (!encode) return set_error(QD_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   PrefillAttnArgs a = {};
   const cuuint32_t estr[4] = {1, 1, 1, 1};

@@ -860,21 +860,9 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_step_kernel(const __grid_cons
 }
 
 // ------------------------------------------------------------------ host side
-static PFN_cuTensorMapEncodeTiled_v12000 tstep_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
 static bool encode_cache_map5(CUtensorMap* m, const void* base, int layers, int batch, int nkv, int64_t cap,
                               int64_t cs_b, int64_t cs_h, int64_t c_ls) {
-  const PFN_cuTensorMapEncodeTiled_v12000 enc = tstep_encode_fn();
+  const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (!enc) return false;
   const cuuint64_t dims[5] = {(cuuint64_t)kHeadDim, (cuuint64_t)cap, (cuuint64_t)nkv, (cuuint64_t)batch,
                               (cuuint64_t)layers};
