@@ -80,3 +80,47 @@ def test_stream_k_partition_covers_every_block_once(T, G):
             assert owners[b] == c
     assert part_begin(T, G, 0) == 0 and part_begin(T, G, G) == T
     assert all(part_begin(T, G, c + 1) - part_begin(T, G, c) in (T // G, T // G + 1) for c in range(G))
+
+
+def test_prompt_entry_points_validate_arguments(lib):
+    """The prompt kernels' entry points reject bad shapes, strides and pointers on the host, before any
+    launch (every call here is invalid, so nothing reaches the GPU)."""
+    P = ctypes.c_void_p
+    a, b, c = P(0x10000), P(0x20000), P(0x30000)  # 16-byte aligned stand-ins, never dereferenced
+    ERR_ARG = 1
+    # qd_tc_gemm(x, ldx, m, w, n, k, out, ldo, res, ldr, epilogue, err, stream)
+    assert lib.qd_tc_gemm(None, 2560, 8, b, 2560, 2560, c, 2560, None, 0, 0, None, None) == ERR_ARG
+    assert lib.qd_tc_gemm(a, 2560, 0, b, 2560, 2560, c, 2560, None, 0, 0, None, None) == ERR_ARG
+    assert lib.qd_tc_gemm(a, 2560, 8, b, 2500, 2560, c, 2560, None, 0, 0, None, None) == ERR_ARG   # n % 128
+    assert lib.qd_tc_gemm(a, 2560, 8, b, 2560, 2500, c, 2560, None, 0, 0, None, None) == ERR_ARG   # k % 64
+    assert lib.qd_tc_gemm(a, 2560, 8, b, 2560, 2560, c, 2560, None, 0, 7, None, None) == ERR_ARG   # epilogue
+    assert lib.qd_tc_gemm(a, 2560, 8, b, 2560, 2560, c, 2560, None, 0, 1, None, None) == ERR_ARG   # RES, no res
+    assert lib.qd_tc_gemm(P(0x10008), 2560, 8, b, 2560, 2560, c, 2560, None, 0, 0, None, None) == ERR_ARG
+    assert lib.qd_tc_gemm(a, 2560, 8, b, 19456, 2560, c, 9000, None, 0, 2, None, None) == ERR_ARG  # ldo < n/2
+    # qd_rmsnorm_rows(x, ldx, m, k, w, eps, out, ldo, stream)
+    assert lib.qd_rmsnorm_rows(a, 2560, 4, 2561, b, 1e-6, c, 2560, None) == ERR_ARG
+    assert lib.qd_rmsnorm_rows(a, 2560, 4, 2560, None, 1e-6, c, 2560, None) == ERR_ARG
+    # qd_prefill_qk_rope(qkv, ldqkv, batch, S, nq, nkv, qn, kn, eps, cos, sin, q_out, ldq, kc, vc, cap, cs_b, cs_h, s)
+    assert lib.qd_prefill_qk_rope(a, 6144, 1, 200, 32, 8, b, b, 1e-6, c, c, a, 4096, b, c, 128, 8 * 128 * 128,
+                                  128 * 128, None) == ERR_ARG                                   # S > cap
+    # qd_prefill_attn(q, ldq, batch, S, q_begin, nq, nkv, kc, vc, cap, cs_b, cs_h, scale, out, ldo, err, stream)
+    cs_h, cs_b = 256 * 128, 8 * 256 * 128
+    assert lib.qd_prefill_attn(a, 4096, 1, 200, 200, 32, 8, b, c, 256, cs_b, cs_h, 0.088, a, 4096, None,
+                               None) == ERR_ARG                                                 # q_begin >= S
+    assert lib.qd_prefill_attn(a, 4096, 1, 200, 0, 30, 8, b, c, 256, cs_b, cs_h, 0.088, a, 4096, None,
+                               None) == ERR_ARG                                                 # nq % nkv
+    assert lib.qd_prefill_attn(a, 4096, 1, 200, 0, 32, 8, b, c, 256, cs_b, 100, 0.088, a, 4096, None,
+                               None) == ERR_ARG                                                 # cs_h < cap*128
+    assert lib.qd_prefill_attn(a, 4000, 1, 200, 0, 32, 8, b, c, 256, cs_b, cs_h, 0.088, a, 4096, None,
+                               None) == ERR_ARG                                                 # ldq < nq*128
+
+
+def test_tc_gemm_plan_tile_choice(lib):
+    """Prompt GEMM plan: 256-wide weight tiles once they alone give every SM a tile, else 128; one CTA per
+    tile up to one per SM (148 here: no device, the default count)."""
+    g, bn = ctypes.c_int(0), ctypes.c_int(0)
+    assert lib.qd_tc_gemm_plan(16384, 19456, 2560, ctypes.byref(g), ctypes.byref(bn)) == 0
+    assert bn.value == 256 and g.value == 148
+    assert lib.qd_tc_gemm_plan(128, 2560, 4096, ctypes.byref(g), ctypes.byref(bn)) == 0
+    assert bn.value == 128 and g.value == 20
+    assert lib.qd_tc_gemm_plan(1, 100, 64, ctypes.byref(g), ctypes.byref(bn)) == 1

@@ -206,8 +206,8 @@ def _attn_ref(q, kc, vc, b, S, nq, nkv, q_begin):
 
 
 @pytest.mark.parametrize("b,S", [(1, 1), (1, 127), (1, 128), (3, 17), (2, 300), (1, 1024)])
-@pytest.mark.parametrize("last_only", [False, True])
-def test_prefill_attn_causal_gqa(b, S, last_only):
+@pytest.mark.parametrize("q_mode", ["all", "last", "middle"])
+def test_prefill_attn_causal_gqa(b, S, q_mode):
     """Against the exact softmax, with NaN in every cache slot past the prompt (never read): P is
     rounded to BF16 before P.V (as flash attention does), so an output may differ by a few ulp of the
     values it averages (|v| <= ~5 here), hence the absolute term."""
@@ -220,7 +220,7 @@ def test_prefill_attn_causal_gqa(b, S, last_only):
     vc = torch.full((b, nkv, cap, D), float("nan"), dtype=BF16)
     kc[:, :, :S] = _rand((b, nkv, S, D), 1.0, g)
     vc[:, :, :S] = _rand((b, nkv, S, D), 1.0, g)
-    q0 = S - 1 if last_only else 0
+    q0 = {"all": 0, "last": S - 1, "middle": S // 2}[q_mode]
     rows = b * (S - q0)
     out = torch.full((rows + 2, nq * D), float("nan"), dtype=BF16, device=DEV)
     ops.prefill_attn(q.to(DEV), b, S, nq, nkv, kc.to(DEV), vc.to(DEV), out[:rows], q_begin=q0)
