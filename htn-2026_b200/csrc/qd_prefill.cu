@@ -739,6 +739,285 @@ __global__ void __launch_bounds__(kPaThreads, 1) prefill_attn_kernel(const __gri
   }
 }
 
+// ------------------------------------------------------------------ prompt causal attention, ping-pong
+// Variant of prefill_attn_kernel with two query tiles per CTA: query heads 2hp and 2hp + 1 of one KV
+// head's group, same 128 queries, so both read every K / V tile the CTA loads. Two softmax warpgroups
+// (warps 0-3 tile A, 4-7 tile B; thread = query row, all 128 keys of a tile in registers) alternate
+// with the tensor core: while one warpgroup computes its P, the MMA warp runs the other tile's P.V and
+// the next S. P is written back over its own S columns in tensor memory (BF16 pairs, 64 columns) and
+// read from there as the A operand of P.V, so shared memory holds only Q (two tiles), and two K and
+// two V stages. Tensor memory: S_A, S_B (128 columns each), O_A, O_B (128 each).
+constexpr int kPpThreads = 320;
+
+struct PpLayout {
+  static constexpr int qa = 0;                  // Q of tile A: 2 dim halves
+  static constexpr int qb = qa + 2 * kPaBox;    // Q of tile B
+  static constexpr int k = qb + 2 * kPaBox;     // K: 2 stages x 2 dim halves
+  static constexpr int v = k + 2 * 2 * kPaBox;  // V: 2 stages x 2 dim halves
+  static constexpr int bars = v + 2 * 2 * kPaBox;
+  static constexpr int nbars = 17;  // qfull, qempty, kfull[2], kempty[2], vfull[2], vempty[2], sfull[2],
+                                    // pfull[2], odone[2], ofree
+  static constexpr int misc = bars + nbars * 8;  // tmem slot, abort, K tiles, V tiles, Q units issued
+  static constexpr int total = misc + 32;
+};
+
+__device__ __forceinline__ void pp_unit(const PrefillAttnArgs& a, int u, int* i, int* kvh, int* hp, int* qt) {
+  const int per = a.batch * a.nkv * 2;
+  *qt = a.n_qt - 1 - u / per;  // >= qt0
+  const int rem = u % per;
+  *i = rem / (a.nkv * 2);
+  const int rr = rem - *i * a.nkv * 2;
+  *kvh = rr >> 1;
+  *hp = rr & 1;
+}
+
+__global__ void __launch_bounds__(kPpThreads, 1) prefill_attn_pp_kernel(const __grid_constant__ PrefillAttnArgs a) {
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const uint32_t sb = smem_u32(smem);
+  const uint32_t bars = sb + PpLayout::bars;
+  const uint32_t qfull = bars, qempty = bars + 8, ofree = bars + 128;
+  auto kfull = [&](int s) { return bars + 16 + 8u * s; };
+  auto kempty = [&](int s) { return bars + 32 + 8u * s; };
+  auto vfull = [&](int s) { return bars + 48 + 8u * s; };
+  auto vempty = [&](int s) { return bars + 64 + 8u * s; };
+  auto sfull = [&](int x) { return bars + 80 + 8u * x; };
+  auto pfull = [&](int x) { return bars + 96 + 8u * x; };
+  auto odone = [&](int x) { return bars + 112 + 8u * x; };
+  static_assert(PpLayout::nbars * 8 == 136, "barrier block: 17 barriers");
+  int* misc = reinterpret_cast<int*>(smem + PpLayout::misc);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = gridDim.x, gq = a.nq / a.nkv;
+  if (tid == 0) {
+    mbar_init(qfull, 1);
+    mbar_init(qempty, 1);
+    mbar_init(ofree, 8);
+    for (int s2 = 0; s2 < 2; ++s2) {
+      mbar_init(kfull(s2), 1);
+      mbar_init(kempty(s2), 1);
+      mbar_init(vfull(s2), 1);
+      mbar_init(vempty(s2), 1);
+      mbar_init(sfull(s2), 1);
+      mbar_init(pfull(s2), 4);
+      mbar_init(odone(s2), 1);
+    }
+    fence_mbar_init();
+    for (int m = 1; m < 8; ++m) misc[m] = 0;
+  }
+  if (warp == 9) tmem_alloc(smem_u32(misc), 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = (uint32_t)misc[0];
+  auto tS = [&](int x) { return tmem + 128u * x; };        // S_A 0-127, S_B 128-255 (P over their first 64)
+  auto tO = [&](int x) { return tmem + 256u + 128u * x; };  // O_A 256-383, O_B 384-511
+  int* abort = misc + 1;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_normal();
+      int t = 0, k = 0, kn = 0, vn = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < a.units && ok; u += G, ++k) {
+        int i, kvh, hp, qt;
+        pp_unit(a, u, &i, &kvh, &hp, &qt);
+        if (k >= 1 && !mbar_wait_abort(qempty, (k - 1) & 1, a.err, kErrWaitEmpty, abort)) break;
+        misc[4] = k + 1;
+        const int ha = kvh * gq + 2 * hp;
+        mbar_arrive_expect_tx(qfull, 4 * kPaBox);
+        tma_load_3d(sb + PpLayout::qa, &a.tq, ha * 128, qt * kPaTile, i, qfull, pol);
+        tma_load_3d(sb + PpLayout::qa + kPaBox, &a.tq, ha * 128 + 64, qt * kPaTile, i, qfull, pol);
+        tma_load_3d(sb + PpLayout::qb, &a.tq, (ha + 1) * 128, qt * kPaTile, i, qfull, pol);
+        tma_load_3d(sb + PpLayout::qb + kPaBox, &a.tq, (ha + 1) * 128 + 64, qt * kPaTile, i, qfull, pol);
+        for (int j = 0; j <= qt; ++j, ++t) {
+          const int st = t & 1;
+          if (t >= 2 && !mbar_wait_abort(kempty(st), ((t >> 1) - 1) & 1, a.err, kErrWaitEmpty, abort)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dk = sb + PpLayout::k + st * 2 * kPaBox;
+          mbar_arrive_expect_tx(kfull(st), 2 * kPaBox);
+          tma_load_4d_pf(dk, &a.tk, 0, j * kPaTile, kvh, i, kfull(st), pol);
+          tma_load_4d_pf(dk + kPaBox, &a.tk, 64, j * kPaTile, kvh, i, kfull(st), pol);
+          misc[2] = ++kn;
+          if (t >= 2 && !mbar_wait_abort(vempty(st), ((t >> 1) - 1) & 1, a.err, kErrWaitEmpty, abort)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dv = sb + PpLayout::v + st * 2 * kPaBox;
+          mbar_arrive_expect_tx(vfull(st), 2 * kPaBox);
+          tma_load_4d_pf(dv, &a.tv, 0, j * kPaTile, kvh, i, vfull(st), pol);
+          tma_load_4d_pf(dv + kPaBox, &a.tv, 64, j * kPaTile, kvh, i, vfull(st), pol);
+          misc[3] = ++vn;
+        }
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_s = umma_idesc_bf16(128), id_o = umma_idesc_bf16(128, false, true);
+      int t = 0, k = 0;
+      bool ok = true;
+      auto issue_s = [&](int x, int tt) {  // S_x(tt) = Q_x K_tt^T; its columns then hold P_x(tt - 1) no more
+        if (ok && tt > 0) ok = mbar_wait_abort(odone(x), (tt - 1) & 1, a.err, kErrWaitFull, abort);
+        tc_fence_after();
+        if (ok) {
+          const uint32_t q = sb + (x ? PpLayout::qb : PpLayout::qa), kt = sb + PpLayout::k + (tt & 1) * 2 * kPaBox;
+#pragma unroll
+          for (int d = 0; d < 8; ++d)  // 16 dims per MMA: +32 B inside a 64-dim half, the next half after 4
+            umma_bf16(tS(x), umma_desc_sw128(q + (d >> 2) * kPaBox + (d & 3) * 32),
+                      umma_desc_sw128(kt + (d >> 2) * kPaBox + (d & 3) * 32), id_s, d > 0 ? 1u : 0u);
+        }
+        umma_commit(sfull(x));
+      };
+      auto issue_pv = [&](int x, int tt, bool first) {  // O_x += P_x(tt) V_tt, P from tensor memory
+        if (ok) ok = mbar_wait_abort(pfull(x), tt & 1, a.err, kErrWaitFull, abort);
+        tc_fence_after();
+        if (ok) {
+          const uint32_t v = sb + PpLayout::v + (tt & 1) * 2 * kPaBox;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)  // 16 keys per MMA: 8 columns of P pairs; V two 8-key atoms
+            umma_bf16_ts(tO(x), tS(x) + 8 * kk, umma_desc_sw128(v + kk * 2048, kPaBox, 1024), id_o,
+                         (first && kk == 0) ? 0u : 1u);
+        }
+        umma_commit(odone(x));
+      };
+      for (int u = blockIdx.x; u < a.units && ok; u += G, ++k) {
+        int i, kvh, hp, qt;
+        pp_unit(a, u, &i, &kvh, &hp, &qt);
+        const int J = qt + 1;
+        if (!mbar_wait_abort(qfull, k & 1, a.err, kErrWaitFull, abort)) break;
+        if (ok) ok = mbar_wait_abort(kfull(t & 1), (t >> 1) & 1, a.err, kErrWaitFull, abort);
+        issue_s(0, t);
+        issue_s(1, t);
+        umma_commit(kempty(t & 1));
+        if (J == 1) umma_commit(qempty);
+        for (int j = 0; j < J; ++j) {
+          const int tt = t + j;
+          if (ok && j == 0 && k >= 1) ok = mbar_wait_abort(ofree, (k - 1) & 1, a.err, kErrWaitFull, abort);
+          if (ok) ok = mbar_wait_abort(vfull(tt & 1), (tt >> 1) & 1, a.err, kErrWaitFull, abort);
+          issue_pv(0, tt, j == 0);
+          if (j + 1 < J) {
+            if (ok) ok = mbar_wait_abort(kfull((tt + 1) & 1), ((tt + 1) >> 1) & 1, a.err, kErrWaitFull, abort);
+            issue_s(0, tt + 1);
+          }
+          issue_pv(1, tt, j == 0);
+          umma_commit(vempty(tt & 1));
+          if (j + 1 < J) {
+            issue_s(1, tt + 1);
+            umma_commit(kempty((tt + 1) & 1));
+            if (j + 2 == J) umma_commit(qempty);
+          }
+        }
+        t += J;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue: warpgroup x = tile x
+    const int x = warp >> 2, wq = warp & 3, r = 32 * wq + lane;
+    const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
+    int t = 0, k = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < a.units; u += G, ++k) {
+      int i, kvh, hp, qt;
+      pp_unit(a, u, &i, &kvh, &hp, &qt);
+      const int h = kvh * gq + 2 * hp + x;
+      const int q = qt * kPaTile + r;  // query position within the sequence
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j <= qt; ++j) {
+        const int tt = t + j;
+        if (ok) ok = mbar_wait_abort(sfull(x), tt & 1, a.err, kErrWaitFull, abort);
+        tc_fence_after();
+        uint32_t sv[128];
+        tmem_ld64(tS(x) + lane_off, sv);
+        tmem_ld64(tS(x) + lane_off + 64, sv + 64);
+        if (j == qt) {  // diagonal tile: keys past the row's query (column > r) do not count
+#pragma unroll
+          for (int e = 0; e < 128; ++e)
+            if (e > r) sv[e] = __float_as_uint(-INFINITY);
+        }
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int e = 0; e < 128; e += 8)
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            m4[c] = fmax3(m4[c], __uint_as_float(sv[e + 2 * c]), __uint_as_float(sv[e + 2 * c + 1]));
+        const float m_new = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * a.scale_log2;
+        // warp-uniform (the TMEM loads / stores of the rescale are warp-collective); O_x holds P.V up to
+        // tile tt - 1 (S_x(tt) was issued after it completed) and P.V of tile tt has not started
+        if (__any_sync(0xffffffffu, m_new > m_used + 8.f)) {
+          const float m_to = fmaxf(m_used, m_new);
+          const float alpha = exp2f(m_used - m_to);  // 0 on the first tile, 1 where the max did not grow
+          if (j > 0) {
+#pragma unroll 1
+            for (int c4 = 0; c4 < 4; ++c4) {
+              uint32_t o[32];
+              tmem_ld32(tO(x) + lane_off + 32 * c4, o);
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+              tmem_st32(tO(x) + lane_off + 32 * c4, o);
+            }
+          }
+          l *= alpha;
+          m_used = m_to;
+        }
+        const float nm = -m_used;
+        float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {  // P pair c = keys 2c, 2c + 1, packed in place over the scores
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * c]), a.scale_log2, nm));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * c + 1]), a.scale_log2, nm));
+          ls[(2 * c) & 7] += p0;
+          ls[(2 * c + 1) & 7] += p1;
+          sv[c] = pack_bf2(p0, p1);
+        }
+        l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+        tmem_st64(tS(x) + lane_off, sv);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pfull(x));
+      }
+      // ---- unit end: O / l for this row
+      const int tl = t + qt;
+      if (ok) ok = mbar_wait_abort(odone(x), tl & 1, a.err, kErrWaitFull, abort);
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      __nv_bfloat16* dst = a.out + ((int64_t)i * (a.S - a.q0) + (q - a.q0)) * a.ldo + (int64_t)h * 128;
+#pragma unroll 1
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t o[32];
+        tmem_ld32(tO(x) + lane_off + 32 * c4, o);
+        if (q < a.S && q >= a.q0) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c4);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            d4[c] = make_uint4(pack_bf2(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
+                               pack_bf2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv),
+                               pack_bf2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv),
+                               pack_bf2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ofree);
+      t += qt + 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 9) tmem_dealloc(tmem, 512);
+  if (tid == 0) {  // no bulk copy may still be writing shared memory when the CTA exits
+    const int kn = misc[2], vn = misc[3], qn = misc[4];
+    for (int it = kn > 2 ? kn - 2 : 0; it < kn; ++it)
+      if (!mbar_wait(kfull(it & 1), (it >> 1) & 1, a.err, kErrDrain)) break;
+    for (int it = vn > 2 ? vn - 2 : 0; it < vn; ++it)
+      if (!mbar_wait(vfull(it & 1), (it >> 1) & 1, a.err, kErrDrain)) break;
+    if (qn > 0) mbar_wait(qfull, (qn - 1) & 1, a.err, kErrDrain);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 template <int BN>
 static int gemm_nst() {
@@ -941,6 +1220,18 @@ extern "C" int qd_prefill_attn(const void* q, int64_t ldq, int batch, int64_t S,
   a.units = (int)units;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.err = err;
+  if (env_int("QD_PREFILL_ATTN", 1) == 2 && (nq_heads / nkv_heads) % 2 == 0) {  // ping-pong variant
+    a.units = (int)(units / 2);  // a unit covers two query heads of one KV head
+    const int smem = PpLayout::total + 1024;
+    static bool configured_pp = false;
+    if (!configured_pp) {
+      cudaError_t e = cudaFuncSetAttribute(prefill_attn_pp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      configured_pp = true;
+    }
+    const int grid = a.units < host_sm_count() ? a.units : host_sm_count();
+    return launch_kernel((const void*)prefill_attn_pp_kernel, dim3(grid), dim3(kPpThreads), smem, 0, stream, &a);
+  }
   const int smem = PaLayout::total;
   static bool configured = false;
   if (!configured) {

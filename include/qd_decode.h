@@ -304,7 +304,9 @@ int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int64_t S, int
  * qd_prefill_qk_rope writes it); k_cache / v_cache [batch, nkv, cap, 128] hold positions 0..S-1
  * (strides cs_b, cs_h). q_begin = 0 is the whole prompt; q_begin = S - 1 gives the last position
  * only (the reference's last layer, engine/engine.py:577-583). Rows are 16-byte aligned, ldq and
- * ldo multiples of 8. */
+ * ldo multiples of 8. QD_PREFILL_ATTN=2 in the environment selects the two-query-tile variant (query
+ * heads 2j and 2j + 1 of a KV head share each K / V tile, P kept in tensor memory); same results up to
+ * the fp32 summation order. */
 int qd_prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, int nq_heads, int nkv_heads,
                     const void* k_cache, const void* v_cache, int64_t cap, int64_t cs_b, int64_t cs_h, float scale,
                     void* out, int64_t ldo, int* err, cudaStream_t stream);

@@ -205,12 +205,15 @@ def _attn_ref(q, kc, vc, b, S, nq, nkv, q_begin):
     return o[:, :, q_begin:].transpose(1, 2).reshape(b * (S - q_begin), nq * D)
 
 
+@pytest.mark.parametrize("variant", ["1", "2"])
 @pytest.mark.parametrize("b,S", [(1, 1), (1, 127), (1, 128), (3, 17), (2, 300), (1, 1024)])
 @pytest.mark.parametrize("q_mode", ["all", "last", "middle"])
-def test_prefill_attn_causal_gqa(b, S, q_mode):
+def test_prefill_attn_causal_gqa(b, S, q_mode, variant, monkeypatch):
     """Against the exact softmax, with NaN in every cache slot past the prompt (never read): P is
     rounded to BF16 before P.V (as flash attention does), so an output may differ by a few ulp of the
-    values it averages (|v| <= ~5 here), hence the absolute term."""
+    values it averages (|v| <= ~5 here), hence the absolute term. Variant 2 is the two-query-tile
+    kernel with P in tensor memory (QD_PREFILL_ATTN=2)."""
+    monkeypatch.setenv("QD_PREFILL_ATTN", variant)
     ops = _ops()
     nq, nkv, D = 32, 8, 128
     cap = S + 40
@@ -229,9 +232,11 @@ def test_prefill_attn_causal_gqa(b, S, q_mode):
     assert torch.isnan(out[rows:].float()).all()
 
 
-def test_prefill_attn_matches_torch_flash_sdpa():
+@pytest.mark.parametrize("variant", ["1", "2"])
+def test_prefill_attn_matches_torch_flash_sdpa(variant, monkeypatch):
     """The same computation as the reference's prompt attention (flash SDPA, enable_gqa), to within
     the BF16 rounding of the probabilities and of the output."""
+    monkeypatch.setenv("QD_PREFILL_ATTN", variant)
     ops = _ops()
     b, S, nq, nkv, D = 2, 700, 32, 8, 128
     g = torch.Generator().manual_seed(77)
@@ -246,7 +251,9 @@ def test_prefill_attn_matches_torch_flash_sdpa():
     _assert_close(out, ref, extra=torch.ones_like(ref), rtol=2.0 ** -6)
 
 
-def test_prefill_attn_deterministic():
+@pytest.mark.parametrize("variant", ["1", "2"])
+def test_prefill_attn_deterministic(variant, monkeypatch):
+    monkeypatch.setenv("QD_PREFILL_ATTN", variant)
     ops = _ops()
     b, S, nq, nkv, D = 2, 513, 32, 8, 128
     g = torch.Generator().manual_seed(3)
