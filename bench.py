@@ -489,7 +489,9 @@ def run_kernel(a):
 
 
 def run_step_kernel(a):
-    """The persistent step kernel alone on a `--layers`-layer synthetic model (profiling case)."""
+    """One decode step alone on a `--layers`-layer synthetic model (profiling case): the persistent step
+    kernel at batch 1-3, the persistent tcgen05 step at batch 4-12, the tcgen05 chain above (or with
+    ENGINE_TC_STEP=chain)."""
     import torch
 
     import engine as E
@@ -503,20 +505,22 @@ def run_step_kernel(a):
         st.ids.copy_(torch.tensor(synth_prompt(B, S), dtype=torch.int64))
         st.pos.fill_(S)
         st.prefill_graph.replay()
+        step = st.step or st.tstep or (lambda: eng._decode_step(st))
         for _ in range(3):
-            st.step()
+            step()
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         for _ in range(a.launches):
-            st.step()
+            step()
         e.record()
         e.synchronize()
     eng.check_device_errors(st)
     us = s.elapsed_time(e) / a.launches * 1e3
     nbytes = weight_bytes(cfg) + B * kv_bytes_per_token(cfg) * (S + 3 + a.launches / 2 + 1)
     peak, kind = _peaks()
-    print(json.dumps({"kernel": "step", "layers": a.layers, "batch": B, "launches": a.launches, "avg_us": round(us, 2),
+    mode = "step" if st.step else ("tc_step" if st.tstep else "tc_chain")
+    print(json.dumps({"kernel": mode, "layers": a.layers, "batch": B, "launches": a.launches, "avg_us": round(us, 2),
                       "algorithmic_bytes": int(nbytes), "achieved_GBs": round(nbytes / us / 1e3, 1),
                       "frac_of_peak": round(nbytes / us / 1e3 / peak, 4), "peak": peak, "peak_kind": kind}))
 

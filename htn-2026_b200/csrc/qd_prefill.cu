@@ -335,52 +335,69 @@ struct QkRopeArgs {
   float eps;
 };
 
-// One warp per (token, head); lane l holds elements 4l..4l+3, so the RoPE partner of element r
-// (r ^ 64) sits in lane l ^ 16. Same arithmetic and rounding points as the decode QKV epilogue
-// (engine/kernels/fused.py:23-81 with pos_mode 0: position = prompt index).
+constexpr int kRopeHeadsPerWarp = 8;  // heads of a token <= 8 warps x 8
+// One CTA of 8 warps per prompt token (position s of sequence i), its warps taking the token's heads in
+// turn (q heads, then k, then v); lane l holds elements 4l..4l+3, so the RoPE partner of element r
+// (r ^ 64) sits in lane l ^ 16. The position's cos / sin entries are loaded once per lane. Same
+// arithmetic and rounding points as the decode QKV epilogue (engine/kernels/fused.py:23-81 with
+// pos_mode 0: position = prompt index).
 __global__ void __launch_bounds__(256) prefill_qk_rope_kernel(const __grid_constant__ QkRopeArgs a) {
-  const int heads = a.nq + 2 * a.nkv;
-  const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (wid >= a.tokens * heads) return;
-  const int lane = threadIdx.x & 31;
-  const int64_t t = wid / heads;
-  const int h = (int)(wid - t * heads);
+  const int64_t t = blockIdx.x;
   const int64_t i = t / a.S, s = t - i * a.S;
-  const uint2 u = *reinterpret_cast<const uint2*>(a.qkv + t * a.ldqkv + (int64_t)h * 128 + 4 * lane);
-  float x[4] = {bf_lo(u.x), bf_hi(u.x), bf_lo(u.y), bf_hi(u.y)};
-  if (h >= a.nq + a.nkv) {  // V head: into the cache as is
-    const int kvh = h - a.nq - a.nkv;
-    *reinterpret_cast<uint2*>(a.v_cache + i * a.cs_b + kvh * a.cs_h + s * 128 + 4 * lane) = u;
-    return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int heads = a.nq + 2 * a.nkv;
+  const uint2 cv = *reinterpret_cast<const uint2*>(a.cos + s * 128 + 4 * lane);
+  const uint2 sv = *reinterpret_cast<const uint2*>(a.sin + s * 128 + 4 * lane);
+  const float cs[4] = {bf_lo(cv.x), bf_hi(cv.x), bf_lo(cv.y), bf_hi(cv.y)};
+  const float sn[4] = {bf_lo(sv.x), bf_hi(sv.x), bf_lo(sv.y), bf_hi(sv.y)};
+  const uint2 qw = *reinterpret_cast<const uint2*>(a.qn + 4 * lane);
+  const uint2 kw = *reinterpret_cast<const uint2*>(a.kn + 4 * lane);
+  const __nv_bfloat16* row = a.qkv + t * a.ldqkv + 4 * lane;
+  uint2 uu[kRopeHeadsPerWarp];  // every load of this warp's heads in flight before the first is used
+#pragma unroll
+  for (int j = 0; j < kRopeHeadsPerWarp; ++j) {
+    const int h = warp + 8 * j;
+    uu[j] = h < heads ? *reinterpret_cast<const uint2*>(row + (int64_t)h * 128) : make_uint2(0u, 0u);
   }
-  float sq = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
-  sq = warp_sum(sq);
-  const float rstd = 1.0f / sqrtf(sq / 128.0f + a.eps);
-  const __nv_bfloat16* nw = h < a.nq ? a.qn : a.kn;
-  float y[4], yp[4];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) y[e] = bf16r(bf16_to_f(nw[4 * lane + e]) * bf16r(x[e] * rstd));
-#pragma unroll
-  for (int e = 0; e < 4; ++e) yp[e] = __shfl_xor_sync(0xffffffffu, y[e], 16);
-  uint32_t o[2];
-#pragma unroll
-  for (int e = 0; e < 4; e += 2) {
-    float r2[2];
-#pragma unroll
-    for (int d = 0; d < 2; ++d) {
-      const int r = 4 * lane + e + d;
-      const float c = bf16_to_f(a.cos[s * 128 + r]);
-      const float sn = bf16_to_f(a.sin[s * 128 + r]);
-      const float rot = (r < 64) ? bf16r(-yp[e + d] * sn) : bf16r(yp[e + d] * sn);
-      r2[d] = bf16r(y[e + d] * c) + rot;
+  for (int j = 0; j < kRopeHeadsPerWarp; ++j) {
+    const int h = warp + 8 * j;
+    if (h >= heads) break;
+    const uint2 u = uu[j];
+    if (h >= a.nq + a.nkv) {  // V head: into the cache as is
+      const int kvh = h - a.nq - a.nkv;
+      *reinterpret_cast<uint2*>(a.v_cache + i * a.cs_b + kvh * a.cs_h + s * 128 + 4 * lane) = u;
+      continue;
     }
-    o[e >> 1] = pack_bf2(r2[0], r2[1]);
+    const float x[4] = {bf_lo(u.x), bf_hi(u.x), bf_lo(u.y), bf_hi(u.y)};
+    const uint2 wv = h < a.nq ? qw : kw;
+    const float nw[4] = {bf_lo(wv.x), bf_hi(wv.x), bf_lo(wv.y), bf_hi(wv.y)};
+    float sq = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+    sq = warp_sum(sq);
+    const float rstd = 1.0f / sqrtf(sq / 128.0f + a.eps);
+    float y[4], yp[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) y[e] = bf16r(nw[e] * bf16r(x[e] * rstd));
+#pragma unroll
+    for (int e = 0; e < 4; ++e) yp[e] = __shfl_xor_sync(0xffffffffu, y[e], 16);
+    uint32_t o[2];
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      float r2[2];
+#pragma unroll
+      for (int d = 0; d < 2; ++d) {
+        // q*cos + rotate_half(q)*sin with every product a BF16 tensor (rotate_half = cat(-q2, q1))
+        const float rot = (lane < 16) ? bf16r(-yp[e + d] * sn[e + d]) : bf16r(yp[e + d] * sn[e + d]);
+        r2[d] = bf16r(y[e + d] * cs[e + d]) + rot;
+      }
+      o[e >> 1] = pack_bf2(r2[0], r2[1]);
+    }
+    const uint2 ov = make_uint2(o[0], o[1]);
+    if (h < a.nq)
+      *reinterpret_cast<uint2*>(a.q_out + t * a.ldq + (int64_t)h * 128 + 4 * lane) = ov;
+    else
+      *reinterpret_cast<uint2*>(a.k_cache + i * a.cs_b + (h - a.nq) * a.cs_h + s * 128 + 4 * lane) = ov;
   }
-  const uint2 ov = make_uint2(o[0], o[1]);
-  if (h < a.nq)
-    *reinterpret_cast<uint2*>(a.q_out + t * a.ldq + (int64_t)h * 128 + 4 * lane) = ov;
-  else
-    *reinterpret_cast<uint2*>(a.k_cache + i * a.cs_b + (h - a.nq) * a.cs_h + s * 128 + 4 * lane) = ov;
 }
 
 // ------------------------------------------------------------------ prompt causal attention
@@ -1139,11 +1156,12 @@ extern "C" int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int
                                   int64_t cs_h, cudaStream_t stream) {
   if (!qkv || !q_norm || !k_norm || !cos || !sin || !q_out || !k_cache || !v_cache)
     return set_error(QD_ERR_ARG, "null pointer");
-  if (batch < 1 || S < 1 || S > cap || nq_heads < 1 || nkv_heads < 1 ||
+  if (batch < 1 || S < 1 || S > cap || nq_heads < 1 || nkv_heads < 1 || nq_heads + 2 * nkv_heads > 8 * kRopeHeadsPerWarp ||
       ldqkv < (int64_t)(nq_heads + 2 * nkv_heads) * 128 || ldq < (int64_t)nq_heads * 128 || ldqkv % 4 || ldq % 4 ||
       cs_h < cap * 128 || cs_b < (int64_t)nkv_heads * cs_h || cs_h % 4 || cs_b % 4)
     return set_error(QD_ERR_ARG, "prefill q/k rope: bad sizes");
-  if (((uintptr_t)qkv | (uintptr_t)q_out | (uintptr_t)k_cache | (uintptr_t)v_cache) & 7)
+  if (((uintptr_t)qkv | (uintptr_t)q_out | (uintptr_t)k_cache | (uintptr_t)v_cache | (uintptr_t)q_norm |
+       (uintptr_t)k_norm | (uintptr_t)cos | (uintptr_t)sin) & 7)
     return set_error(QD_ERR_ARG, "prefill q/k rope: 8-byte alignment");
   QkRopeArgs a = {};
   a.qkv = static_cast<const __nv_bfloat16*>(qkv);
@@ -1163,10 +1181,8 @@ extern "C" int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int
   a.nq = nq_heads;
   a.nkv = nkv_heads;
   a.eps = eps;
-  const int64_t warps = a.tokens * (nq_heads + 2 * nkv_heads);
-  const int64_t blocks = (warps + 7) / 8;
-  if (blocks > INT32_MAX) return set_error(QD_ERR_UNSUPPORTED, "prefill q/k rope: too many tokens");
-  return launch_kernel((const void*)prefill_qk_rope_kernel, dim3((unsigned)blocks), dim3(256), 0, 0, stream, &a);
+  if (a.tokens > INT32_MAX) return set_error(QD_ERR_UNSUPPORTED, "prefill q/k rope: too many tokens");
+  return launch_kernel((const void*)prefill_qk_rope_kernel, dim3((unsigned)a.tokens), dim3(256), 0, 0, stream, &a);
 }
 
 extern "C" int qd_prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, int nq_heads,
