@@ -741,19 +741,22 @@ def run_sweep_prefill(a):
             x = torch.randn((M, k), generator=g, device=dev).to(torch.bfloat16)
             out = torch.empty((M, n), dtype=torch.bfloat16, device=dev)
             epi = {"o": ops.Gemv.RES, "down": ops.Gemv.RES, "gu": ops.Gemv.SWIGLU}.get(name, ops.Gemv.STORE)
-            cases = [("tc_gemm", "store", lambda i: ops.tc_gemm(x, wp, n, out, err=err))]
+            grid, bn, ks, nb = ops.tc_gemm_plan(M, n, k)
+            sc = torch.zeros((max(nb, 1),), dtype=torch.uint8, device=dev)
+            cases = [("tc_gemm", "store", lambda i: ops.tc_gemm(x, wp, n, out, err=err, scratch=sc))]
             if epi == ops.Gemv.RES:
-                cases.append(("tc_gemm", "fused", lambda i: ops.tc_gemm(x, wp, n, out, res=out, epilogue=epi, err=err)))
+                cases.append(("tc_gemm", "fused", lambda i: ops.tc_gemm(x, wp, n, out, res=out, epilogue=epi, err=err,
+                                                                       scratch=sc)))
             elif epi == ops.Gemv.SWIGLU:
                 cases.append(("tc_gemm", "fused", lambda i: ops.tc_gemm(x, wp, n, out[:, : n // 2], epilogue=epi,
-                                                                       err=err)))
+                                                                       err=err, scratch=sc)))
             cases.append(("cublas", "store", lambda i: torch.matmul(x, w.t(), out=out)))
-            grid, bn = ops.tc_gemm_plan(M, n, k)
             for path, ep, fn in cases:
                 ms = _time_cycle(fn, 1, launches)
                 tf = 2 * M * n * k / (ms / 1e3) / 1e12
                 print(json.dumps({"sweep": "prefill", "shape": name, "n": n, "k": k, "M": M, "path": path,
                                   "epilogue": ep, "tile_n": bn if path == "tc_gemm" else None,
+                                  "ksplit": ks if path == "tc_gemm" else None,
                                   "grid": grid if path == "tc_gemm" else None, "us": round(ms * 1e3, 2),
                                   "TFLOPs": round(tf, 1), "frac_tensor": round(tf / tpeak, 4),
                                   "peak_tflops": tpeak}), flush=True)

@@ -39,8 +39,17 @@ struct alignas(64) GemmArgs {
   const __nv_bfloat16* res;
   int64_t ldo, ldr, m, n;
   int kblocks, ngroups, m_tiles, n_tiles, tiles, nst;
+  int ksplit;       // K split of every tile (1: none); work unit u = tile u / ksplit, split u % ksplit
+  int units;        // tiles x ksplit
+  float* partials;  // ksplit > 1: [m_tiles * n_tiles][ksplit][128][BN] fp32 accumulator partials
   int* err;
 };
+
+// K-block range of split s of ksplit over kblocks
+__device__ __forceinline__ void gemm_krange(const GemmArgs& a, int s, int* kb0, int* kb1) {
+  *kb0 = (int)((int64_t)s * a.kblocks / a.ksplit);
+  *kb1 = (int)((int64_t)(s + 1) * a.kblocks / a.ksplit);
+}
 
 template <int BN>
 struct GemmLayout {
@@ -91,6 +100,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int cta = blockIdx.x, G = gridDim.x;
+  if (a.ksplit > 1) grid_dep_launch();  // the split-K sum kernel may start; it waits for this grid to end
   if (tid == 0) {
     for (int s = 0; s < nst; ++s) {
       mbar_init(full_bar(s), 1);
@@ -117,11 +127,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
       const uint64_t pol = policy_evict_normal();
       int slot = 0, round = 0, issued = 0;
       bool ok = true;
-      for (int t = cta; t < a.tiles && ok; t += G) {
-        int mt, nt;
-        gemm_tile(a, t, &mt, &nt);
+      for (int u = cta; u < a.units && ok; u += G) {
+        int mt, nt, kb0, kb1;
+        gemm_tile(a, u / a.ksplit, &mt, &nt);
+        gemm_krange(a, u % a.ksplit, &kb0, &kb1);
         const int g0 = nt * (BN / 128);
-        for (int kb = 0; kb < a.kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (round > 0 && !mbar_wait_abort(empty_bar(slot), (round - 1) & 1, a.err, kErrWaitEmpty, abort)) {
             ok = false;
             break;
@@ -151,11 +162,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
       constexpr uint32_t idesc = umma_idesc_bf16(BN);
       int slot = 0, fph = 0, i = 0;
       bool ok = true;
-      for (int t = cta; t < a.tiles && ok; t += G, ++i) {
+      for (int u = cta; u < a.units && ok; u += G, ++i) {
         const int buf = i & 1;
         if (i >= 2 && !mbar_wait_abort(acce_bar(buf), ((i >> 1) - 1) & 1, a.err, kErrWaitFull, abort)) break;
         tc_fence_after();
-        for (int kb = 0; kb < a.kblocks; ++kb) {
+        int kb0, kb1;
+        gemm_krange(a, u % a.ksplit, &kb0, &kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_abort(full_bar(slot), fph, a.err, kErrWaitFull, abort)) {
             ok = false;
             break;
@@ -165,7 +178,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
 #pragma unroll
           for (int j = 0; j < 4; ++j)
             umma_bf16(tmem + buf * BN, umma_desc_sw128(sa + 32 * j), umma_desc_sw128(sb + 32 * j), idesc,
-                      (kb | j) ? 1u : 0u);
+                      (kb > kb0 || j) ? 1u : 0u);
           umma_commit(empty_bar(slot));
           if (++slot == nst) {
             slot = 0;
@@ -178,15 +191,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
   } else {
     // ------------------------------------------------------------ epilogue: thread = token row
     int i = 0;
-    for (int t = cta; t < a.tiles; t += G, ++i) {
+    for (int u = cta; u < a.units; u += G, ++i) {
       const int buf = i & 1;
       if (!mbar_wait_abort(accf_bar(buf), (i >> 1) & 1, a.err, kErrWaitFull, abort)) break;
       tc_fence_after();
+      const int t = u / a.ksplit;
       int mt, nt;
       gemm_tile(a, t, &mt, &nt);
       const int64_t row = (int64_t)mt * 128 + 32 * warp + lane;
       const bool live = row < a.m;
       const uint32_t tb = tmem + ((uint32_t)(32 * warp) << 16) + buf * BN;
+      if (a.ksplit > 1) {
+        // split-K: this split's fp32 accumulator rows go to the partials (live rows only); the sum over
+        // the splits and the epilogue run in gemm_splitk_sum_kernel
+        const int s = u - t * a.ksplit;
+        float* prow =
+            a.partials + ((((int64_t)mt * a.n_tiles + nt) * a.ksplit + s) * 128 + 32 * warp + lane) * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tmem_ld32(tb + c, v);
+          if (!live) continue;
+          float4* d4 = reinterpret_cast<float4*>(prow + c);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            __stcg(d4 + q, make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                       __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acce_bar(buf));
+        continue;
+      }
       if constexpr (EPI == GEMM_SWIGLU) {
         // group g of the interleaved gate/up matrix: 64 gate rows, then the 64 up rows of the same
         // outputs 64g..64g+63
@@ -1052,6 +1088,107 @@ static int gemm_bn(int64_t m, int64_t n) {
   return mt * ((n + 255) / 256) >= host_sm_count() ? 256 : 128;
 }
 
+// ---------------------------------------------------------------- split-K sum + epilogue
+// out = epilogue(sum over splits s = 0, 1, .. of the fp32 partials, in that order): the same bits on every
+// run. Thread (x, y) = four consecutive output columns of one token row: with every split's float4 in
+// flight at once the partials (just written, still in L2) stream at full width. Launched right behind the
+// GEMM (programmatic dependent launch); griddepcontrol.wait holds it until the GEMM's partials are visible.
+constexpr int kMaxKsplit = 16;
+
+struct SplitSumArgs {
+  const float* partials;  // [m_tiles * n_tiles][ksplit][128][bn]
+  __nv_bfloat16* out;
+  const __nv_bfloat16* res;
+  int64_t ldo, ldr;
+  int m, quads;  // token rows; output columns / 4
+  int ksplit, bn_shift, n_tiles;
+};
+
+__device__ __forceinline__ float4 split_sum(const SplitSumArgs& a, int mt, int r, int gc) {
+  const int nt = gc >> a.bn_shift, bn = 1 << a.bn_shift;
+  const float* p = a.partials + ((((int64_t)mt * a.n_tiles + nt) * a.ksplit) * 128 + r) * bn + (gc & (bn - 1));
+  const int64_t sstride = (int64_t)128 * bn;
+  float4 v[kMaxKsplit];
+#pragma unroll
+  for (int s = 0; s < kMaxKsplit; ++s)
+    if (s < a.ksplit) v[s] = __ldcg(reinterpret_cast<const float4*>(p + s * sstride));
+  float4 acc = v[0];
+#pragma unroll
+  for (int s = 1; s < kMaxKsplit; ++s)
+    if (s < a.ksplit) {
+      acc.x += v[s].x;
+      acc.y += v[s].y;
+      acc.z += v[s].z;
+      acc.w += v[s].w;
+    }
+  return acc;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(256) gemm_splitk_sum_kernel(const __grid_constant__ SplitSumArgs a) {
+  grid_dep_wait();
+  const int qd = blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = blockIdx.y * blockDim.y + threadIdx.y;
+  if (qd >= a.quads || row >= a.m) return;
+  const int mt = row >> 7, r = row & 127, o = 4 * qd;  // o: first output column
+  float y[4];
+  if constexpr (EPI == GEMM_SWIGLU) {
+    // output column o of group g = o / 64: gate at weight row 128 g + o % 64, up 64 rows further
+    const int gc = (o >> 6) * 128 + (o & 63);
+    const float4 g4 = split_sum(a, mt, r, gc), u4 = split_sum(a, mt, r, gc + 64);
+    const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float gb = bf16r(gv[e]);
+      y[e] = bf16r(gb / (1.0f + expf(-gb))) * bf16r(uv[e]);
+    }
+  } else {
+    const float4 s4 = split_sum(a, mt, r, o);
+    y[0] = bf16r(s4.x);
+    y[1] = bf16r(s4.y);
+    y[2] = bf16r(s4.z);
+    y[3] = bf16r(s4.w);
+    if constexpr (EPI == GEMM_RES) {
+      const uint2 u = *reinterpret_cast<const uint2*>(a.res + (int64_t)row * a.ldr + o);
+      y[0] += bf_lo(u.x);
+      y[1] += bf_hi(u.x);
+      y[2] += bf_lo(u.y);
+      y[3] += bf_hi(u.y);
+    }
+  }
+  *reinterpret_cast<uint2*>(a.out + (int64_t)row * a.ldo + o) = make_uint2(pack_bf2(y[0], y[1]), pack_bf2(y[2], y[3]));
+}
+
+// Split of K per tile when the tiles alone leave most SMs idle (short prompts): as many splits as keep
+// every unit in one wave (tiles x splits <= SMs), each split at least 8 K-blocks, at most kMaxKsplit.
+// QD_GEMM_KSPLIT forces a split (1 = none). The scratch holds the fp32 partials.
+constexpr int64_t kGemmMaxSplitTiles = 1024;
+struct GemmPlan {
+  int bn, grid, ksplit;
+  int64_t tiles, scratch_bytes;
+};
+static GemmPlan gemm_plan(int64_t m, int64_t n, int64_t k) {
+  GemmPlan p;
+  p.bn = gemm_bn(m, n);
+  p.tiles = ((m + 127) / 128) * ((n + p.bn - 1) / p.bn);
+  const int sms = host_sm_count();
+  const int64_t kblocks = k / 64;
+  int64_t ks = 1;
+  if (p.tiles * 2 <= sms) {
+    ks = sms / p.tiles;
+    if (ks > kblocks / 8) ks = kblocks / 8;
+  }
+  const int forced = env_int("QD_GEMM_KSPLIT", 0);
+  if (forced >= 1) ks = forced > kblocks ? kblocks : forced;
+  if (ks > kMaxKsplit) ks = kMaxKsplit;
+  if (ks < 1 || p.tiles > kGemmMaxSplitTiles) ks = 1;
+  p.ksplit = (int)ks;
+  const int64_t units = p.tiles * ks;
+  p.grid = (int)(units < sms ? units : sms);
+  p.scratch_bytes = ks > 1 ? p.tiles * ks * 128 * p.bn * 4 : 0;
+  return p;
+}
+
 template <int BN, int EPI>
 static int launch_gemm(const GemmArgs& a, int grid, cudaStream_t stream) {
   auto kern = tc_gemm_kernel<BN, EPI>;
@@ -1069,18 +1206,20 @@ static int launch_gemm(const GemmArgs& a, int grid, cudaStream_t stream) {
 
 using namespace qd;
 
-extern "C" int qd_tc_gemm_plan(int64_t m, int64_t n, int64_t k, int* grid, int* bn) {
+extern "C" int qd_tc_gemm_plan(int64_t m, int64_t n, int64_t k, int* grid, int* bn, int* ksplit,
+                               int64_t* scratch_bytes) {
   if (m < 1 || n < 128 || n % 128 || k < 64 || k % 64) return set_error(QD_ERR_ARG, "tc gemm plan: bad sizes");
-  const int b = gemm_bn(m, n);
-  const int64_t tiles = ((m + 127) / 128) * ((n + b - 1) / b);
-  const int64_t g = tiles < host_sm_count() ? tiles : host_sm_count();
-  if (grid) *grid = (int)g;
-  if (bn) *bn = b;
+  const GemmPlan p = gemm_plan(m, n, k);
+  if (grid) *grid = p.grid;
+  if (bn) *bn = p.bn;
+  if (ksplit) *ksplit = p.ksplit;
+  if (scratch_bytes) *scratch_bytes = p.scratch_bytes;
   return QD_OK;
 }
 
 extern "C" int qd_tc_gemm(const void* x, int64_t ldx, int64_t m, const void* w_packed, int64_t n, int64_t k, void* out,
-                          int64_t ldo, const void* res, int64_t ldr, int epilogue, int* err, cudaStream_t stream) {
+                          int64_t ldo, const void* res, int64_t ldr, int epilogue, void* scratch, int64_t scratch_bytes,
+                          int* err, cudaStream_t stream) {
   if (!x || !w_packed || !out) return set_error(QD_ERR_ARG, "null pointer");
   if (m < 1 || n < 128 || n % 128 || k < 64 || k % 64 || ldx < k || ldx % 8 || ldo % 8)
     return set_error(QD_ERR_ARG, "tc gemm: m >= 1, n %% 128 == 0, k %% 64 == 0, ldx >= k, ldx/ldo %% 8 == 0");
@@ -1104,7 +1243,13 @@ extern "C" int qd_tc_gemm(const void* x, int64_t ldx, int64_t m, const void* w_p
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(QD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   }
-  const int bn = gemm_bn(m, n);
+  const GemmPlan gp = gemm_plan(m, n, k);
+  const int bn = gp.bn;
+  if (gp.scratch_bytes > 0 && (!scratch || scratch_bytes < gp.scratch_bytes || !aligned16(scratch)))
+    return set_error(QD_ERR_SCRATCH, "tc gemm: split-K needs %lld B of 16-byte aligned scratch (have %lld)",
+                     (long long)gp.scratch_bytes, (long long)scratch_bytes);
+  a.ksplit = gp.ksplit;
+  a.partials = gp.ksplit > 1 ? static_cast<float*>(scratch) : nullptr;
   a.w = static_cast<const char*>(w_packed);
   a.out = static_cast<__nv_bfloat16*>(out);
   a.res = static_cast<const __nv_bfloat16*>(res);
@@ -1119,18 +1264,39 @@ extern "C" int qd_tc_gemm(const void* x, int64_t ldx, int64_t m, const void* w_p
   const int64_t tiles = (int64_t)a.m_tiles * a.n_tiles;
   if (tiles > INT32_MAX) return set_error(QD_ERR_UNSUPPORTED, "tc gemm: too many tiles");
   a.tiles = (int)tiles;
+  if (tiles * gp.ksplit > INT32_MAX) return set_error(QD_ERR_UNSUPPORTED, "tc gemm: too many work units");
+  a.units = (int)(tiles * gp.ksplit);
   a.err = err;
-  const int grid = a.tiles < host_sm_count() ? a.tiles : host_sm_count();
+  const int grid = gp.grid;
+  int rc;
   if (bn == 256) {
     a.nst = gemm_nst<256>();
-    if (epilogue == GEMM_STORE) return launch_gemm<256, GEMM_STORE>(a, grid, stream);
-    if (epilogue == GEMM_RES) return launch_gemm<256, GEMM_RES>(a, grid, stream);
-    return launch_gemm<256, GEMM_SWIGLU>(a, grid, stream);
+    rc = epilogue == GEMM_STORE ? launch_gemm<256, GEMM_STORE>(a, grid, stream)
+         : epilogue == GEMM_RES ? launch_gemm<256, GEMM_RES>(a, grid, stream)
+                                : launch_gemm<256, GEMM_SWIGLU>(a, grid, stream);
+  } else {
+    a.nst = gemm_nst<128>();
+    rc = epilogue == GEMM_STORE ? launch_gemm<128, GEMM_STORE>(a, grid, stream)
+         : epilogue == GEMM_RES ? launch_gemm<128, GEMM_RES>(a, grid, stream)
+                                : launch_gemm<128, GEMM_SWIGLU>(a, grid, stream);
   }
-  a.nst = gemm_nst<128>();
-  if (epilogue == GEMM_STORE) return launch_gemm<128, GEMM_STORE>(a, grid, stream);
-  if (epilogue == GEMM_RES) return launch_gemm<128, GEMM_RES>(a, grid, stream);
-  return launch_gemm<128, GEMM_SWIGLU>(a, grid, stream);
+  if (rc != QD_OK || gp.ksplit == 1) return rc;
+  SplitSumArgs sa = {};
+  sa.partials = a.partials;
+  sa.out = a.out;
+  sa.res = a.res;
+  sa.ldo = ldo;
+  sa.ldr = ldr;
+  sa.m = (int)m;
+  sa.quads = (int)((epilogue == GEMM_SWIGLU ? n / 2 : n) / 4);
+  sa.ksplit = gp.ksplit;
+  sa.bn_shift = bn == 256 ? 8 : 7;
+  sa.n_tiles = a.n_tiles;
+  const dim3 block(64, 4), sgrid((unsigned)((sa.quads + 63) / 64), (unsigned)((m + 3) / 4));
+  const void* kern = epilogue == GEMM_STORE ? (const void*)gemm_splitk_sum_kernel<GEMM_STORE>
+                     : epilogue == GEMM_RES ? (const void*)gemm_splitk_sum_kernel<GEMM_RES>
+                                            : (const void*)gemm_splitk_sum_kernel<GEMM_SWIGLU>;
+  return launch_kernel(kern, sgrid, block, 0, 1, stream, &sa);
 }
 
 extern "C" int qd_rmsnorm_rows(const void* x, int64_t ldx, int64_t m, int64_t k, const void* norm_w, float eps,

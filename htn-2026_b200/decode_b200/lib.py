@@ -84,9 +84,9 @@ PROTOTYPES = {
     "qd_attn_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64,
                                c_int64, c_int64, c_int, c_int64, c_float, c_void_p, c_int64, c_void_p, c_int,
                                c_void_p]),
-    "qd_tc_gemm_plan": (c_int, [c_int64, c_int64, c_int64, P_INT, P_INT]),
+    "qd_tc_gemm_plan": (c_int, [c_int64, c_int64, c_int64, P_INT, P_INT, P_INT, P_I64]),
     "qd_tc_gemm": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_void_p,
-                           c_int64, c_int, c_void_p, c_void_p]),
+                           c_int64, c_int, c_void_p, c_int64, c_void_p, c_void_p]),
     "qd_rmsnorm_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_float, c_void_p, c_int64, c_void_p]),
     "qd_prefill_qk_rope": (c_int, [c_void_p, c_int64, c_int, c_int64, c_int, c_int, c_void_p, c_void_p, c_float,
                                    c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64,

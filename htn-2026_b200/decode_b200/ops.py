@@ -271,21 +271,27 @@ class TcLmHeadArgmax(_TcOp):
 
 
 # ------------------------------------------------------------------------------------ prompt (prefill)
-def tc_gemm(x, w, n: int, out, res=None, epilogue: int = L.QD_EPI_STORE, err=None):
+def tc_gemm(x, w, n: int, out, res=None, epilogue: int = L.QD_EPI_STORE, err=None, scratch=None):
     """out = epilogue(x @ W^T) on the tensor cores for any number of token rows (qd_tc_gemm): x [m, k]
-    BF16 (unit column stride), W packed [n, k]; SWIGLU writes n / 2 columns."""
+    BF16 (unit column stride), W packed [n, k]; SWIGLU writes n / 2 columns. `scratch` (uint8, at least
+    tc_gemm_plan's bytes, any contents) is needed when the plan splits K; without one a buffer is allocated."""
     _check_bf16(x, w, out, res)
     m, k = x.shape
     assert x.stride(1) == 1 and out.stride(1) == 1 and out.shape[0] == m
+    need = tc_gemm_plan(m, n, k)[3]
+    if need and (scratch is None or scratch.numel() < need):
+        scratch = torch.empty((need,), dtype=torch.uint8, device=x.device)
     L.call("qd_tc_gemm", _ptr(x), x.stride(0), m, _ptr(w), n, k, _ptr(out), out.stride(0), _ptr(res),
-           res.stride(0) if res is not None else 0, epilogue, _ptr(err), _stream())
+           res.stride(0) if res is not None else 0, epilogue, _ptr(scratch) if need else None,
+           scratch.numel() if need else 0, _ptr(err), _stream())
     return out
 
 
-def tc_gemm_plan(m: int, n: int, k: int) -> tuple[int, int]:
-    g, bn = ctypes.c_int(0), ctypes.c_int(0)
-    L.call("qd_tc_gemm_plan", m, n, k, ctypes.byref(g), ctypes.byref(bn))
-    return g.value, bn.value
+def tc_gemm_plan(m: int, n: int, k: int) -> tuple[int, int, int, int]:
+    """(grid, tile width, K split, scratch bytes) of qd_tc_gemm for this shape."""
+    g, bn, ks, nb = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int64(0)
+    L.call("qd_tc_gemm_plan", m, n, k, ctypes.byref(g), ctypes.byref(bn), ctypes.byref(ks), ctypes.byref(nb))
+    return g.value, bn.value, ks.value, nb.value
 
 
 def rmsnorm_rows(x, w, eps: float, out):

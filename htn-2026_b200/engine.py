@@ -232,27 +232,32 @@ class Engine:
             q = torch.empty((M, nq * D), dtype=BF16, device=dev)
             att = torch.empty((M, nq * D), dtype=BF16, device=dev)
             act = torch.empty((M, I), dtype=BF16, device=dev)
+            # one split-K partials scratch for every GEMM of the chunk (they run in stream order)
+            shapes = [(M, n_qkv, H), (M, H, nq * D), (M, 2 * I, H), (M, H, I), (b, H, nq * D), (b, 2 * I, H),
+                      (b, H, I), (b, vrows, H)]
+            nb = max(ops.tc_gemm_plan(*s)[3] for s in shapes)
+            sc = torch.empty((max(nb, 16),), dtype=torch.uint8, device=dev)
             ops.embed(st.ids[r0:r1].reshape(M), self.e_packed, self.vocab, x, err, pdl=False)
             xl, hl = x.view(b, S, H)[:, -1], h[:b]  # the last position of every sequence
             for i in range(self.n_layers):
                 kc, vc = st.k_all[i, r0:r1], st.v_all[i, r0:r1]
                 ops.rmsnorm_rows(x, self.ln1[i], eps, h)
-                ops.tc_gemm(h, self.w_qkv[i], n_qkv, qkv, err=err)
+                ops.tc_gemm(h, self.w_qkv[i], n_qkv, qkv, err=err, scratch=sc)
                 ops.prefill_qk_rope(qkv, b, S, nq, nkv, self.qn[i], self.kn[i], eps, st.cos, st.sin, q, kc, vc)
                 if i == last_layer:  # only the last position continues (engine/engine.py:577-583)
                     ops.prefill_attn(q, b, S, nq, nkv, kc, vc, att[:b], q_begin=S - 1, err=err)
-                    ops.tc_gemm(att[:b], self.w_o[i], H, xl, res=xl, epilogue=RES, err=err)
+                    ops.tc_gemm(att[:b], self.w_o[i], H, xl, res=xl, epilogue=RES, err=err, scratch=sc)
                     ops.rmsnorm_rows(xl, self.ln2[i], eps, hl)
-                    ops.tc_gemm(hl, self.w_gu[i], 2 * I, act[:b], epilogue=SWIGLU, err=err)
-                    ops.tc_gemm(act[:b], self.w_down[i], H, xl, res=xl, epilogue=RES, err=err)
+                    ops.tc_gemm(hl, self.w_gu[i], 2 * I, act[:b], epilogue=SWIGLU, err=err, scratch=sc)
+                    ops.tc_gemm(act[:b], self.w_down[i], H, xl, res=xl, epilogue=RES, err=err, scratch=sc)
                     break
                 ops.prefill_attn(q, b, S, nq, nkv, kc, vc, att, err=err)
-                ops.tc_gemm(att, self.w_o[i], H, x, res=x, epilogue=RES, err=err)
+                ops.tc_gemm(att, self.w_o[i], H, x, res=x, epilogue=RES, err=err, scratch=sc)
                 ops.rmsnorm_rows(x, self.ln2[i], eps, h)
-                ops.tc_gemm(h, self.w_gu[i], 2 * I, act, epilogue=SWIGLU, err=err)
-                ops.tc_gemm(act, self.w_down[i], H, x, res=x, epilogue=RES, err=err)
+                ops.tc_gemm(h, self.w_gu[i], 2 * I, act, epilogue=SWIGLU, err=err, scratch=sc)
+                ops.tc_gemm(act, self.w_down[i], H, x, res=x, epilogue=RES, err=err, scratch=sc)
             ops.rmsnorm_rows(xl, self.final_norm, eps, hl)
-            ops.tc_gemm(hl, self.e_packed, vrows, logits[r0:r1], err=err)
+            ops.tc_gemm(hl, self.e_packed, vrows, logits[r0:r1], err=err, scratch=sc)
         logits = logits[:, :self.vocab]
         st.tok.copy_(torch.argmax(logits, dim=-1))
         return logits

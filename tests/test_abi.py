@@ -88,15 +88,15 @@ def test_prompt_entry_points_validate_arguments(lib):
     P = ctypes.c_void_p
     a, b, c = P(0x10000), P(0x20000), P(0x30000)  # 16-byte aligned stand-ins, never dereferenced
     ERR_ARG = 1
-    # qd_tc_gemm(x, ldx, m, w, n, k, out, ldo, res, ldr, epilogue, err, stream)
-    assert lib.qd_tc_gemm(None, 2560, 8, b, 2560, 2560, c, 2560, None, 0, 0, None, None) == ERR_ARG
-    assert lib.qd_tc_gemm(a, 2560, 0, b, 2560, 2560, c, 2560, None, 0, 0, None, None) == ERR_ARG
-    assert lib.qd_tc_gemm(a, 2560, 8, b, 2500, 2560, c, 2560, None, 0, 0, None, None) == ERR_ARG   # n % 128
-    assert lib.qd_tc_gemm(a, 2560, 8, b, 2560, 2500, c, 2560, None, 0, 0, None, None) == ERR_ARG   # k % 64
-    assert lib.qd_tc_gemm(a, 2560, 8, b, 2560, 2560, c, 2560, None, 0, 7, None, None) == ERR_ARG   # epilogue
-    assert lib.qd_tc_gemm(a, 2560, 8, b, 2560, 2560, c, 2560, None, 0, 1, None, None) == ERR_ARG   # RES, no res
-    assert lib.qd_tc_gemm(P(0x10008), 2560, 8, b, 2560, 2560, c, 2560, None, 0, 0, None, None) == ERR_ARG
-    assert lib.qd_tc_gemm(a, 2560, 8, b, 19456, 2560, c, 9000, None, 0, 2, None, None) == ERR_ARG  # ldo < n/2
+    # qd_tc_gemm(x, ldx, m, w, n, k, out, ldo, res, ldr, epilogue, scratch, scratch_bytes, err, stream)
+    assert lib.qd_tc_gemm(None, 2560, 8, b, 2560, 2560, c, 2560, None, 0, 0, None, 0, None, None) == ERR_ARG
+    assert lib.qd_tc_gemm(a, 2560, 0, b, 2560, 2560, c, 2560, None, 0, 0, None, 0, None, None) == ERR_ARG
+    assert lib.qd_tc_gemm(a, 2560, 8, b, 2500, 2560, c, 2560, None, 0, 0, None, 0, None, None) == ERR_ARG   # n % 128
+    assert lib.qd_tc_gemm(a, 2560, 8, b, 2560, 2500, c, 2560, None, 0, 0, None, 0, None, None) == ERR_ARG   # k % 64
+    assert lib.qd_tc_gemm(a, 2560, 8, b, 2560, 2560, c, 2560, None, 0, 7, None, 0, None, None) == ERR_ARG   # epilogue
+    assert lib.qd_tc_gemm(a, 2560, 8, b, 2560, 2560, c, 2560, None, 0, 1, None, 0, None, None) == ERR_ARG   # RES, no res
+    assert lib.qd_tc_gemm(P(0x10008), 2560, 8, b, 2560, 2560, c, 2560, None, 0, 0, None, 0, None, None) == ERR_ARG
+    assert lib.qd_tc_gemm(a, 2560, 8, b, 19456, 2560, c, 9000, None, 0, 2, None, 0, None, None) == ERR_ARG  # ldo < n/2
     # qd_rmsnorm_rows(x, ldx, m, k, w, eps, out, ldo, stream)
     assert lib.qd_rmsnorm_rows(a, 2560, 4, 2561, b, 1e-6, c, 2560, None) == ERR_ARG
     assert lib.qd_rmsnorm_rows(a, 2560, 4, 2560, None, 1e-6, c, 2560, None) == ERR_ARG
@@ -116,11 +116,17 @@ def test_prompt_entry_points_validate_arguments(lib):
 
 
 def test_tc_gemm_plan_tile_choice(lib):
-    """Prompt GEMM plan: 256-wide weight tiles once they alone give every SM a tile, else 128; one CTA per
-    tile up to one per SM (148 here: no device, the default count)."""
-    g, bn = ctypes.c_int(0), ctypes.c_int(0)
-    assert lib.qd_tc_gemm_plan(16384, 19456, 2560, ctypes.byref(g), ctypes.byref(bn)) == 0
-    assert bn.value == 256 and g.value == 148
-    assert lib.qd_tc_gemm_plan(128, 2560, 4096, ctypes.byref(g), ctypes.byref(bn)) == 0
-    assert bn.value == 128 and g.value == 20
-    assert lib.qd_tc_gemm_plan(1, 100, 64, ctypes.byref(g), ctypes.byref(bn)) == 1
+    """Prompt GEMM plan: 256-wide weight tiles once they alone give every SM a tile, else 128; K split
+    across CTAs when the tiles leave most SMs idle (as many splits as fit one wave, >= 8 K-blocks a
+    split), the fp32 partials in scratch; 148 SMs here (no device: the default count)."""
+    g, bn, ks, nb = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int64(0)
+    args = (ctypes.byref(g), ctypes.byref(bn), ctypes.byref(ks), ctypes.byref(nb))
+    assert lib.qd_tc_gemm_plan(16384, 19456, 2560, *args) == 0
+    assert (bn.value, g.value, ks.value, nb.value) == (256, 148, 1, 0)
+    assert lib.qd_tc_gemm_plan(128, 2560, 4096, *args) == 0          # O of a 128-token prompt: 20 tiles
+    assert (bn.value, ks.value, g.value, nb.value) == (128, 7, 140, 20 * 7 * 128 * 128 * 4)
+    assert lib.qd_tc_gemm_plan(128, 6144, 2560, *args) == 0          # QKV: 48 tiles, 40 K-blocks
+    assert (ks.value, g.value) == (3, 144)
+    assert lib.qd_tc_gemm_plan(1, 2560, 640, *args) == 0             # 10 K-blocks: no split
+    assert (ks.value, nb.value) == (1, 0)
+    assert lib.qd_tc_gemm_plan(1, 100, 64, *args) == 1

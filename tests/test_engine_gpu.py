@@ -142,10 +142,13 @@ def test_poisoned_cache_slots_are_never_read(engines):
 def test_prefill_row_chunks_are_bit_identical(engines, monkeypatch):
     """A prompt batch over one prefill chunk (at most 16384 tokens per chunk, engine/engine.py:79, :189)
     runs as several chunks of whole sequences. Every prompt kernel is row-independent and deterministic,
-    so the first-token logits, the cache and the decoded logits equal the one-chunk run's bit for bit."""
+    so the first-token logits, the cache and the decoded logits equal the one-chunk run's bit for bit.
+    The GEMMs' K split is chosen from the chunk's token count (it changes the fp32 summation order), so
+    it is pinned to none here."""
     import engine as E
     from decode_b200 import synth
 
+    monkeypatch.setenv("QD_GEMM_KSPLIT", "1")
     eng, _, cfg = engines(2)
     p = synth.random_prompt(5, 40, cfg["vocab_size"], seed=41)
     eng.state = None

@@ -64,10 +64,69 @@ def test_tc_gemm_store(m, n, k, bn, monkeypatch):
 def test_tc_gemm_plan_picks_wide_tiles_for_large_prompts():
     ops = _ops()
     sms = ops.sm_count()
-    grid, bn = ops.tc_gemm_plan(16384, 19456, 2560)
-    assert bn == 256 and grid == sms
-    grid, bn = ops.tc_gemm_plan(128, 2560, 4096)
-    assert bn == 128 and grid == 20
+    grid, bn, ks, nb = ops.tc_gemm_plan(16384, 19456, 2560)
+    assert bn == 256 and grid == sms and ks == 1 and nb == 0
+    grid, bn, ks, nb = ops.tc_gemm_plan(128, 2560, 4096)
+    assert bn == 128 and ks > 1 and grid == min(sms, 20 * ks) and nb > 0
+
+
+@pytest.mark.parametrize("ksplit", ["", "2", "3"])
+@pytest.mark.parametrize("m,n,k,epi", [(128, 2560, 4096, "res"), (1, 2560, 9728, "res"), (77, 6144, 2560, "store"),
+                                       (128, 19456, 2560, "swiglu"), (300, 2560, 640, "store")])
+def test_tc_gemm_split_k(m, n, k, epi, ksplit, monkeypatch):
+    """K split across CTAs (the plan's own choice, or forced): every tile's fp32 partials summed in split
+    order by the second launch, then the same epilogues; deterministic on a reused scratch."""
+    if ksplit:
+        monkeypatch.setenv("QD_GEMM_KSPLIT", ksplit)
+    ops = _ops()
+    g = torch.Generator().manual_seed(m + n + k)
+    x, w = _rand((m, k), 1.0, g), _rand((n, k), 0.02, g)
+    _, _, ks, nb = ops.tc_gemm_plan(m, n, k)
+    scratch = torch.full((max(nb, 1),), 0x7F, dtype=torch.uint8, device=DEV)  # contents do not matter
+    xd = x.to(DEV)
+    if epi == "swiglu":
+        inter = n // 2
+        wp = ops.pack_gate_up(w[:inter].to(DEV), w[inter:].to(DEV))
+        outs = [torch.empty((m, inter), dtype=BF16, device=DEV) for _ in range(2)]
+        for o in outs:
+            ops.tc_gemm(xd, wp, n, o, epilogue=ops.Gemv.SWIGLU, scratch=scratch)
+        gu = _ref(x, w).to(BF16)
+        gv, uv = gu[:, :inter].float().cpu(), gu[:, inter:].float().cpu()
+        sv = torch.nn.functional.silu(gv)
+        _assert_close(outs[0], Q.swiglu(gu.cpu(), inter), extra=(1.1 * gv.abs() * uv.abs() + sv.abs() * uv.abs()),
+                      rtol=2.0 ** -6)
+    elif epi == "res":
+        wp = ops.pack_matrix(w.to(DEV))
+        res = _rand((m, n), 1.0, g).to(DEV)
+        outs = [res.clone() for _ in range(2)]
+        for o in outs:
+            ops.tc_gemm(xd, wp, n, o, res=o, epilogue=ops.Gemv.RES, scratch=scratch)
+        y = _ref(x, w).to(BF16).float()
+        _assert_close(outs[0], (res.float() + y).to(BF16), extra=y)
+    else:
+        wp = ops.pack_matrix(w.to(DEV))
+        outs = [torch.empty((m, n), dtype=BF16, device=DEV) for _ in range(2)]
+        for o in outs:
+            ops.tc_gemm(xd, wp, n, o, scratch=scratch)
+        _assert_close(outs[0], _ref(x, w).to(BF16))
+    assert torch.equal(outs[0], outs[1])
+
+
+def test_tc_gemm_split_k_scratch_shared_across_shapes():
+    """One scratch (arbitrary contents) serves split-K launches of different shapes in stream order, as
+    the prompt forward uses it: each gives the bits of a launch on a fresh scratch."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(11)
+    shapes = [(128, 2560, 4096), (128, 6144, 2560), (1, 2560, 9728), (40, 2560, 1280), (128, 2560, 4096)]
+    plans = [ops.tc_gemm_plan(*s) for s in shapes]
+    assert all(p[2] > 1 for p in plans)
+    shared = torch.full((max(p[3] for p in plans),), 0xA5, dtype=torch.uint8, device=DEV)
+    for (m, n, k), (_, _, _, nb) in zip(shapes, plans):
+        x, w = _rand((m, k), 1.0, g).to(DEV), ops.pack_matrix(_rand((n, k), 0.02, g).to(DEV))
+        a = ops.tc_gemm(x, w, n, torch.empty((m, n), dtype=BF16, device=DEV), scratch=shared)
+        b = ops.tc_gemm(x, w, n, torch.empty((m, n), dtype=BF16, device=DEV),
+                        scratch=torch.zeros((nb,), dtype=torch.uint8, device=DEV))
+        assert torch.equal(a, b), (m, n, k)
 
 
 @pytest.mark.parametrize("bn", ["128", "256"])
