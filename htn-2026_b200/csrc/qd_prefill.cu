@@ -39,16 +39,27 @@ struct alignas(64) GemmArgs {
   const __nv_bfloat16* res;
   int64_t ldo, ldr, m, n;
   int kblocks, ngroups, m_tiles, n_tiles, tiles, nst;
-  int ksplit;       // K split of every tile (1: none); work unit u = tile u / ksplit, split u % ksplit
-  int units;        // tiles x ksplit
-  float* partials;  // ksplit > 1: [m_tiles * n_tiles][ksplit][128][BN] fp32 accumulator partials
+  // work units: tiles [0, full_tiles) whole (unit u = tile u), then every later tile in ksplit K-ranges
+  // (unit full_tiles + j * ksplit + s = split s of tile full_tiles + j)
+  int full_tiles, ksplit, units;
+  float* partials;  // [tiles - full_tiles][ksplit][128][BN] fp32 accumulator partials of the split tiles
   int* err;
 };
 
-// K-block range of split s of ksplit over kblocks
-__device__ __forceinline__ void gemm_krange(const GemmArgs& a, int s, int* kb0, int* kb1) {
-  *kb0 = (int)((int64_t)s * a.kblocks / a.ksplit);
-  *kb1 = (int)((int64_t)(s + 1) * a.kblocks / a.ksplit);
+// unit u -> tile t, split s (-1: the whole tile) and its K-block range [kb0, kb1)
+__device__ __forceinline__ void gemm_unit(const GemmArgs& a, int u, int* t, int* s, int* kb0, int* kb1) {
+  if (u < a.full_tiles) {
+    *t = u;
+    *s = -1;
+    *kb0 = 0;
+    *kb1 = a.kblocks;
+    return;
+  }
+  const int v = u - a.full_tiles, j = v / a.ksplit, sp = v - j * a.ksplit;
+  *t = a.full_tiles + j;
+  *s = sp;
+  *kb0 = (int)((int64_t)sp * a.kblocks / a.ksplit);
+  *kb1 = (int)((int64_t)(sp + 1) * a.kblocks / a.ksplit);
 }
 
 template <int BN>
@@ -69,11 +80,11 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 
 // tile index -> (token tile, weight tile): groups of kGroupM token tiles, weight tiles outer within
 // a group
-__device__ __forceinline__ void gemm_tile(const GemmArgs& a, int t, int* mt, int* nt) {
-  const int per_group = kGroupM * a.n_tiles;
+__device__ __forceinline__ void gemm_tile(int m_tiles, int n_tiles, int t, int* mt, int* nt) {
+  const int per_group = kGroupM * n_tiles;
   const int grp = t / per_group, rem = t - grp * per_group;
   const int m0 = grp * kGroupM;
-  const int gm = (a.m_tiles - m0) < kGroupM ? (a.m_tiles - m0) : kGroupM;
+  const int gm = (m_tiles - m0) < kGroupM ? (m_tiles - m0) : kGroupM;
   *mt = m0 + rem % gm;
   *nt = rem / gm;
 }
@@ -128,9 +139,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
       int slot = 0, round = 0, issued = 0;
       bool ok = true;
       for (int u = cta; u < a.units && ok; u += G) {
-        int mt, nt, kb0, kb1;
-        gemm_tile(a, u / a.ksplit, &mt, &nt);
-        gemm_krange(a, u % a.ksplit, &kb0, &kb1);
+        int t, sp, mt, nt, kb0, kb1;
+        gemm_unit(a, u, &t, &sp, &kb0, &kb1);
+        gemm_tile(a.m_tiles, a.n_tiles, t, &mt, &nt);
         const int g0 = nt * (BN / 128);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (round > 0 && !mbar_wait_abort(empty_bar(slot), (round - 1) & 1, a.err, kErrWaitEmpty, abort)) {
@@ -166,8 +177,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
         const int buf = i & 1;
         if (i >= 2 && !mbar_wait_abort(acce_bar(buf), ((i >> 1) - 1) & 1, a.err, kErrWaitFull, abort)) break;
         tc_fence_after();
-        int kb0, kb1;
-        gemm_krange(a, u % a.ksplit, &kb0, &kb1);
+        int t, sp, kb0, kb1;
+        gemm_unit(a, u, &t, &sp, &kb0, &kb1);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_abort(full_bar(slot), fph, a.err, kErrWaitFull, abort)) {
             ok = false;
@@ -195,18 +206,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
       const int buf = i & 1;
       if (!mbar_wait_abort(accf_bar(buf), (i >> 1) & 1, a.err, kErrWaitFull, abort)) break;
       tc_fence_after();
-      const int t = u / a.ksplit;
-      int mt, nt;
-      gemm_tile(a, t, &mt, &nt);
+      int t, sp, kb0, kb1, mt, nt;
+      gemm_unit(a, u, &t, &sp, &kb0, &kb1);
+      gemm_tile(a.m_tiles, a.n_tiles, t, &mt, &nt);
       const int64_t row = (int64_t)mt * 128 + 32 * warp + lane;
       const bool live = row < a.m;
       const uint32_t tb = tmem + ((uint32_t)(32 * warp) << 16) + buf * BN;
-      if (a.ksplit > 1) {
+      if (sp >= 0) {
         // split-K: this split's fp32 accumulator rows go to the partials (live rows only); the sum over
         // the splits and the epilogue run in gemm_splitk_sum_kernel
-        const int s = u - t * a.ksplit;
         float* prow =
-            a.partials + ((((int64_t)mt * a.n_tiles + nt) * a.ksplit + s) * 128 + 32 * warp + lane) * BN;
+            a.partials + (((int64_t)(t - a.full_tiles) * a.ksplit + sp) * 128 + 32 * warp + lane) * BN;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t v[32];
@@ -1089,25 +1099,24 @@ static int gemm_bn(int64_t m, int64_t n) {
 }
 
 // ---------------------------------------------------------------- split-K sum + epilogue
-// out = epilogue(sum over splits s = 0, 1, .. of the fp32 partials, in that order): the same bits on every
-// run. Thread (x, y) = four consecutive output columns of one token row: with every split's float4 in
-// flight at once the partials (just written, still in L2) stream at full width. Launched right behind the
-// GEMM (programmatic dependent launch); griddepcontrol.wait holds it until the GEMM's partials are visible.
+// For every split tile: out = epilogue(sum over splits s = 0, 1, .. of the fp32 partials, in that order),
+// the same bits on every run. Block (x, y) = 256 threads over output quads (four consecutive columns) of
+// split tile y, quad-fastest within a row; every split's float4 is in flight at once, so the partials
+// (just written, still in L2) stream at full width. Launched right behind the GEMM (programmatic
+// dependent launch); griddepcontrol.wait holds it until the GEMM's partials are visible.
 constexpr int kMaxKsplit = 16;
 
 struct SplitSumArgs {
-  const float* partials;  // [m_tiles * n_tiles][ksplit][128][bn]
+  const float* partials;  // [split tiles][ksplit][128][bn]
   __nv_bfloat16* out;
   const __nv_bfloat16* res;
-  int64_t ldo, ldr;
-  int m, quads;  // token rows; output columns / 4
-  int ksplit, bn_shift, n_tiles;
+  int64_t ldo, ldr, m, n;
+  int full_tiles, m_tiles, n_tiles, ngroups, ksplit;
+  int bn_shift, qpt_shift;  // log2 tile width; log2 output quads per tile row
 };
 
-__device__ __forceinline__ float4 split_sum(const SplitSumArgs& a, int mt, int r, int gc) {
-  const int nt = gc >> a.bn_shift, bn = 1 << a.bn_shift;
-  const float* p = a.partials + ((((int64_t)mt * a.n_tiles + nt) * a.ksplit) * 128 + r) * bn + (gc & (bn - 1));
-  const int64_t sstride = (int64_t)128 * bn;
+__device__ __forceinline__ float4 split_sum(const SplitSumArgs& a, const float* p) {
+  const int64_t sstride = (int64_t)128 << a.bn_shift;
   float4 v[kMaxKsplit];
 #pragma unroll
   for (int s = 0; s < kMaxKsplit; ++s)
@@ -1127,45 +1136,58 @@ __device__ __forceinline__ float4 split_sum(const SplitSumArgs& a, int mt, int r
 template <int EPI>
 __global__ void __launch_bounds__(256) gemm_splitk_sum_kernel(const __grid_constant__ SplitSumArgs a) {
   grid_dep_wait();
-  const int qd = blockIdx.x * blockDim.x + threadIdx.x;
-  const int row = blockIdx.y * blockDim.y + threadIdx.y;
-  if (qd >= a.quads || row >= a.m) return;
-  const int mt = row >> 7, r = row & 127, o = 4 * qd;  // o: first output column
+  const int j = blockIdx.y;
+  const int idx = blockIdx.x * 256 + threadIdx.x;
+  const int r = idx >> a.qpt_shift, oc = (idx - (r << a.qpt_shift)) * 4;  // tile row; first output column
+  if (r >= 128) return;
+  int mt, nt;
+  gemm_tile(a.m_tiles, a.n_tiles, a.full_tiles + j, &mt, &nt);
+  const int64_t row = (int64_t)mt * 128 + r;
+  if (row >= a.m) return;
+  const int bn = 1 << a.bn_shift;
+  const float* pt = a.partials + (((int64_t)j * a.ksplit) * 128 + r) * bn;
   float y[4];
+  int64_t col;
   if constexpr (EPI == GEMM_SWIGLU) {
-    // output column o of group g = o / 64: gate at weight row 128 g + o % 64, up 64 rows further
-    const int gc = (o >> 6) * 128 + (o & 63);
-    const float4 g4 = split_sum(a, mt, r, gc), u4 = split_sum(a, mt, r, gc + 64);
+    // tile output column oc: group h = oc / 64 of the tile, gate at tile column 128 h + oc % 64, up 64 further
+    const int h = oc >> 6, jj = oc & 63, g = nt * (bn >> 7) + h;
+    if (g >= a.ngroups) return;  // the repeated last group of an odd group count
+    const float4 g4 = split_sum(a, pt + h * 128 + jj), u4 = split_sum(a, pt + h * 128 + 64 + jj);
     const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float gb = bf16r(gv[e]);
       y[e] = bf16r(gb / (1.0f + expf(-gb))) * bf16r(uv[e]);
     }
+    col = (int64_t)g * 64 + jj;
   } else {
-    const float4 s4 = split_sum(a, mt, r, o);
+    col = (int64_t)nt * bn + oc;
+    if (col >= a.n) return;
+    const float4 s4 = split_sum(a, pt + oc);
     y[0] = bf16r(s4.x);
     y[1] = bf16r(s4.y);
     y[2] = bf16r(s4.z);
     y[3] = bf16r(s4.w);
     if constexpr (EPI == GEMM_RES) {
-      const uint2 u = *reinterpret_cast<const uint2*>(a.res + (int64_t)row * a.ldr + o);
+      const uint2 u = *reinterpret_cast<const uint2*>(a.res + row * a.ldr + col);
       y[0] += bf_lo(u.x);
       y[1] += bf_hi(u.x);
       y[2] += bf_lo(u.y);
       y[3] += bf_hi(u.y);
     }
   }
-  *reinterpret_cast<uint2*>(a.out + (int64_t)row * a.ldo + o) = make_uint2(pack_bf2(y[0], y[1]), pack_bf2(y[2], y[3]));
+  *reinterpret_cast<uint2*>(a.out + row * a.ldo + col) = make_uint2(pack_bf2(y[0], y[1]), pack_bf2(y[2], y[3]));
 }
 
-// Split of K per tile when the tiles alone leave most SMs idle (short prompts): as many splits as keep
-// every unit in one wave (tiles x splits <= SMs), each split at least 8 K-blocks, at most kMaxKsplit.
-// QD_GEMM_KSPLIT forces a split (1 = none). The scratch holds the fp32 partials.
+// Stream-K style plan: the tiles that fill whole waves (tiles / SMs of them, x SMs) run whole; the tiles of
+// the last, partial wave are split along K into as many ranges as keep them in one wave (at most SMs /
+// remaining tiles, each >= 8 K-blocks, at most kMaxKsplit), so a short prompt's few tiles, or a ragged
+// last wave, still spread over every SM. QD_GEMM_KSPLIT forces the split of every tile (1 = none).
+// The scratch holds the split tiles' fp32 partials.
 constexpr int64_t kGemmMaxSplitTiles = 1024;
 struct GemmPlan {
   int bn, grid, ksplit;
-  int64_t tiles, scratch_bytes;
+  int64_t tiles, full_tiles, scratch_bytes;
 };
 static GemmPlan gemm_plan(int64_t m, int64_t n, int64_t k) {
   GemmPlan p;
@@ -1173,19 +1195,24 @@ static GemmPlan gemm_plan(int64_t m, int64_t n, int64_t k) {
   p.tiles = ((m + 127) / 128) * ((n + p.bn - 1) / p.bn);
   const int sms = host_sm_count();
   const int64_t kblocks = k / 64;
-  int64_t ks = 1;
-  if (p.tiles * 2 <= sms) {
-    ks = sms / p.tiles;
-    if (ks > kblocks / 8) ks = kblocks / 8;
-  }
+  const int64_t rem = p.tiles % sms;
+  int64_t ks = rem ? sms / rem : 1;
+  if (ks > kblocks / 8) ks = kblocks / 8;
+  p.full_tiles = p.tiles - rem;
   const int forced = env_int("QD_GEMM_KSPLIT", 0);
-  if (forced >= 1) ks = forced > kblocks ? kblocks : forced;
+  if (forced >= 1) {
+    ks = forced > kblocks ? kblocks : forced;
+    p.full_tiles = 0;
+  }
   if (ks > kMaxKsplit) ks = kMaxKsplit;
-  if (ks < 1 || p.tiles > kGemmMaxSplitTiles) ks = 1;
+  if (ks < 2 || p.tiles - p.full_tiles > kGemmMaxSplitTiles) {
+    ks = 1;
+    p.full_tiles = p.tiles;
+  }
   p.ksplit = (int)ks;
-  const int64_t units = p.tiles * ks;
+  const int64_t units = p.full_tiles + (p.tiles - p.full_tiles) * ks;
   p.grid = (int)(units < sms ? units : sms);
-  p.scratch_bytes = ks > 1 ? p.tiles * ks * 128 * p.bn * 4 : 0;
+  p.scratch_bytes = ks > 1 ? (p.tiles - p.full_tiles) * ks * 128 * p.bn * 4 : 0;
   return p;
 }
 
@@ -1264,8 +1291,10 @@ extern "C" int qd_tc_gemm(const void* x, int64_t ldx, int64_t m, const void* w_p
   const int64_t tiles = (int64_t)a.m_tiles * a.n_tiles;
   if (tiles > INT32_MAX) return set_error(QD_ERR_UNSUPPORTED, "tc gemm: too many tiles");
   a.tiles = (int)tiles;
-  if (tiles * gp.ksplit > INT32_MAX) return set_error(QD_ERR_UNSUPPORTED, "tc gemm: too many work units");
-  a.units = (int)(tiles * gp.ksplit);
+  const int64_t units = gp.full_tiles + (tiles - gp.full_tiles) * gp.ksplit;
+  if (units > INT32_MAX) return set_error(QD_ERR_UNSUPPORTED, "tc gemm: too many work units");
+  a.full_tiles = (int)gp.full_tiles;
+  a.units = (int)units;
   a.err = err;
   const int grid = gp.grid;
   int rc;
@@ -1287,12 +1316,16 @@ extern "C" int qd_tc_gemm(const void* x, int64_t ldx, int64_t m, const void* w_p
   sa.res = a.res;
   sa.ldo = ldo;
   sa.ldr = ldr;
-  sa.m = (int)m;
-  sa.quads = (int)((epilogue == GEMM_SWIGLU ? n / 2 : n) / 4);
+  sa.m = m;
+  sa.n = n;
+  sa.full_tiles = a.full_tiles;
+  sa.m_tiles = a.m_tiles;
+  sa.n_tiles = a.n_tiles;
+  sa.ngroups = a.ngroups;
   sa.ksplit = gp.ksplit;
   sa.bn_shift = bn == 256 ? 8 : 7;
-  sa.n_tiles = a.n_tiles;
-  const dim3 block(64, 4), sgrid((unsigned)((sa.quads + 63) / 64), (unsigned)((m + 3) / 4));
+  sa.qpt_shift = sa.bn_shift - (epilogue == GEMM_SWIGLU ? 3 : 2);  // BN / 8 or BN / 4 quads per tile row
+  const dim3 block(256), sgrid((unsigned)((128 << sa.qpt_shift) / 256), (unsigned)(tiles - gp.full_tiles));
   const void* kern = epilogue == GEMM_STORE ? (const void*)gemm_splitk_sum_kernel<GEMM_STORE>
                      : epilogue == GEMM_RES ? (const void*)gemm_splitk_sum_kernel<GEMM_RES>
                                             : (const void*)gemm_splitk_sum_kernel<GEMM_SWIGLU>;

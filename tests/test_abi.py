@@ -117,8 +117,8 @@ def test_prompt_entry_points_validate_arguments(lib):
 
 def test_tc_gemm_plan_tile_choice(lib):
     """Prompt GEMM plan: 256-wide weight tiles once they alone give every SM a tile, else 128; K split
-    across CTAs when the tiles leave most SMs idle (as many splits as fit one wave, >= 8 K-blocks a
-    split), the fp32 partials in scratch; 148 SMs here (no device: the default count)."""
+    across CTAs for the tiles of the last, partial wave (as many splits as fit one wave, >= 8 K-blocks a
+    split), their fp32 partials in scratch; 148 SMs here (no device: the default count)."""
     g, bn, ks, nb = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int64(0)
     args = (ctypes.byref(g), ctypes.byref(bn), ctypes.byref(ks), ctypes.byref(nb))
     assert lib.qd_tc_gemm_plan(16384, 19456, 2560, *args) == 0
@@ -129,4 +129,6 @@ def test_tc_gemm_plan_tile_choice(lib):
     assert (ks.value, g.value) == (3, 144)
     assert lib.qd_tc_gemm_plan(1, 2560, 640, *args) == 0             # 10 K-blocks: no split
     assert (ks.value, nb.value) == (1, 0)
+    assert lib.qd_tc_gemm_plan(1024, 2560, 9728, *args) == 0         # 160 tiles: 148 whole, the last 12 split
+    assert (bn.value, ks.value, g.value, nb.value) == (128, 12, 148, 12 * 12 * 128 * 128 * 4)
     assert lib.qd_tc_gemm_plan(1, 100, 64, *args) == 1

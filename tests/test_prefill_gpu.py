@@ -70,14 +70,25 @@ def test_tc_gemm_plan_picks_wide_tiles_for_large_prompts():
     assert bn == 128 and ks > 1 and grid == min(sms, 20 * ks) and nb > 0
 
 
-@pytest.mark.parametrize("ksplit", ["", "2", "3"])
-@pytest.mark.parametrize("m,n,k,epi", [(128, 2560, 4096, "res"), (1, 2560, 9728, "res"), (77, 6144, 2560, "store"),
-                                       (128, 19456, 2560, "swiglu"), (300, 2560, 640, "store")])
+SPLIT_CASES = [("", 128, 2560, 4096, "res"), ("", 1, 2560, 9728, "res"), ("", 77, 6144, 2560, "store"),
+               ("", 128, 19456, 2560, "swiglu"), ("", 300, 2560, 640, "store"),
+               # whole waves of whole tiles, then the last wave's tiles split (hybrid)
+               ("", 1024, 2560, 9728, "res"), ("", 1000, 2560, 4096, "store"), ("", 1024, 19456, 2560, "swiglu"),
+               ("", 1100, 6144, 2560, "store")]
+SPLIT_CASES += [(ks, m, n, k, e) for ks in ("2", "3") for (_, m, n, k, e) in SPLIT_CASES[:5]]
+# 256-wide tiles over an odd group count: the repeated last group is never stored
+SPLIT_CASES += [("2/256", 77, 384, 1280, "store"), ("3/256", 130, 384, 1280, "swiglu")]
+
+
+@pytest.mark.parametrize("ksplit,m,n,k,epi", SPLIT_CASES)
 def test_tc_gemm_split_k(m, n, k, epi, ksplit, monkeypatch):
-    """K split across CTAs (the plan's own choice, or forced): every tile's fp32 partials summed in split
-    order by the second launch, then the same epilogues; deterministic on a reused scratch."""
+    """K split across CTAs (the plan's own choice, or forced): the split tiles' fp32 partials summed in
+    split order by the second launch, then the same epilogues; deterministic on a reused scratch."""
     if ksplit:
-        monkeypatch.setenv("QD_GEMM_KSPLIT", ksplit)
+        ks_env, _, bn_env = ksplit.partition("/")
+        monkeypatch.setenv("QD_GEMM_KSPLIT", ks_env)
+        if bn_env:
+            monkeypatch.setenv("QD_GEMM_BN", bn_env)
     ops = _ops()
     g = torch.Generator().manual_seed(m + n + k)
     x, w = _rand((m, k), 1.0, g), _rand((n, k), 0.02, g)
@@ -171,8 +182,9 @@ def test_tc_gemm_swiglu_gate_up(m, bn, monkeypatch):
 
 
 def test_tc_gemm_deterministic_and_tile_width_independent(monkeypatch):
-    """Each output is one tile's fp32 accumulation in K order: the same bits for either tile width and
-    on every run."""
+    """Without a K split each output is one tile's fp32 accumulation in K order: the same bits for either
+    tile width and on every run."""
+    monkeypatch.setenv("QD_GEMM_KSPLIT", "1")
     ops = _ops()
     g = torch.Generator().manual_seed(5)
     m, n, k = 2000, 6144, 2560
