@@ -542,6 +542,30 @@ def _time_cycle(fn, copies, launches):
     return s.elapsed_time(e) / launches
 
 
+def _time_graph(fn, copies, launches):
+    """Average device time of fn(i) in ms with the launches captured in one CUDA graph (as the engine
+    replays them: no host launch cost), cycling over `copies` operand sets."""
+    import torch
+
+    for i in range(min(3, launches)):
+        fn(i % copies)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(launches):
+            fn(i % copies)
+    g.replay()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(3):
+        g.replay()
+    e.record()
+    e.synchronize()
+    del g
+    return s.elapsed_time(e) / (3 * launches)
+
+
 def run_sweep_linear(a):
     """the five decode projections (K -> N) at M in {1, 4, 16, 64}, each with its plain
     BF16 store and with its fused epilogue, on three paths:
@@ -719,7 +743,8 @@ def run_sweep_prefill(a):
     """Prompt projections (prefill, engine/engine.py:550-592) at M tokens in {128, 1024, 16384} (the
     prompt of config 1, one config-4 sequence, a full 16384-token prefill chunk): qd_tc_gemm over the
     packed weights (plain store and fused epilogue) against cuBLAS (torch.matmul on row-major
-    weights, store only). Flops = 2MNK, against the measured dense BF16 peak. Then the engine's whole
+    weights, store only), each timed as a CUDA graph replay over weight copies that exceed the L2.
+    Flops = 2MNK, against the measured dense BF16 peak. Then the engine's whole
     prompt forward for configs 1 and 4 (one GPU's shard: 8 x 1024), timed by CUDA events around the
     prefill graph."""
     import torch
@@ -735,24 +760,27 @@ def run_sweep_prefill(a):
     err = torch.zeros((1,), dtype=torch.int32, device=dev)
     launches = max(a.launches, 12)
     for name, n, k in shapes:
-        w = (torch.randn((n, k), generator=g, device=dev) * 0.02).to(torch.bfloat16)
-        wp = ops.pack_matrix(w)
+        # enough weight copies to exceed twice the L2, so every launch streams its weights from HBM as the
+        # prompt forward's layers do
+        copies = max(1, -(-2 * 126 * 2 ** 20 // (2 * n * k)))
+        ws = [(torch.randn((n, k), generator=g, device=dev) * 0.02).to(torch.bfloat16) for _ in range(copies)]
+        wps = [ops.pack_matrix(w) for w in ws]
         for M in (128, 1024, 16384):
             x = torch.randn((M, k), generator=g, device=dev).to(torch.bfloat16)
             out = torch.empty((M, n), dtype=torch.bfloat16, device=dev)
             epi = {"o": ops.Gemv.RES, "down": ops.Gemv.RES, "gu": ops.Gemv.SWIGLU}.get(name, ops.Gemv.STORE)
             grid, bn, ks, nb = ops.tc_gemm_plan(M, n, k)
             sc = torch.zeros((max(nb, 1),), dtype=torch.uint8, device=dev)
-            cases = [("tc_gemm", "store", lambda i: ops.tc_gemm(x, wp, n, out, err=err, scratch=sc))]
+            cases = [("tc_gemm", "store", lambda i: ops.tc_gemm(x, wps[i], n, out, err=err, scratch=sc))]
             if epi == ops.Gemv.RES:
-                cases.append(("tc_gemm", "fused", lambda i: ops.tc_gemm(x, wp, n, out, res=out, epilogue=epi, err=err,
-                                                                       scratch=sc)))
-            elif epi == ops.Gemv.SWIGLU:
-                cases.append(("tc_gemm", "fused", lambda i: ops.tc_gemm(x, wp, n, out[:, : n // 2], epilogue=epi,
+                cases.append(("tc_gemm", "fused", lambda i: ops.tc_gemm(x, wps[i], n, out, res=out, epilogue=epi,
                                                                        err=err, scratch=sc)))
-            cases.append(("cublas", "store", lambda i: torch.matmul(x, w.t(), out=out)))
+            elif epi == ops.Gemv.SWIGLU:
+                cases.append(("tc_gemm", "fused", lambda i: ops.tc_gemm(x, wps[i], n, out[:, : n // 2], epilogue=epi,
+                                                                       err=err, scratch=sc)))
+            cases.append(("cublas", "store", lambda i: torch.matmul(x, ws[i].t(), out=out)))
             for path, ep, fn in cases:
-                ms = _time_cycle(fn, 1, launches)
+                ms = _time_graph(fn, copies, max(launches, copies))
                 tf = 2 * M * n * k / (ms / 1e3) / 1e12
                 print(json.dumps({"sweep": "prefill", "shape": name, "n": n, "k": k, "M": M, "path": path,
                                   "epilogue": ep, "tile_n": bn if path == "tc_gemm" else None,
@@ -762,7 +790,7 @@ def run_sweep_prefill(a):
                                   "peak_tflops": tpeak}), flush=True)
             assert int(err.item()) == 0
             del x, out
-        del w, wp
+        del ws, wps
         torch.cuda.empty_cache()
     # causal prompt attention: qd_prefill_attn against PyTorch's flash SDPA (the reference's call)
     nq, nkv, D = 32, 8, 128
@@ -776,7 +804,7 @@ def run_sweep_prefill(a):
         for path, fn in (("qd_prefill_attn", lambda i: ops.prefill_attn(q, b, S, nq, nkv, kc, vc, out, err=err)),
                          ("torch_flash_sdpa", lambda i: torch.nn.functional.scaled_dot_product_attention(
                              q4, kc, vc, is_causal=True, scale=D ** -0.5, enable_gqa=True))):
-            ms = _time_cycle(fn, 1, launches)
+            ms = _time_graph(fn, 1, launches)
             tf = flops / (ms / 1e3) / 1e12
             print(json.dumps({"sweep": "prefill_attn", "batch": b, "prompt": S, "path": path, "us": round(ms * 1e3, 2),
                               "TFLOPs": round(tf, 1), "frac_tensor": round(tf / tpeak, 4)}), flush=True)

@@ -111,7 +111,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int cta = blockIdx.x, G = gridDim.x;
-  if (a.ksplit > 1) grid_dep_launch();  // the split-K sum kernel may start; it waits for this grid to end
+  // programmatic dependent launch both ways. Before griddepcontrol.wait this grid touches no activation
+  // and holds no tensor memory (a co-resident CTA of the previous grid may still need to allocate some):
+  // it initialises its barriers and the producer prefetches its first weight blocks (never written by
+  // the prompt forward) into L2. The next kernel is let in only once the tensor memory is held.
   if (tid == 0) {
     for (int s = 0; s < nst; ++s) {
       mbar_init(full_bar(s), 1);
@@ -125,10 +128,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
     misc[1] = 0;
     misc[2] = 0;
   }
+  if (warp == 4 && lane == 0 && cta < a.units) {
+    // the first unit's weight blocks into L2 (up to 256 KiB) while the previous kernel runs
+    int t, sp, mt, nt, kb0, kb1;
+    gemm_unit(a, cta, &t, &sp, &kb0, &kb1);
+    gemm_tile(a.m_tiles, a.n_tiles, t, &mt, &nt);
+    const int nkb = (kb1 - kb0) < 16 / (BN / 128) ? (kb1 - kb0) : 16 / (BN / 128);
+    for (int h = 0; h < BN / 128; ++h) {
+      const int g = nt * (BN / 128) + h;
+      if (g < a.ngroups)
+        prefetch_l2(a.w + ((int64_t)g * a.kblocks + kb0) * kBlockBytes, (uint32_t)(nkb * kBlockBytes));
+    }
+  }
+  grid_dep_wait();
   if (warp == 5) tmem_alloc(smem_u32(misc), kCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dep_launch();
   const uint32_t tmem = (uint32_t)misc[0];
   int* abort = misc + 1;
 
@@ -331,6 +348,8 @@ struct RmsArgs {
 // One CTA of 256 threads per row: out = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))) (Qwen3RMSNorm's
 // cast placement, engine/engine.py:505-509).
 __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const __grid_constant__ RmsArgs a) {
+  grid_dep_wait();  // launched as a programmatic dependent of the previous prompt kernel
+  grid_dep_launch();
   __shared__ float wsum[8];
   const int64_t m = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -388,6 +407,8 @@ constexpr int kRopeHeadsPerWarp = 8;  // heads of a token <= 8 warps x 8
 // arithmetic and rounding points as the decode QKV epilogue (engine/kernels/fused.py:23-81 with
 // pos_mode 0: position = prompt index).
 __global__ void __launch_bounds__(256) prefill_qk_rope_kernel(const __grid_constant__ QkRopeArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t t = blockIdx.x;
   const int64_t i = t / a.S, s = t - i * a.S;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -528,6 +549,7 @@ __device__ __forceinline__ void pa_unit(const PrefillAttnArgs& a, int u, int* i,
 }
 
 __global__ void __launch_bounds__(kPaThreads, 1) prefill_attn_kernel(const __grid_constant__ PrefillAttnArgs a) {
+  grid_dep_wait();  // holds no tensor memory while it waits; lets the next kernel in once it does
   // the layout needs all but a few hundred bytes of the 227 KiB, so there is no room to realign: dynamic
   // shared memory starts 1 KiB-aligned on sm_100 (nothing static precedes it); if not, flag and do nothing
   extern __shared__ __align__(1024) char smem_raw[];
@@ -571,6 +593,7 @@ __global__ void __launch_bounds__(kPaThreads, 1) prefill_attn_kernel(const __gri
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dep_launch();
   const uint32_t tmem = (uint32_t)misc[0];
   const uint32_t tS = tmem, tO = tmem + 256;  // S[2] in columns 0-255, O in 256-383
   int* abort = misc + 1;
@@ -835,6 +858,7 @@ __device__ __forceinline__ void pp_unit(const PrefillAttnArgs& a, int u, int* i,
 }
 
 __global__ void __launch_bounds__(kPpThreads, 1) prefill_attn_pp_kernel(const __grid_constant__ PrefillAttnArgs a) {
+  grid_dep_wait();  // holds no tensor memory while it waits; lets the next kernel in once it does
   extern __shared__ __align__(1024) char smem_raw[];
   char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sb = smem_u32(smem);
@@ -871,6 +895,7 @@ __global__ void __launch_bounds__(kPpThreads, 1) prefill_attn_pp_kernel(const __
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dep_launch();
   const uint32_t tmem = (uint32_t)misc[0];
   auto tS = [&](int x) { return tmem + 128u * x; };        // S_A 0-127, S_B 128-255 (P over their first 64)
   auto tO = [&](int x) { return tmem + 256u + 128u * x; };  // O_A 256-383, O_B 384-511
@@ -1136,6 +1161,7 @@ __device__ __forceinline__ float4 split_sum(const SplitSumArgs& a, const float* 
 template <int EPI>
 __global__ void __launch_bounds__(256) gemm_splitk_sum_kernel(const __grid_constant__ SplitSumArgs a) {
   grid_dep_wait();
+  grid_dep_launch();
   const int j = blockIdx.y;
   const int idx = blockIdx.x * 256 + threadIdx.x;
   const int r = idx >> a.qpt_shift, oc = (idx - (r << a.qpt_shift)) * 4;  // tile row; first output column
@@ -1226,7 +1252,7 @@ static int launch_gemm(const GemmArgs& a, int grid, cudaStream_t stream) {
     if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured = smem;
   }
-  return launch_kernel((const void*)kern, dim3(grid), dim3(kGemmThreads), smem, 0, stream, (void*)&a);
+  return launch_kernel((const void*)kern, dim3(grid), dim3(kGemmThreads), smem, 1, stream, (void*)&a);
 }
 
 }  // namespace qd
@@ -1346,7 +1372,7 @@ extern "C" int qd_rmsnorm_rows(const void* x, int64_t ldx, int64_t m, int64_t k,
   a.ldo = ldo;
   a.k = k;
   a.eps = eps;
-  return launch_kernel((const void*)rmsnorm_rows_kernel, dim3((unsigned)m), dim3(256), 0, 0, stream, &a);
+  return launch_kernel((const void*)rmsnorm_rows_kernel, dim3((unsigned)m), dim3(256), 0, 1, stream, &a);
 }
 
 extern "C" int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int64_t S, int nq_heads, int nkv_heads,
@@ -1381,7 +1407,7 @@ extern "C" int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int
   a.nkv = nkv_heads;
   a.eps = eps;
   if (a.tokens > INT32_MAX) return set_error(QD_ERR_UNSUPPORTED, "prefill q/k rope: too many tokens");
-  return launch_kernel((const void*)prefill_qk_rope_kernel, dim3((unsigned)a.tokens), dim3(256), 0, 0, stream, &a);
+  return launch_kernel((const void*)prefill_qk_rope_kernel, dim3((unsigned)a.tokens), dim3(256), 0, 1, stream, &a);
 }
 
 extern "C" int qd_prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, int nq_heads,
@@ -1445,7 +1471,7 @@ extern "C" int qd_prefill_attn(const void* q, int64_t ldq, int batch, int64_t S,
       configured_pp = true;
     }
     const int grid = a.units < host_sm_count() ? a.units : host_sm_count();
-    return launch_kernel((const void*)prefill_attn_pp_kernel, dim3(grid), dim3(kPpThreads), smem, 0, stream, &a);
+    return launch_kernel((const void*)prefill_attn_pp_kernel, dim3(grid), dim3(kPpThreads), smem, 1, stream, &a);
   }
   const int smem = PaLayout::total;
   static bool configured = false;
@@ -1455,5 +1481,5 @@ extern "C" int qd_prefill_attn(const void* q, int64_t ldq, int batch, int64_t S,
     configured = true;
   }
   const int grid = units < host_sm_count() ? (int)units : host_sm_count();
-  return launch_kernel((const void*)prefill_attn_kernel, dim3(grid), dim3(kPaThreads), smem, 0, stream, &a);
+  return launch_kernel((const void*)prefill_attn_kernel, dim3(grid), dim3(kPaThreads), smem, 1, stream, &a);
 }
