@@ -48,6 +48,9 @@ def _args():
     p.add_argument("--cpu-steps", type=int, default=96, help="decode steps in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--speculate", type=int, default=0,
+                   help="also time the end-to-end run with exact prompt-lookup speculation of this verify width "
+                        "(batch 1; reported as e2e_speculative, not the headline)")
     p.add_argument("--kernel", default=None, choices=["qkv", "o", "gu", "down", "lm", "attn", "attn_stream", "attn_tc", "step",
                                                       "prefill_gu", "prefill_attn"],
                    help="time one decode kernel alone (small profiling case; random packed weights on the GPU)")
@@ -300,6 +303,29 @@ def run_ours(a):
                "note": "decode tokens/s between the first and last yield of Engine.generate (host prompt list in, "
                        "host token lists out); the prompt upload is amortised over the steps in h2d_bytes_per_step"}
 
+    e2e_spec = None
+    if a.speculate and B == 1 and a.new > 1:
+        # exact prompt-lookup speculation (engine/engine.py:759-828) through the same public call; the
+        # emitted tokens must equal the plain run's up to a near-tie flip
+        plain = [t[0] for t in eng.generate(prompt, a.new)]
+        eng.speculate = a.speculate
+        list(eng.generate(prompt, a.new))  # untimed: builds the state with the verify buffers
+        stamps = []
+        t0 = time.perf_counter()
+        for _ in eng.generate(prompt, a.new):
+            stamps.append(time.perf_counter())
+        spec_toks = [t[0] for t in eng.generate(prompt, a.new)]
+        verifies = eng.state.spec_stats["verifies"]
+        eng.speculate = 0
+        eng.state = None
+        same = next((i for i, (x, y) in enumerate(zip(plain, spec_toks)) if x != y), len(plain))
+        dec = stamps[-1] - stamps[0]
+        e2e_spec = {"value": round((a.new - 1) / dec, 2), "unit": "tokens/s", "verify_width": a.speculate,
+                    "verifies": verifies, "tokens_per_verify": round((a.new - 1) / max(verifies, 1), 3),
+                    "ttft_ms": round(1e3 * (stamps[0] - t0), 3), "tokens_equal_to_plain": same,
+                    "note": "decode tokens/s between the first and last yield of Engine.generate with speculation; "
+                            "the prompt and the random-init weights decide how many drafts are accepted"}
+
     # ---------------- roofline of the dominant kernel and of the whole step
     peak, peak_kind = _peaks()
     L_avg = S + W + K / 2
@@ -354,6 +380,8 @@ def run_ours(a):
                "clocks": clk.summary(), "e2e": e2e, "cpu_baseline": cpu,
                "gpu_launches": K * (1 if st.tstep is not None else
                                     {"persistent": 1, "kernels": 2 + 5 * a.layers, "tc": 3 + 7 * a.layers}[st.mode])}
+        if e2e_spec is not None:
+            out["e2e_speculative"] = e2e_spec
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.barrier()

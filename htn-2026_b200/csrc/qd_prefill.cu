@@ -396,6 +396,7 @@ struct QkRopeArgs {
   __nv_bfloat16* q_out;  // [b * S, nq * 128]
   __nv_bfloat16 *k_cache, *v_cache;
   int64_t ldqkv, ldq, S, cs_b, cs_h, tokens;
+  int64_t pos0;  // position of the first token of every sequence (token i * S + s sits at pos0 + s)
   int nq, nkv;
   float eps;
 };
@@ -410,7 +411,7 @@ __global__ void __launch_bounds__(256) prefill_qk_rope_kernel(const __grid_const
   grid_dep_wait();
   grid_dep_launch();
   const int64_t t = blockIdx.x;
-  const int64_t i = t / a.S, s = t - i * a.S;
+  const int64_t i = t / a.S, s = t - i * a.S + a.pos0;  // s: the token's position
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int heads = a.nq + 2 * a.nkv;
   const uint2 cv = *reinterpret_cast<const uint2*>(a.cos + s * 128 + 4 * lane);
@@ -496,6 +497,7 @@ struct alignas(64) PrefillAttnArgs {
   __nv_bfloat16* out;  // [b * (S - q0), nq * 128]: row i * (S - q0) + s - q0
   int64_t ldo, S, q0;
   int batch, nq, nkv, n_qt, qt0, units;
+  int qrow0;  // q tensor-map row of position 0 is -qrow0 (0: q holds every position; q0: only q0..S-1)
   float scale_log2;
   int* err;
 };
@@ -610,8 +612,8 @@ __global__ void __launch_bounds__(kPaThreads, 1) prefill_attn_kernel(const __gri
         if (k >= 1 && !mbar_wait_abort(qempty, (k - 1) & 1, a.err, kErrWaitEmpty, abort)) break;
         misc[4] = k + 1;
         mbar_arrive_expect_tx(qfull, 2 * kPaBox);
-        tma_load_3d(sb + PaLayout::q, &a.tq, h * 128, qt * kPaTile, i, qfull, pol);
-        tma_load_3d(sb + PaLayout::q + kPaBox, &a.tq, h * 128 + 64, qt * kPaTile, i, qfull, pol);
+        tma_load_3d(sb + PaLayout::q, &a.tq, h * 128, qt * kPaTile - a.qrow0, i, qfull, pol);
+        tma_load_3d(sb + PaLayout::q + kPaBox, &a.tq, h * 128 + 64, qt * kPaTile - a.qrow0, i, qfull, pol);
         const int kvh = h / (a.nq / a.nkv);
         for (int j = 0; j <= qt; ++j, ++t) {
           const int st = t & 1;
@@ -914,10 +916,10 @@ __global__ void __launch_bounds__(kPpThreads, 1) prefill_attn_pp_kernel(const __
         misc[4] = k + 1;
         const int ha = kvh * gq + 2 * hp;
         mbar_arrive_expect_tx(qfull, 4 * kPaBox);
-        tma_load_3d(sb + PpLayout::qa, &a.tq, ha * 128, qt * kPaTile, i, qfull, pol);
-        tma_load_3d(sb + PpLayout::qa + kPaBox, &a.tq, ha * 128 + 64, qt * kPaTile, i, qfull, pol);
-        tma_load_3d(sb + PpLayout::qb, &a.tq, (ha + 1) * 128, qt * kPaTile, i, qfull, pol);
-        tma_load_3d(sb + PpLayout::qb + kPaBox, &a.tq, (ha + 1) * 128 + 64, qt * kPaTile, i, qfull, pol);
+        tma_load_3d(sb + PpLayout::qa, &a.tq, ha * 128, qt * kPaTile - a.qrow0, i, qfull, pol);
+        tma_load_3d(sb + PpLayout::qa + kPaBox, &a.tq, ha * 128 + 64, qt * kPaTile - a.qrow0, i, qfull, pol);
+        tma_load_3d(sb + PpLayout::qb, &a.tq, (ha + 1) * 128, qt * kPaTile - a.qrow0, i, qfull, pol);
+        tma_load_3d(sb + PpLayout::qb + kPaBox, &a.tq, (ha + 1) * 128 + 64, qt * kPaTile - a.qrow0, i, qfull, pol);
         for (int j = 0; j <= qt; ++j, ++t) {
           const int st = t & 1;
           if (t >= 2 && !mbar_wait_abort(kempty(st), ((t >> 1) - 1) & 1, a.err, kErrWaitEmpty, abort)) {
@@ -1379,9 +1381,19 @@ extern "C" int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int
                                   const void* q_norm, const void* k_norm, float eps, const void* cos, const void* sin,
                                   void* q_out, int64_t ldq, void* k_cache, void* v_cache, int64_t cap, int64_t cs_b,
                                   int64_t cs_h, cudaStream_t stream) {
+  return qd_prefill_qk_rope_at(qkv, ldqkv, batch, S, 0, nq_heads, nkv_heads, q_norm, k_norm, eps, cos, sin, q_out, ldq,
+                               k_cache, v_cache, cap, cs_b, cs_h, stream);
+}
+
+extern "C" int qd_prefill_qk_rope_at(const void* qkv, int64_t ldqkv, int batch, int64_t S, int64_t pos0, int nq_heads,
+                                     int nkv_heads, const void* q_norm, const void* k_norm, float eps, const void* cos,
+                                     const void* sin, void* q_out, int64_t ldq, void* k_cache, void* v_cache,
+                                     int64_t cap, int64_t cs_b, int64_t cs_h, cudaStream_t stream) {
   if (!qkv || !q_norm || !k_norm || !cos || !sin || !q_out || !k_cache || !v_cache)
     return set_error(QD_ERR_ARG, "null pointer");
-  if (batch < 1 || S < 1 || S > cap || nq_heads < 1 || nkv_heads < 1 || nq_heads + 2 * nkv_heads > 8 * kRopeHeadsPerWarp ||
+  if (pos0 < 0 || pos0 > cap) return set_error(QD_ERR_ARG, "prefill q/k rope: pos0 outside [0, cap]");
+  if (batch < 1 || S < 1 || S > cap - pos0 || nq_heads < 1 || nkv_heads < 1 ||
+      nq_heads + 2 * nkv_heads > 8 * kRopeHeadsPerWarp ||
       ldqkv < (int64_t)(nq_heads + 2 * nkv_heads) * 128 || ldq < (int64_t)nq_heads * 128 || ldqkv % 4 || ldq % 4 ||
       cs_h < cap * 128 || cs_b < (int64_t)nkv_heads * cs_h || cs_h % 4 || cs_b % 4)
     return set_error(QD_ERR_ARG, "prefill q/k rope: bad sizes");
@@ -1403,6 +1415,7 @@ extern "C" int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int
   a.cs_b = cs_b;
   a.cs_h = cs_h;
   a.tokens = (int64_t)batch * S;
+  a.pos0 = pos0;
   a.nq = nq_heads;
   a.nkv = nkv_heads;
   a.eps = eps;
@@ -1410,9 +1423,27 @@ extern "C" int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int
   return launch_kernel((const void*)prefill_qk_rope_kernel, dim3((unsigned)a.tokens), dim3(256), 0, 1, stream, &a);
 }
 
+static int prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, bool q_compact, int nq_heads,
+                        int nkv_heads, const void* k_cache, const void* v_cache, int64_t cap, int64_t cs_b,
+                        int64_t cs_h, float scale, void* out, int64_t ldo, int* err, cudaStream_t stream);
+
 extern "C" int qd_prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, int nq_heads,
                                int nkv_heads, const void* k_cache, const void* v_cache, int64_t cap, int64_t cs_b,
                                int64_t cs_h, float scale, void* out, int64_t ldo, int* err, cudaStream_t stream) {
+  return prefill_attn(q, ldq, batch, S, q_begin, false, nq_heads, nkv_heads, k_cache, v_cache, cap, cs_b, cs_h, scale,
+                      out, ldo, err, stream);
+}
+
+extern "C" int qd_prefill_attn_rows(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, int nq_heads,
+                                    int nkv_heads, const void* k_cache, const void* v_cache, int64_t cap, int64_t cs_b,
+                                    int64_t cs_h, float scale, void* out, int64_t ldo, int* err, cudaStream_t stream) {
+  return prefill_attn(q, ldq, batch, S, q_begin, true, nq_heads, nkv_heads, k_cache, v_cache, cap, cs_b, cs_h, scale,
+                      out, ldo, err, stream);
+}
+
+static int prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, bool q_compact, int nq_heads,
+                        int nkv_heads, const void* k_cache, const void* v_cache, int64_t cap, int64_t cs_b,
+                        int64_t cs_h, float scale, void* out, int64_t ldo, int* err, cudaStream_t stream) {
   if (!q || !k_cache || !v_cache || !out) return set_error(QD_ERR_ARG, "null pointer");
   if (batch < 1 || S < 1 || S > cap || q_begin < 0 || q_begin >= S || nq_heads < 1 || nkv_heads < 1 ||
       nq_heads % nkv_heads || ldq < (int64_t)nq_heads * 128 || ldo < (int64_t)nq_heads * 128 || ldq % 8 ||
@@ -1428,8 +1459,11 @@ extern "C" int qd_prefill_attn(const void* q, int64_t ldq, int batch, int64_t S,
   PrefillAttnArgs a = {};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   {
-    const cuuint64_t dims[3] = {(cuuint64_t)nq_heads * 128, (cuuint64_t)S, (cuuint64_t)batch};
-    const cuuint64_t strides[2] = {(cuuint64_t)ldq * 2, (cuuint64_t)(S * ldq * 2)};
+    // q rows of every sequence: positions 0..S-1, or (q_compact) only q_begin..S-1, loaded at row
+    // coordinate position - qrow0 (the rows before q_begin of the first query tile read as zero)
+    const int64_t qrows = q_compact ? S - q_begin : S;
+    const cuuint64_t dims[3] = {(cuuint64_t)nq_heads * 128, (cuuint64_t)qrows, (cuuint64_t)batch};
+    const cuuint64_t strides[2] = {(cuuint64_t)ldq * 2, (cuuint64_t)(qrows * ldq * 2)};
     const cuuint32_t box[3] = {64, (cuuint32_t)kPaTile, 1};
     if (encode(&a.tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1453,6 +1487,7 @@ extern "C" int qd_prefill_attn(const void* q, int64_t ldq, int batch, int64_t S,
   a.ldo = ldo;
   a.S = S;
   a.q0 = q_begin;
+  a.qrow0 = q_compact ? (int)q_begin : 0;
   a.qt0 = (int)qt0;
   a.batch = batch;
   a.nq = nq_heads;

@@ -93,6 +93,11 @@ PROTOTYPES = {
                                    c_int64, c_void_p]),
     "qd_prefill_attn": (c_int, [c_void_p, c_int64, c_int, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p, c_int64,
                                 c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_void_p]),
+    "qd_prefill_attn_rows": (c_int, [c_void_p, c_int64, c_int, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p,
+                                     c_int64, c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_void_p]),
+    "qd_prefill_qk_rope_at": (c_int, [c_void_p, c_int64, c_int, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p,
+                                      c_float, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64,
+                                      c_int64, c_int64, c_void_p]),
 }
 
 QD_OK, QD_ERR_ARG, QD_ERR_SCRATCH, QD_ERR_CUDA, QD_ERR_UNSUPPORTED = 0, 1, 2, 3, 4

@@ -304,23 +304,27 @@ def rmsnorm_rows(x, w, eps: float, out):
 
 
 def prefill_qk_rope(qkv, batch: int, S: int, nq: int, nkv: int, q_norm, k_norm, eps: float, cos, sin, q_out,
-                    k_cache, v_cache):
-    """q/k RMSNorm + RoPE of the prompt positions 0..S-1, K/V into the caches (qd_prefill_qk_rope).
-    qkv [batch * S, (nq + 2 nkv) * 128]; q_out [batch * S, nq * 128]; caches [batch, nkv, cap, 128]."""
+                    k_cache, v_cache, pos0: int = 0):
+    """q/k RMSNorm + RoPE of the positions pos0..pos0+S-1, K/V into the caches (qd_prefill_qk_rope, or
+    qd_prefill_qk_rope_at when pos0 > 0). qkv [batch * S, (nq + 2 nkv) * 128]; q_out [batch * S, nq * 128];
+    caches [batch, nkv, cap, 128]."""
     _check_bf16(qkv, q_norm, k_norm, cos, sin, q_out, k_cache, v_cache)
     assert k_cache.stride() == v_cache.stride() and qkv.stride(1) == 1 and q_out.stride(1) == 1
-    L.call("qd_prefill_qk_rope", _ptr(qkv), qkv.stride(0), batch, S, nq, nkv, _ptr(q_norm), _ptr(k_norm), eps,
-           _ptr(cos), _ptr(sin), _ptr(q_out), q_out.stride(0), _ptr(k_cache), _ptr(v_cache), k_cache.shape[2],
+    L.call("qd_prefill_qk_rope_at", _ptr(qkv), qkv.stride(0), batch, S, pos0, nq, nkv, _ptr(q_norm), _ptr(k_norm),
+           eps, _ptr(cos), _ptr(sin), _ptr(q_out), q_out.stride(0), _ptr(k_cache), _ptr(v_cache), k_cache.shape[2],
            k_cache.stride(0), k_cache.stride(1), _stream())
     return q_out
 
 
-def prefill_attn(q, batch: int, S: int, nq: int, nkv: int, k_cache, v_cache, out, q_begin: int = 0, err=None):
-    """Causal GQA attention of the prompt positions q_begin..S-1 over the cached keys 0..s
-    (qd_prefill_attn): q [batch * S, nq * 128] token-major; out [batch * (S - q_begin), nq * 128]."""
+def prefill_attn(q, batch: int, S: int, nq: int, nkv: int, k_cache, v_cache, out, q_begin: int = 0, err=None,
+                 q_rows: bool = False):
+    """Causal GQA attention of the positions q_begin..S-1 over the cached keys 0..s (qd_prefill_attn):
+    q [batch * S, nq * 128] token-major, or with q_rows only the computed rows [batch * (S - q_begin), nq * 128]
+    (qd_prefill_attn_rows); out [batch * (S - q_begin), nq * 128]."""
     _check_bf16(q, k_cache, v_cache, out)
     assert k_cache.stride() == v_cache.stride() and q.stride(1) == 1 and out.stride(1) == 1
-    L.call("qd_prefill_attn", _ptr(q), q.stride(0), batch, S, q_begin, nq, nkv, _ptr(k_cache), _ptr(v_cache),
+    L.call("qd_prefill_attn_rows" if q_rows else "qd_prefill_attn", _ptr(q), q.stride(0), batch, S, q_begin, nq, nkv,
+           _ptr(k_cache), _ptr(v_cache),
            k_cache.shape[2], k_cache.stride(0), k_cache.stride(1), 1.0 / math.sqrt(128), _ptr(out), out.stride(0),
            _ptr(err), _stream())
     return out

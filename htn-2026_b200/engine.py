@@ -40,6 +40,7 @@ sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 from decode_b200 import lib as qdlib  # noqa: E402
 from decode_b200 import ops  # noqa: E402
+from decode_b200 import spec  # noqa: E402
 from decode_b200.loader import load_checkpoint  # noqa: E402
 
 DEVICE = os.environ.get("ENGINE_DEVICE", "cuda:0")
@@ -57,6 +58,9 @@ TC_PERSISTENT_MAX_BATCH = int(os.environ.get("ENGINE_TC_PERSISTENT_MAX_BATCH", "
 PREFILL_TOKENS = 16384    # prefill processes at most this many tokens per row chunk (engine/engine.py:79)
 USE_GRAPHS = os.environ.get("ENGINE_GRAPHS", "1") != "0"
 USE_PDL = os.environ.get("ENGINE_PDL", "1") != "0"
+# exact prompt-lookup speculative decoding at batch 1: verify width T = k + 1 (0 = off; the reference's
+# default at batch 1 is 7, engine/engine.py:162)
+SPEC_T = int(os.environ.get("ENGINE_SPEC_T", "0"))
 # "persistent": one launch per decode step (qd_decode_step); "kernels": 1 + 5 x layers + 1 launches;
 # "tc": the tensor-core kernels (used from TC_MIN_BATCH up): one persistent launch per step, or the
 # chain of 1 + 7 x layers + 2 launches (TC_STEP)
@@ -80,10 +84,10 @@ def rope_tables(cap: int, head_dim: int, theta: float):
 class _State:
     """Everything shape-dependent for one (batch, prompt length, new tokens)."""
 
-    def __init__(self, eng: "Engine", B: int, S: int, N: int):
+    def __init__(self, eng: "Engine", B: int, S: int, N: int, spec_T: int = 0):
         dev = eng.device
         self.B, self.S, self.N = B, S, N
-        cap = self.capacity = S + N
+        cap = self.capacity = S + N + spec_T  # a verify writes up to T - 1 slots past the last emitted token
         Lyr, H, I = eng.n_layers, eng.hidden, eng.inter
         nq, nkv, D = eng.nq, eng.nkv, eng.head_dim
         self.k_all = torch.zeros((Lyr, B, nkv, cap, D), dtype=BF16, device=dev)
@@ -130,6 +134,66 @@ class _State:
         self.events = [torch.cuda.Event() for _ in range(max(N, 1))]
         self.prefill_graph = self.decode_graph = None
         self.prefill_logits = None
+        self.verify = _Verify(eng, self, spec_T) if spec_T else None
+
+
+class _Verify:
+    """Speculative verify forward of one sequence (the reference's `_verify`, engine/engine.py:479-498):
+    T tokens at positions pos0 .. pos0 + T - 1 after a cached prefix of pos0 tokens. The projections run
+    on the decode GEMVs with the T tokens as activation rows (RMSNorm fused where the decode step fuses
+    it); q/k RMSNorm + RoPE + the K/V of the T positions by qd_prefill_qk_rope_at; the T rows attend
+    causally over the cache by qd_prefill_attn_rows; the LM head's argmax gives, for every row t, the
+    greedy token after the prefix ending at row t."""
+
+    def __init__(self, eng: "Engine", st: "_State", T: int):
+        if not 2 <= T <= MAX_BATCH:
+            raise ValueError(f"speculative verify width must be in [2, {MAX_BATCH}], got {T}")
+        dev = eng.device
+        H, I, nq, nkv, D, eps = eng.hidden, eng.inter, eng.nq, eng.nkv, eng.head_dim, eng.eps
+        self.T = T
+        n_qkv = (nq + 2 * nkv) * D
+        self.tok = torch.zeros((T,), dtype=torch.int64, device=dev)
+        self.out = torch.zeros((T,), dtype=torch.int64, device=dev)
+        self.x = torch.zeros((T, H), dtype=BF16, device=dev)
+        self.qkv = torch.zeros((T, n_qkv), dtype=BF16, device=dev)
+        self.q = torch.zeros((T, nq * D), dtype=BF16, device=dev)
+        self.att = torch.zeros((T, nq * D), dtype=BF16, device=dev)
+        self.act = torch.zeros((T, I), dtype=BF16, device=dev)
+        self.qkv_op = ops.Gemv(T, n_qkv, H, ops.Gemv.STORE, dev, eps=eps)
+        self.o = ops.Gemv(T, H, nq * D, ops.Gemv.RES, dev, eps=eps)
+        self.gu = ops.Gemv(T, 2 * I, H, ops.Gemv.SWIGLU, dev, eps=eps)
+        self.down = ops.Gemv(T, H, I, ops.Gemv.RES, dev, eps=eps)
+        self.lm = ops.LmHeadArgmax(T, eng.vocab, H, dev, eps=eps)
+        pin = torch.cuda.is_available()
+        self.tok_host = torch.empty((T,), dtype=torch.int64, pin_memory=pin)
+        self.out_host = torch.empty((T,), dtype=torch.int64, pin_memory=pin)
+        self.event = torch.cuda.Event()
+
+    def launch(self, eng: "Engine", st: "_State", pos0: int) -> None:
+        """Enqueue the verify of self.tok at positions pos0 .. pos0 + T - 1 (the result lands in self.out)."""
+        T, nq, nkv, eps, err = self.T, eng.nq, eng.nkv, eng.eps, st.err
+        ops.embed(self.tok, eng.e_packed, eng.vocab, self.x, err, USE_PDL)
+        for i in range(eng.n_layers):
+            kc, vc = st.k_all[i], st.v_all[i]
+            self.qkv_op(self.x, eng.w_qkv[i], self.qkv, norm_w=eng.ln1[i], err=err, pdl=USE_PDL)
+            ops.prefill_qk_rope(self.qkv, 1, T, nq, nkv, eng.qn[i], eng.kn[i], eps, st.cos, st.sin, self.q, kc, vc,
+                                pos0=pos0)
+            ops.prefill_attn(self.q, 1, pos0 + T, nq, nkv, kc, vc, self.att, q_begin=pos0, err=err, q_rows=True)
+            self.o(self.att, eng.w_o[i], self.x, res=self.x, err=err, pdl=USE_PDL)
+            self.gu(self.x, eng.w_gu[i], self.act, norm_w=eng.ln2[i], err=err, pdl=USE_PDL)
+            self.down(self.act, eng.w_down[i], self.x, res=self.x, err=err, pdl=USE_PDL)
+        self.lm(self.x, eng.e_packed, eng.final_norm, self.out, err=err, pdl=USE_PDL)
+
+    def __call__(self, eng: "Engine", st: "_State", row: list[int], pos0: int) -> list[int]:
+        """Greedy token after every prefix of `row` (T tokens at positions pos0 ..), on the host."""
+        with torch.inference_mode():
+            self.tok_host.copy_(torch.tensor(row, dtype=torch.int64))
+            self.tok.copy_(self.tok_host, non_blocking=True)
+            self.launch(eng, st, pos0)
+            self.out_host.copy_(self.out, non_blocking=True)
+            self.event.record()
+        self.event.synchronize()
+        return self.out_host.tolist()
 
 
 class Engine:
@@ -208,6 +272,7 @@ class Engine:
         torch.cuda.synchronize()
         self.state = None
         self.sm_count = ops.sm_count()
+        self.speculate = SPEC_T  # verify width of exact speculative decoding at batch 1 (0 = plain greedy)
 
     # ------------------------------------------------------------------ model step
     def _prefill(self, st: _State) -> torch.Tensor:
@@ -332,7 +397,8 @@ class Engine:
         self.state = None
         gc.collect()
         torch.cuda.empty_cache()
-        st = _State(self, B, S, N)
+        spec_T = self.speculate if (self.speculate and B == 1 and N > 1) else 0
+        st = _State(self, B, S, N, spec_T)
         t0 = time.perf_counter()
         with torch.inference_mode():
             side = torch.cuda.Stream()
@@ -343,6 +409,8 @@ class Engine:
                     if N > 1:
                         st.pos.fill_(S)
                         self._decode_step(st)
+                    if st.verify is not None:
+                        st.verify.launch(self, st, S - 1)
             torch.cuda.current_stream().wait_stream(side)
             torch.cuda.synchronize()
             self.check_device_errors(st)
@@ -401,6 +469,32 @@ class Engine:
             timing.extend(a.elapsed_time(b) for a, b in ev)
         yield st.host[N - 1].tolist()
 
+    def _stream_spec(self, st: _State, input_ids, N: int):
+        """Exact prompt-lookup speculative decoding of one sequence (engine/engine.py:759-828): after the
+        prompt forward, every verify runs T = k + 1 tokens (the last emitted token and a k-token
+        prompt-lookup draft) and emits the accepted drafts plus the greedy token after them; yields
+        exactly N steps. The emitted tokens are the verify forward's greedy tokens."""
+        S, vf = st.S, st.verify
+        k = vf.T - 1
+        with torch.inference_mode():
+            st.ids_host.copy_(torch.tensor(input_ids, dtype=torch.int64))
+            st.ids.copy_(st.ids_host, non_blocking=True)
+            st.pos.fill_(S)
+            if st.prefill_graph is not None:
+                st.prefill_graph.replay()
+            else:
+                st.prefill_logits = self._prefill(st)
+            st.host[0].copy_(st.tok, non_blocking=True)
+            st.events[0].record()
+        st.events[0].synchronize()
+        first = st.host[0].tolist()
+        yield first
+        st.spec_stats = {}
+        for tok in spec.stream(list(input_ids[0]) + first, S, N, k, lambda row, pos0: vf(self, st, row, pos0),
+                               st.spec_stats):
+            yield [tok]
+        self.check_device_errors(st)
+
     # ------------------------------------------------------------------ API
     def generate(self, input_ids: list[list[int]], max_new_tokens: int):
         N = int(max_new_tokens)
@@ -410,12 +504,16 @@ class Engine:
         if B < 1 or S < 1 or any(len(r) != S for r in input_ids):
             raise ValueError("input_ids must be a non-empty batch of equal-length rows")
         st = self.state
-        if st is None or (st.B, st.S, st.N) != (B, S, N):
+        spec_T = self.speculate if (self.speculate and B == 1 and N > 1) else 0
+        if st is None or (st.B, st.S, st.N) != (B, S, N) or (st.verify.T if st.verify else 0) != spec_T:
             st = self._build(B, S, N)
         gc_was = gc.isenabled()
         gc.disable()
         try:
-            yield from self._stream(st, input_ids, N)
+            if st.verify is not None:
+                yield from self._stream_spec(st, input_ids, N)
+            else:
+                yield from self._stream(st, input_ids, N)
         finally:
             if gc_was:
                 gc.enable()

@@ -301,6 +301,15 @@ int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int64_t S, int
                        int64_t ldq, void* k_cache, void* v_cache, int64_t cap, int64_t cs_b, int64_t cs_h,
                        cudaStream_t stream);
 
+/* As qd_prefill_qk_rope with the tokens of every sequence at positions pos0 .. pos0 + S - 1 (token i * S + s
+ * at pos0 + s: cos / sin row and cache slot pos0 + s; pos0 + S <= cap): the speculative verify's
+ * qk_norm_rope_cache (engine/kernels/fused.py:23-98 with pos_mode 2, called from engine/engine.py:489-490)
+ * for sequences that share the position, and a prompt continued after a cached prefix. */
+int qd_prefill_qk_rope_at(const void* qkv, int64_t ldqkv, int batch, int64_t S, int64_t pos0, int nq_heads,
+                          int nkv_heads, const void* q_norm, const void* k_norm, float eps, const void* cos,
+                          const void* sin, void* q_out, int64_t ldq, void* k_cache, void* v_cache, int64_t cap,
+                          int64_t cs_b, int64_t cs_h, cudaStream_t stream);
+
 /* Prompt causal attention (flash attention on the tensor cores): replaces the prefill's
  * F.scaled_dot_product_attention(q, K, V, is_causal=True, enable_gqa=True) (engine/engine.py:579,
  * :584, :517-531). For every sequence i < batch, query head h and prompt position s in
@@ -315,6 +324,14 @@ int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int64_t S, int
 int qd_prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, int nq_heads, int nkv_heads,
                     const void* k_cache, const void* v_cache, int64_t cap, int64_t cs_b, int64_t cs_h, float scale,
                     void* out, int64_t ldo, int* err, cudaStream_t stream);
+
+/* As qd_prefill_attn with q holding only the query rows that are computed: q[i * (S - q_begin) + s - q_begin]
+ * for positions s in [q_begin, S) (the layout of out). The speculative verify's attention (VerifyAttention,
+ * engine/kernels/decode_attn.py:122-206, engine/engine.py:491): the S - q_begin verify tokens attend
+ * causally to the cached prefix and to each other. */
+int qd_prefill_attn_rows(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, int nq_heads,
+                         int nkv_heads, const void* k_cache, const void* v_cache, int64_t cap, int64_t cs_b,
+                         int64_t cs_h, float scale, void* out, int64_t ldo, int* err, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -71,6 +71,60 @@ def test_generate_matches_reference_golden(engines, case):
                 break
 
 
+@pytest.mark.parametrize("T", [3, 7])
+def test_speculative_generate_matches_reference_golden(engines, T):
+    """Exact prompt-lookup speculation (batch 1, verify width T): the emitted tokens follow the
+    reference's greedy tokens under the same tie rule as plain decoding."""
+    g = load_golden("config0")
+    eng, state, cfg = engines(g["spec"]["layers"])
+    eng.speculate = T
+    try:
+        steps = list(eng.generate(g["prompt"], g["spec"]["new"]))
+        assert eng.state.verify is not None and eng.state.verify.T == T
+    finally:
+        eng.speculate = 0
+        eng.state = None
+    assert len(steps) == g["spec"]["new"] and all(len(s) == 1 for s in steps)
+    toks, ref = [s[0] for s in steps], g["native"]["tokens"][0]
+    tol = max(TOL, 2 * g["self_drift"]["max_logsoftmax_diff"])
+    for t in range(len(ref)):
+        if toks[t] != ref[t]:
+            assert _golden_token_ok(toks[t], g["native"]["steps"][t], 0, tol), (T, t)
+            break
+
+
+@pytest.mark.parametrize("T", [2, 4, 8])
+def test_speculative_matches_plain_greedy(engines, T):
+    """Speculation emits the plain greedy tokens of this engine (a repetitive prompt, so drafts get
+    accepted): identical up to any step where the plain run's own top-2 logit gap is a near-tie."""
+    from decode_b200 import synth
+
+    eng, _, cfg = engines(2)
+    base = synth.random_prompt(1, 12, cfg["vocab_size"], seed=5)[0]
+    prompt = [base * 4]
+    N = 48
+    eng.state = None
+    plain, logits = eng.generate_with_logits(prompt, N)
+    eng.state = None
+    eng.speculate = T
+    try:
+        steps = list(eng.generate(prompt, N))
+        verifies = eng.state.spec_stats["verifies"]
+    finally:
+        eng.speculate = 0
+        eng.state = None
+    toks = [s[0] for s in steps]
+    assert len(toks) == N and 1 <= verifies <= N - 1
+    # the verify forward is other kernels (GEMV rows, prompt attention): a flip is allowed only where the
+    # plain run's top-2 gap is within the calibrated bound of the golden tests
+    tol = max(TOL, 2 * load_golden("config0")["self_drift"]["max_logsoftmax_diff"])
+    for t in range(N):
+        if toks[t] != plain[0][t]:
+            top2 = logits[t][0].float().topk(2).values
+            assert float(top2[0] - top2[1]) <= tol, (T, t)
+            break
+
+
 @pytest.mark.parametrize("case", ["config0", "b3_s17"])
 def test_teacher_forced_logits_within_tolerance(engines, case):
     g = load_golden(case)

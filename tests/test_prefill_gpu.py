@@ -336,3 +336,57 @@ def test_prefill_attn_deterministic(variant, monkeypatch):
     ops.prefill_attn(q, b, S, nq, nkv, kc, vc, o1)
     ops.prefill_attn(q, b, S, nq, nkv, kc, vc, o2)
     assert torch.equal(o1, o2)
+
+
+@pytest.mark.parametrize("b,S,T", [(1, 9, 7), (1, 300, 50), (2, 140, 8), (3, 17, 17)])
+def test_prefill_qk_rope_at_equals_whole_prompt(b, S, T):
+    """Tokens at positions S - T .. S - 1 (qd_prefill_qk_rope_at, the speculative verify's q/k RoPE and
+    K/V write) give the bits of the same tokens inside a whole-prompt call, and write no other slot."""
+    ops = _ops()
+    nq, nkv, D, eps = 32, 8, 128, 1e-6
+    cap, pos0 = S + 5, S - T
+    g = torch.Generator().manual_seed(b + S + T)
+    qkv = _rand((b * S, (nq + 2 * nkv) * D), 1.0, g).to(DEV)
+    qn = (1.0 + 0.1 * torch.randn(D, generator=g)).to(BF16).to(DEV)
+    kn = (1.0 + 0.1 * torch.randn(D, generator=g)).to(BF16).to(DEV)
+    cos, sin = (t.to(DEV) for t in Q.rope_tables(cap, D, 5e6))
+    q_all = torch.empty((b * S, nq * D), dtype=BF16, device=DEV)
+    kc_all = torch.full((b, nkv, cap, D), float("nan"), dtype=BF16, device=DEV)
+    vc_all = torch.full_like(kc_all, float("nan"))
+    ops.prefill_qk_rope(qkv, b, S, nq, nkv, qn, kn, eps, cos, sin, q_all, kc_all, vc_all)
+    tail = qkv.view(b, S, -1)[:, pos0:].reshape(b * T, -1)
+    q_t = torch.empty((b * T, nq * D), dtype=BF16, device=DEV)
+    kc = torch.full_like(kc_all, float("nan"))
+    vc = torch.full_like(kc_all, float("nan"))
+    ops.prefill_qk_rope(tail, b, T, nq, nkv, qn, kn, eps, cos, sin, q_t, kc, vc, pos0=pos0)
+    assert torch.equal(q_t, q_all.view(b, S, -1)[:, pos0:].reshape(b * T, -1))
+    assert torch.equal(kc[:, :, pos0:S], kc_all[:, :, pos0:S]) and torch.equal(vc[:, :, pos0:S], vc_all[:, :, pos0:S])
+    assert torch.isnan(kc[:, :, :pos0].float()).all() and torch.isnan(kc[:, :, S:].float()).all()
+    assert torch.isnan(vc[:, :, :pos0].float()).all() and torch.isnan(vc[:, :, S:].float()).all()
+
+
+@pytest.mark.parametrize("variant", ["1", "2"])
+@pytest.mark.parametrize("b,S,q0", [(1, 7, 0), (1, 300, 250), (1, 135, 127), (2, 140, 133), (3, 17, 16),
+                                    (1, 1030, 1023)])
+def test_prefill_attn_rows(b, S, q0, variant, monkeypatch):
+    """q holding only the computed rows (qd_prefill_attn_rows, the speculative verify's attention over the
+    cached prefix), including query rows that cross a 128-row tile, against the exact softmax as the
+    full-q call is. (Not bit-equal to the full-q call: the rows of a query tile before q_begin read as
+    zero here, and a warp's rescale decision is shared by its rows.)"""
+    monkeypatch.setenv("QD_PREFILL_ATTN", variant)
+    ops = _ops()
+    nq, nkv, D = 32, 8, 128
+    g = torch.Generator().manual_seed(b * 7 + S + q0)
+    q = _rand((b * S, nq * D), 1.0, g).to(DEV)
+    kc = _rand((b, nkv, S + 3, D), 1.0, g).to(DEV)
+    vc = _rand((b, nkv, S + 3, D), 1.0, g).to(DEV)
+    rows = b * (S - q0)
+    qr = q.view(b, S, -1)[:, q0:].reshape(rows, -1).clone()
+    out = torch.full((rows + 2, nq * D), float("nan"), dtype=BF16, device=DEV)
+    ops.prefill_attn(qr, b, S, nq, nkv, kc, vc, out[:rows], q_begin=q0, q_rows=True)
+    ref = _attn_ref(q, kc, vc, b, S, nq, nkv, q0).float()
+    _assert_close(out[:rows], ref, extra=torch.ones_like(ref), rtol=2.0 ** -6)
+    assert torch.isnan(out[rows:].float()).all()
+    again = torch.empty((rows, nq * D), dtype=BF16, device=DEV)
+    ops.prefill_attn(qr, b, S, nq, nkv, kc, vc, again, q_begin=q0, q_rows=True)
+    assert torch.equal(out[:rows], again)

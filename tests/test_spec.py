@@ -1,0 +1,91 @@
+"""Host side of exact prompt-lookup speculative decoding (decode_b200/spec.py) on the CPU.
+
+The draft index is checked against a brute-force restatement of the reference's rule
+(engine/engine.py:776-808: the continuation of the latest earlier occurrence of the last 3-gram, else
+2-gram, padded with the last token), also when the history grows by several tokens between lookups;
+the loop against a toy deterministic "model" whose greedy continuation is known: speculation must
+emit exactly the greedy tokens, and it must save verifies once the text repeats.
+"""
+
+import random
+
+import pytest
+
+from decode_b200 import spec
+
+
+def _brute_draft(seq, k):
+    last, n = seq[-1], len(seq)
+    p = None
+    for j in range(n - 2, 1, -1):  # n-grams ending at j <= n - 2 (their continuation exists)
+        if seq[j - 2:j + 1] == seq[-3:]:
+            p = j + 1
+            break
+    if p is None:
+        for j in range(n - 2, 0, -1):
+            if seq[j - 1:j + 1] == seq[-2:]:
+                p = j + 1
+                break
+    d = seq[p:p + k] if p is not None else []
+    return d + [last] * (k - len(d))
+
+
+@pytest.mark.parametrize("seed", range(20))
+def test_draft_matches_brute_force_as_the_history_grows(seed):
+    rnd = random.Random(seed)
+    vocab = rnd.choice([3, 5, 12])
+    seq = [rnd.randrange(vocab) for _ in range(rnd.randrange(2, 12))]
+    look = spec.PromptLookup(seq)
+    for _ in range(25):
+        k = rnd.randrange(1, 8)
+        assert look.draft(k) == _brute_draft(seq, k)
+        seq.extend(rnd.randrange(vocab) for _ in range(rnd.randrange(1, 5)))
+        look.register()
+
+
+def test_draft_without_history_pads_with_the_last_token():
+    assert spec.PromptLookup([7, 9]).draft(3) == [9, 9, 9]
+    assert spec.PromptLookup([4]).draft(2) == [4, 4]
+    # 2-gram (1, 2) occurred: its continuation [3, 1] then padding
+    assert spec.PromptLookup([1, 2, 3, 1, 2]).draft(4) == [3, 1, 2, 2]
+
+
+def test_accept_takes_the_matching_prefix_and_the_next_greedy_token():
+    assert spec.accept([5, 1, 2, 3], [1, 2, 3, 4]) == [1, 2, 3, 4]  # every draft accepted
+    assert spec.accept([5, 1, 2, 3], [1, 9, 3, 4]) == [1, 9]        # second draft rejected
+    assert spec.accept([5, 1, 2, 3], [8, 2, 3, 4]) == [8]           # none accepted: one token
+
+
+def _toy_next(prefix):
+    """A deterministic 'model': greedy next token from the last two tokens (so the text cycles within
+    25 steps)."""
+    return (prefix[-1] * 2 + prefix[-2] + 1) % 5 if len(prefix) > 1 else 1
+
+
+def _toy_verify(history):
+    def verify(row, pos0):
+        assert len(history) == pos0 + 1 and history[-1] == row[0]  # starts at the last emitted token
+        pre = history[:pos0] + [row[0]]
+        out = []
+        for t in range(len(row)):
+            out.append(_toy_next(pre))
+            if t + 1 < len(row):
+                pre = pre + [row[t + 1]]
+        return out
+    return verify
+
+
+@pytest.mark.parametrize("k", [1, 3, 6])
+@pytest.mark.parametrize("S,N", [(5, 1), (5, 2), (3, 40), (9, 100)])
+def test_stream_emits_exactly_the_greedy_tokens(k, S, N):
+    prompt = [(3 * i + 2) % 5 for i in range(S)]
+    greedy = list(prompt)
+    for _ in range(N):
+        greedy.append(_toy_next(greedy))
+    seq = prompt + [greedy[S]]
+    stats = {}
+    out = [greedy[S]] + list(spec.stream(seq, S, N, k, _toy_verify(seq), stats))
+    assert out == greedy[S:S + N]
+    assert stats["verifies"] <= max(0, N - 1)
+    if N >= 100 and k >= 3:  # the toy text cycles: drafts from earlier cycles get accepted
+        assert stats["verifies"] < (N - 1) / 2
