@@ -136,12 +136,50 @@ def load(path: str | None = None) -> ctypes.CDLL:
     return lib
 
 
+_RECORDING: list | None = None
+
+
 def call(name: str, *args) -> None:
-    """Call an int-returning entry point and raise QDError on a non-zero status."""
+    """Call an int-returning entry point and raise QDError on a non-zero status (inside `recording`,
+    collect (name, args) instead)."""
+    if _RECORDING is not None:
+        _RECORDING.append((name, list(args)))
+        return
     lib = load()
     rc = getattr(lib, name)(*args)
     if rc != QD_OK:
         raise QDError(name, rc, lib.qd_last_error().decode(errors="replace"))
+
+
+class recording:
+    """Collect the entry-point calls made inside the block as (name, argument list) instead of running
+    them, for a caller that replays a fixed launch sequence with `replay` (the Python-side argument
+    checks of the wrappers run once, when recorded)."""
+
+    def __enter__(self) -> list:
+        global _RECORDING
+        if _RECORDING is not None:
+            raise RuntimeError("recordings do not nest")
+        _RECORDING = []
+        return _RECORDING
+
+    def __exit__(self, *exc) -> None:
+        global _RECORDING
+        _RECORDING = None
+
+
+def bind(recorded: list) -> list:
+    """(entry point, argument list) pairs of a recording, ready for `replay`."""
+    lib = load()
+    return [(getattr(lib, name), name, args) for name, args in recorded]
+
+
+def replay(bound: list) -> None:
+    """Run a bound recording in order; raise QDError at the first non-zero status."""
+    for fn, name, args in bound:
+        rc = fn(*args)
+        if rc != QD_OK:
+            raise QDError(name, rc, load().qd_last_error().decode(errors="replace"))
 
 
 def describe_device_error(code: int) -> str:

@@ -132,3 +132,26 @@ def test_tc_gemm_plan_tile_choice(lib):
     assert lib.qd_tc_gemm_plan(1024, 2560, 9728, *args) == 0         # 160 tiles: 148 whole, the last 12 split
     assert (bn.value, ks.value, g.value, nb.value) == (128, 12, 148, 12 * 12 * 128 * 128 * 4)
     assert lib.qd_tc_gemm_plan(1, 100, 64, *args) == 1
+
+
+def test_recorded_calls_replay_in_order_and_raise_on_error():
+    """lib.recording / bind / replay (the speculative verify's launch list): calls are collected with
+    their argument lists, replayed with edited arguments, and a non-zero status raises QDError."""
+    from decode_b200 import lib as qdlib
+
+    g, bn, ks, nb = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int64(0)
+    out = (ctypes.byref(g), ctypes.byref(bn), ctypes.byref(ks), ctypes.byref(nb))
+    with qdlib.recording() as rec:
+        qdlib.call("qd_tc_gemm_plan", 128, 2560, 4096, *out)
+    assert [name for name, _ in rec] == ["qd_tc_gemm_plan"] and g.value == 0  # nothing ran yet
+    bound = qdlib.bind(rec)
+    qdlib.replay(bound)
+    assert (bn.value, ks.value) == (128, 7)
+    bound[0][2][0] = 16384  # edit the recorded arguments in place, as the verify does per round
+    bound[0][2][1] = 19456
+    bound[0][2][2] = 2560
+    qdlib.replay(bound)
+    assert (bn.value, ks.value, nb.value) == (256, 1, 0)
+    bound[0][2][1] = 100  # n % 128 != 0
+    with pytest.raises(qdlib.QDError):
+        qdlib.replay(bound)
