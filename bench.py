@@ -52,7 +52,7 @@ def _args():
                    help="also time the end-to-end run with exact prompt-lookup speculation of this verify width "
                         "(batch 1; reported as e2e_speculative, not the headline)")
     p.add_argument("--kernel", default=None, choices=["qkv", "o", "gu", "down", "lm", "attn", "attn_stream", "attn_tc", "step",
-                                                      "prefill_gu", "prefill_attn"],
+                                                      "prefill_gu", "prefill_attn", "prefill_fwd"],
                    help="time one decode kernel alone (small profiling case; random packed weights on the GPU)")
     p.add_argument("--launches", type=int, default=8)
     p.add_argument("--tc", action="store_true", help="with --kernel: the tcgen05 kernel (activations pre-packed)")
@@ -388,6 +388,42 @@ def run_ours(a):
         dist.destroy_process_group()
 
 
+def run_prefill_forward(a):
+    """The engine's whole prompt forward (`--layers` layers, batch 1, `--prompt` tokens; random-init
+    weights) as a CUDA graph replayed `--launches` times after the engine's own build: the profiling
+    case for the launch list of the time to first token. Prints avg ms per forward and the number of
+    library kernels one forward launches."""
+    import torch
+
+    import engine as E
+
+    state, cfg = make_model(a.layers)
+    eng = E.Engine.from_state_dict(state, cfg, "cuda:0")
+    del state
+    st = eng._build(1, a.prompt, 1)
+    with torch.inference_mode():
+        st.ids.copy_(torch.tensor(synth_prompt(1, a.prompt), dtype=torch.int64))
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(a.launches):
+        st.prefill_graph.replay()
+    e.record()
+    e.synchronize()
+    eng.check_device_errors(st)
+    with qdlib_recording() as rec:
+        eng._prefill(st)
+    print(json.dumps({"kernel": "prefill_fwd", "layers": a.layers, "prompt": a.prompt, "launches": a.launches,
+                      "avg_ms": round(s.elapsed_time(e) / a.launches, 3),
+                      "library_launches_per_forward": sum(1 for name, _ in rec if not name.endswith("_plan"))}))
+
+
+def qdlib_recording():
+    from decode_b200 import lib as qdlib
+
+    return qdlib.recording()
+
+
 def run_prefill_kernel(a):
     """One prompt kernel alone on `--prompt` tokens of one sequence (profiling case): prefill_gu is
     qd_tc_gemm with the SwiGLU epilogue on the gate/up shape (x [S, 2560] N(0, 1), packed weights
@@ -434,6 +470,8 @@ def run_kernel(a):
     torch.cuda.set_device(dev)
     if a.kernel == "step":
         return run_step_kernel(a)
+    if a.kernel == "prefill_fwd":
+        return run_prefill_forward(a)
     if a.kernel in ("prefill_gu", "prefill_attn"):
         return run_prefill_kernel(a)
     H, I, V, nq, nkv, D, B, L = 2560, 9728, 151936, 32, 8, 128, a.batch, a.layers
