@@ -315,13 +315,14 @@ def run_ours(a):
         for _ in eng.generate(prompt, a.new):
             stamps.append(time.perf_counter())
         spec_toks = [t[0] for t in eng.generate(prompt, a.new)]
-        verifies = eng.state.spec_stats["verifies"]
+        verifies, plain_steps = eng.state.spec_stats["verifies"], eng.state.spec_stats["plain_steps"]
         eng.speculate = 0
         eng.state = None
         same = next((i for i, (x, y) in enumerate(zip(plain, spec_toks)) if x != y), len(plain))
         dec = stamps[-1] - stamps[0]
         e2e_spec = {"value": round((a.new - 1) / dec, 2), "unit": "tokens/s", "verify_width": a.speculate,
-                    "verifies": verifies, "tokens_per_verify": round((a.new - 1) / max(verifies, 1), 3),
+                    "verifies": verifies, "plain_steps": plain_steps,
+                    "tokens_per_verify": round((a.new - 1 - plain_steps) / max(verifies, 1), 3),
                     "ttft_ms": round(1e3 * (stamps[0] - t0), 3), "tokens_equal_to_plain": same,
                     "note": "decode tokens/s between the first and last yield of Engine.generate with speculation; "
                             "the prompt and the random-init weights decide how many drafts are accepted"}

@@ -53,19 +53,75 @@ def accept(row: list[int], greedy: list[int]) -> list[int]:
     return greedy[:a + 1]
 
 
-def stream(seq: list[int], S: int, N: int, k: int, verify, stats: dict | None = None):
+class Gate:
+    """When speculation pays (a policy of this engine; the reference instead times one warm-up run,
+    engine/engine.py:83-85). After every verify it compares the tokens the last few verifies emitted
+    with what one verify costs in plain decode steps (measured as the generation runs); while
+    speculation does not pay, the next `backoff` tokens come from plain steps, the back-off doubling
+    each time (up to `max_backoff`) and resetting once speculation pays again."""
+
+    def __init__(self, window: int = 4, backoff: int = 8, max_backoff: int = 128, prior_cost: float = 1.4):
+        self.window, self.min_backoff, self.max_backoff = window, backoff, max_backoff
+        self.backoff = backoff
+        self.recent: list[int] = []
+        self.t_verify, self.n_verify, self.t_step, self.n_step = 0.0, 0, 0.0, 0
+        self.prior_cost = prior_cost
+
+    def cost(self) -> float:
+        """One verify in plain steps: measured once both have run, the prior before."""
+        if self.n_verify and self.n_step:
+            return (self.t_verify / self.n_verify) / (self.t_step / self.n_step)
+        return self.prior_cost
+
+    def verified(self, emitted: int, seconds: float) -> int:
+        """Record one verify; returns how many plain steps to run next (0: keep speculating)."""
+        self.t_verify += seconds
+        self.n_verify += 1
+        self.recent = (self.recent + [emitted])[-self.window:]
+        if len(self.recent) < self.window or sum(self.recent) / len(self.recent) >= self.cost():
+            if len(self.recent) == self.window:
+                self.backoff = self.min_backoff
+            return 0
+        plain, self.backoff = self.backoff, min(2 * self.backoff, self.max_backoff)
+        self.recent = []
+        return plain
+
+    def stepped(self, seconds: float) -> None:
+        self.t_step += seconds
+        self.n_step += 1
+
+
+def stream(seq: list[int], S: int, N: int, k: int, verify, stats: dict | None = None, step=None,
+           gate: Gate | None = None):
     """The speculative loop after the prompt forward (engine/engine.py:788-828, one sequence): `seq` is
     the prompt (S tokens) plus the first generated token; yields generated tokens 2..N, one at a time.
     verify(row, pos0) returns the greedy token after every prefix of row (k + 1 tokens at positions
-    pos0 ..); every verify starts at the last emitted token, so pos0 + k + 1 <= S + N + k - 1."""
+    pos0 ..); every verify starts at the last emitted token, so pos0 + k + 1 <= S + N + k - 1. With
+    `step` (one plain decode step: step(token, pos) -> the greedy token after it) and a `gate`, rounds
+    the gate rejects run plain steps instead; both emit greedy tokens."""
+    import time
+
     look = PromptLookup(seq)
     yielded = len(seq) - S
     stats = {} if stats is None else stats
-    stats["verifies"] = 0
+    stats["verifies"] = stats["plain_steps"] = 0
+    plain = 0
     while yielded < N:
-        row = [seq[-1]] + look.draft(k)
-        seq.extend(accept(row, verify(row, len(seq) - 1)))
-        stats["verifies"] += 1
+        if plain and step is not None:
+            t0 = time.perf_counter()
+            seq.append(step(seq[-1], len(seq) - 1))
+            if gate is not None:
+                gate.stepped(time.perf_counter() - t0)
+            stats["plain_steps"] += 1
+            plain -= 1
+        else:
+            row = [seq[-1]] + look.draft(k)
+            t0 = time.perf_counter()
+            got = accept(row, verify(row, len(seq) - 1))
+            seq.extend(got)
+            stats["verifies"] += 1
+            if gate is not None and step is not None:
+                plain = gate.verified(len(got), time.perf_counter() - t0)
         look.register()
         while yielded < N and len(seq) - S > yielded:
             yield seq[S + yielded]

@@ -61,6 +61,8 @@ USE_PDL = os.environ.get("ENGINE_PDL", "1") != "0"
 # exact prompt-lookup speculative decoding at batch 1: verify width T = k + 1 (0 = off; the reference's
 # default at batch 1 is 7, engine/engine.py:162)
 SPEC_T = int(os.environ.get("ENGINE_SPEC_T", "0"))
+# while drafts are not accepted often enough to pay for a verify, fall back to plain decode steps
+SPEC_GATE = os.environ.get("ENGINE_SPEC_GATE", "1") != "0"
 # "persistent": one launch per decode step (qd_decode_step); "kernels": 1 + 5 x layers + 1 launches;
 # "tc": the tensor-core kernels (used from TC_MIN_BATCH up): one persistent launch per step, or the
 # chain of 1 + 7 x layers + 2 launches (TC_STEP)
@@ -180,6 +182,8 @@ class _Verify:
         pin = torch.cuda.is_available()
         self.tok_host = torch.empty((T,), dtype=torch.int64, pin_memory=pin)
         self.out_host = torch.empty((T,), dtype=torch.int64, pin_memory=pin)
+        self.step_host = torch.empty((2,), dtype=torch.int64, pin_memory=pin)  # plain-step fallback: tok, pos
+        self.step_out = torch.empty((1,), dtype=torch.int64, pin_memory=pin)
         self.event = torch.cuda.Event()
         self.calls = None  # the recorded launch sequence (its positions and stream are set per verify)
 
@@ -537,10 +541,28 @@ class Engine:
         first = st.host[0].tolist()
         yield first
         st.spec_stats = {}
+        step = (lambda tok, pos: self._plain_step(st, tok, pos)) if SPEC_GATE else None
         for tok in spec.stream(list(input_ids[0]) + first, S, N, k, lambda row, pos0: vf(self, st, row, pos0),
-                               st.spec_stats):
+                               st.spec_stats, step=step, gate=spec.Gate() if SPEC_GATE else None):
             yield [tok]
         self.check_device_errors(st)
+
+    def _plain_step(self, st: _State, tok: int, pos: int) -> int:
+        """One plain decode step of a batch-1 state from the host's token and position (the speculative
+        loop's fallback): the greedy token after `tok` at `pos`."""
+        vf = st.verify
+        with torch.inference_mode():
+            vf.step_host[0], vf.step_host[1] = tok, pos
+            st.tok.copy_(vf.step_host[0:1], non_blocking=True)
+            st.pos.copy_(vf.step_host[1:2], non_blocking=True)
+            if st.decode_graph is not None:
+                st.decode_graph.replay()
+            else:
+                self._decode_step(st)
+            vf.step_out.copy_(st.tok, non_blocking=True)
+            vf.event.record()
+        vf.event.synchronize()
+        return int(vf.step_out[0])
 
     # ------------------------------------------------------------------ API
     def generate(self, input_ids: list[list[int]], max_new_tokens: int):

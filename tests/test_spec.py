@@ -89,3 +89,63 @@ def test_stream_emits_exactly_the_greedy_tokens(k, S, N):
     assert stats["verifies"] <= max(0, N - 1)
     if N >= 100 and k >= 3:  # the toy text cycles: drafts from earlier cycles get accepted
         assert stats["verifies"] < (N - 1) / 2
+
+
+def _long_next(prefix):
+    """A 'model' whose text does not repeat for a long while: drafts (nearly) never match."""
+    return (prefix[-1] * 31 + len(prefix) * 17 + 5) % 1009
+
+
+def _verify_with(next_fn, history):
+    def verify(row, pos0):
+        assert len(history) == pos0 + 1 and history[-1] == row[0]
+        pre, out = history[:pos0] + [row[0]], []
+        for t in range(len(row)):
+            out.append(next_fn(pre))
+            if t + 1 < len(row):
+                pre = pre + [row[t + 1]]
+        return out
+    return verify
+
+
+def _step_with(next_fn, history):
+    def step(tok, pos):
+        assert len(history) == pos + 1 and history[-1] == tok
+        return next_fn(history)
+    return step
+
+
+@pytest.mark.parametrize("next_fn,expect_plain", [(_long_next, True), (_toy_next, False)])
+def test_gated_stream_falls_back_to_plain_steps_and_stays_exact(next_fn, expect_plain):
+    """With the gate, rounds whose drafts keep failing become plain steps (so speculation costs little
+    where it cannot help); where the text repeats, speculation keeps running. Either way the emitted
+    tokens are the greedy ones."""
+    S, N, k = 6, 300, 6
+    prompt = [(5 * i + 1) % 5 for i in range(S)]
+    greedy = list(prompt)
+    for _ in range(N):
+        greedy.append(next_fn(greedy))
+    seq = prompt + [greedy[S]]
+    stats = {}
+    gate = spec.Gate(prior_cost=1.4)
+    out = [greedy[S]] + list(spec.stream(seq, S, N, k, _verify_with(next_fn, seq), stats,
+                                         step=_step_with(next_fn, seq), gate=gate))
+    assert out == greedy[S:S + N]
+    if expect_plain:
+        assert stats["plain_steps"] > 0.8 * N and stats["verifies"] < 0.2 * N
+    else:
+        assert stats["plain_steps"] == 0
+
+
+def test_gate_backoff_doubles_and_resets():
+    g = spec.Gate(window=2, backoff=4, max_backoff=16, prior_cost=1.5)
+    assert g.verified(1, 1.0) == 0          # window not full yet
+    assert g.verified(1, 1.0) == 4          # 1 token per verify < 1.5: four plain steps
+    assert g.verified(1, 1.0) == 0
+    assert g.verified(1, 1.0) == 8          # doubled
+    assert g.verified(1, 1.0) == 0 and g.verified(1, 1.0) == 16 and g.verified(1, 1.0) == 0
+    assert g.verified(1, 1.0) == 16         # capped
+    assert g.verified(3, 1.0) == 0 and g.verified(3, 1.0) == 0  # pays again: back-off resets
+    assert g.backoff == 4
+    g.stepped(0.5)                           # measured: one verify = 1.0 / 0.5 = 2 steps
+    assert abs(g.cost() - 2.0) < 1e-9
