@@ -125,6 +125,37 @@ def test_speculative_matches_plain_greedy(engines, T):
             break
 
 
+def test_speculation_gate_falls_back_to_plain_steps(engines):
+    """On a uniform-random prompt drafts are rarely accepted: the gate hands most tokens to plain decode
+    steps on the same cache, and the emitted tokens stay this engine's plain greedy tokens (up to a
+    near-tie flip of the plain run)."""
+    from decode_b200 import synth
+
+    eng, _, cfg = engines(2)
+    prompt = synth.random_prompt(1, 40, cfg["vocab_size"], seed=9)
+    N = 96
+    eng.state = None
+    plain, logits = eng.generate_with_logits(prompt, N)
+    eng.state = None
+    eng.speculate = 4
+    try:
+        toks = [s[0] for s in eng.generate(prompt, N)]
+        stats = dict(eng.state.spec_stats)
+    finally:
+        eng.speculate = 0
+        eng.state = None
+    assert len(toks) == N and stats["verifies"] >= 4
+    if stats["verifies"] * 2 > N:  # drafts kept paying: nothing to fall back from
+        pytest.skip(f"drafts accepted on this prompt ({stats})")
+    assert stats["plain_steps"] > 0
+    tol = max(TOL, 2 * load_golden("config0")["self_drift"]["max_logsoftmax_diff"])
+    for t in range(N):
+        if toks[t] != plain[0][t]:
+            top2 = logits[t][0].float().topk(2).values
+            assert float(top2[0] - top2[1]) <= tol, t
+            break
+
+
 @pytest.mark.parametrize("case", ["config0", "b3_s17"])
 def test_teacher_forced_logits_within_tolerance(engines, case):
     g = load_golden(case)
