@@ -86,9 +86,10 @@ class Gate:
         self.recent = []
         return plain
 
-    def stepped(self, seconds: float) -> None:
+    def stepped(self, seconds: float, n: int = 1) -> None:
+        """Record n plain steps that took `seconds` together."""
         self.t_step += seconds
-        self.n_step += 1
+        self.n_step += n
 
 
 def stream(seq: list[int], S: int, N: int, k: int, verify, stats: dict | None = None, step=None,
@@ -97,8 +98,9 @@ def stream(seq: list[int], S: int, N: int, k: int, verify, stats: dict | None = 
     the prompt (S tokens) plus the first generated token; yields generated tokens 2..N, one at a time.
     verify(row, pos0) returns the greedy token after every prefix of row (k + 1 tokens at positions
     pos0 ..); every verify starts at the last emitted token, so pos0 + k + 1 <= S + N + k - 1. With
-    `step` (one plain decode step: step(token, pos) -> the greedy token after it) and a `gate`, rounds
-    the gate rejects run plain steps instead; both emit greedy tokens."""
+    `step` (plain decode steps: step(token, pos, n) yields the n greedy tokens after `token` at `pos`,
+    one at a time) and a `gate`, the tokens the gate hands to plain steps come from `step`; both emit
+    greedy tokens."""
     import time
 
     look = PromptLookup(seq)
@@ -108,12 +110,16 @@ def stream(seq: list[int], S: int, N: int, k: int, verify, stats: dict | None = 
     plain = 0
     while yielded < N:
         if plain and step is not None:
+            n = min(plain, N - yielded)
             t0 = time.perf_counter()
-            seq.append(step(seq[-1], len(seq) - 1))
+            for tok in step(seq[-1], len(seq) - 1, n):
+                seq.append(tok)
+                yield tok
+                yielded += 1
             if gate is not None:
-                gate.stepped(time.perf_counter() - t0)
-            stats["plain_steps"] += 1
-            plain -= 1
+                gate.stepped(time.perf_counter() - t0, n)
+            stats["plain_steps"] += n
+            plain = 0
         else:
             row = [seq[-1]] + look.draft(k)
             t0 = time.perf_counter()

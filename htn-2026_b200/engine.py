@@ -183,7 +183,6 @@ class _Verify:
         self.tok_host = torch.empty((T,), dtype=torch.int64, pin_memory=pin)
         self.out_host = torch.empty((T,), dtype=torch.int64, pin_memory=pin)
         self.step_host = torch.empty((2,), dtype=torch.int64, pin_memory=pin)  # plain-step fallback: tok, pos
-        self.step_out = torch.empty((1,), dtype=torch.int64, pin_memory=pin)
         self.event = torch.cuda.Event()
         self.calls = None  # the recorded launch sequence (its positions and stream are set per verify)
 
@@ -541,28 +540,34 @@ class Engine:
         first = st.host[0].tolist()
         yield first
         st.spec_stats = {}
-        step = (lambda tok, pos: self._plain_step(st, tok, pos)) if SPEC_GATE else None
+        step = (lambda tok, pos, n: self._plain_steps(st, tok, pos, n)) if SPEC_GATE else None
         for tok in spec.stream(list(input_ids[0]) + first, S, N, k, lambda row, pos0: vf(self, st, row, pos0),
                                st.spec_stats, step=step, gate=spec.Gate() if SPEC_GATE else None):
             yield [tok]
         self.check_device_errors(st)
 
-    def _plain_step(self, st: _State, tok: int, pos: int) -> int:
-        """One plain decode step of a batch-1 state from the host's token and position (the speculative
-        loop's fallback): the greedy token after `tok` at `pos`."""
+    def _plain_steps(self, st: _State, tok: int, pos: int, n: int):
+        """n plain decode steps of a batch-1 state from the host's token and position (the speculative
+        loop's fallback), yielding the greedy tokens one at a time. As in `_stream`, the GPU runs a step
+        ahead of the host: each decode-graph replay takes its token and position from the previous one."""
         vf = st.verify
         with torch.inference_mode():
             vf.step_host[0], vf.step_host[1] = tok, pos
             st.tok.copy_(vf.step_host[0:1], non_blocking=True)
             st.pos.copy_(vf.step_host[1:2], non_blocking=True)
-            if st.decode_graph is not None:
-                st.decode_graph.replay()
-            else:
-                self._decode_step(st)
-            vf.step_out.copy_(st.tok, non_blocking=True)
-            vf.event.record()
-        vf.event.synchronize()
-        return int(vf.step_out[0])
+        for t in range(n):
+            with torch.inference_mode():
+                if st.decode_graph is not None:
+                    st.decode_graph.replay()
+                else:
+                    self._decode_step(st)
+                st.host[t].copy_(st.tok, non_blocking=True)
+                st.events[t].record()
+            if t:
+                st.events[t - 1].synchronize()
+                yield int(st.host[t - 1][0])
+        st.events[n - 1].synchronize()
+        yield int(st.host[n - 1][0])
 
     # ------------------------------------------------------------------ API
     def generate(self, input_ids: list[list[int]], max_new_tokens: int):

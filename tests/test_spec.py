@@ -109,9 +109,10 @@ def _verify_with(next_fn, history):
 
 
 def _step_with(next_fn, history):
-    def step(tok, pos):
+    def step(tok, pos, n):
         assert len(history) == pos + 1 and history[-1] == tok
-        return next_fn(history)
+        for _ in range(n):
+            yield next_fn(history)  # the caller appends each token before asking for the next
     return step
 
 
