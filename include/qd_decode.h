@@ -275,10 +275,12 @@ int qd_tc_decode_step(const qd_step_desc* desc, void* xh, void* xa, void* xi, vo
  * (row stride ldx, 16-byte aligned, ldx % 8 == 0), W packed [n, k] (n % 128 == 0, k % 64 == 0).
  * Epilogues as qd_gemv: QD_EPI_STORE out = bf16(y); QD_EPI_RES out = bf16(res + bf16(y)) (out may
  * alias res); QD_EPI_SWIGLU (W = the interleaved gate/up matrix) out [m, n / 2] =
- * bf16(bf16(silu(bf16 g)) * bf16 u). One launch; when the tiles alone would leave most SMs idle (short
- * prompts), K is split across CTAs: each split stores its fp32 partial in the caller's scratch and a
- * second launch (programmatic dependent launch, same stream) sums the partials in split order
- * (deterministic) and applies the epilogue. qd_tc_gemm_plan reports the grid, tile width, K split and
+ * bf16(bf16(silu(bf16 g)) * bf16 u). One launch, persistent over the tiles; the tiles that fill whole
+ * waves of SMs run whole, and the tiles of a last, partial wave (all of them for a short prompt) are split
+ * along K across CTAs: each split stores its fp32 partial in the caller's scratch and a second launch
+ * (programmatic dependent launch, same stream) sums the partials in split order (deterministic) and
+ * applies the epilogue. Every launch waits for the previous kernel of the stream (griddepcontrol.wait)
+ * before reading x or res. qd_tc_gemm_plan reports the grid, tile width, K split and
  * the scratch bytes needed (0 without a split; otherwise 16-byte aligned, any contents; launches that
  * share one scratch run in stream order, so one buffer of the largest size serves every shape). */
 int qd_tc_gemm_plan(int64_t m, int64_t n, int64_t k, int* grid, int* bn, int* ksplit, int64_t* scratch_bytes);
