@@ -48,6 +48,8 @@ def _args():
     p.add_argument("--cpu-steps", type=int, default=96, help="decode steps in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-config4", action="store_true",
+                   help="skip the config-4 leg (global batch 64 split over the ranks, prompt 1024)")
     p.add_argument("--speculate", type=int, default=0,
                    help="also time the end-to-end run with exact prompt-lookup speculation of this verify width "
                         "(batch 1; reported as e2e_speculative, not the headline)")
@@ -352,6 +354,10 @@ def run_ours(a):
                     "peak_kind": peak_kind, "avg_launch_us": round(gu_ms * 1e3, 2), "algorithmic_bytes": gu_bytes,
                     "traffic": (prof or {}).get("traffic_bytes_per_launch")}
 
+    c4 = None
+    if not a.no_config4 and a.layers == 36:
+        c4 = config4_leg(eng, cfg, a, world, rank, local, peak)
+
     cpu = None
     if rank == 0 and not a.no_cpu_baseline:
         try:
@@ -383,10 +389,73 @@ def run_ours(a):
                                     {"persistent": 1, "kernels": 2 + 5 * a.layers, "tc": 3 + 7 * a.layers}[st.mode])}
         if e2e_spec is not None:
             out["e2e_speculative"] = e2e_spec
+        if c4 is not None:
+            out["config4"] = c4
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def config4_leg(eng, cfg, a, world, rank, local, peak):
+    """BASELINE config 4 under the same launch: a global batch of 64 sequences (prompt 1024, 512 new)
+    split over the ranks (64 / N each, the shard launcher's contiguous split), no collective on the hot
+    path. Each rank runs its own prompt forward and then decode steps; K steps (at most 64) are timed on
+    the device, centred on the middle of the 512 new tokens (the steps before them run untimed), between
+    barriers, and the max over ranks is taken. value = 64 * K / that time. The per-GPU roofline counts
+    the weights plus the rank's KV cache read at the timed positions."""
+    import torch
+    import torch.distributed as dist
+
+    from decode_b200 import shard, synth
+
+    GB, S, NEW = 64, 1024, 512
+    lo, hi = shard.split_rows(GB, world)[rank] if rank < min(world, GB) else (0, 0)
+    b = hi - lo
+    K = max(1, min(a.steps, 64))
+    W = max(3, NEW // 2 - K // 2)
+    prompt = synth.random_prompt(GB, S, cfg["vocab_size"], seed=4)[lo:hi]
+    eng.state = None
+    st = eng._build(b, S, NEW)
+    with torch.inference_mode():
+        st.ids.copy_(torch.tensor(prompt, dtype=torch.int64))
+        st.pos.fill_(S)
+        st.prefill_graph.replay()
+        for _ in range(W):
+            st.decode_graph.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        stream = torch.cuda.current_stream()
+        t_s, t_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t_s.record(stream)
+        for _ in range(K):
+            st.decode_graph.replay()
+        t_e.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        eng.check_device_errors(st)
+    ms = t_s.elapsed_time(t_e)
+    ms_max = ms
+    if world > 1:
+        tt = torch.tensor([ms], device=f"cuda:{local}")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_max = float(tt.item())
+    L_avg = S + W + K / 2
+    step_bytes = weight_bytes(cfg) + b * kv_bytes_per_token(cfg) * (L_avg + 1)
+    per_gpu = step_bytes / (ms / K / 1e3) / 1e9
+    mode = st.mode + ("+persistent" if st.tstep is not None else ("+chain" if st.mode == "tc" else ""))
+    eng.state = None
+    return {"workload": "BASELINE config 4: Qwen3-4B arch 36 layers, global batch 64 split over the GPUs, "
+                        "prompt 1024, decode steps timed at new tokens "
+                        f"{W + 1}..{W + K} of 512", "value": round(GB * K / (ms_max / 1e3), 1),
+            "unit": "tokens/s", "global_batch": GB, "batch_per_gpu": b, "n_gpus": world, "steps": K,
+            "ms_per_step": round(ms_max / K, 4), "step_mode": mode, "scaling": "strong",
+            "roofline_per_gpu": {"bytes_per_step": int(step_bytes), "achieved": round(per_gpu, 1), "peak": peak,
+                                 "unit": "GB/s", "frac": round(per_gpu / peak, 4)},
+            "roofline_tokens_per_s": round(GB * peak * 1e9 / step_bytes, 1)}
 
 
 def run_prefill_forward(a):

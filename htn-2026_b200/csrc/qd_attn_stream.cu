@@ -427,11 +427,6 @@ extern "C" int qd_attn_decode_stream(const void* q, const void* k_cache, const v
   a.tickets = reinterpret_cast<int*>(sc + ot);
   a.err = err;
   const int smem = (int)sizeof(StreamSmem);
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    configured = true;
-  }
+  if (int rc = set_max_dynamic_smem((const void*)attn_stream_kernel, smem)) return rc;
   return launch_kernel((const void*)attn_stream_kernel, dim3(grid), dim3(kSThreads), smem, pdl, stream, &a);
 }

@@ -525,11 +525,6 @@ extern "C" int qd_attn_decode_tc(const void* q, const void* k_cache, const void*
   a.tickets = reinterpret_cast<int*>(sc + ot);
   a.err = err;
   const int smem = TcAttnLayout::total + 1024;  // + base alignment slack
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    configured = true;
-  }
+  if (int rc = set_max_dynamic_smem((const void*)attn_tc_kernel, smem)) return rc;
   return launch_kernel((const void*)attn_tc_kernel, dim3(grid), dim3(kTThreads), smem, pdl, stream, &a);
 }

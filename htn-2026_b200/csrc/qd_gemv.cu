@@ -163,12 +163,7 @@ bool make_plan(int64_t n_rows, int64_t k, int M, int grid_hint, Plan* p) {
 template <int M, int MODE>
 static int launch_m(const GemvArgs& a, int smem, int pdl, cudaStream_t stream) {
   auto kern = gemv_kernel<M, MODE>;
-  static int configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    configured = smem;
-  }
+  if (int rc = set_max_dynamic_smem((const void*)kern, smem)) return rc;
   return launch_kernel((const void*)kern, dim3(a.grid), dim3(kThreads), smem, pdl, stream, (void*)&a);
 }
 

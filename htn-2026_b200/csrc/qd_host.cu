@@ -1,6 +1,9 @@
 // Library identification, error reporting and the shared launch helper.
 #include <cstdarg>
 #include <cstdio>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "qd_host.h"
 
@@ -37,6 +40,21 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
   }
   return fn;
+}
+
+int set_max_dynamic_smem(const void* func, int smem) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;  // (kernel, device) -> limit set
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lock(mu);
+  int& have = done[std::make_pair(func, dev)];
+  if (smem <= have) return QD_OK;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  have = smem;
+  return QD_OK;
 }
 
 int launch_kernel(const void* func, dim3 grid, dim3 block, int smem, int pdl, cudaStream_t stream, void* arg) {

@@ -17,6 +17,10 @@ int host_sm_count();
 // cudaLaunchKernelEx of a kernel whose only parameter is the struct at `arg`; `pdl` adds the
 // programmatic-stream-serialization attribute so the kernel may start before its predecessor ends.
 int launch_kernel(const void* func, dim3 grid, dim3 block, int smem, int pdl, cudaStream_t stream, void* arg);
+// Raise `func`'s dynamic shared memory limit to at least `smem` bytes on the current device. The
+// attribute belongs to the device's context, so the largest value set so far is remembered per
+// (kernel, device) pair, under a lock: a process that drives several GPUs sets it on each of them.
+int set_max_dynamic_smem(const void* func, int smem);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -389,6 +389,63 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const __grid_constant
   }
 }
 
+// ------------------------------------------------------------------ row argmax (the prompt's first token)
+struct ArgmaxArgs {
+  const __nv_bfloat16* logits;  // [rows, ld]
+  int64_t* out;                 // [rows]
+  int64_t ld, n;                // n = entries per row that compete (the vocabulary)
+};
+
+// The better of two (value, index) candidates: the larger value, the lower index on an exact tie.
+__device__ __forceinline__ bool argmax_better(float v, int64_t i, float bv, int64_t bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+// One CTA of 256 threads per row: out[row] = the index of the row's largest BF16 logit, the lowest
+// index among exact ties (the greedy rule the reference applies to the prompt's last-position logits,
+// engine/engine.py:583-591). 16-byte loads over the row, a scalar tail past the last full vector,
+// then a butterfly across each warp and one pass over the 8 warp winners.
+__global__ void __launch_bounds__(256) argmax_rows_kernel(const __grid_constant__ ArgmaxArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  __shared__ float wv[8];
+  __shared__ int64_t wi[8];
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const __nv_bfloat16* r = a.logits + row * a.ld;
+  float best = -INFINITY;
+  int64_t bidx = INT64_MAX;
+  const int64_t n8 = a.n >> 3;
+  for (int64_t q = tid; q < n8; q += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(r + q * 8);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float lo = bf_lo(u[e]), hi = bf_hi(u[e]);
+      const int64_t i = q * 8 + 2 * e;
+      if (argmax_better(lo, i, best, bidx)) best = lo, bidx = i;
+      if (argmax_better(hi, i + 1, best, bidx)) best = hi, bidx = i + 1;
+    }
+  }
+  for (int64_t i = n8 * 8 + tid; i < a.n; i += 256) {
+    const float v = __bfloat162float(r[i]);
+    if (argmax_better(v, i, best, bidx)) best = v, bidx = i;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float v = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t i = __shfl_xor_sync(0xffffffffu, bidx, o);
+    if (argmax_better(v, i, best, bidx)) best = v, bidx = i;
+  }
+  if (lane == 0) wv[warp] = best, wi[warp] = bidx;
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < 8; ++w)
+      if (argmax_better(wv[w], wi[w], best, bidx)) best = wv[w], bidx = wi[w];
+    a.out[row] = bidx == INT64_MAX ? 0 : bidx;  // a row of NaN only: index 0
+  }
+}
+
 // ------------------------------------------------------------------ prompt q/k norm + RoPE + cache write
 struct QkRopeArgs {
   const __nv_bfloat16* qkv;  // [b * S, (nq + 2 nkv) * 128], token t = i * S + s
@@ -1248,12 +1305,7 @@ template <int BN, int EPI>
 static int launch_gemm(const GemmArgs& a, int grid, cudaStream_t stream) {
   auto kern = tc_gemm_kernel<BN, EPI>;
   const int smem = GemmLayout<BN>::total(a.nst) + 1024;
-  static int configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    configured = smem;
-  }
+  if (int rc = set_max_dynamic_smem((const void*)kern, smem)) return rc;
   return launch_kernel((const void*)kern, dim3(grid), dim3(kGemmThreads), smem, 1, stream, (void*)&a);
 }
 
@@ -1375,6 +1427,19 @@ extern "C" int qd_rmsnorm_rows(const void* x, int64_t ldx, int64_t m, int64_t k,
   a.k = k;
   a.eps = eps;
   return launch_kernel((const void*)rmsnorm_rows_kernel, dim3((unsigned)m), dim3(256), 0, 1, stream, &a);
+}
+
+extern "C" int qd_argmax_rows(const void* logits, int64_t ld, int64_t n, int64_t rows, int64_t* out,
+                              cudaStream_t stream) {
+  if (!logits || !out) return set_error(QD_ERR_ARG, "null pointer");
+  if (rows < 1 || rows > INT32_MAX || n < 1 || ld < n || ld % 8) return set_error(QD_ERR_ARG, "argmax: bad sizes");
+  if (!aligned16(logits)) return set_error(QD_ERR_ARG, "argmax: logits not 16-byte aligned");
+  ArgmaxArgs a = {};
+  a.logits = static_cast<const __nv_bfloat16*>(logits);
+  a.out = out;
+  a.ld = ld;
+  a.n = n;
+  return launch_kernel((const void*)argmax_rows_kernel, dim3((unsigned)rows), dim3(256), 0, 1, stream, &a);
 }
 
 extern "C" int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int64_t S, int nq_heads, int nkv_heads,
@@ -1499,22 +1564,12 @@ static int prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_
   if (env_int("QD_PREFILL_ATTN", 1) == 2 && (nq_heads / nkv_heads) % 2 == 0) {  // ping-pong variant
     a.units = (int)(units / 2);  // a unit covers two query heads of one KV head
     const int smem = PpLayout::total + 1024;
-    static bool configured_pp = false;
-    if (!configured_pp) {
-      cudaError_t e = cudaFuncSetAttribute(prefill_attn_pp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-      configured_pp = true;
-    }
+    if (int rc = set_max_dynamic_smem((const void*)prefill_attn_pp_kernel, smem)) return rc;
     const int grid = a.units < host_sm_count() ? a.units : host_sm_count();
     return launch_kernel((const void*)prefill_attn_pp_kernel, dim3(grid), dim3(kPpThreads), smem, 1, stream, &a);
   }
   const int smem = PaLayout::total;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    configured = true;
-  }
+  if (int rc = set_max_dynamic_smem((const void*)prefill_attn_kernel, smem)) return rc;
   const int grid = units < host_sm_count() ? (int)units : host_sm_count();
   return launch_kernel((const void*)prefill_attn_kernel, dim3(grid), dim3(kPaThreads), smem, 1, stream, &a);
 }

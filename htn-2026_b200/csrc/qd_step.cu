@@ -626,12 +626,7 @@ static int step_plan(const qd_step_desc* d, StepPlan* p) {
 template <int M>
 static int launch_step(const StepArgs& a, int smem, cudaStream_t stream) {
   auto kern = step_kernel<M>;
-  static int configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    configured = smem;
-  }
+  if (int rc = set_max_dynamic_smem((const void*)kern, smem)) return rc;
   int per_sm = 0;
   cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
   if (e != cudaSuccess || per_sm < 1)

@@ -379,12 +379,7 @@ template <int N, int MODE>
 static int tc_launch_nm(const GemvArgs& a, int pdl, cudaStream_t stream) {
   auto kern = tc_gemv_kernel<N, MODE>;
   const int smem = tc_layout(N, a.nst).total + 1024;  // + alignment slack
-  static int configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    configured = smem;
-  }
+  if (int rc = set_max_dynamic_smem((const void*)kern, smem)) return rc;
   return launch_kernel((const void*)kern, dim3(a.grid), dim3(kTcThreads), smem, pdl, stream, (void*)&a);
 }
 

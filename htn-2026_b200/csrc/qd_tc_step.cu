@@ -945,12 +945,7 @@ static int tc_step_plan(const qd_step_desc* d, TcStepPlan* p) {
 template <int N>
 static int launch_tc_step(const TcStepArgs& a, int smem, cudaStream_t stream) {
   auto kern = tc_step_kernel<N>;
-  static int configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return set_error(QD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    configured = smem;
-  }
+  if (int rc = set_max_dynamic_smem((const void*)kern, smem)) return rc;
   int per_sm = 0;
   cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kPThreads, smem);
   if (e != cudaSuccess || per_sm < 1)

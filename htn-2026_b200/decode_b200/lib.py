@@ -88,6 +88,7 @@ PROTOTYPES = {
     "qd_tc_gemm": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_void_p,
                            c_int64, c_int, c_void_p, c_int64, c_void_p, c_void_p]),
     "qd_rmsnorm_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_float, c_void_p, c_int64, c_void_p]),
+    "qd_argmax_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
     "qd_prefill_qk_rope": (c_int, [c_void_p, c_int64, c_int, c_int64, c_int, c_int, c_void_p, c_void_p, c_float,
                                    c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                                    c_int64, c_void_p]),

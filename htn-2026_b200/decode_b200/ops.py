@@ -303,6 +303,17 @@ def rmsnorm_rows(x, w, eps: float, out):
     return out
 
 
+def argmax_rows(logits, n: int, out):
+    """out[i] = index of the largest of logits[i, :n], lowest index on exact ties (qd_argmax_rows).
+    logits [rows, ld] BF16 with unit column stride; out int64 [rows]."""
+    _check_bf16(logits)
+    assert logits.stride(1) == 1 and out.dtype == torch.int64 and out.is_contiguous()
+    rows = logits.shape[0]
+    assert out.numel() >= rows and n <= logits.shape[1]
+    L.call("qd_argmax_rows", _ptr(logits), logits.stride(0), n, rows, _ptr(out), _stream())
+    return out
+
+
 def prefill_qk_rope(qkv, batch: int, S: int, nq: int, nkv: int, q_norm, k_norm, eps: float, cos, sin, q_out,
                     k_cache, v_cache, pos0: int = 0):
     """q/k RMSNorm + RoPE of the positions pos0..pos0+S-1, K/V into the caches (qd_prefill_qk_rope, or

@@ -1,56 +1,69 @@
-"""Prompt-lookup drafts for exact speculative decoding (engine/engine.py:759-828, the reference's
-`_stream_spec`).
+"""Host side of exact prompt-lookup speculative decoding (the reference's `_stream_spec`,
+engine/engine.py:759-828).
 
-A sequence's history (prompt + generated tokens) is indexed by its 3-grams and 2-grams, each mapped to
-the index just after its latest occurrence whose continuation exists. The draft after the history
-`seq` is the continuation of the latest earlier occurrence of seq[-3:] (else of seq[-2:]), k tokens
-long, padded with seq[-1] when shorter or when neither n-gram occurred. The verify forward runs the T =
-k + 1 tokens [seq[-1]] + draft at positions len(seq) - 1 ..; its greedy token after every prefix decides
-how many draft tokens are accepted (`accept`), so the emitted tokens are the verify forward's own
-greedy tokens whatever the draft was.
+Drafting rule (kept from the reference, because it decides which tokens get proposed and so how many
+verifies a generation takes): the draft after a history is the continuation of the latest earlier
+occurrence of its last 3 tokens, else of its last 2, cut to k tokens and padded with the last token
+(k copies of it when neither occurred). `NgramDrafter` keeps, per n-gram order, a table from each
+n-gram to the index just after its latest occurrence that already has a continuation; it is fed one
+token at a time, so a lookup never rescans the history.
+
+A verify forward runs T = k + 1 tokens, [last emitted] + draft, and returns the greedy token after each
+prefix of that row. `verified_tokens` keeps the drafts the model agrees with and the model's own token
+after them, so what is emitted is always the verify forward's greedy output, whatever was drafted.
 """
 
 from __future__ import annotations
 
-
-class PromptLookup:
-    """n-gram index of one sequence (engine/engine.py:776-787 register, :802-808 the draft)."""
-
-    def __init__(self, seq: list[int]):
-        self.seq = seq  # shared with the caller, which extends it
-        self.i3: dict[tuple[int, int, int], int] = {}
-        self.i2: dict[tuple[int, int], int] = {}
-        self.reg = 1  # next n-gram end index to register
-        self.register()
-
-    def register(self) -> None:
-        """Index the n-grams ending at j for every j whose continuation seq[j + 1] exists."""
-        seq, i3, i2 = self.seq, self.i3, self.i2
-        for j in range(self.reg, len(seq) - 1):
-            i2[(seq[j - 1], seq[j])] = j + 1
-            if j >= 2:
-                i3[(seq[j - 2], seq[j - 1], seq[j])] = j + 1
-        self.reg = max(self.reg, len(seq) - 1)
-
-    def draft(self, k: int) -> list[int]:
-        seq = self.seq
-        last = seq[-1]
-        p = self.i3.get((seq[-3], seq[-2], last)) if len(seq) >= 3 else None
-        if p is None and len(seq) >= 2:
-            p = self.i2.get((seq[-2], last))
-        d = seq[p:p + k] if p is not None else []
-        return d + [last] * (k - len(d))
+import time
+from itertools import takewhile
 
 
-def accept(row: list[int], greedy: list[int]) -> list[int]:
-    """Tokens emitted by one verify (engine/engine.py:819-825): row = [last] + draft, greedy[t] = the
-    greedy token after row[:t + 1]. The leading drafts that equal the greedy tokens are accepted, then
-    the greedy token after them."""
-    k = len(row) - 1
-    a = 0
-    while a < k and row[a + 1] == greedy[a]:
-        a += 1
-    return greedy[:a + 1]
+class NgramDrafter:
+    """Draft proposals from a token history, by n-gram lookup (longest order first)."""
+
+    def __init__(self, history=(), orders=(3, 2)):
+        self.orders = tuple(sorted(orders, reverse=True))
+        self.history: list[int] = []
+        # order -> {n-gram: index where its latest continued occurrence's continuation starts}
+        self.next_at: dict[int, dict[tuple, int]] = {n: {} for n in self.orders}
+        for tok in history:
+            self.push(tok)
+
+    def push(self, tok: int) -> None:
+        """Append one token. It is the continuation of every n-gram that ends just before it, so
+        those n-grams now point here."""
+        h = self.history
+        here = len(h)
+        for n in self.orders:
+            if here >= n:
+                self.next_at[n][tuple(h[here - n:])] = here
+        h.append(tok)
+
+    def extend(self, toks) -> None:
+        for tok in toks:
+            self.push(tok)
+
+    def propose(self, k: int) -> list[int]:
+        """k draft tokens to follow the current history."""
+        h = self.history
+        for n in self.orders:
+            if len(h) < n:
+                continue
+            at = self.next_at[n].get(tuple(h[-n:]))
+            if at is not None:
+                cont = h[at:at + k]
+                return cont + [h[-1]] * (k - len(cont))
+        return [h[-1]] * k
+
+
+def verified_tokens(row: list[int], greedy: list[int]) -> list[int]:
+    """What one verify emits. row = [last emitted] + drafts; greedy[i] = the model's token after
+    row[:i + 1]. Draft i + 1 stands only if it equals greedy[i] (the token the model itself would have
+    produced at that point) and every draft before it stood; the model's token after the last standing
+    draft is emitted too."""
+    agreed = sum(1 for _ in takewhile(lambda pair: pair[0] == pair[1], zip(row[1:], greedy)))
+    return greedy[:agreed + 1]
 
 
 class Gate:
@@ -69,7 +82,7 @@ class Gate:
 
     def cost(self) -> float:
         """One verify in plain steps: measured once both have run, the prior before."""
-        if self.n_verify and self.n_step:
+        if self.n_verify and self.n_step and self.t_step > 0:
             return (self.t_verify / self.n_verify) / (self.t_step / self.n_step)
         return self.prior_cost
 
@@ -94,41 +107,49 @@ class Gate:
 
 def stream(seq: list[int], S: int, N: int, k: int, verify, stats: dict | None = None, step=None,
            gate: Gate | None = None):
-    """The speculative loop after the prompt forward (engine/engine.py:788-828, one sequence): `seq` is
-    the prompt (S tokens) plus the first generated token; yields generated tokens 2..N, one at a time.
-    verify(row, pos0) returns the greedy token after every prefix of row (k + 1 tokens at positions
-    pos0 ..); every verify starts at the last emitted token, so pos0 + k + 1 <= S + N + k - 1. With
-    `step` (plain decode steps: step(token, pos, n) yields the n greedy tokens after `token` at `pos`,
-    one at a time) and a `gate`, the tokens the gate hands to plain steps come from `step`; both emit
-    greedy tokens."""
-    import time
+    """The speculative loop after the prompt forward (one sequence). `seq` is the prompt (S tokens)
+    plus the first generated token; it is extended in place with every emitted token, and generated
+    tokens 2..N are yielded one at a time.
 
-    look = PromptLookup(seq)
-    yielded = len(seq) - S
+    verify(row, pos0) returns the greedy token after every prefix of row (k + 1 tokens at positions
+    pos0 ..); a verify always starts at the last emitted token, so pos0 + k + 1 <= S + N + k - 1.
+    With `step` (plain decode steps: step(token, pos, n) yields the n greedy tokens after `token` at
+    `pos`, one at a time) and a `gate`, the runs of tokens the gate hands to plain steps come from
+    `step`. Both emit greedy tokens, so the output does not depend on the gate. The gate's clock for
+    plain steps runs only while `step` produces a token, not while the caller consumes one."""
+    drafter = NgramDrafter(seq)
+    done = len(seq) - S  # generated tokens already delivered (the first one came from the prefill)
     stats = {} if stats is None else stats
     stats["verifies"] = stats["plain_steps"] = 0
-    plain = 0
-    while yielded < N:
-        if plain and step is not None:
-            n = min(plain, N - yielded)
-            t0 = time.perf_counter()
-            for tok in step(seq[-1], len(seq) - 1, n):
+    plain_run = 0
+    while done < N:
+        if plain_run and step is not None:
+            n = min(plain_run, N - done)
+            plain_run = 0
+            tokens = step(seq[-1], len(seq) - 1, n)
+            busy = 0.0
+            for _ in range(n):
+                t0 = time.perf_counter()
+                tok = next(tokens)
+                busy += time.perf_counter() - t0
                 seq.append(tok)
+                drafter.push(tok)
+                done += 1
                 yield tok
-                yielded += 1
-            if gate is not None:
-                gate.stepped(time.perf_counter() - t0, n)
             stats["plain_steps"] += n
-            plain = 0
-        else:
-            row = [seq[-1]] + look.draft(k)
-            t0 = time.perf_counter()
-            got = accept(row, verify(row, len(seq) - 1))
-            seq.extend(got)
-            stats["verifies"] += 1
-            if gate is not None and step is not None:
-                plain = gate.verified(len(got), time.perf_counter() - t0)
-        look.register()
-        while yielded < N and len(seq) - S > yielded:
-            yield seq[S + yielded]
-            yielded += 1
+            if gate is not None:
+                gate.stepped(busy, n)
+            continue
+        row = [seq[-1]] + drafter.propose(k)
+        t0 = time.perf_counter()
+        got = verified_tokens(row, verify(row, len(seq) - 1))
+        spent = time.perf_counter() - t0
+        stats["verifies"] += 1
+        if gate is not None and step is not None:
+            plain_run = gate.verified(len(got), spent)
+        for tok in got:
+            seq.append(tok)
+            drafter.push(tok)
+        for tok in got[:N - done]:
+            done += 1
+            yield tok

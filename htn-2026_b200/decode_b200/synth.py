@@ -127,8 +127,11 @@ def make_state_dict(cfg: dict, seed: int = 0, std: float = 0.02, threads: int | 
     return out
 
 
-def write_checkpoint(path: str, cfg: dict, seed: int = 0, state: dict | None = None) -> str:
-    """Write config.json + model.safetensors under `path` (created if missing); returns path."""
+def write_checkpoint(path: str, cfg: dict, seed: int = 0, state: dict | None = None, shards: int = 1) -> str:
+    """Write config.json and the weights under `path` (created if missing); returns path. shards == 1:
+    one model.safetensors; shards > 1: model-0000i-of-0000n.safetensors files (tensors dealt out in
+    order, by size) plus the model.safetensors.index.json weight map, as Hugging Face saves large
+    checkpoints."""
     from safetensors.torch import save_file
 
     os.makedirs(path, exist_ok=True)
@@ -136,8 +139,23 @@ def write_checkpoint(path: str, cfg: dict, seed: int = 0, state: dict | None = N
         state = make_state_dict(cfg, seed)
     with open(os.path.join(path, "config.json"), "w") as f:
         json.dump(hf_config_json(cfg), f, indent=1)
-    save_file({k: v.contiguous() for k, v in state.items()}, os.path.join(path, "model.safetensors"),
-              metadata={"format": "pt"})
+    if shards <= 1:
+        save_file({k: v.contiguous() for k, v in state.items()}, os.path.join(path, "model.safetensors"),
+                  metadata={"format": "pt"})
+    else:
+        names = list(state)
+        total = sum(state[n].numel() for n in names)
+        groups, acc = [[] for _ in range(shards)], 0
+        for n in names:  # contiguous runs of roughly total / shards elements each
+            groups[min(shards - 1, acc * shards // max(total, 1))].append(n)
+            acc += state[n].numel()
+        weight_map = {}
+        for i, group in enumerate(groups):
+            fn = f"model-{i + 1:05d}-of-{shards:05d}.safetensors"
+            save_file({n: state[n].contiguous() for n in group}, os.path.join(path, fn), metadata={"format": "pt"})
+            weight_map.update({n: fn for n in group})
+        with open(os.path.join(path, "model.safetensors.index.json"), "w") as f:
+            json.dump({"metadata": {"total_size": 2 * total}, "weight_map": weight_map}, f, indent=1)
     with open(os.path.join(path, "synth.json"), "w") as f:
         json.dump({"seed": seed, "std": 0.02, "generator": "torch CPU normal_ per 4Mi-element chunk"}, f)
     return path

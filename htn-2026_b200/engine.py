@@ -23,12 +23,14 @@ Weights are packed once at load into the kernels' blocked layout (decode_b200/op
 kept. The prompt forward (prefill, engine/engine.py:550-592) runs on the same packed weights through
 the library's tcgen05 GEMM (qd_tc_gemm, fused residual / SwiGLU epilogues), row RMSNorm, prompt
 q/k-norm + RoPE + KV-cache kernel and tcgen05 causal flash attention (qd_prefill_attn). It is
-captured in a CUDA graph too. The stream loop keeps the GPU one step ahead of the
-host like engine/engine.py:719-757.
+captured in a CUDA graph too. Tokens reach the host through a ring of pinned slots (`_TokenRing`): the
+GPU runs up to ENGINE_AHEAD decode steps ahead of the caller, who gets each step's token list as soon as
+its copy has landed (the reference's stream loop, engine/engine.py:719-757, keeps one step ahead).
 """
 
 from __future__ import annotations
 
+import contextlib
 import gc
 import os
 import sys
@@ -67,6 +69,8 @@ SPEC_GATE = os.environ.get("ENGINE_SPEC_GATE", "1") != "0"
 # "tc": the tensor-core kernels (used from TC_MIN_BATCH up): one persistent launch per step, or the
 # chain of 1 + 7 x layers + 2 launches (TC_STEP)
 STEP_MODE = os.environ.get("ENGINE_STEP", "persistent")
+# decode steps the GPU may have queued beyond the one whose tokens the caller is waiting for
+AHEAD = max(1, int(os.environ.get("ENGINE_AHEAD", "2")))
 
 
 def log(msg):
@@ -81,6 +85,84 @@ def rope_tables(cap: int, head_dim: int, theta: float):
     freqs = (inv_freq[None, :, None].float() @ pos[:, None, :].float()).transpose(1, 2)
     emb = torch.cat((freqs, freqs), dim=-1)
     return emb.cos()[0].to(BF16).contiguous(), emb.sin()[0].to(BF16).contiguous()
+
+
+class _TokenRing:
+    """Delivers each decode step's token vector from the device to the host.
+
+    `post` enqueues, on the current stream, a copy of the device token vector into the next pinned
+    slot and records an event behind it; `take` waits for the oldest posted copy and returns it as a
+    list. A ring of `slots` slots lets the device run up to slots - 1 steps ahead of the host; a slot is
+    reused only after `take` has read it."""
+
+    def __init__(self, batch: int, slots: int, pin: bool):
+        self.buf = torch.empty((slots, batch), dtype=torch.int64, pin_memory=pin)
+        self.landed = [torch.cuda.Event() for _ in range(slots)]
+        self.posted = self.taken = 0
+
+    def reset(self) -> None:
+        self.posted = self.taken = 0
+
+    def in_flight(self) -> int:
+        return self.posted - self.taken
+
+    def post(self, tok: torch.Tensor) -> None:
+        if self.in_flight() == len(self.landed):
+            raise RuntimeError("token ring overrun: take() before posting more steps")
+        i = self.posted % len(self.landed)
+        self.buf[i].copy_(tok, non_blocking=True)
+        self.landed[i].record()
+        self.posted += 1
+
+    def take(self) -> list[int]:
+        i = self.taken % len(self.landed)
+        self.landed[i].synchronize()
+        self.taken += 1
+        return self.buf[i].tolist()
+
+
+class _StepTimer:
+    """Optional CUDA-event brackets around each enqueued step (prefill first), read after the run."""
+
+    def __init__(self):
+        self.pairs = []
+
+    @contextlib.contextmanager
+    def span(self):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        yield
+        b.record()
+        self.pairs.append((a, b))
+
+    def ms(self) -> list[float]:
+        return [a.elapsed_time(b) for a, b in self.pairs]
+
+
+def prefill_chunks(batch: int, prompt_len: int, max_tokens: int) -> list[tuple[int, int]]:
+    """Row ranges [r0, r1) of whole sequences for the prompt forward, each holding at most max_tokens
+    tokens (or one sequence when a single prompt is longer), so a long batch runs as several forwards
+    of bounded activation size (the reference bounds its prefill the same way, engine/engine.py:79)."""
+    per = max(1, max_tokens // prompt_len)
+    return [(r0, min(batch, r0 + per)) for r0 in range(0, batch, per)]
+
+
+def _timed(timer: _StepTimer, fn, st) -> None:
+    with timer.span():
+        fn(st)
+
+
+@contextlib.contextmanager
+def _collector_paused():
+    """Python's cyclic garbage collector paused while tokens stream: a collection pass on the caller's
+    thread would delay the next launch. Restored to its previous state afterwards."""
+    was_on = gc.isenabled()
+    gc.disable()
+    try:
+        yield
+    finally:
+        if was_on:
+            gc.enable()
 
 
 class _State:
@@ -129,11 +211,10 @@ class _State:
         self.tstep = ops.TcDecodeStep(eng, self) if (self.mode == "tc" and persistent_tc) else None
         self.tstep_logits = None
         self.step_logits = None
-        self.rows = max(1, min(B, PREFILL_TOKENS // S))
+        self.chunks = prefill_chunks(B, S, PREFILL_TOKENS)
         pin = torch.cuda.is_available()
-        self.host = torch.empty((max(N, 1), B), dtype=torch.int64, pin_memory=pin)
-        self.ids_host = torch.empty((B, S), dtype=torch.int64, pin_memory=pin)
-        self.events = [torch.cuda.Event() for _ in range(max(N, 1))]
+        self.prompt_host = torch.empty((B, S), dtype=torch.int64, pin_memory=pin)  # staging of the prompt upload
+        self.ring = _TokenRing(B, AHEAD + 1, pin)
         self.prefill_graph = self.decode_graph = None
         self.prefill_logits = None
         self.verify = _Verify(eng, self, spec_T) if spec_T else None
@@ -338,8 +419,7 @@ class Engine:
         RES, SWIGLU = ops.Gemv.RES, ops.Gemv.SWIGLU
         last_layer = self.n_layers - 1
         logits = torch.empty((B, vrows), dtype=BF16, device=dev)
-        for r0 in range(0, B, st.rows):
-            r1 = min(B, r0 + st.rows)
+        for r0, r1 in st.chunks:
             b, M = r1 - r0, (r1 - r0) * S
             x = torch.empty((M, H), dtype=BF16, device=dev)
             h = torch.empty((M, H), dtype=BF16, device=dev)
@@ -373,9 +453,8 @@ class Engine:
                 ops.tc_gemm(act, self.w_down[i], H, x, res=x, epilogue=RES, err=err, scratch=sc)
             ops.rmsnorm_rows(xl, self.final_norm, eps, hl)
             ops.tc_gemm(hl, self.e_packed, vrows, logits[r0:r1], err=err, scratch=sc)
-        logits = logits[:, :self.vocab]
-        st.tok.copy_(torch.argmax(logits, dim=-1))
-        return logits
+        ops.argmax_rows(logits, self.vocab, st.tok)  # the first generated token of every sequence
+        return logits[:, :self.vocab]
 
     def _decode_step(self, st: _State, logits: torch.Tensor | None = None) -> None:
         """One token per sequence at st.pos, all in libqd_decode: one persistent launch, or
@@ -480,94 +559,91 @@ class Engine:
         self.state = st
         return st
 
+    def _upload_prompt(self, st: _State, input_ids) -> None:
+        """Prompt ids into the device buffer the prefill graph reads (through pinned staging), and the
+        decode position reset to the prompt length: everything a replay of a new request needs."""
+        st.prompt_host.copy_(torch.as_tensor(input_ids, dtype=torch.int64))
+        st.ids.copy_(st.prompt_host, non_blocking=True)
+        st.pos.fill_(st.S)
+
+    def _enqueue_prefill(self, st: _State) -> None:
+        if st.prefill_graph is None:
+            st.prefill_logits = self._prefill(st)
+        else:
+            st.prefill_graph.replay()
+
+    def _enqueue_decode(self, st: _State) -> None:
+        if st.decode_graph is None:
+            self._decode_step(st)
+        else:
+            st.decode_graph.replay()
+
     def _stream(self, st: _State, input_ids, N: int, timing: list | None = None):
-        """Greedy stream of N steps; keeps the GPU one step ahead of the host (engine/engine.py:719-757)."""
-        B, S = st.B, st.S
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(N)] \
-            if timing is not None else None
+        """Greedy token lists of N steps. The prefill and then the decode steps are enqueued while the
+        caller consumes earlier steps; at most AHEAD steps sit queued beyond the one being delivered.
+        With `timing` (a list), the device milliseconds of every step are appended to it at the end."""
+        ring, timer = st.ring, (_StepTimer() if timing is not None else None)
+        run = (lambda fn: fn(st)) if timer is None else (lambda fn: _timed(timer, fn, st))
+        ring.reset()
         with torch.inference_mode():
-            st.ids_host.copy_(torch.tensor(input_ids, dtype=torch.int64))
-            st.ids.copy_(st.ids_host, non_blocking=True)
-            st.pos.fill_(S)
-            if ev:
-                ev[0][0].record()
-            if st.prefill_graph is not None:
-                st.prefill_graph.replay()
-            else:
-                st.prefill_logits = self._prefill(st)
-            if ev:
-                ev[0][1].record()
-            st.host[0].copy_(st.tok, non_blocking=True)
-            st.events[0].record()
-        for t in range(1, N):
-            with torch.inference_mode():
-                if ev:
-                    ev[t][0].record()
-                if st.decode_graph is not None:
-                    st.decode_graph.replay()
-                else:
-                    self._decode_step(st)
-                if ev:
-                    ev[t][1].record()
-                st.host[t].copy_(st.tok, non_blocking=True)
-                st.events[t].record()
-            st.events[t - 1].synchronize()
-            yield st.host[t - 1].tolist()
-        st.events[N - 1].synchronize()
-        self.check_device_errors(st)
-        if ev:
-            timing.extend(a.elapsed_time(b) for a, b in ev)
-        yield st.host[N - 1].tolist()
+            self._upload_prompt(st, input_ids)
+            run(self._enqueue_prefill)
+            ring.post(st.tok)
+        enqueued = 1
+        for delivered in range(N):
+            while enqueued < N and ring.in_flight() <= AHEAD:
+                with torch.inference_mode():
+                    run(self._enqueue_decode)
+                    ring.post(st.tok)
+                enqueued += 1
+            row = ring.take()
+            if delivered == N - 1:  # everything has run: surface a device-side error before the last list
+                self.check_device_errors(st)
+                if timer is not None:
+                    timing.extend(timer.ms())
+            yield row
 
     def _stream_spec(self, st: _State, input_ids, N: int):
-        """Exact prompt-lookup speculative decoding of one sequence (engine/engine.py:759-828): after the
-        prompt forward, every verify runs T = k + 1 tokens (the last emitted token and a k-token
-        prompt-lookup draft) and emits the accepted drafts plus the greedy token after them; yields
-        exactly N steps. The emitted tokens are the verify forward's greedy tokens."""
+        """Exact prompt-lookup speculative decoding of one sequence (the reference's _stream_spec,
+        engine/engine.py:759-828): after the prompt forward, every verify runs T = k + 1 tokens (the last
+        emitted token and a k-token draft from the sequence's own history) and emits the accepted drafts
+        plus the greedy token after them; exactly N steps are yielded. The emitted tokens are the verify
+        forward's greedy tokens whatever the draft was."""
         S, vf = st.S, st.verify
-        k = vf.T - 1
+        ring = st.ring
+        ring.reset()
         with torch.inference_mode():
-            st.ids_host.copy_(torch.tensor(input_ids, dtype=torch.int64))
-            st.ids.copy_(st.ids_host, non_blocking=True)
-            st.pos.fill_(S)
-            if st.prefill_graph is not None:
-                st.prefill_graph.replay()
-            else:
-                st.prefill_logits = self._prefill(st)
-            st.host[0].copy_(st.tok, non_blocking=True)
-            st.events[0].record()
-        st.events[0].synchronize()
-        first = st.host[0].tolist()
+            self._upload_prompt(st, input_ids)
+            self._enqueue_prefill(st)
+            ring.post(st.tok)
+        first = ring.take()
         yield first
         st.spec_stats = {}
-        step = (lambda tok, pos, n: self._plain_steps(st, tok, pos, n)) if SPEC_GATE else None
-        for tok in spec.stream(list(input_ids[0]) + first, S, N, k, lambda row, pos0: vf(self, st, row, pos0),
-                               st.spec_stats, step=step, gate=spec.Gate() if SPEC_GATE else None):
+        plain = (lambda tok, pos, n: self._plain_steps(st, tok, pos, n)) if SPEC_GATE else None
+        for tok in spec.stream(list(input_ids[0]) + first, S, N, vf.T - 1, lambda row, pos0: vf(self, st, row, pos0),
+                               st.spec_stats, step=plain, gate=spec.Gate() if SPEC_GATE else None):
             yield [tok]
         self.check_device_errors(st)
 
     def _plain_steps(self, st: _State, tok: int, pos: int, n: int):
-        """n plain decode steps of a batch-1 state from the host's token and position (the speculative
-        loop's fallback), yielding the greedy tokens one at a time. As in `_stream`, the GPU runs a step
-        ahead of the host: each decode-graph replay takes its token and position from the previous one."""
-        vf = st.verify
+        """n plain decode steps of a batch-1 state continuing from the host's token at position `pos` (the
+        speculative loop's fallback), yielding the n greedy tokens one at a time. The first replay takes
+        its token and position from the host; each later one from the replay before it, so the device
+        runs ahead of the caller through the token ring as in `_stream`."""
+        vf, ring = st.verify, st.ring
+        ring.reset()
         with torch.inference_mode():
             vf.step_host[0], vf.step_host[1] = tok, pos
             st.tok.copy_(vf.step_host[0:1], non_blocking=True)
             st.pos.copy_(vf.step_host[1:2], non_blocking=True)
-        for t in range(n):
-            with torch.inference_mode():
-                if st.decode_graph is not None:
-                    st.decode_graph.replay()
-                else:
-                    self._decode_step(st)
-                st.host[t].copy_(st.tok, non_blocking=True)
-                st.events[t].record()
-            if t:
-                st.events[t - 1].synchronize()
-                yield int(st.host[t - 1][0])
-        st.events[n - 1].synchronize()
-        yield int(st.host[n - 1][0])
+        enqueued = 0
+        for _ in range(n):
+            while enqueued < n and ring.in_flight() <= AHEAD:
+                with torch.inference_mode():
+                    self._enqueue_decode(st)
+                    ring.post(st.tok)
+                enqueued += 1
+            yield ring.take()[0]
 
     # ------------------------------------------------------------------ API
     def generate(self, input_ids: list[list[int]], max_new_tokens: int):
@@ -577,23 +653,22 @@ class Engine:
         B, S = len(input_ids), len(input_ids[0])
         if B < 1 or S < 1 or any(len(r) != S for r in input_ids):
             raise ValueError("input_ids must be a non-empty batch of equal-length rows")
-        st = self.state
         spec_T = self.speculate if (self.speculate and B == 1 and N > 1) else 0
-        if st is None or (st.B, st.S, st.N) != (B, S, N) or (st.verify.T if st.verify else 0) != spec_T:
+        st = self.state
+        fits = st is not None and (st.B, st.S, st.N) == (B, S, N) and (st.verify.T if st.verify else 0) == spec_T
+        if not fits:
             st = self._build(B, S, N)
-        gc_was = gc.isenabled()
-        gc.disable()
-        try:
-            if st.verify is not None:
-                yield from self._stream_spec(st, input_ids, N)
-            else:
-                yield from self._stream(st, input_ids, N)
-        finally:
-            if gc_was:
-                gc.enable()
+        stream = self._stream_spec if st.verify is not None else self._stream
+        with _collector_paused():
+            yield from stream(st, input_ids, N)
 
-    def generate_with_logits(self, input_ids: list[list[int]], max_new_tokens: int):
-        """Test hook: eager (un-graphed) greedy run returning (tokens [B][N], list of N host logits [B, V])."""
+    def generate_with_logits(self, input_ids: list[list[int]], max_new_tokens: int,
+                             forced: list[list[int]] | None = None):
+        """Test hook: eager (un-graphed) greedy run returning (tokens [B][N], list of N host logits [B, V]).
+        With `forced` (tokens [B][N]), step t decodes from forced[:, t - 1] instead of the engine's own
+        token: teacher forcing, so step t's logits are the engine's logits after the forced prefix (the
+        reference checks its tiers this way, engine/engine.py:974-996). The returned tokens are still
+        the engine's own argmax at every step."""
         N = int(max_new_tokens)
         B, S = len(input_ids), len(input_ids[0])
         st = self.state
@@ -609,7 +684,9 @@ class Engine:
             lg = self._prefill(st)
             toks.append(st.tok.tolist())
             logits.append(lg.cpu())
-            for _ in range(1, N):
+            for t in range(1, N):
+                if forced is not None:
+                    st.tok.copy_(torch.tensor([row[t - 1] for row in forced], dtype=torch.int64))
                 self._decode_step(st, logits=buf)
                 toks.append(st.tok.tolist())
                 logits.append(buf.cpu())

@@ -1,7 +1,8 @@
 /* qd_decode.h - C ABI of the B200 (sm_100a) Qwen3 greedy-decode kernels.
  *
  * Every entry point takes raw device pointers, sizes and a CUDA stream; nothing here allocates,
- * synchronises or reads device memory on the host, so every call can be captured in a CUDA graph.
+ * synchronises or reads device memory on the host. The entry points that take their scratch from the
+ * caller can be captured in a CUDA graph.
  * All buffers are caller-owned. Scratch buffers (split-K partial sums and tickets) are sized by the
  * matching *_plan call, must be zero-filled once after allocation, and are left zero-ready by every
  * successful launch. Two launches that share a scratch buffer must not overlap on the GPU.
@@ -94,9 +95,11 @@ int qd_gemv(const void* x, int64_t ldx, const void* w_packed, int64_t n, int64_t
  * grid_hint 0, but no grid or scratch: scratch is a 4 MiB array compiled into the library, which every
  * GPU that loads it holds until exit; shapes whose plan needs more return QD_ERR_UNSUPPORTED. The
  * first call on each device looks up that array's device address (with that device current); make
- * this first call before any stream capture begins. Every call clears the array's tickets (a memset
- * on the stream) and reuses the array, so calls that may overlap on the GPU (other streams, other
- * threads) race and must be serialized by the caller. It has no counterpart in the reference. */
+ * this first call before any stream capture begins. The address is then kept for the life of the
+ * process, so a device reset (cudaDeviceReset) or a re-created primary context between calls is not
+ * supported. Every call clears the array's tickets (a memset on the stream) and reuses the array, so
+ * calls that may overlap on the GPU (other streams, other threads) race and must be serialized by the
+ * caller. It has no counterpart in the reference. */
 int qd_gemv_noalloc(const void* x, int64_t ldx, const void* w_packed, int64_t n, int64_t k, int m, void* out,
                     int64_t ldo, const void* res, int64_t ldr, const void* norm_w, float eps, int epilogue, int* err,
                     int pdl, cudaStream_t stream);
@@ -293,6 +296,12 @@ int qd_tc_gemm(const void* x, int64_t ldx, int64_t m, const void* w_packed, int6
  * 16-byte aligned rows. */
 int qd_rmsnorm_rows(const void* x, int64_t ldx, int64_t m, int64_t k, const void* norm_w, float eps, void* out,
                     int64_t ldo, cudaStream_t stream);
+
+/* Greedy token of each row of BF16 logits: out[i] = argmax over j < n of logits[i * ld + j], the lowest
+ * index among exact ties. Replaces the torch.argmax over the prompt's last-position logits that picks
+ * the first generated token (engine/engine.py:583-591). ld % 8 == 0, logits 16-byte aligned. Launched
+ * as a programmatic dependent (it waits for the kernel before it). */
+int qd_argmax_rows(const void* logits, int64_t ld, int64_t n, int64_t rows, int64_t* out, cudaStream_t stream);
 
 /* Prompt q/k RMSNorm + RoPE + KV-cache write: replaces qk_norm_rope_cache with pos_mode 0
  * (engine/kernels/fused.py:23-98, called from engine/engine.py:566-572). qkv [batch * S, (nq + 2 nkv) * 128]

@@ -1,8 +1,11 @@
 """Generate the golden decode fixtures by running the reference engine itself on CPU.
 
-Run in the build container (the only place the reference source exists):
+Run where the reference source tree exists, naming it (there is no default location):
 
-    python tests/golden/make_golden.py            # writes tests/golden/*.json
+    QD_REFERENCE=<path to the reference checkout> python tests/golden/make_golden.py [case ...]
+    python tests/golden/make_golden.py --reference <path> [case ...]
+
+With no case names every case below is written to tests/golden/<case>.json.
 
 For each case it builds the seeded synthetic checkpoint (decode_b200.synth), imports the reference
 `engine/engine.py` with ENGINE_DEVICE=cpu and records
@@ -30,7 +33,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(REPO, "htn-2026_b200"))
 
-REFERENCE = os.environ.get("QD_REFERENCE", "/root/reference")
+REFERENCE = os.environ.get("QD_REFERENCE")  # the reference checkout; set by --reference too
 N_PROBES = 16
 TOPK = 8
 
@@ -39,6 +42,10 @@ CASES = {
     "config0": dict(layers=4, batch=1, prompt=64, new=32, prompt_seed=0),
     # batch > 1 and a short prompt (exercises per-row state and the batch dimension)
     "b3_s17": dict(layers=2, batch=3, prompt=17, new=8, prompt_seed=5),
+    # BASELINE config 1 at full size: 36 layers, batch 1, 128-token uniform prompt (seed 0), 256 new
+    "config1": dict(layers=36, batch=1, prompt=128, new=256, prompt_seed=0),
+    # config 4's per-GPU shape (8 of the 64 sequences, 1024-token prompts) on 4 layers, 16 new tokens
+    "config4_b8": dict(layers=4, batch=8, prompt=1024, new=16, prompt_seed=4),
 }
 
 
@@ -146,7 +153,17 @@ def run_case(name: str, spec: dict) -> dict:
 
 
 def main(argv):
-    names = argv[1:] or list(CASES)
+    global REFERENCE
+    args = list(argv[1:])
+    if "--reference" in args:
+        i = args.index("--reference")
+        REFERENCE = args[i + 1]
+        del args[i:i + 2]
+        os.environ["QD_REFERENCE"] = REFERENCE  # carried into the per-case re-exec below
+    if not REFERENCE or not os.path.isfile(os.path.join(REFERENCE, "engine", "engine.py")):
+        sys.exit("name the reference checkout: QD_REFERENCE=<path> or --reference <path> "
+                 "(it must hold engine/engine.py)")
+    names = args or list(CASES)
     for name in names:
         res = run_case(name, CASES[name])
         out = os.path.join(HERE, f"{name}.json")

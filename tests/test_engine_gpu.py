@@ -238,12 +238,12 @@ def test_prefill_row_chunks_are_bit_identical(engines, monkeypatch):
     p = synth.random_prompt(5, 40, cfg["vocab_size"], seed=41)
     eng.state = None
     toks1, lg1 = eng.generate_with_logits(p, 3)
-    assert eng.state.rows == 5
+    assert eng.state.chunks == [(0, 5)]
     k1, v1 = eng.state.k_all[:, :, :, :40].clone(), eng.state.v_all[:, :, :, :40].clone()
     monkeypatch.setattr(E, "PREFILL_TOKENS", 100)  # 2 sequences of 40 tokens per chunk: 3 chunks
     eng.state = None
     toks2, lg2 = eng.generate_with_logits(p, 3)
-    assert eng.state.rows == 2
+    assert eng.state.chunks == [(0, 2), (2, 4), (4, 5)]
     assert toks1 == toks2
     assert all(torch.equal(a, b) for a, b in zip(lg1, lg2))
     assert torch.equal(k1, eng.state.k_all[:, :, :, :40]) and torch.equal(v1, eng.state.v_all[:, :, :, :40])

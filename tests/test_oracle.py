@@ -19,14 +19,22 @@ def _summ(logits, probes):
     return vals, idx, torch.logsumexp(lf, -1), lf[:, probes]
 
 
-@pytest.mark.parametrize("case", ["config0", "b3_s17"])
+@pytest.mark.parametrize("case", ["config0", "b3_s17", "config4_b8", "config1"])
 def test_oracle_matches_reference_golden(case):
+    """The oracle restates the reference's tier 1, so it reproduces tier 1's tokens and logits bit for bit
+    (config1 is BASELINE config 1 at full size: 36 layers, 256 tokens). The reference's tier 0 (the
+    Transformers loop) follows the same tokens up to its own exact-tie flips: where tier 0 and tier 1
+    part, tier 0's top-2 logits are equal."""
     g = load_golden(case)
     state, cfg = synth_state(g["spec"]["layers"])
     orc = Q.Qwen3Oracle(state, cfg)
     toks, logits = orc.generate(g["prompt"], g["spec"]["new"])
-    assert toks == g["native"]["tokens"]
     assert toks == g["tier1"]["tokens"]
+    for b, (nat, t1) in enumerate(zip(g["native"]["tokens"], g["tier1"]["tokens"])):
+        t = next((i for i, (x, y) in enumerate(zip(nat, t1)) if x != y), None)
+        if t is not None:
+            top = g["native"]["steps"][t]["top_vals"][b]
+            assert top[0] == top[1], (case, b, t)
     probes = g["probe_ids"]
     for t, step in enumerate(g["tier1"]["steps"]):
         vals, idx, lse, pv = _summ(logits[t], probes)

@@ -8,6 +8,7 @@ emit exactly the greedy tokens, and it must save verifies once the text repeats.
 """
 
 import random
+import time
 
 import pytest
 
@@ -35,25 +36,30 @@ def test_draft_matches_brute_force_as_the_history_grows(seed):
     rnd = random.Random(seed)
     vocab = rnd.choice([3, 5, 12])
     seq = [rnd.randrange(vocab) for _ in range(rnd.randrange(2, 12))]
-    look = spec.PromptLookup(seq)
+    drafter = spec.NgramDrafter(seq)
     for _ in range(25):
         k = rnd.randrange(1, 8)
-        assert look.draft(k) == _brute_draft(seq, k)
-        seq.extend(rnd.randrange(vocab) for _ in range(rnd.randrange(1, 5)))
-        look.register()
+        assert drafter.propose(k) == _brute_draft(seq, k)
+        more = [rnd.randrange(vocab) for _ in range(rnd.randrange(1, 5))]
+        seq.extend(more)
+        drafter.extend(more)
+        assert drafter.history == seq
 
 
 def test_draft_without_history_pads_with_the_last_token():
-    assert spec.PromptLookup([7, 9]).draft(3) == [9, 9, 9]
-    assert spec.PromptLookup([4]).draft(2) == [4, 4]
+    assert spec.NgramDrafter([7, 9]).propose(3) == [9, 9, 9]
+    assert spec.NgramDrafter([4]).propose(2) == [4, 4]
     # 2-gram (1, 2) occurred: its continuation [3, 1] then padding
-    assert spec.PromptLookup([1, 2, 3, 1, 2]).draft(4) == [3, 1, 2, 2]
+    assert spec.NgramDrafter([1, 2, 3, 1, 2]).propose(4) == [3, 1, 2, 2]
+    # the 3-gram wins over a later 2-gram occurrence: (5, 1, 2) continues with 8, (1, 2) last with 3
+    assert spec.NgramDrafter([5, 1, 2, 8, 1, 2, 3, 5, 1, 2]).propose(2) == [8, 1]
 
 
-def test_accept_takes_the_matching_prefix_and_the_next_greedy_token():
-    assert spec.accept([5, 1, 2, 3], [1, 2, 3, 4]) == [1, 2, 3, 4]  # every draft accepted
-    assert spec.accept([5, 1, 2, 3], [1, 9, 3, 4]) == [1, 9]        # second draft rejected
-    assert spec.accept([5, 1, 2, 3], [8, 2, 3, 4]) == [8]           # none accepted: one token
+def test_verified_tokens_take_the_agreeing_drafts_and_the_next_greedy_token():
+    assert spec.verified_tokens([5, 1, 2, 3], [1, 2, 3, 4]) == [1, 2, 3, 4]  # every draft stands
+    assert spec.verified_tokens([5, 1, 2, 3], [1, 9, 3, 4]) == [1, 9]        # second draft rejected
+    assert spec.verified_tokens([5, 1, 2, 3], [8, 2, 3, 4]) == [8]           # none stands: one token
+    assert spec.verified_tokens([5, 1, 9, 3], [1, 2, 3, 4]) == [1, 2]        # a later match does not count
 
 
 def _toy_next(prefix):
@@ -136,6 +142,25 @@ def test_gated_stream_falls_back_to_plain_steps_and_stays_exact(next_fn, expect_
         assert stats["plain_steps"] > 0.8 * N and stats["verifies"] < 0.2 * N
     else:
         assert stats["plain_steps"] == 0
+
+
+def test_gate_clock_excludes_the_consumers_time():
+    """Plain steps are timed only while the step generator produces a token: a slow consumer between
+    tokens must not make plain steps look expensive (which would bias the gate toward speculating)."""
+    S, N, k = 6, 60, 4
+    prompt = [(5 * i + 1) % 5 for i in range(S)]
+    greedy = list(prompt)
+    for _ in range(N):
+        greedy.append(_long_next(greedy))
+    seq = prompt + [greedy[S]]
+    gate = spec.Gate(window=1, backoff=8, prior_cost=1.4)
+    out = [greedy[S]]
+    for tok in spec.stream(seq, S, N, k, _verify_with(_long_next, seq), {}, step=_step_with(_long_next, seq),
+                           gate=gate):
+        out.append(tok)
+        time.sleep(0.002)  # the consumer's own work between tokens
+    assert out == greedy[S:S + N]
+    assert gate.n_step > 0 and gate.t_step / gate.n_step < 1e-3
 
 
 def test_gate_backoff_doubles_and_resets():

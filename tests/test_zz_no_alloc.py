@@ -5,9 +5,11 @@ is owned end to end by its own pool allocator, a plugin inside such a host witho
 handle, or a latency-critical loop that must not call cudaMalloc because it can synchronize the
 device. Its scratch is a fixed 4 MiB array inside the library instead of a caller buffer. This test
 calls it through the C ABI (ctypes) several times in a row, including a change of shape (which must
-not inherit the previous call's tickets), and compares every output with qd_gemv's, with the
-tolerance the other projection tests use. Collected last so a failure here leaves every other
-result in place; it also passes alone in a fresh process.
+not inherit the previous call's tickets) and a repeat of the first shape after it, and compares every
+output with qd_gemv's. Both entry points run the same plan and grid, and the split-K partial sums are
+added in a fixed CTA order, so the outputs must be bit-identical: a stale ticket or partial left in the
+shared array by an earlier call would show as a difference of even one ulp. Collected last so a
+failure here leaves every other result in place; it also passes alone in a fresh process.
 """
 
 import ctypes
@@ -18,7 +20,6 @@ import torch
 pytestmark = pytest.mark.gpu
 BF16 = torch.bfloat16
 DEV = "cuda:0"
-RTOL = 2.0 ** -7
 
 
 def _p(t):
@@ -35,9 +36,8 @@ def _noalloc(lib, x, w, n, k, m, out, res, norm_w, epi):
     assert int(err.item()) == 0
 
 
-def _close(a, b):
-    a, b = a.float().cpu(), b.float().cpu()
-    assert ((a - b).abs() <= RTOL * b.abs() + 1e-3).all(), float((a - b).abs().max())
+def _same(a, b, what):
+    assert torch.equal(a, b), (what, float((a.float() - b.float()).abs().max()))
 
 
 def test_noalloc_matches_regular_gemv_on_consecutive_calls():
@@ -46,12 +46,15 @@ def test_noalloc_matches_regular_gemv_on_consecutive_calls():
 
     lib = L.load()
     g = torch.Generator().manual_seed(7)
-    cases = [  # (m, n, k, epilogue, norm): gate/up + SwiGLU twice, then O-projection shape with residual
+    cases = [  # (m, n, k, epilogue, norm): gate/up + SwiGLU twice, the O-projection shape with residual,
+        # the down-projection shape, and gate/up once more after the shape changes
         (3, 19456, 2560, ops.Gemv.SWIGLU, True),
         (3, 19456, 2560, ops.Gemv.SWIGLU, True),
         (2, 2560, 4096, ops.Gemv.RES, False),
+        (1, 2560, 9728, ops.Gemv.RES, False),
+        (3, 19456, 2560, ops.Gemv.SWIGLU, True),
     ]
-    for m, n, k, epi, norm in cases:
+    for i, (m, n, k, epi, norm) in enumerate(cases):
         x = (torch.randn((m, k), generator=g)).to(BF16).to(DEV)
         w = ops.pack_matrix((torch.randn((n, k), generator=g) * 0.02).to(BF16).to(DEV))
         nw = (1.0 + 0.1 * torch.randn(k, generator=g)).to(BF16).to(DEV) if norm else None
@@ -65,7 +68,7 @@ def test_noalloc_matches_regular_gemv_on_consecutive_calls():
         if res is not None:
             out.copy_(res)
         _noalloc(lib, x, w, n, k, m, out, out if res is not None else None, nw, epi)
-        _close(out, ref)
+        _same(out, ref, (i, m, n, k))
 
 
 def test_noalloc_rejects_oversized_plans():
