@@ -57,6 +57,9 @@ def _args():
                                                       "prefill_gu", "prefill_attn", "prefill_fwd"],
                    help="time one decode kernel alone (small profiling case; random packed weights on the GPU)")
     p.add_argument("--launches", type=int, default=8)
+    p.add_argument("--trace", action="store_true",
+                   help="with --kernel step at batch 1-3: also run one step with the per-CTA timeline stamps on and "
+                        "print the per-op timeline summary")
     p.add_argument("--tc", action="store_true", help="with --kernel: the tcgen05 kernel (activations pre-packed)")
     p.add_argument("--sweep", default=None, choices=["linear", "attn", "prefill"],
                    help="BASELINE config 2 (decode linear shapes x batch x kernel path) or config 3 (GQA decode "
@@ -659,6 +662,73 @@ def run_step_kernel(a):
     print(json.dumps({"kernel": mode, "layers": a.layers, "batch": B, "launches": a.launches, "avg_us": round(us, 2),
                       "algorithmic_bytes": int(nbytes), "achieved_GBs": round(nbytes / us / 1e3, 1),
                       "frac_of_peak": round(nbytes / us / 1e3 / peak, 4), "peak": peak, "peak_kind": kind}))
+    if a.trace and st.step is not None:
+        print(json.dumps(step_timeline(eng, st, cfg, peak)))
+
+
+OPS = ("qkv", "attn", "o", "gate_up", "down")
+
+
+def step_timeline(eng, st, cfg, peak):
+    """One persistent decode step (batch 1-3) with its timeline stamps on: per CTA and op, %globaltimer at
+    0 = input ready (its dependency wait passed), 1 = input staged in shared memory, 2 = the op's blocks
+    consumed and its segments flushed (finalize epilogues included), 3 = the producer issued the op's
+    last weight block. Summarised over the middle layers (first and last two left out) as times
+    relative to the previous op's last `done` (the critical path), and the interval the producer spent
+    issuing each projection's blocks against that projection's streaming time at the peak."""
+    import statistics
+
+    import torch
+
+    from decode_b200 import ops
+
+    L, G = eng.n_layers, ops.sm_count()
+    nops = 2 + 5 * L
+    trace = torch.zeros((G * nops * 4,), dtype=torch.int64, device=eng.device)
+    traced = ops.DecodeStep(eng, st, trace=trace)
+    with torch.inference_mode():
+        st.step()
+        traced()
+        torch.cuda.synchronize()
+    eng.check_device_errors(st)
+    t = trace.view(G, nops, 4).cpu().double()
+    t0 = float(t[:, 0, 2].min())  # embedding done on the first CTA
+    t = (t - t0) / 1e3               # microseconds from the step's start
+    H, I, nq, nkv = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_attention_heads"], cfg["num_key_value_heads"]
+    wbytes = {"qkv": 2 * (nq + 2 * nkv) * 128 * H, "attn": 0, "o": 2 * H * nq * 128, "gate_up": 4 * I * H,
+              "down": 2 * H * I}
+    layers = list(range(2, L - 2)) if L > 5 else list(range(1, L))
+    med = lambda v: round(statistics.median(v), 2) if v else None  # noqa: E731
+    rows = {}
+    for k, name in enumerate(OPS):
+        wait, stage, work, issue, span = [], [], [], [], []
+        for l in layers:
+            op, prev = 1 + 5 * l + k, 1 + 5 * l + k - 1
+            prev_done = float(t[:, prev, 2].max())
+            ready = float(t[:, op, 0].max())
+            done = float(t[:, op, 2].max())
+            wait.append(ready - prev_done)
+            span.append(done - prev_done)
+            if name != "attn":  # the attention op records no `staged` stamp and streams no weights
+                staged = float(t[:, op, 1].max())
+                stage.append(staged - ready)
+                work.append(done - staged)
+                prev_proj = {0: 1 + 5 * (l - 1) + 4, 2: 1 + 5 * l, 3: 1 + 5 * l + 2, 4: 1 + 5 * l + 3}[k]
+                issue.append(float(t[:, op, 3].max()) - float(t[:, prev_proj, 3].max()))
+        rows[name] = {"wait_us": med(wait), "stage_us": med(stage), "work_us": med(work), "span_us": med(span),
+                      "producer_issue_interval_us": med(issue),
+                      "stream_us_at_peak": round(wbytes[name] / (peak * 1e3), 2)}
+    layer_us = [float(t[:, 1 + 5 * (l + 1), 0].max()) - float(t[:, 1 + 5 * l, 0].max()) for l in layers[:-1]]
+    lm = 1 + 5 * L
+    return {"timeline": "persistent step, per-op medians over layers %d..%d" % (layers[0], layers[-1]),
+            "layer_us": med(layer_us), "layer_stream_us_at_peak": round(sum(wbytes.values()) / (peak * 1e3), 2),
+            "ops": rows, "lm_head_span_us": round(float(t[:, lm, 2].max()) - float(t[:, lm - 1, 2].max()), 2),
+            "step_us": round(float(t[:, lm, 2].max()), 2),
+            "definitions": {"wait": "last CTA past its dependency wait - previous op's last done",
+                            "stage": "last CTA staged - last CTA ready", "work": "last done - last staged",
+                            "span": "last done - previous op's last done",
+                            "producer_issue_interval": "producer's last block of this projection issued - its last "
+                                                       "block of the previous projection (max over CTAs)"}}
 
 
 def _time_cycle(fn, copies, launches):
