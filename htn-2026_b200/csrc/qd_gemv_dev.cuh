@@ -57,6 +57,7 @@ struct GemvArgs {
   int out_npad;    // SWIGLU: 0 = row-major out; else out is the next projection's packed operand
   int* done;       // optional: +1 (release) per finalized row group
   int pos_ready;   // QKV: flags[2] already holds the position and aux its cos/sin rows
+  int* finalized;  // QKV, optional (shared memory): [0] = count, [1..] = the row groups this CTA finalized
   // QKV
   const __nv_bfloat16 *q_norm, *k_norm, *cos, *sin;
   const int64_t* pos;
@@ -460,6 +461,9 @@ __device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64
     }
   }
   if (finalized && a.done) signal_done(a.done, tid);
+  if constexpr (MODE == MODE_QKV) {
+    if (finalized && a.finalized && tid == 0) a.finalized[1 + a.finalized[0]++] = g;
+  }
   named_bar(kBarConsumers, kConsumers);
 }
 
