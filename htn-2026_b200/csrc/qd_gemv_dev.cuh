@@ -33,6 +33,8 @@ constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;  // + one producer warp
 constexpr int kBarConsumers = 1;           // named barrier of the 256 consumer threads
 constexpr int kStageBatch = 5;             // activation chunks per thread in flight (k <= 10240 in one pass)
+constexpr int kNormPre = 2;                // RMSNorm weight chunks per thread preloaded (k <= 4096); more are
+                                           // loaded in the normalising pass
 
 struct GemvArgs {
   const __nv_bfloat16* x;
@@ -57,7 +59,6 @@ struct GemvArgs {
   int out_npad;    // SWIGLU: 0 = row-major out; else out is the next projection's packed operand
   int* done;       // optional: +1 (release) per finalized row group
   int pos_ready;   // QKV: flags[2] already holds the position and aux its cos/sin rows
-  int* finalized;  // QKV, optional (shared memory): [0] = count, [1..] = the row groups this CTA finalized
   // QKV
   const __nv_bfloat16 *q_norm, *k_norm, *cos, *sin;
   const int64_t* pos;
@@ -151,11 +152,11 @@ template <int M>
 __device__ void stage_x(const GemvArgs& a, __nv_bfloat16* xs, float* wsum, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   const int kv8 = (int)(a.k >> 3);
-  // the norm weights this thread applies, loaded with its first activation row (k <= 10240)
-  uint4 nwv[kStageBatch];
+  // the first norm weights this thread applies, loaded with its first activation row
+  uint4 nwv[kNormPre];
   if (a.norm_w) {
 #pragma unroll
-    for (int j = 0; j < kStageBatch; ++j) {
+    for (int j = 0; j < kNormPre; ++j) {
       const int q = j * kConsumers + tid;
       nwv[j] = q < kv8 ? *reinterpret_cast<const uint4*>(a.norm_w + q * 8) : make_uint4(0u, 0u, 0u, 0u);
     }
@@ -197,13 +198,10 @@ __device__ void stage_x(const GemvArgs& a, __nv_bfloat16* xs, float* wsum, int t
 #pragma unroll
       for (int w8 = 0; w8 < kConsumerWarps; ++w8) ss += wsum[m * kConsumerWarps + w8];
       const float rstd = 1.0f / sqrtf(ss / (float)a.k + a.eps);
-#pragma unroll
-      for (int j = 0; j < kStageBatch; ++j) {
-        const int q = j * kConsumers + tid;
-        if (q >= kv8) continue;
+      // xs chunk q (8 values) <- bf16(w * bf16(x * rstd)), w the norm weights of chunk q
+      auto norm_chunk = [&](int q, const uint4 wv) {
         uint4* p = reinterpret_cast<uint4*>(xs + (int64_t)m * a.k + q * 8);
         const uint4 xv = *p;
-        const uint4 wv = nwv[j];
         const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
         const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
         uint32_t o[4];
@@ -214,7 +212,12 @@ __device__ void stage_x(const GemvArgs& a, __nv_bfloat16* xs, float* wsum, int t
           o[e] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
         }
         *p = make_uint4(o[0], o[1], o[2], o[3]);
-      }
+      };
+#pragma unroll
+      for (int j = 0; j < kNormPre; ++j)  // preloaded weights (constant indices: they stay in registers)
+        if (j * kConsumers + tid < kv8) norm_chunk(j * kConsumers + tid, nwv[j]);
+      for (int q = kNormPre * kConsumers + tid; q < kv8; q += kConsumers)
+        norm_chunk(q, *reinterpret_cast<const uint4*>(a.norm_w + q * 8));
     }
     named_bar(kBarConsumers, kConsumers);
   }
@@ -461,9 +464,6 @@ __device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64
     }
   }
   if (finalized && a.done) signal_done(a.done, tid);
-  if constexpr (MODE == MODE_QKV) {
-    if (finalized && a.finalized && tid == 0) a.finalized[1 + a.finalized[0]++] = g;
-  }
   named_bar(kBarConsumers, kConsumers);
 }
 
