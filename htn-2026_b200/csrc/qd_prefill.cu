@@ -454,6 +454,9 @@ struct QkRopeArgs {
   __nv_bfloat16 *k_cache, *v_cache;
   int64_t ldqkv, ldq, S, cs_b, cs_h, tokens;
   int64_t pos0;  // position of the first token of every sequence (token i * S + s sits at pos0 + s)
+  const int32_t* rope_pos;  // optional, per token: the RoPE position (the cache slot stays pos0 + s)
+  int64_t cap;
+  int* err;
   int nq, nkv;
   float eps;
 };
@@ -468,11 +471,19 @@ __global__ void __launch_bounds__(256) prefill_qk_rope_kernel(const __grid_const
   grid_dep_wait();
   grid_dep_launch();
   const int64_t t = blockIdx.x;
-  const int64_t i = t / a.S, s = t - i * a.S + a.pos0;  // s: the token's position
+  const int64_t i = t / a.S, s = t - i * a.S + a.pos0;  // s: the token's position (and cache slot)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int heads = a.nq + 2 * a.nkv;
-  const uint2 cv = *reinterpret_cast<const uint2*>(a.cos + s * 128 + 4 * lane);
-  const uint2 sv = *reinterpret_cast<const uint2*>(a.sin + s * 128 + 4 * lane);
+  int64_t rp = s;  // RoPE position: the slot, or the caller's per-token position (a token-tree node's depth)
+  if (a.rope_pos) {
+    rp = a.rope_pos[t];
+    if (rp < 0 || rp >= a.cap) {
+      if (threadIdx.x == 0 && a.err) atomicOr(a.err, QD_DEVERR_POS);
+      rp = rp < 0 ? 0 : a.cap - 1;
+    }
+  }
+  const uint2 cv = *reinterpret_cast<const uint2*>(a.cos + rp * 128 + 4 * lane);
+  const uint2 sv = *reinterpret_cast<const uint2*>(a.sin + rp * 128 + 4 * lane);
   const float cs[4] = {bf_lo(cv.x), bf_hi(cv.x), bf_lo(cv.y), bf_hi(cv.y)};
   const float sn[4] = {bf_lo(sv.x), bf_hi(sv.x), bf_lo(sv.y), bf_hi(sv.y)};
   const uint2 qw = *reinterpret_cast<const uint2*>(a.qn + 4 * lane);
@@ -1450,10 +1461,10 @@ extern "C" int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int
                                k_cache, v_cache, cap, cs_b, cs_h, stream);
 }
 
-extern "C" int qd_prefill_qk_rope_at(const void* qkv, int64_t ldqkv, int batch, int64_t S, int64_t pos0, int nq_heads,
-                                     int nkv_heads, const void* q_norm, const void* k_norm, float eps, const void* cos,
-                                     const void* sin, void* q_out, int64_t ldq, void* k_cache, void* v_cache,
-                                     int64_t cap, int64_t cs_b, int64_t cs_h, cudaStream_t stream) {
+static int qk_rope(const void* qkv, int64_t ldqkv, int batch, int64_t S, int64_t pos0, const int32_t* rope_pos,
+                   int nq_heads, int nkv_heads, const void* q_norm, const void* k_norm, float eps, const void* cos,
+                   const void* sin, void* q_out, int64_t ldq, void* k_cache, void* v_cache, int64_t cap, int64_t cs_b,
+                   int64_t cs_h, int* err, cudaStream_t stream) {
   if (!qkv || !q_norm || !k_norm || !cos || !sin || !q_out || !k_cache || !v_cache)
     return set_error(QD_ERR_ARG, "null pointer");
   if (pos0 < 0 || pos0 > cap) return set_error(QD_ERR_ARG, "prefill q/k rope: pos0 outside [0, cap]");
@@ -1484,8 +1495,28 @@ extern "C" int qd_prefill_qk_rope_at(const void* qkv, int64_t ldqkv, int batch, 
   a.nq = nq_heads;
   a.nkv = nkv_heads;
   a.eps = eps;
+  a.rope_pos = rope_pos;
+  a.cap = cap;
+  a.err = err;
   if (a.tokens > INT32_MAX) return set_error(QD_ERR_UNSUPPORTED, "prefill q/k rope: too many tokens");
   return launch_kernel((const void*)prefill_qk_rope_kernel, dim3((unsigned)a.tokens), dim3(256), 0, 1, stream, &a);
+}
+
+extern "C" int qd_prefill_qk_rope_at(const void* qkv, int64_t ldqkv, int batch, int64_t S, int64_t pos0, int nq_heads,
+                                     int nkv_heads, const void* q_norm, const void* k_norm, float eps, const void* cos,
+                                     const void* sin, void* q_out, int64_t ldq, void* k_cache, void* v_cache,
+                                     int64_t cap, int64_t cs_b, int64_t cs_h, cudaStream_t stream) {
+  return qk_rope(qkv, ldqkv, batch, S, pos0, nullptr, nq_heads, nkv_heads, q_norm, k_norm, eps, cos, sin, q_out, ldq,
+                 k_cache, v_cache, cap, cs_b, cs_h, nullptr, stream);
+}
+
+extern "C" int qd_tree_qk_rope(const void* qkv, int64_t ldqkv, int T, int64_t slot0, const int32_t* rope_pos,
+                               int nq_heads, int nkv_heads, const void* q_norm, const void* k_norm, float eps,
+                               const void* cos, const void* sin, void* q_out, int64_t ldq, void* k_cache,
+                               void* v_cache, int64_t cap, int64_t cs_h, int* err, cudaStream_t stream) {
+  if (!rope_pos) return set_error(QD_ERR_ARG, "tree q/k rope: null positions");
+  return qk_rope(qkv, ldqkv, 1, T, slot0, rope_pos, nq_heads, nkv_heads, q_norm, k_norm, eps, cos, sin, q_out, ldq,
+                 k_cache, v_cache, cap, (int64_t)nkv_heads * cs_h, cs_h, err, stream);
 }
 
 static int prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, bool q_compact, int nq_heads,

@@ -43,6 +43,7 @@ sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 from decode_b200 import lib as qdlib  # noqa: E402
 from decode_b200 import ops  # noqa: E402
 from decode_b200 import spec  # noqa: E402
+from decode_b200 import tree as tree_spec  # noqa: E402
 from decode_b200.loader import load_checkpoint  # noqa: E402
 
 DEVICE = os.environ.get("ENGINE_DEVICE", "cuda:0")
@@ -65,6 +66,10 @@ USE_PDL = os.environ.get("ENGINE_PDL", "1") != "0"
 SPEC_T = int(os.environ.get("ENGINE_SPEC_T", "0"))
 # while drafts are not accepted often enough to pay for a verify, fall back to plain decode steps
 SPEC_GATE = os.environ.get("ENGINE_SPEC_GATE", "1") != "0"
+# exact token-tree speculative decoding at batch 1: tree nodes per verify (0 = off; the reference uses
+# trees of 32 nodes at batch 1, engine/engine.py:169) and their deepest level (engine/engine.py:833)
+TREE_T = int(os.environ.get("ENGINE_TREE_T", "0"))
+TREE_DEPTH = int(os.environ.get("ENGINE_TREE_DEPTH", "12"))
 # "persistent": one launch per decode step (qd_decode_step); "kernels": 1 + 5 x layers + 1 launches;
 # "tc": the tensor-core kernels (used from TC_MIN_BATCH up): one persistent launch per step, or the
 # chain of 1 + 7 x layers + 2 launches (TC_STEP)
@@ -168,10 +173,11 @@ def _collector_paused():
 class _State:
     """Everything shape-dependent for one (batch, prompt length, new tokens)."""
 
-    def __init__(self, eng: "Engine", B: int, S: int, N: int, spec_T: int = 0):
+    def __init__(self, eng: "Engine", B: int, S: int, N: int, spec_T: int = 0, tree_T: int = 0):
         dev = eng.device
         self.B, self.S, self.N = B, S, N
-        cap = self.capacity = S + N + spec_T  # a verify writes up to T - 1 slots past the last emitted token
+        # a verify writes up to T - 1 slots past the last emitted token
+        cap = self.capacity = S + N + max(spec_T, tree_T)
         Lyr, H, I = eng.n_layers, eng.hidden, eng.inter
         nq, nkv, D = eng.nq, eng.nkv, eng.head_dim
         self.k_all = torch.zeros((Lyr, B, nkv, cap, D), dtype=BF16, device=dev)
@@ -215,9 +221,11 @@ class _State:
         pin = torch.cuda.is_available()
         self.prompt_host = torch.empty((B, S), dtype=torch.int64, pin_memory=pin)  # staging of the prompt upload
         self.ring = _TokenRing(B, AHEAD + 1, pin)
+        self.step_host = torch.empty((2,), dtype=torch.int64, pin_memory=pin)  # plain-step fallback: tok, pos
         self.prefill_graph = self.decode_graph = None
         self.prefill_logits = None
         self.verify = _Verify(eng, self, spec_T) if spec_T else None
+        self.tree = _TreeVerify(eng, self, tree_T) if tree_T else None
 
 
 class _Verify:
@@ -263,7 +271,6 @@ class _Verify:
         pin = torch.cuda.is_available()
         self.tok_host = torch.empty((T,), dtype=torch.int64, pin_memory=pin)
         self.out_host = torch.empty((T,), dtype=torch.int64, pin_memory=pin)
-        self.step_host = torch.empty((2,), dtype=torch.int64, pin_memory=pin)  # plain-step fallback: tok, pos
         self.event = torch.cuda.Event()
         self.calls = None  # the recorded launch sequence (its positions and stream are set per verify)
 
@@ -325,6 +332,110 @@ class _Verify:
             self.event.record()
         self.event.synchronize()
         return self.out_host.tolist()
+
+
+class _TreeVerify:
+    """Verify forward of a token tree (the reference's tree verify, engine/engine.py:830-936): the T nodes
+    run as T activation rows through the tcgen05 projections; node i's q/k are rotated at pos0 + depth(i)
+    and its K/V written to slot pos0 + i (qd_tree_qk_rope); every node attends to the cached prefix
+    [0, pos0) and to its ancestors (qd_tree_attn); the LM head's argmax gives the greedy token at every
+    node. After the walk, the accepted nodes' K/V move to consecutive slots (qd_tree_compact). The
+    ~8 x layers + 3 launches are recorded once and replayed with the prefix position patched."""
+
+    def __init__(self, eng: "Engine", st: "_State", T: int):
+        if not 2 <= T <= 32:
+            raise ValueError(f"token-tree verify width must be in [2, 32], got {T}")
+        dev = eng.device
+        H, I, nq, nkv, D = eng.hidden, eng.inter, eng.nq, eng.nkv, eng.head_dim
+        self.T, self.depth = T, max(1, min(TREE_DEPTH, T - 1))
+        n_qkv = (nq + 2 * nkv) * D
+        self.tok = torch.zeros((T,), dtype=torch.int64, device=dev)
+        self.rope_pos = torch.zeros((T,), dtype=torch.int32, device=dev)
+        self.anc = torch.zeros((T,), dtype=torch.int32, device=dev)
+        self.moves = torch.zeros((32, 2), dtype=torch.int32, device=dev)
+        self.out = torch.zeros((T,), dtype=torch.int64, device=dev)
+        self.x = torch.zeros((T, H), dtype=BF16, device=dev)
+        self.qkv = torch.zeros((T, n_qkv), dtype=BF16, device=dev)
+        self.q = torch.zeros((T, nq * D), dtype=BF16, device=dev)
+        self.att = torch.zeros((T, nq * D), dtype=BF16, device=dev)
+        self.xp_h = ops.PackedActivations(T, H, dev)
+        self.xp_a = ops.PackedActivations(T, nq * D, dev)
+        self.xp_i = ops.PackedActivations(T, I, dev)
+        self.qkv_op = ops.TcGemv(T, n_qkv, H, ops.TcGemv.STORE, dev)
+        self.o = ops.TcGemv(T, H, nq * D, ops.TcGemv.RES, dev)
+        self.gu = ops.TcGemv(T, 2 * I, H, ops.TcGemv.SWIGLU_PACKED, dev)
+        self.down = ops.TcGemv(T, H, I, ops.TcGemv.RES, dev)
+        self.lm = ops.TcLmHeadArgmax(T, eng.vocab, H, dev)
+        pin = torch.cuda.is_available()
+        self.tok_host = torch.zeros((T,), dtype=torch.int64, pin_memory=pin)
+        self.pos_host = torch.zeros((T,), dtype=torch.int32, pin_memory=pin)
+        self.anc_host = torch.zeros((T,), dtype=torch.int32, pin_memory=pin)
+        self.moves_host = torch.zeros((32, 2), dtype=torch.int32, pin_memory=pin)
+        self.out_host = torch.zeros((T,), dtype=torch.int64, pin_memory=pin)
+        self.event = torch.cuda.Event()
+        self.calls = None
+
+    def _enqueue(self, eng: "Engine", st: "_State", pos0: int) -> None:
+        T, nq, nkv, eps, err, pdl = self.T, eng.nq, eng.nkv, eng.eps, st.err, USE_PDL
+        ops.embed(self.tok, eng.e_packed, eng.vocab, self.x, err, pdl)
+        for i in range(eng.n_layers):
+            kc, vc = st.k_all[i, 0], st.v_all[i, 0]
+            self.xp_h.pack(self.x, eng.ln1[i], eps, pdl)
+            self.qkv_op(self.xp_h, eng.w_qkv[i], self.qkv, err=err, pdl=pdl)
+            ops.tree_qk_rope(self.qkv, T, pos0, self.rope_pos, nq, nkv, eng.qn[i], eng.kn[i], eps, st.cos, st.sin,
+                             self.q, kc, vc, err=err)
+            ops.tree_attn(self.q, T, nq, nkv, kc, vc, pos0, self.anc, self.att)
+            self.o(self.xp_a.pack(self.att, None, eps, pdl), eng.w_o[i], self.x, res=self.x, err=err, pdl=pdl)
+            self.xp_h.pack(self.x, eng.ln2[i], eps, pdl)
+            self.gu(self.xp_h, eng.w_gu[i], self.xp_i, err=err, pdl=pdl)
+            self.down(self.xp_i, eng.w_down[i], self.x, res=self.x, err=err, pdl=pdl)
+        self.lm(self.xp_h.pack(self.x, eng.final_norm, eps, pdl), eng.e_packed, self.out, err=err, pdl=pdl)
+
+    def launch(self, eng: "Engine", st: "_State", pos0: int) -> None:
+        if self.calls is None:
+            with qdlib.recording() as rec:
+                self._enqueue(eng, st, 0)
+            self.calls = qdlib.bind(rec)
+            self.rope = [c[2] for c in self.calls if c[1] == "qd_tree_qk_rope"]
+            self.attn = [c[2] for c in self.calls if c[1] == "qd_tree_attn"]
+            assert len(self.rope) == len(self.attn) == eng.n_layers
+        stream = torch.cuda.current_stream().cuda_stream
+        for args in self.rope:
+            args[3] = pos0  # slot0
+        for args in self.attn:
+            args[9] = pos0  # prefix
+        for _, _, args in self.calls:
+            args[-1] = stream
+        qdlib.replay(self.calls)
+
+    def __call__(self, eng: "Engine", st: "_State", tree: "tree_spec.TokenTree", pos0: int):
+        """Greedy token at every node of `tree` (its root at position pos0), and the commit callback
+        that moves the accepted path's keys / values into place."""
+        if pos0 + self.T > st.capacity:
+            raise RuntimeError("token tree past the cache capacity")
+        tok, dep, masks = tree.padded(self.T)
+        with torch.inference_mode():
+            self.tok_host.copy_(torch.tensor(tok, dtype=torch.int64))
+            self.pos_host.copy_(torch.tensor([pos0 + d for d in dep], dtype=torch.int32))
+            # 32-bit masks as int32 (two's complement): the kernel reads them as uint32
+            self.anc_host.copy_(torch.tensor([m - (1 << 32) if m >= 1 << 31 else m for m in masks], dtype=torch.int32))
+            self.tok.copy_(self.tok_host, non_blocking=True)
+            self.rope_pos.copy_(self.pos_host, non_blocking=True)
+            self.anc.copy_(self.anc_host, non_blocking=True)
+            self.launch(eng, st, pos0)
+            self.out_host.copy_(self.out, non_blocking=True)
+            self.event.record()
+        self.event.synchronize()
+        greedy = self.out_host.tolist()
+
+        def commit(path, p0):
+            moves = tree_spec.compaction_moves(path, p0)
+            if moves:
+                with torch.inference_mode():
+                    self.moves_host[:len(moves)].copy_(torch.tensor(moves, dtype=torch.int32))
+                    self.moves.copy_(self.moves_host, non_blocking=True)
+                    ops.tree_compact(st.k_all, st.v_all, self.moves, len(moves))
+        return greedy, commit
 
 
 class Engine:
@@ -404,6 +515,7 @@ class Engine:
         self.state = None
         self.sm_count = ops.sm_count()
         self.speculate = SPEC_T  # verify width of exact speculative decoding at batch 1 (0 = plain greedy)
+        self.tree = TREE_T  # nodes per token tree of exact tree speculation at batch 1 (0 = off; wins over speculate)
 
     # ------------------------------------------------------------------ model step
     def _prefill(self, st: _State) -> torch.Tensor:
@@ -512,8 +624,10 @@ class Engine:
         code = int(st.err.item())
         if code:
             # counters and tickets may be left mid-step: clear every scratch buffer before raising
+            extra = [v for side in (st.verify, st.tree) if side is not None
+                     for v in (side.qkv_op, side.o, side.gu, side.down, side.lm)]
             for plan in (st.qkv, st.attn, st.o, st.gu, st.down, st.lm, st.step, st.step_logits, st.tstep,
-                         st.tstep_logits):
+                         st.tstep_logits, *extra):
                 if plan is not None:
                     plan.scratch.zero_()
             st.err.zero_()
@@ -526,8 +640,9 @@ class Engine:
         self.state = None
         gc.collect()
         torch.cuda.empty_cache()
-        spec_T = self.speculate if (self.speculate and B == 1 and N > 1) else 0
-        st = _State(self, B, S, N, spec_T)
+        tree_T = self.tree if (self.tree and B == 1 and N > 1) else 0
+        spec_T = self.speculate if (self.speculate and B == 1 and N > 1 and not tree_T) else 0
+        st = _State(self, B, S, N, spec_T, tree_T)
         t0 = time.perf_counter()
         with torch.inference_mode():
             side = torch.cuda.Stream()
@@ -540,6 +655,8 @@ class Engine:
                         self._decode_step(st)
                     if st.verify is not None:
                         st.verify.launch(self, st, S - 1)
+                    if st.tree is not None:
+                        st.tree.launch(self, st, S - 1)
             torch.cuda.current_stream().wait_stream(side)
             torch.cuda.synchronize()
             self.check_device_errors(st)
@@ -625,17 +742,38 @@ class Engine:
             yield [tok]
         self.check_device_errors(st)
 
+    def _stream_tree(self, st: _State, input_ids, N: int):
+        """Exact token-tree speculative decoding of one sequence (the reference's tree stream,
+        engine/engine.py:830-936): after the prompt forward, every round verifies a drafted tree of
+        st.tree.T nodes in one forward and emits the model's greedy tokens along the accepted path plus
+        the one after it; exactly N steps are yielded."""
+        S, tv, ring = st.S, st.tree, st.ring
+        ring.reset()
+        with torch.inference_mode():
+            self._upload_prompt(st, input_ids)
+            self._enqueue_prefill(st)
+            ring.post(st.tok)
+        first = ring.take()
+        yield first
+        st.spec_stats = {}
+        plain = (lambda tok, pos, n: self._plain_steps(st, tok, pos, n)) if SPEC_GATE else None
+        for tok in tree_spec.stream(list(input_ids[0]) + first, S, N, tv.T, tv.depth,
+                                    lambda tree, pos0: tv(self, st, tree, pos0), st.spec_stats, step=plain,
+                                    gate=spec.Gate() if SPEC_GATE else None):
+            yield [tok]
+        self.check_device_errors(st)
+
     def _plain_steps(self, st: _State, tok: int, pos: int, n: int):
         """n plain decode steps of a batch-1 state continuing from the host's token at position `pos` (the
         speculative loop's fallback), yielding the n greedy tokens one at a time. The first replay takes
         its token and position from the host; each later one from the replay before it, so the device
         runs ahead of the caller through the token ring as in `_stream`."""
-        vf, ring = st.verify, st.ring
+        ring = st.ring
         ring.reset()
         with torch.inference_mode():
-            vf.step_host[0], vf.step_host[1] = tok, pos
-            st.tok.copy_(vf.step_host[0:1], non_blocking=True)
-            st.pos.copy_(vf.step_host[1:2], non_blocking=True)
+            st.step_host[0], st.step_host[1] = tok, pos
+            st.tok.copy_(st.step_host[0:1], non_blocking=True)
+            st.pos.copy_(st.step_host[1:2], non_blocking=True)
         enqueued = 0
         for _ in range(n):
             while enqueued < n and ring.in_flight() <= AHEAD:
@@ -653,12 +791,15 @@ class Engine:
         B, S = len(input_ids), len(input_ids[0])
         if B < 1 or S < 1 or any(len(r) != S for r in input_ids):
             raise ValueError("input_ids must be a non-empty batch of equal-length rows")
-        spec_T = self.speculate if (self.speculate and B == 1 and N > 1) else 0
+        tree_T = self.tree if (self.tree and B == 1 and N > 1) else 0
+        spec_T = self.speculate if (self.speculate and B == 1 and N > 1 and not tree_T) else 0
         st = self.state
-        fits = st is not None and (st.B, st.S, st.N) == (B, S, N) and (st.verify.T if st.verify else 0) == spec_T
+        fits = st is not None and (st.B, st.S, st.N) == (B, S, N) and (st.verify.T if st.verify else 0) == spec_T \
+            and (st.tree.T if st.tree else 0) == tree_T
         if not fits:
             st = self._build(B, S, N)
-        stream = self._stream_spec if st.verify is not None else self._stream
+        stream = self._stream_tree if st.tree is not None else (self._stream_spec if st.verify is not None else
+                                                                 self._stream)
         with _collector_paused():
             yield from stream(st, input_ids, N)
 

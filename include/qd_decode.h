@@ -297,6 +297,30 @@ int qd_tc_gemm(const void* x, int64_t ldx, int64_t m, const void* w_packed, int6
 int qd_rmsnorm_rows(const void* x, int64_t ldx, int64_t m, int64_t k, const void* norm_w, float eps, void* out,
                     int64_t ldo, cudaStream_t stream);
 
+/* ---------------------------------------------------------------- token-tree verification
+ * Replace the reference's tree kernels (engine/kernels/tree.py:25-164: tree q/k RoPE at depth positions,
+ * ancestor-masked attention, KV compaction) for exact token-tree speculation at batch 1. The T nodes of
+ * a draft tree (node 0 = the last emitted token, parents before children) are T activation rows.
+ *
+ * qd_tree_qk_rope: per-node q/k RMSNorm + RoPE as qd_prefill_qk_rope_at, node t's K/V written to cache
+ * slot slot0 + t but rotated at position rope_pos[t] (device int32 [T]: slot0 + its depth); caches
+ * [nkv, cap, 128] (head stride cs_h). A position outside [0, cap) is clamped and flags QD_DEVERR_POS.
+ * qd_tree_attn: out[t] = attention of node t's query heads over cache slots [0, prefix) and the tree
+ * slots prefix + j with bit j of anc[t] set (device uint32 [T]: node t and its ancestors); 1 <= T <= 32,
+ * prefix + T <= cap, 4 query heads per KV head. Same arithmetic as qd_attn_decode.
+ * qd_tree_compact: for each move i in order (device int32 [n][2]: source slot, destination slot), the
+ * key and value rows of every layer and KV head are copied from the source to the destination slot;
+ * caches [layers][nkv][cap][128] at layer stride layer_stride (batch 1), n <= 64. */
+int qd_tree_qk_rope(const void* qkv, int64_t ldqkv, int T, int64_t slot0, const int32_t* rope_pos, int nq_heads,
+                    int nkv_heads, const void* q_norm, const void* k_norm, float eps, const void* cos, const void* sin,
+                    void* q_out, int64_t ldq, void* k_cache, void* v_cache, int64_t cap, int64_t cs_h, int* err,
+                    cudaStream_t stream);
+int qd_tree_attn(const void* q, int64_t ldq, int T, int nq_heads, int nkv_heads, const void* k_cache,
+                 const void* v_cache, int64_t cap, int64_t cs_h, int64_t prefix, const uint32_t* anc, float scale,
+                 void* out, int64_t ldo, cudaStream_t stream);
+int qd_tree_compact(void* k_cache, void* v_cache, int layers, int64_t layer_stride, int nkv_heads, int64_t cs_h,
+                    int64_t cap, const int32_t* moves, int n, cudaStream_t stream);
+
 /* Greedy token of each row of BF16 logits: out[i] = argmax over j < n of logits[i * ld + j], the lowest
  * index among exact ties. Replaces the torch.argmax over the prompt's last-position logits that picks
  * the first generated token (engine/engine.py:583-591). ld % 8 == 0, logits 16-byte aligned. Launched
