@@ -53,6 +53,9 @@ def _args():
     p.add_argument("--speculate", type=int, default=0,
                    help="also time the end-to-end run with exact prompt-lookup speculation of this verify width "
                         "(batch 1; reported as e2e_speculative, not the headline)")
+    p.add_argument("--tree", type=int, default=0,
+                   help="also time the end-to-end run with exact token-tree speculation of this many nodes per tree "
+                        "(batch 1; reported as e2e_tree, not the headline)")
     p.add_argument("--kernel", default=None, choices=["qkv", "o", "gu", "down", "lm", "attn", "attn_stream", "attn_tc", "step",
                                                       "prefill_gu", "prefill_attn", "prefill_fwd"],
                    help="time one decode kernel alone (small profiling case; random packed weights on the GPU)")
@@ -332,6 +335,46 @@ def run_ours(a):
                     "note": "decode tokens/s between the first and last yield of Engine.generate with speculation; "
                             "the prompt and the random-init weights decide how many drafts are accepted"}
 
+    e2e_tree = None
+    if a.tree and B == 1 and a.new > 1:
+        # exact token-tree speculation through the same public call; its tokens must equal the plain run's
+        # up to a near-tie flip
+        plain = [t[0] for t in eng.generate(prompt, a.new)]
+        eng.tree = a.tree
+        list(eng.generate(prompt, a.new))  # untimed: builds the state with the tree buffers
+        stamps = []
+        t0 = time.perf_counter()
+        for _ in eng.generate(prompt, a.new):
+            stamps.append(time.perf_counter())
+        tree_toks = [t[0] for t in eng.generate(prompt, a.new)]
+        stats = dict(eng.state.spec_stats)
+        tv, st_t = eng.state.tree, eng.state
+        # one verify of a full tree alone, device time (the prefix at the prompt's end)
+        from decode_b200 import tree as tree_mod
+
+        probe = tree_mod.TokenTree(prompt[0][-1], a.tree)
+        while len(probe) < a.tree:
+            probe.insert([len(probe) % 1000, (len(probe) * 7) % 1000], 4)
+        with torch.inference_mode():
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            tv(eng, st_t, probe, S - 1)
+            ev[0].record()
+            for _ in range(5):
+                tv(eng, st_t, probe, S - 1)
+            ev[1].record()
+            ev[1].synchronize()
+        eng.tree = 0
+        eng.state = None
+        same = next((i for i, (x, y) in enumerate(zip(plain, tree_toks)) if x != y), len(plain))
+        dec = stamps[-1] - stamps[0]
+        e2e_tree = {"value": round((a.new - 1) / dec, 2), "unit": "tokens/s", "tree_nodes": a.tree,
+                    "verifies": stats["verifies"], "plain_steps": stats["plain_steps"],
+                    "accepted_drafts": stats["accepted"], "verify_ms": round(ev[0].elapsed_time(ev[1]) / 5, 3),
+                    "tokens_equal_to_plain": same,
+                    "note": "decode tokens/s between the first and last yield of Engine.generate with token trees; "
+                            "verify_ms = one verify of a full tree including its host round trip; the prompt and "
+                            "the random-init weights decide how many drafts are accepted"}
+
     # ---------------- roofline of the dominant kernel and of the whole step
     peak, peak_kind = _peaks()
     L_avg = S + W + K / 2
@@ -394,6 +437,8 @@ def run_ours(a):
             out["e2e_speculative"] = e2e_spec
         if c4 is not None:
             out["config4"] = c4
+        if e2e_tree is not None:
+            out["e2e_tree"] = e2e_tree
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.barrier()
