@@ -357,10 +357,10 @@ def run_ours(a):
             probe.insert([len(probe) % 1000, (len(probe) * 7) % 1000], 4)
         with torch.inference_mode():
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-            tv(eng, st_t, probe, S - 1)
+            tv(eng, st_t, [probe], [S - 1])
             ev[0].record()
             for _ in range(5):
-                tv(eng, st_t, probe, S - 1)
+                tv(eng, st_t, [probe], [S - 1])
             ev[1].record()
             ev[1].synchronize()
         eng.tree = 0

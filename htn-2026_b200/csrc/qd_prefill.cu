@@ -455,6 +455,7 @@ struct QkRopeArgs {
   int64_t ldqkv, ldq, S, cs_b, cs_h, tokens;
   int64_t pos0;  // position of the first token of every sequence (token i * S + s sits at pos0 + s)
   const int32_t* rope_pos;  // optional, per token: the RoPE position (the cache slot stays pos0 + s)
+  const int32_t* slot0;     // optional, per sequence: its first token's cache slot, in place of pos0
   int64_t cap;
   int* err;
   int nq, nkv;
@@ -471,7 +472,18 @@ __global__ void __launch_bounds__(256) prefill_qk_rope_kernel(const __grid_const
   grid_dep_wait();
   grid_dep_launch();
   const int64_t t = blockIdx.x;
-  const int64_t i = t / a.S, s = t - i * a.S + a.pos0;  // s: the token's position (and cache slot)
+  const int64_t i = t / a.S;
+  int64_t s = t - i * a.S + a.pos0;  // s: the token's position (and cache slot)
+  bool store_kv = true;
+  if (a.slot0) {  // the sequence's slots start at slot0[i]: all S of them must lie in the cache
+    const int64_t s0 = a.slot0[i];
+    s = s0 + (t - i * a.S);
+    if (s0 < 0 || s0 + a.S > a.cap) {
+      if (threadIdx.x == 0 && a.err) atomicOr(a.err, QD_DEVERR_POS);
+      store_kv = false;
+      s = 0;
+    }
+  }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int heads = a.nq + 2 * a.nkv;
   int64_t rp = s;  // RoPE position: the slot, or the caller's per-token position (a token-tree node's depth)
@@ -502,7 +514,7 @@ __global__ void __launch_bounds__(256) prefill_qk_rope_kernel(const __grid_const
     const uint2 u = uu[j];
     if (h >= a.nq + a.nkv) {  // V head: into the cache as is
       const int kvh = h - a.nq - a.nkv;
-      *reinterpret_cast<uint2*>(a.v_cache + i * a.cs_b + kvh * a.cs_h + s * 128 + 4 * lane) = u;
+      if (store_kv) *reinterpret_cast<uint2*>(a.v_cache + i * a.cs_b + kvh * a.cs_h + s * 128 + 4 * lane) = u;
       continue;
     }
     const float x[4] = {bf_lo(u.x), bf_hi(u.x), bf_lo(u.y), bf_hi(u.y)};
@@ -531,7 +543,7 @@ __global__ void __launch_bounds__(256) prefill_qk_rope_kernel(const __grid_const
     const uint2 ov = make_uint2(o[0], o[1]);
     if (h < a.nq)
       *reinterpret_cast<uint2*>(a.q_out + t * a.ldq + (int64_t)h * 128 + 4 * lane) = ov;
-    else
+    else if (store_kv)
       *reinterpret_cast<uint2*>(a.k_cache + i * a.cs_b + (h - a.nq) * a.cs_h + s * 128 + 4 * lane) = ov;
   }
 }
@@ -1461,8 +1473,8 @@ extern "C" int qd_prefill_qk_rope(const void* qkv, int64_t ldqkv, int batch, int
                                k_cache, v_cache, cap, cs_b, cs_h, stream);
 }
 
-static int qk_rope(const void* qkv, int64_t ldqkv, int batch, int64_t S, int64_t pos0, const int32_t* rope_pos,
-                   int nq_heads, int nkv_heads, const void* q_norm, const void* k_norm, float eps, const void* cos,
+static int qk_rope(const void* qkv, int64_t ldqkv, int batch, int64_t S, int64_t pos0, const int32_t* slot0,
+                   const int32_t* rope_pos, int nq_heads, int nkv_heads, const void* q_norm, const void* k_norm, float eps, const void* cos,
                    const void* sin, void* q_out, int64_t ldq, void* k_cache, void* v_cache, int64_t cap, int64_t cs_b,
                    int64_t cs_h, int* err, cudaStream_t stream) {
   if (!qkv || !q_norm || !k_norm || !cos || !sin || !q_out || !k_cache || !v_cache)
@@ -1496,6 +1508,7 @@ static int qk_rope(const void* qkv, int64_t ldqkv, int batch, int64_t S, int64_t
   a.nkv = nkv_heads;
   a.eps = eps;
   a.rope_pos = rope_pos;
+  a.slot0 = slot0;
   a.cap = cap;
   a.err = err;
   if (a.tokens > INT32_MAX) return set_error(QD_ERR_UNSUPPORTED, "prefill q/k rope: too many tokens");
@@ -1506,17 +1519,18 @@ extern "C" int qd_prefill_qk_rope_at(const void* qkv, int64_t ldqkv, int batch, 
                                      int nkv_heads, const void* q_norm, const void* k_norm, float eps, const void* cos,
                                      const void* sin, void* q_out, int64_t ldq, void* k_cache, void* v_cache,
                                      int64_t cap, int64_t cs_b, int64_t cs_h, cudaStream_t stream) {
-  return qk_rope(qkv, ldqkv, batch, S, pos0, nullptr, nq_heads, nkv_heads, q_norm, k_norm, eps, cos, sin, q_out, ldq,
-                 k_cache, v_cache, cap, cs_b, cs_h, nullptr, stream);
+  return qk_rope(qkv, ldqkv, batch, S, pos0, nullptr, nullptr, nq_heads, nkv_heads, q_norm, k_norm, eps, cos, sin,
+                 q_out, ldq, k_cache, v_cache, cap, cs_b, cs_h, nullptr, stream);
 }
 
-extern "C" int qd_tree_qk_rope(const void* qkv, int64_t ldqkv, int T, int64_t slot0, const int32_t* rope_pos,
-                               int nq_heads, int nkv_heads, const void* q_norm, const void* k_norm, float eps,
-                               const void* cos, const void* sin, void* q_out, int64_t ldq, void* k_cache,
-                               void* v_cache, int64_t cap, int64_t cs_h, int* err, cudaStream_t stream) {
-  if (!rope_pos) return set_error(QD_ERR_ARG, "tree q/k rope: null positions");
-  return qk_rope(qkv, ldqkv, 1, T, slot0, rope_pos, nq_heads, nkv_heads, q_norm, k_norm, eps, cos, sin, q_out, ldq,
-                 k_cache, v_cache, cap, (int64_t)nkv_heads * cs_h, cs_h, err, stream);
+extern "C" int qd_tree_qk_rope(const void* qkv, int64_t ldqkv, int batch, int T, const int32_t* slot0,
+                               const int32_t* rope_pos, int nq_heads, int nkv_heads, const void* q_norm,
+                               const void* k_norm, float eps, const void* cos, const void* sin, void* q_out,
+                               int64_t ldq, void* k_cache, void* v_cache, int64_t cap, int64_t cs_b, int64_t cs_h,
+                               int* err, cudaStream_t stream) {
+  if (!slot0 || !rope_pos) return set_error(QD_ERR_ARG, "tree q/k rope: null slot or position array");
+  return qk_rope(qkv, ldqkv, batch, T, 0, slot0, rope_pos, nq_heads, nkv_heads, q_norm, k_norm, eps, cos, sin, q_out,
+                 ldq, k_cache, v_cache, cap, cs_b, cs_h, err, stream);
 }
 
 static int prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, bool q_compact, int nq_heads,

@@ -1,13 +1,15 @@
 // Token-tree verification kernels, sm_100a: attention of the T nodes of a draft tree over the cached
 // prefix and their own ancestors, and the compaction of the accepted path's keys / values.
 //
-// A verify forward runs the T nodes of a token tree (node 0 = the last emitted token, parents before
-// children) as T activation rows. Node i's keys / values go to cache slot prefix + i and are rotated
-// at position prefix + depth(i) (qd_tree_qk_rope). Node i attends to every cached key [0, prefix) and
-// to the tree slots of its ancestors and itself: anc[i] bit j set <=> node j is node i or one of its
-// ancestors. Once the accepted path is known, the keys / values of its nodes move from their tree
+// A verify forward runs the T nodes of one token tree per sequence (node 0 = the sequence's last emitted
+// token, parents before children) as B x T activation rows, row b * T + i = node i of sequence b.
+// Node i's keys / values go to slot prefix[b] + i of its sequence's cache and are rotated at position
+// prefix[b] + depth(i) (qd_tree_qk_rope). Node i attends to every cached key [0, prefix[b]) and to the
+// tree slots of its ancestors and itself: anc[row] bit j set <=> node j is node i or one of its
+// ancestors. Once the accepted paths are known, the keys / values of their nodes move from their tree
 // slots to the consecutive slots prefix + depth, where the next step expects them (qd_tree_compact);
-// their rotation already used that position.
+// their rotation already used that position. The prefixes live in device memory, so one recorded or
+// captured verify serves every round.
 #include "qd_common.cuh"
 #include "qd_host.h"
 
@@ -19,18 +21,20 @@ constexpr int kTreeGroup = 4;  // query heads per KV head
 constexpr int kHeadDimTree = 128;
 
 struct TreeAttnArgs {
-  const __nv_bfloat16* q;  // [T, nq * 128], row stride ldq
-  const __nv_bfloat16 *k, *v;  // [nkv, cap, 128], head stride cs_h
-  __nv_bfloat16* out;          // [T, nq * 128], row stride ldo
-  const uint32_t* anc;         // [T] ancestor masks
-  int64_t ldq, ldo, cs_h, prefix;
+  const __nv_bfloat16* q;  // [B * T, nq * 128], row stride ldq
+  const __nv_bfloat16 *k, *v;  // [B, nkv, cap, 128], sequence stride cs_b, head stride cs_h
+  __nv_bfloat16* out;          // [B * T, nq * 128], row stride ldo
+  const uint32_t* anc;         // [B * T] ancestor masks
+  const int32_t* prefix;       // [B] cached keys before each sequence's tree (= its root's slot)
+  int* err;
+  int64_t ldq, ldo, cs_b, cs_h, cap;
   int T, nq;
   float scale;
 };
 
-// One CTA of 4 warps per (KV head, tree node): the node's 4 query heads of that KV head attend over the
-// visible keys, in slot order (virtual key v < prefix + T; slot v is visible when v < prefix or the
-// node's mask has bit v - prefix). Each warp takes 8 keys per pass (4 lanes per key for q.k, dims
+// One CTA of 4 warps per (KV head, tree row): the node's 4 query heads of that KV head attend over the
+// visible keys of its sequence, in slot order (virtual key v < prefix + T; slot v is visible when
+// v < prefix or the node's mask has bit v - prefix). Each warp takes 8 keys per pass (4 lanes per key for q.k, dims
 // 4 lane.. 4 lane + 3 for P.V); fp32 scores and online softmax, probabilities rounded to BF16 before P.V,
 // fp32 accumulation, the 4 warps' (max, sum, acc) combined in warp order - the arithmetic of the decode
 // attention's units.
@@ -40,8 +44,15 @@ __global__ void __launch_bounds__(kTreeThreads) tree_attn_kernel(const __grid_co
   __shared__ float wm[kTreeWarps][kTreeGroup], wl[kTreeWarps][kTreeGroup];
   grid_dep_wait();
   grid_dep_launch();
-  const int kvh = blockIdx.x, node = blockIdx.y;
+  const int kvh = blockIdx.x, node = blockIdx.y, seq = node / a.T;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, kj = lane >> 2, qd = lane & 3;
+  const int64_t prefix = a.prefix[seq];
+  if (prefix < 0 || prefix + a.T > a.cap) {  // the tree would reach past the cache: zeros, error flag
+    if (tid == 0 && a.err) atomicOr(a.err, QD_DEVERR_POS);
+    for (int h = 0; h < kTreeGroup; ++h)
+      a.out[node * a.ldo + (int64_t)(kvh * kTreeGroup + h) * kHeadDimTree + tid] = __float2bfloat16_rn(0.f);
+    return;
+  }
   for (int h = 0; h < kTreeGroup; ++h) {
     const uint16_t u = __ldcg(reinterpret_cast<const unsigned short*>(a.q + node * a.ldq) +
                               (int64_t)(kvh * kTreeGroup + h) * kHeadDimTree + tid);
@@ -49,10 +60,10 @@ __global__ void __launch_bounds__(kTreeThreads) tree_attn_kernel(const __grid_co
   }
   __syncthreads();
   const uint32_t mask = a.anc[node];
-  const int64_t nv = a.prefix + a.T;
-  const __nv_bfloat16* kbase = a.k + (int64_t)kvh * a.cs_h;
-  const __nv_bfloat16* vbase = a.v + (int64_t)kvh * a.cs_h;
-  auto visible = [&](int64_t v) { return v < a.prefix || (v < nv && ((mask >> (int)(v - a.prefix)) & 1u)); };
+  const int64_t nv = prefix + a.T;
+  const __nv_bfloat16* kbase = a.k + seq * a.cs_b + (int64_t)kvh * a.cs_h;
+  const __nv_bfloat16* vbase = a.v + seq * a.cs_b + (int64_t)kvh * a.cs_h;
+  auto visible = [&](int64_t v) { return v < prefix || (v < nv && ((mask >> (int)(v - prefix)) & 1u)); };
   float m_run[kTreeGroup], l_run[kTreeGroup], acc[kTreeGroup][4];
 #pragma unroll
   for (int h = 0; h < kTreeGroup; ++h) {
@@ -144,22 +155,24 @@ __global__ void __launch_bounds__(kTreeThreads) tree_attn_kernel(const __grid_co
 }
 
 struct TreeCompactArgs {
-  __nv_bfloat16 *k, *v;   // [layers][nkv][cap][128] (batch 1)
-  int64_t layer_stride, cs_h;
-  const int32_t* moves;  // [n][2]: source slot, destination slot, applied in order
-  int n;
+  __nv_bfloat16 *k, *v;   // [layers][B][nkv][cap][128]
+  int64_t layer_stride, cs_b, cs_h;
+  const int32_t* moves;  // [n][3]: sequence, source slot, destination slot, applied in order
+  int n, batch;
   int64_t cap;
 };
 
 // One CTA of 128 threads per (layer, KV head): for each move in order, the 128 values of the key and of
-// the value at the source slot are copied to the destination slot.
+// the value at the source slot of the move's sequence are copied to its destination slot.
 __global__ void __launch_bounds__(128) tree_compact_kernel(const __grid_constant__ TreeCompactArgs a) {
   grid_dep_wait();
   grid_dep_launch();
-  const int64_t base = (int64_t)blockIdx.y * a.layer_stride + (int64_t)blockIdx.x * a.cs_h;
+  const int64_t head = (int64_t)blockIdx.y * a.layer_stride + (int64_t)blockIdx.x * a.cs_h;
   for (int i = 0; i < a.n; ++i) {
-    const int64_t s0 = a.moves[2 * i], d0 = a.moves[2 * i + 1];
-    if (s0 < 0 || s0 >= a.cap || d0 < 0 || d0 >= a.cap) continue;  // outside the cache: nothing moves
+    const int64_t b = a.moves[3 * i], s0 = a.moves[3 * i + 1], d0 = a.moves[3 * i + 2];
+    // outside the batch or the cache: nothing moves (uniform over the CTA, so the barriers stay matched)
+    if (b < 0 || b >= a.batch || s0 < 0 || s0 >= a.cap || d0 < 0 || d0 >= a.cap) continue;
+    const int64_t base = head + b * a.cs_b;
     const int64_t src = base + s0 * kHeadDimTree + threadIdx.x;
     const int64_t dst = base + d0 * kHeadDimTree + threadIdx.x;
     const __nv_bfloat16 kv = a.k[src], vv = a.v[src];
@@ -174,15 +187,17 @@ __global__ void __launch_bounds__(128) tree_compact_kernel(const __grid_constant
 
 using namespace qd;
 
-extern "C" int qd_tree_attn(const void* q, int64_t ldq, int T, int nq_heads, int nkv_heads, const void* k_cache,
-                            const void* v_cache, int64_t cap, int64_t cs_h, int64_t prefix, const uint32_t* anc,
-                            float scale, void* out, int64_t ldo, cudaStream_t stream) {
-  if (!q || !k_cache || !v_cache || !anc || !out) return set_error(QD_ERR_ARG, "tree attention: null pointer");
-  if (T < 1 || T > 32 || nkv_heads < 1 || nq_heads != kTreeGroup * nkv_heads || prefix < 0 || prefix + T > cap ||
-      cs_h < cap * kHeadDimTree || ldq < (int64_t)nq_heads * kHeadDimTree || ldo < (int64_t)nq_heads * kHeadDimTree ||
-      ldq % 8 || cs_h % 8)
-    return set_error(QD_ERR_ARG, "tree attention: bad sizes (1 <= T <= 32, 4 query heads per KV head, "
-                                 "prefix + T <= cap)");
+extern "C" int qd_tree_attn(const void* q, int64_t ldq, int batch, int T, int nq_heads, int nkv_heads,
+                            const void* k_cache, const void* v_cache, int64_t cap, int64_t cs_b, int64_t cs_h,
+                            const int32_t* prefix, const uint32_t* anc, float scale, void* out, int64_t ldo, int* err,
+                            cudaStream_t stream) {
+  if (!q || !k_cache || !v_cache || !prefix || !anc || !out)
+    return set_error(QD_ERR_ARG, "tree attention: null pointer");
+  if (batch < 1 || T < 1 || T > 32 || (int64_t)batch * T > 65535 || nkv_heads < 1 ||
+      nq_heads != kTreeGroup * nkv_heads || T > cap || cs_h < cap * kHeadDimTree ||
+      cs_b < (int64_t)nkv_heads * cs_h || ldq < (int64_t)nq_heads * kHeadDimTree ||
+      ldo < (int64_t)nq_heads * kHeadDimTree || ldq % 8 || cs_h % 8 || cs_b % 8)
+    return set_error(QD_ERR_ARG, "tree attention: bad sizes (1 <= T <= 32, 4 query heads per KV head, T <= cap)");
   if (!aligned16(k_cache) || !aligned16(v_cache)) return set_error(QD_ERR_ARG, "tree attention: cache alignment");
   TreeAttnArgs a = {};
   a.q = static_cast<const __nv_bfloat16*>(q);
@@ -190,30 +205,37 @@ extern "C" int qd_tree_attn(const void* q, int64_t ldq, int T, int nq_heads, int
   a.v = static_cast<const __nv_bfloat16*>(v_cache);
   a.out = static_cast<__nv_bfloat16*>(out);
   a.anc = anc;
+  a.prefix = prefix;
+  a.err = err;
   a.ldq = ldq;
   a.ldo = ldo;
+  a.cs_b = cs_b;
   a.cs_h = cs_h;
-  a.prefix = prefix;
+  a.cap = cap;
   a.T = T;
   a.nq = nq_heads;
   a.scale = scale;
-  return launch_kernel((const void*)tree_attn_kernel, dim3(nkv_heads, T), dim3(kTreeThreads), 0, 1, stream, &a);
+  return launch_kernel((const void*)tree_attn_kernel, dim3(nkv_heads, batch * T), dim3(kTreeThreads), 0, 1, stream,
+                       &a);
 }
 
-extern "C" int qd_tree_compact(void* k_cache, void* v_cache, int layers, int64_t layer_stride, int nkv_heads,
-                               int64_t cs_h, int64_t cap, const int32_t* moves, int n, cudaStream_t stream) {
+extern "C" int qd_tree_compact(void* k_cache, void* v_cache, int layers, int64_t layer_stride, int batch,
+                               int64_t cs_b, int nkv_heads, int64_t cs_h, int64_t cap, const int32_t* moves, int n,
+                               cudaStream_t stream) {
   if (n == 0) return QD_OK;
   if (!k_cache || !v_cache || !moves) return set_error(QD_ERR_ARG, "tree compact: null pointer");
-  if (layers < 1 || nkv_heads < 1 || n < 0 || n > 64 || cs_h < cap * kHeadDimTree ||
-      layer_stride < (int64_t)nkv_heads * cs_h)
+  if (layers < 1 || layers > 65535 || batch < 1 || nkv_heads < 1 || n < 0 || n > 4096 || cs_h < cap * kHeadDimTree ||
+      cs_b < (int64_t)nkv_heads * cs_h || layer_stride < (int64_t)batch * cs_b)
     return set_error(QD_ERR_ARG, "tree compact: bad sizes");
   TreeCompactArgs a = {};
   a.k = static_cast<__nv_bfloat16*>(k_cache);
   a.v = static_cast<__nv_bfloat16*>(v_cache);
   a.layer_stride = layer_stride;
+  a.cs_b = cs_b;
   a.cs_h = cs_h;
   a.moves = moves;
   a.n = n;
+  a.batch = batch;
   a.cap = cap;
   return launch_kernel((const void*)tree_compact_kernel, dim3(nkv_heads, layers), dim3(128), 0, 1, stream, &a);
 }

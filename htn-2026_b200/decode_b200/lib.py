@@ -89,12 +89,13 @@ PROTOTYPES = {
                            c_int64, c_int, c_void_p, c_int64, c_void_p, c_void_p]),
     "qd_rmsnorm_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_float, c_void_p, c_int64, c_void_p]),
     "qd_argmax_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
-    "qd_tree_qk_rope": (c_int, [c_void_p, c_int64, c_int, c_int64, c_void_p, c_int, c_int, c_void_p, c_void_p, c_float,
-                                c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
-                                c_void_p]),
-    "qd_tree_attn": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int64,
-                             c_void_p, c_float, c_void_p, c_int64, c_void_p]),
-    "qd_tree_compact": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int, c_int64, c_int64, c_void_p, c_int, c_void_p]),
+    "qd_tree_qk_rope": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p,
+                                c_float, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64,
+                                c_int64, c_void_p, c_void_p]),
+    "qd_tree_attn": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int64, c_int64,
+                             c_int64, c_void_p, c_void_p, c_float, c_void_p, c_int64, c_void_p, c_void_p]),
+    "qd_tree_compact": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int, c_int64, c_int, c_int64, c_int64, c_void_p,
+                                c_int, c_void_p]),
     "qd_prefill_qk_rope": (c_int, [c_void_p, c_int64, c_int, c_int64, c_int, c_int, c_void_p, c_void_p, c_float,
                                    c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                                    c_int64, c_void_p]),

@@ -303,34 +303,40 @@ def rmsnorm_rows(x, w, eps: float, out):
     return out
 
 
-def tree_qk_rope(qkv, T: int, slot0: int, rope_pos, nq: int, nkv: int, q_norm, k_norm, eps: float, cos, sin, q_out,
-                 k_cache, v_cache, err=None):
-    """q/k RMSNorm + RoPE of T token-tree nodes (qd_tree_qk_rope): node t rotated at rope_pos[t] (device int32),
-    its K/V at cache slot slot0 + t. qkv [T, (nq + 2 nkv) * 128]; q_out [T, nq * 128]; caches [nkv, cap, 128]."""
+def tree_qk_rope(qkv, B: int, T: int, slot0, rope_pos, nq: int, nkv: int, q_norm, k_norm, eps: float, cos, sin,
+                 q_out, k_cache, v_cache, err=None):
+    """q/k RMSNorm + RoPE of the T token-tree nodes of each of B sequences (qd_tree_qk_rope): row b * T + t
+    rotated at rope_pos[row] (device int32 [B * T]), its K/V at slot slot0[b] + t (device int32 [B]) of
+    sequence b. qkv [B * T, (nq + 2 nkv) * 128]; q_out [B * T, nq * 128]; caches [B, nkv, cap, 128]."""
     _check_bf16(qkv, q_norm, k_norm, cos, sin, q_out, k_cache, v_cache)
-    assert rope_pos.dtype == torch.int32 and rope_pos.numel() >= T and k_cache.stride() == v_cache.stride()
-    L.call("qd_tree_qk_rope", _ptr(qkv), qkv.stride(0), T, slot0, _ptr(rope_pos), nq, nkv, _ptr(q_norm), _ptr(k_norm),
-           eps, _ptr(cos), _ptr(sin), _ptr(q_out), q_out.stride(0), _ptr(k_cache), _ptr(v_cache), k_cache.shape[-2],
-           k_cache.stride(-3), _ptr(err), _stream())
+    assert rope_pos.dtype == torch.int32 and rope_pos.numel() >= B * T
+    assert slot0.dtype == torch.int32 and slot0.numel() >= B
+    assert k_cache.dim() == 4 and k_cache.shape[0] >= B and k_cache.stride() == v_cache.stride()
+    L.call("qd_tree_qk_rope", _ptr(qkv), qkv.stride(0), B, T, _ptr(slot0), _ptr(rope_pos), nq, nkv, _ptr(q_norm),
+           _ptr(k_norm), eps, _ptr(cos), _ptr(sin), _ptr(q_out), q_out.stride(0), _ptr(k_cache), _ptr(v_cache),
+           k_cache.shape[-2], k_cache.stride(0), k_cache.stride(1), _ptr(err), _stream())
 
 
-def tree_attn(q, T: int, nq: int, nkv: int, k_cache, v_cache, prefix: int, anc, out):
-    """Ancestor-masked attention of T token-tree nodes (qd_tree_attn): q / out [T, nq * 128]; caches
-    [nkv, cap, 128]; anc device uint32 [T] (passed as int32)."""
+def tree_attn(q, B: int, T: int, nq: int, nkv: int, k_cache, v_cache, prefix, anc, out, err=None):
+    """Ancestor-masked attention of the T token-tree nodes of each of B sequences (qd_tree_attn): q / out
+    [B * T, nq * 128]; caches [B, nkv, cap, 128]; prefix device int32 [B] (each tree's root slot); anc
+    device uint32 [B * T] (passed as int32)."""
     _check_bf16(q, k_cache, v_cache, out)
-    assert anc.dtype == torch.int32 and anc.numel() >= T and k_cache.stride() == v_cache.stride()
-    L.call("qd_tree_attn", _ptr(q), q.stride(0), T, nq, nkv, _ptr(k_cache), _ptr(v_cache), k_cache.shape[-2],
-           k_cache.stride(-3), prefix, _ptr(anc), 1.0 / math.sqrt(128), _ptr(out), out.stride(0), _stream())
+    assert anc.dtype == torch.int32 and anc.numel() >= B * T and prefix.dtype == torch.int32 and prefix.numel() >= B
+    assert k_cache.dim() == 4 and k_cache.shape[0] >= B and k_cache.stride() == v_cache.stride()
+    L.call("qd_tree_attn", _ptr(q), q.stride(0), B, T, nq, nkv, _ptr(k_cache), _ptr(v_cache), k_cache.shape[-2],
+           k_cache.stride(0), k_cache.stride(1), _ptr(prefix), _ptr(anc), 1.0 / math.sqrt(128), _ptr(out),
+           out.stride(0), _ptr(err), _stream())
     return out
 
 
 def tree_compact(k_all, v_all, moves, n: int):
-    """Move the accepted path's K/V rows of every layer (qd_tree_compact): caches [layers, 1, nkv, cap, 128];
-    moves device int32 [n, 2] (source slot, destination slot), applied in order."""
+    """Move the accepted paths' K/V rows of every layer (qd_tree_compact): caches [layers, B, nkv, cap, 128];
+    moves device int32 [n, 3] (sequence, source slot, destination slot), applied in order."""
     _check_bf16(k_all, v_all)
-    assert k_all.shape[1] == 1 and k_all.stride() == v_all.stride() and moves.dtype == torch.int32
-    L.call("qd_tree_compact", _ptr(k_all), _ptr(v_all), k_all.shape[0], k_all.stride(0), k_all.shape[2],
-           k_all.stride(2), k_all.shape[3], _ptr(moves), n, _stream())
+    assert k_all.dim() == 5 and k_all.stride() == v_all.stride() and moves.dtype == torch.int32
+    L.call("qd_tree_compact", _ptr(k_all), _ptr(v_all), k_all.shape[0], k_all.stride(0), k_all.shape[1],
+           k_all.stride(1), k_all.shape[2], k_all.stride(2), k_all.shape[3], _ptr(moves), n, _stream())
 
 
 def argmax_rows(logits, n: int, out):

@@ -206,3 +206,48 @@ def stream(seq: list[int], S: int, N: int, capacity: int, depth: int, verify, st
         for tok in emitted[:N - done]:
             done += 1
             yield tok
+
+
+def stream_batch(seqs: list[list[int]], S: int, N: int, capacity: int, depth: int, verify, stats: dict | None = None):
+    """The token-tree loop for B sequences after the prompt forward (the reference's batched tree stream,
+    engine/engine.py:830-908). `seqs[b]` is prompt b (S tokens) plus its first generated token; each list
+    is extended in place. Every round drafts one tree per unfinished sequence and verifies all of them in
+    one forward: verify(trees, pos0s) gets a tree (None for a finished sequence, whose rows are inert) and
+    the position of its root per sequence, and returns (greedy tokens per sequence, a callback given the
+    accepted paths that moves their keys / values). Sequences accept different numbers of drafts, so step
+    t (t = 2..N) is yielded as the list of B tokens once every sequence has its t-th token."""
+    B = len(seqs)
+    drafters = [TreeDrafter(s) for s in seqs]
+    stats = {} if stats is None else stats
+    stats["verifies"] = stats["accepted"] = stats["plain_steps"] = 0
+    yielded = 1
+    while yielded < N:
+        trees, chains, pos0s = [], [], []
+        for b in range(B):
+            if len(seqs[b]) - S >= N:  # finished: its rows go to slots past the prompt, never read again
+                trees.append(None)
+                chains.append(None)
+                pos0s.append(S)
+            else:
+                tree, chain = drafters[b].build(capacity, depth)
+                trees.append(tree)
+                chains.append(chain)
+                pos0s.append(len(seqs[b]) - 1)
+        greedy, commit = verify(trees, pos0s)
+        paths = []
+        for b in range(B):
+            if trees[b] is None:
+                paths.append(None)
+                continue
+            emitted, path = trees[b].walk(greedy[b])
+            drafters[b].learn(trees[b], chains[b], greedy[b], path)
+            for tok in emitted:
+                seqs[b].append(tok)
+                drafters[b].push(tok)
+            paths.append(path)
+            stats["accepted"] += len(path)
+        commit(paths, pos0s)
+        stats["verifies"] += 1
+        while yielded < N and all(len(s) - S > yielded for s in seqs):
+            yield [s[S + yielded] for s in seqs]
+            yielded += 1

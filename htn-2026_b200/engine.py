@@ -66,10 +66,12 @@ USE_PDL = os.environ.get("ENGINE_PDL", "1") != "0"
 SPEC_T = int(os.environ.get("ENGINE_SPEC_T", "0"))
 # while drafts are not accepted often enough to pay for a verify, fall back to plain decode steps
 SPEC_GATE = os.environ.get("ENGINE_SPEC_GATE", "1") != "0"
-# exact token-tree speculative decoding at batch 1: tree nodes per verify (0 = off; the reference uses
-# trees of 32 nodes at batch 1, engine/engine.py:169) and their deepest level (engine/engine.py:833)
+# exact token-tree speculative decoding: tree nodes per sequence and verify (0 = off), at most
+# TREE_MAX_ROWS // batch of them (the reference's rule: 32 nodes up to batch 2, fewer per sequence above,
+# no trees past batch 32, engine/engine.py:166-172), and their deepest level (engine/engine.py:833)
 TREE_T = int(os.environ.get("ENGINE_TREE_T", "0"))
 TREE_DEPTH = int(os.environ.get("ENGINE_TREE_DEPTH", "12"))
+TREE_MAX_ROWS = 64
 # "persistent": one launch per decode step (qd_decode_step); "kernels": 1 + 5 x layers + 1 launches;
 # "tc": the tensor-core kernels (used from TC_MIN_BATCH up): one persistent launch per step, or the
 # chain of 1 + 7 x layers + 2 launches (TC_STEP)
@@ -335,101 +337,119 @@ class _Verify:
 
 
 class _TreeVerify:
-    """Verify forward of a token tree (the reference's tree verify, engine/engine.py:830-936): the T nodes
-    run as T activation rows through the tcgen05 projections; node i's q/k are rotated at pos0 + depth(i)
-    and its K/V written to slot pos0 + i (qd_tree_qk_rope); every node attends to the cached prefix
-    [0, pos0) and to its ancestors (qd_tree_attn); the LM head's argmax gives the greedy token at every
-    node. After the walk, the accepted nodes' K/V move to consecutive slots (qd_tree_compact). The
-    ~8 x layers + 3 launches are recorded once and replayed with the prefix position patched."""
+    """Verify forward of one token tree per sequence (the reference's tree verify, engine/engine.py:418-462,
+    830-936): the B x T nodes run as activation rows (row b * T + i = node i of sequence b) through the
+    tcgen05 projections; node i's q/k are rotated at prefix[b] + depth(i) and its K/V written to slot
+    prefix[b] + i of its sequence (qd_tree_qk_rope); every node attends to its sequence's cached prefix and
+    to its ancestors (qd_tree_attn); the LM head's argmax gives the greedy token at every node. After the
+    walks, the accepted nodes' K/V move to consecutive slots (qd_tree_compact). The per-round inputs
+    (tokens, positions, masks, prefixes) live in device buffers, so the ~8 x layers + 3 launches are
+    recorded once and replayed unchanged."""
 
     def __init__(self, eng: "Engine", st: "_State", T: int):
         if not 2 <= T <= 32:
             raise ValueError(f"token-tree verify width must be in [2, 32], got {T}")
+        B = st.B
+        if B * T > TREE_MAX_ROWS:
+            raise ValueError(f"token-tree verify of {B} x {T} rows > {TREE_MAX_ROWS}")
         dev = eng.device
         H, I, nq, nkv, D = eng.hidden, eng.inter, eng.nq, eng.nkv, eng.head_dim
-        self.T, self.depth = T, max(1, min(TREE_DEPTH, T - 1))
+        self.B, self.T, self.depth = B, T, max(1, min(TREE_DEPTH, T - 1))
+        M = self.M = B * T
         n_qkv = (nq + 2 * nkv) * D
-        self.tok = torch.zeros((T,), dtype=torch.int64, device=dev)
-        self.rope_pos = torch.zeros((T,), dtype=torch.int32, device=dev)
-        self.anc = torch.zeros((T,), dtype=torch.int32, device=dev)
-        self.moves = torch.zeros((32, 2), dtype=torch.int32, device=dev)
-        self.out = torch.zeros((T,), dtype=torch.int64, device=dev)
-        self.x = torch.zeros((T, H), dtype=BF16, device=dev)
-        self.qkv = torch.zeros((T, n_qkv), dtype=BF16, device=dev)
-        self.q = torch.zeros((T, nq * D), dtype=BF16, device=dev)
-        self.att = torch.zeros((T, nq * D), dtype=BF16, device=dev)
-        self.xp_h = ops.PackedActivations(T, H, dev)
-        self.xp_a = ops.PackedActivations(T, nq * D, dev)
-        self.xp_i = ops.PackedActivations(T, I, dev)
-        self.qkv_op = ops.TcGemv(T, n_qkv, H, ops.TcGemv.STORE, dev)
-        self.o = ops.TcGemv(T, H, nq * D, ops.TcGemv.RES, dev)
-        self.gu = ops.TcGemv(T, 2 * I, H, ops.TcGemv.SWIGLU_PACKED, dev)
-        self.down = ops.TcGemv(T, H, I, ops.TcGemv.RES, dev)
-        self.lm = ops.TcLmHeadArgmax(T, eng.vocab, H, dev)
+        self.tok = torch.zeros((M,), dtype=torch.int64, device=dev)
+        # int32 inputs in one buffer (one upload): RoPE positions [M], ancestor masks [M], root slots [B]
+        self.ints = torch.zeros((2 * M + B,), dtype=torch.int32, device=dev)
+        self.rope_pos, self.anc, self.prefix = self.ints[:M], self.ints[M:2 * M], self.ints[2 * M:]
+        self.moves = torch.zeros((M, 3), dtype=torch.int32, device=dev)
+        self.out = torch.zeros((M,), dtype=torch.int64, device=dev)
+        self.x = torch.zeros((M, H), dtype=BF16, device=dev)
+        self.qkv = torch.zeros((M, n_qkv), dtype=BF16, device=dev)
+        self.q = torch.zeros((M, nq * D), dtype=BF16, device=dev)
+        self.att = torch.zeros((M, nq * D), dtype=BF16, device=dev)
+        self.xp_h = ops.PackedActivations(M, H, dev)
+        self.xp_a = ops.PackedActivations(M, nq * D, dev)
+        self.xp_i = ops.PackedActivations(M, I, dev)
+        self.qkv_op = ops.TcGemv(M, n_qkv, H, ops.TcGemv.STORE, dev)
+        self.o = ops.TcGemv(M, H, nq * D, ops.TcGemv.RES, dev)
+        self.gu = ops.TcGemv(M, 2 * I, H, ops.TcGemv.SWIGLU_PACKED, dev)
+        self.down = ops.TcGemv(M, H, I, ops.TcGemv.RES, dev)
+        self.lm = ops.TcLmHeadArgmax(M, eng.vocab, H, dev)
         pin = torch.cuda.is_available()
-        self.tok_host = torch.zeros((T,), dtype=torch.int64, pin_memory=pin)
-        self.pos_host = torch.zeros((T,), dtype=torch.int32, pin_memory=pin)
-        self.anc_host = torch.zeros((T,), dtype=torch.int32, pin_memory=pin)
-        self.moves_host = torch.zeros((32, 2), dtype=torch.int32, pin_memory=pin)
-        self.out_host = torch.zeros((T,), dtype=torch.int64, pin_memory=pin)
+        self.tok_host = torch.zeros((M,), dtype=torch.int64, pin_memory=pin)
+        self.ints_host = torch.zeros((2 * M + B,), dtype=torch.int32, pin_memory=pin)
+        self.moves_host = torch.zeros((M, 3), dtype=torch.int32, pin_memory=pin)
+        self.out_host = torch.zeros((M,), dtype=torch.int64, pin_memory=pin)
         self.event = torch.cuda.Event()
         self.calls = None
 
-    def _enqueue(self, eng: "Engine", st: "_State", pos0: int) -> None:
-        T, nq, nkv, eps, err, pdl = self.T, eng.nq, eng.nkv, eng.eps, st.err, USE_PDL
+    def _enqueue(self, eng: "Engine", st: "_State") -> None:
+        B, T, nq, nkv, eps, err, pdl = self.B, self.T, eng.nq, eng.nkv, eng.eps, st.err, USE_PDL
         ops.embed(self.tok, eng.e_packed, eng.vocab, self.x, err, pdl)
         for i in range(eng.n_layers):
-            kc, vc = st.k_all[i, 0], st.v_all[i, 0]
+            kc, vc = st.k_all[i], st.v_all[i]
             self.xp_h.pack(self.x, eng.ln1[i], eps, pdl)
             self.qkv_op(self.xp_h, eng.w_qkv[i], self.qkv, err=err, pdl=pdl)
-            ops.tree_qk_rope(self.qkv, T, pos0, self.rope_pos, nq, nkv, eng.qn[i], eng.kn[i], eps, st.cos, st.sin,
-                             self.q, kc, vc, err=err)
-            ops.tree_attn(self.q, T, nq, nkv, kc, vc, pos0, self.anc, self.att)
+            ops.tree_qk_rope(self.qkv, B, T, self.prefix, self.rope_pos, nq, nkv, eng.qn[i], eng.kn[i], eps, st.cos,
+                             st.sin, self.q, kc, vc, err=err)
+            ops.tree_attn(self.q, B, T, nq, nkv, kc, vc, self.prefix, self.anc, self.att, err=err)
             self.o(self.xp_a.pack(self.att, None, eps, pdl), eng.w_o[i], self.x, res=self.x, err=err, pdl=pdl)
             self.xp_h.pack(self.x, eng.ln2[i], eps, pdl)
             self.gu(self.xp_h, eng.w_gu[i], self.xp_i, err=err, pdl=pdl)
             self.down(self.xp_i, eng.w_down[i], self.x, res=self.x, err=err, pdl=pdl)
         self.lm(self.xp_h.pack(self.x, eng.final_norm, eps, pdl), eng.e_packed, self.out, err=err, pdl=pdl)
 
-    def launch(self, eng: "Engine", st: "_State", pos0: int) -> None:
+    def prime(self, root_slot: int) -> None:
+        """Fill the device inputs with root-only trees at `root_slot` (every row attends to the prefix
+        and itself), for warm-up launches."""
+        B, T, M = self.B, self.T, self.M
+        ints = [root_slot + (i % T > 0) for i in range(M)] + [1 << (i % T) if i % T < 31 else -(1 << 31)
+                                                                for i in range(M)] + [root_slot] * B
+        self.tok.zero_()
+        self.ints.copy_(torch.tensor(ints, dtype=torch.int32))
+
+    def launch(self, eng: "Engine", st: "_State") -> None:
+        """Run the verify forward on the current stream over the device buffers' current contents."""
         if self.calls is None:
             with qdlib.recording() as rec:
-                self._enqueue(eng, st, 0)
+                self._enqueue(eng, st)
             self.calls = qdlib.bind(rec)
-            self.rope = [c[2] for c in self.calls if c[1] == "qd_tree_qk_rope"]
-            self.attn = [c[2] for c in self.calls if c[1] == "qd_tree_attn"]
-            assert len(self.rope) == len(self.attn) == eng.n_layers
         stream = torch.cuda.current_stream().cuda_stream
-        for args in self.rope:
-            args[3] = pos0  # slot0
-        for args in self.attn:
-            args[9] = pos0  # prefix
         for _, _, args in self.calls:
             args[-1] = stream
         qdlib.replay(self.calls)
 
-    def __call__(self, eng: "Engine", st: "_State", tree: "tree_spec.TokenTree", pos0: int):
-        """Greedy token at every node of `tree` (its root at position pos0), and the commit callback
-        that moves the accepted path's keys / values into place."""
-        if pos0 + self.T > st.capacity:
-            raise RuntimeError("token tree past the cache capacity")
-        tok, dep, masks = tree.padded(self.T)
+    def __call__(self, eng: "Engine", st: "_State", trees: list, pos0s: list[int]):
+        """Greedy token at every node of each sequence's tree (its root at position pos0s[b]; a None tree
+        runs inert rows), and the commit callback that, given the accepted path of each sequence (None
+        for none), moves the paths' keys / values into place."""
+        B, T = self.B, self.T
+        tok, pos, anc = [], [], []
+        for b in range(B):
+            if pos0s[b] < 0 or pos0s[b] + T > st.capacity:
+                raise RuntimeError("token tree past the cache capacity")
+            tree = trees[b]
+            if tree is None:
+                tree = tree_spec.TokenTree(0, T)
+            t, d, m = tree.padded(T)
+            tok += t
+            pos += [pos0s[b] + x for x in d]
+            anc += [x - (1 << 32) if x >= 1 << 31 else x for x in m]  # 32-bit masks as int32 (two's complement)
         with torch.inference_mode():
             self.tok_host.copy_(torch.tensor(tok, dtype=torch.int64))
-            self.pos_host.copy_(torch.tensor([pos0 + d for d in dep], dtype=torch.int32))
-            # 32-bit masks as int32 (two's complement): the kernel reads them as uint32
-            self.anc_host.copy_(torch.tensor([m - (1 << 32) if m >= 1 << 31 else m for m in masks], dtype=torch.int32))
+            self.ints_host.copy_(torch.tensor(pos + anc + list(pos0s), dtype=torch.int32))
             self.tok.copy_(self.tok_host, non_blocking=True)
-            self.rope_pos.copy_(self.pos_host, non_blocking=True)
-            self.anc.copy_(self.anc_host, non_blocking=True)
-            self.launch(eng, st, pos0)
+            self.ints.copy_(self.ints_host, non_blocking=True)
+            self.launch(eng, st)
             self.out_host.copy_(self.out, non_blocking=True)
             self.event.record()
         self.event.synchronize()
-        greedy = self.out_host.tolist()
+        g = self.out_host.tolist()
+        greedy = [g[b * T:(b + 1) * T] for b in range(B)]
 
-        def commit(path, p0):
-            moves = tree_spec.compaction_moves(path, p0)
+        def commit(paths, p0s):
+            moves = [(b, src, dst) for b, path in enumerate(paths) if path
+                     for src, dst in tree_spec.compaction_moves(path, p0s[b])]
             if moves:
                 with torch.inference_mode():
                     self.moves_host[:len(moves)].copy_(torch.tensor(moves, dtype=torch.int32))
@@ -515,7 +535,7 @@ class Engine:
         self.state = None
         self.sm_count = ops.sm_count()
         self.speculate = SPEC_T  # verify width of exact speculative decoding at batch 1 (0 = plain greedy)
-        self.tree = TREE_T  # nodes per token tree of exact tree speculation at batch 1 (0 = off; wins over speculate)
+        self.tree = TREE_T  # nodes per token tree of exact tree speculation (0 = off; wins over speculate)
 
     # ------------------------------------------------------------------ model step
     def _prefill(self, st: _State) -> torch.Tensor:
@@ -634,14 +654,22 @@ class Engine:
             raise RuntimeError(f"decode kernels reported a device error: {qdlib.describe_device_error(code)}")
 
     # ------------------------------------------------------------------ shapes, graphs
+    def _side_widths(self, B: int, N: int) -> tuple[int, int]:
+        """(token-tree nodes per sequence, prompt-lookup verify width) for a request of B sequences and N
+        new tokens; 0 = off. Trees are cut to TREE_MAX_ROWS // B nodes and need at least 2; prompt-lookup
+        speculation runs at batch 1 only and yields to trees."""
+        tree_T = min(self.tree, TREE_MAX_ROWS // B) if (self.tree and N > 1) else 0
+        tree_T = tree_T if tree_T >= 2 else 0
+        spec_T = self.speculate if (self.speculate and B == 1 and N > 1 and not tree_T) else 0
+        return tree_T, spec_T
+
     def _build(self, B: int, S: int, N: int) -> _State:
         if B > TC_MAX_BATCH:
             raise NotImplementedError(f"batch {B} > {TC_MAX_BATCH} per GPU: shard the batch across GPUs")
         self.state = None
         gc.collect()
         torch.cuda.empty_cache()
-        tree_T = self.tree if (self.tree and B == 1 and N > 1) else 0
-        spec_T = self.speculate if (self.speculate and B == 1 and N > 1 and not tree_T) else 0
+        tree_T, spec_T = self._side_widths(B, N)
         st = _State(self, B, S, N, spec_T, tree_T)
         t0 = time.perf_counter()
         with torch.inference_mode():
@@ -656,7 +684,8 @@ class Engine:
                     if st.verify is not None:
                         st.verify.launch(self, st, S - 1)
                     if st.tree is not None:
-                        st.tree.launch(self, st, S - 1)
+                        st.tree.prime(S - 1)
+                        st.tree.launch(self, st)
             torch.cuda.current_stream().wait_stream(side)
             torch.cuda.synchronize()
             self.check_device_errors(st)
@@ -743,10 +772,12 @@ class Engine:
         self.check_device_errors(st)
 
     def _stream_tree(self, st: _State, input_ids, N: int):
-        """Exact token-tree speculative decoding of one sequence (the reference's tree stream,
-        engine/engine.py:830-936): after the prompt forward, every round verifies a drafted tree of
-        st.tree.T nodes in one forward and emits the model's greedy tokens along the accepted path plus
-        the one after it; exactly N steps are yielded."""
+        """Exact token-tree speculative decoding (the reference's tree stream, engine/engine.py:830-936):
+        after the prompt forward, every round verifies one drafted tree of st.tree.T nodes per sequence
+        in one forward and emits the model's greedy tokens along each accepted path plus the one after
+        it; exactly N steps are yielded. At batch 1 runs of plain decode steps stand in while trees do not
+        pay (spec.Gate); at batch > 1 the sequences' positions drift apart, and the decode step takes one
+        position, so every round is a tree verify."""
         S, tv, ring = st.S, st.tree, st.ring
         ring.reset()
         with torch.inference_mode():
@@ -756,9 +787,19 @@ class Engine:
         first = ring.take()
         yield first
         st.spec_stats = {}
+        seqs = [list(row) + [t] for row, t in zip(input_ids, first)]
+        if st.B > 1:
+            yield from tree_spec.stream_batch(seqs, S, N, tv.T, tv.depth,
+                                              lambda trees, pos0s: tv(self, st, trees, pos0s), st.spec_stats)
+            self.check_device_errors(st)
+            return
+
+        def verify(tree, pos0):
+            greedy, commit = tv(self, st, [tree], [pos0])
+            return greedy[0], lambda path, p0: commit([path], [p0])
+
         plain = (lambda tok, pos, n: self._plain_steps(st, tok, pos, n)) if SPEC_GATE else None
-        for tok in tree_spec.stream(list(input_ids[0]) + first, S, N, tv.T, tv.depth,
-                                    lambda tree, pos0: tv(self, st, tree, pos0), st.spec_stats, step=plain,
+        for tok in tree_spec.stream(seqs[0], S, N, tv.T, tv.depth, verify, st.spec_stats, step=plain,
                                     gate=spec.Gate() if SPEC_GATE else None):
             yield [tok]
         self.check_device_errors(st)
@@ -791,8 +832,7 @@ class Engine:
         B, S = len(input_ids), len(input_ids[0])
         if B < 1 or S < 1 or any(len(r) != S for r in input_ids):
             raise ValueError("input_ids must be a non-empty batch of equal-length rows")
-        tree_T = self.tree if (self.tree and B == 1 and N > 1) else 0
-        spec_T = self.speculate if (self.speculate and B == 1 and N > 1 and not tree_T) else 0
+        tree_T, spec_T = self._side_widths(B, N)
         st = self.state
         fits = st is not None and (st.B, st.S, st.N) == (B, S, N) and (st.verify.T if st.verify else 0) == spec_T \
             and (st.tree.T if st.tree else 0) == tree_T

@@ -299,27 +299,33 @@ int qd_rmsnorm_rows(const void* x, int64_t ldx, int64_t m, int64_t k, const void
 
 /* ---------------------------------------------------------------- token-tree verification
  * Replace the reference's tree kernels (engine/kernels/tree.py:25-164: tree q/k RoPE at depth positions,
- * ancestor-masked attention, KV compaction) for exact token-tree speculation at batch 1. The T nodes of
- * a draft tree (node 0 = the last emitted token, parents before children) are T activation rows.
+ * ancestor-masked attention, KV compaction) for exact token-tree speculation. Each of the B sequences
+ * verifies one draft tree of T nodes (node 0 = its last emitted token, parents before children); row
+ * b * T + t of the B * T activation rows is node t of sequence b. slot0 / prefix (device int32 [B]) is
+ * the cache slot of each sequence's root: node t's keys / values go to slot prefix[b] + t. Caches are
+ * [B][nkv][cap][128] (sequence stride cs_b, head stride cs_h).
  *
- * qd_tree_qk_rope: per-node q/k RMSNorm + RoPE as qd_prefill_qk_rope_at, node t's K/V written to cache
- * slot slot0 + t but rotated at position rope_pos[t] (device int32 [T]: slot0 + its depth); caches
- * [nkv, cap, 128] (head stride cs_h). A position outside [0, cap) is clamped and flags QD_DEVERR_POS.
- * qd_tree_attn: out[t] = attention of node t's query heads over cache slots [0, prefix) and the tree
- * slots prefix + j with bit j of anc[t] set (device uint32 [T]: node t and its ancestors); 1 <= T <= 32,
- * prefix + T <= cap, 4 query heads per KV head. Same arithmetic as qd_attn_decode.
- * qd_tree_compact: for each move i in order (device int32 [n][2]: source slot, destination slot), the
- * key and value rows of every layer and KV head are copied from the source to the destination slot;
- * caches [layers][nkv][cap][128] at layer stride layer_stride (batch 1), n <= 64. */
-int qd_tree_qk_rope(const void* qkv, int64_t ldqkv, int T, int64_t slot0, const int32_t* rope_pos, int nq_heads,
-                    int nkv_heads, const void* q_norm, const void* k_norm, float eps, const void* cos, const void* sin,
-                    void* q_out, int64_t ldq, void* k_cache, void* v_cache, int64_t cap, int64_t cs_h, int* err,
-                    cudaStream_t stream);
-int qd_tree_attn(const void* q, int64_t ldq, int T, int nq_heads, int nkv_heads, const void* k_cache,
-                 const void* v_cache, int64_t cap, int64_t cs_h, int64_t prefix, const uint32_t* anc, float scale,
-                 void* out, int64_t ldo, cudaStream_t stream);
-int qd_tree_compact(void* k_cache, void* v_cache, int layers, int64_t layer_stride, int nkv_heads, int64_t cs_h,
-                    int64_t cap, const int32_t* moves, int n, cudaStream_t stream);
+ * qd_tree_qk_rope: per-node q/k RMSNorm + RoPE as qd_prefill_qk_rope_at, rotated at position
+ * rope_pos[row] (device int32 [B * T]: the root's slot + the node's depth). A position outside [0, cap)
+ * is clamped and flags QD_DEVERR_POS; a sequence whose slots slot0[b] .. slot0[b] + T - 1 leave the
+ * cache writes no keys / values and flags QD_DEVERR_POS.
+ * qd_tree_attn: out[row] = attention of the node's query heads over its sequence's cache slots
+ * [0, prefix[b]) and the tree slots prefix[b] + j with bit j of anc[row] set (device uint32 [B * T]: the
+ * node and its ancestors); 1 <= T <= 32, 4 query heads per KV head. Same arithmetic as qd_attn_decode.
+ * A sequence with prefix[b] < 0 or prefix[b] + T > cap gets zeros and flags QD_DEVERR_POS in *err.
+ * qd_tree_compact: for each move i in order (device int32 [n][3]: sequence, source slot, destination
+ * slot), the key and value rows of every layer and KV head are copied from the source to the destination
+ * slot of that sequence; caches [layers][B][nkv][cap][128] at layer stride layer_stride; moves naming a
+ * sequence or slot outside the cache are skipped; n <= 4096. */
+int qd_tree_qk_rope(const void* qkv, int64_t ldqkv, int batch, int T, const int32_t* slot0, const int32_t* rope_pos,
+                    int nq_heads, int nkv_heads, const void* q_norm, const void* k_norm, float eps, const void* cos,
+                    const void* sin, void* q_out, int64_t ldq, void* k_cache, void* v_cache, int64_t cap,
+                    int64_t cs_b, int64_t cs_h, int* err, cudaStream_t stream);
+int qd_tree_attn(const void* q, int64_t ldq, int batch, int T, int nq_heads, int nkv_heads, const void* k_cache,
+                 const void* v_cache, int64_t cap, int64_t cs_b, int64_t cs_h, const int32_t* prefix,
+                 const uint32_t* anc, float scale, void* out, int64_t ldo, int* err, cudaStream_t stream);
+int qd_tree_compact(void* k_cache, void* v_cache, int layers, int64_t layer_stride, int batch, int64_t cs_b,
+                    int nkv_heads, int64_t cs_h, int64_t cap, const int32_t* moves, int n, cudaStream_t stream);
 
 /* Greedy token of each row of BF16 logits: out[i] = argmax over j < n of logits[i * ld + j], the lowest
  * index among exact ties. Replaces the torch.argmax over the prompt's last-position logits that picks

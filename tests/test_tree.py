@@ -136,3 +136,48 @@ def test_gated_tree_stream_falls_back_to_plain_steps_and_stays_exact():
                                       step=_step_with(_long_next, seq), gate=spec.Gate(prior_cost=1.4)))
     assert out == greedy[S:S + N]
     assert stats["plain_steps"] > 0.8 * N
+
+
+def _batch_verify(next_fn, seqs, log):
+    """verify(trees, pos0s) over B toy sequences: each unfinished tree's root is its sequence's last token
+    at position pos0; a finished sequence gets None."""
+    def verify(trees, pos0s):
+        greedy = []
+        for b, tree in enumerate(trees):
+            if tree is None:
+                greedy.append(None)
+                continue
+            greedy.append(_greedy_verify(next_fn, seqs[b])(tree, pos0s[b])[0])
+        log.append([t is None for t in trees])
+
+        def commit(paths, p0s):
+            assert [p is None for p in paths] == [t is None for t in trees] and list(p0s) == list(pos0s)
+        return greedy, commit
+    return verify
+
+
+@pytest.mark.parametrize("cap,depth", [(2, 1), (8, 4), (16, 12)])
+@pytest.mark.parametrize("B,S,N", [(2, 5, 1), (3, 5, 2), (4, 3, 60), (2, 9, 150)])
+def test_batched_tree_stream_yields_every_sequences_greedy_tokens(cap, depth, B, S, N):
+    prompts = [[(3 * i + 2 + b) % 5 for i in range(S)] for b in range(B)]
+    nexts = [_cycle_next, _long_next]
+    fn = lambda p: nexts[p[0] % 2](p)  # noqa: E731  (sequences follow different rules by their first token)
+    greedy = []
+    for p in prompts:
+        g = list(p)
+        for _ in range(N + cap):
+            g.append(fn(g))
+        greedy.append(g)
+    seqs = [p + [g[S]] for p, g in zip(prompts, greedy)]
+    log, stats = [], {}
+    steps = [[s[S] for s in seqs]] + list(T.stream_batch(seqs, S, N, cap, depth, _batch_verify(fn, seqs, log), stats))
+    assert len(steps) == N and all(len(st) == B for st in steps)
+    for b in range(B):
+        assert [st[b] for st in steps] == greedy[b][S:S + N]
+        assert seqs[b][:S + N] == greedy[b][:S + N]  # overshoot past N is still the greedy continuation
+    assert stats["verifies"] == len(log)
+    if N > 1:
+        # a sequence drops out of the verifies once it has N tokens, and only then
+        for b in range(B):
+            col = [row[b] for row in log]
+            assert col == sorted(col)
