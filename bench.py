@@ -146,8 +146,9 @@ def make_model(layers: int):
     return synth.make_state_dict(cfg, seed=0), cfg
 
 
-def cpu_reference(state, cfg, prompt, steps: int, threads: int | None = None):
-    """Time the reference's Transformers greedy loop (oracle.native) on the host cores."""
+def cpu_reference(state, cfg, prompt, steps: int, threads: int | None = None, warmup: int = 0):
+    """Time the reference's Transformers greedy loop (oracle.native) on the host cores: `warmup` untimed
+    decode steps after the prompt, then `steps` timed ones."""
     import torch
 
     from oracle import native
@@ -156,14 +157,14 @@ def cpu_reference(state, cfg, prompt, steps: int, threads: int | None = None):
     torch.set_num_threads(threads)
     model = native.build_model(state, cfg)
     t0 = time.perf_counter()
-    _, _, times = native.greedy(model, prompt, steps + 1, keep_logits=False)
+    _, _, times = native.greedy(model, prompt, warmup + steps + 1, keep_logits=False)
     total = time.perf_counter() - t0
-    dec = times[1:]
+    dec = times[1 + warmup:]
     return {"value": len(prompt) * len(dec) / sum(dec), "unit": "tokens/s", "cores": torch.get_num_threads(),
             "kind": "port", "ttft_s": times[0], "decode_ms_per_step": 1e3 * sum(dec) / len(dec),
             "sample": f"Transformers CPU greedy decode (reference tier 0 restated), {cfg['num_hidden_layers']} layers, "
-                      f"batch {len(prompt)}, prompt {len(prompt[0])}, {len(dec)} decode steps after prefill "
-                      f"({total:.1f} s total)"}
+                      f"batch {len(prompt)}, prompt {len(prompt[0])}, {len(dec)} timed decode steps after prefill "
+                      f"and {warmup} untimed ones ({total:.1f} s total)"}
 
 
 def run_reference(a):
@@ -175,9 +176,10 @@ def run_reference(a):
 
     prompt = synth.random_prompt(a.batch, a.prompt, cfg["vocab_size"], seed=0)
     steps = max(1, min(a.steps, a.cpu_steps))
-    r = cpu_reference(state, cfg, prompt, steps)
+    W = max(0, a.warmup)
+    r = cpu_reference(state, cfg, prompt, steps, warmup=W)
     out = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": a.gpus,
-           "steps": steps, "warmup": 1, "ms_per_step": r["decode_ms_per_step"], "higher_is_better": True,
+           "steps": steps, "warmup": W, "ms_per_step": r["decode_ms_per_step"], "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights, "
            "uniform-random prompt)",
            "config": {"workload": f"BASELINE config 1 (Qwen3-4B arch, {a.layers} layers, batch {a.batch}, prompt "
