@@ -179,6 +179,25 @@ __device__ __forceinline__ int ld_volatile(const int* p) {
   asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// Bounded wait (one thread) until *cnt >= target: one acquire load per try (the load orders the caller's
+// later reads after the releases it observed), the abort flag and the clock read only every 64 tries.
+// Returns false when another CTA raised *abort, or when kWaitLimitNs passed (then err |= code and
+// *abort = 1).
+__device__ __forceinline__ bool wait_count_ge(const int* cnt, int target, int* abort, int* err, int code) {
+  if (ld_acquire(cnt) >= target) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (ld_acquire(cnt) >= target) return true;
+    if ((i & 63u) == 0) {
+      if (abort && ld_volatile(abort)) return false;
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        if (err) atomicOr(err, code);
+        if (abort) atomicExch(abort, 1);
+        return false;
+      }
+    }
+  }
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -104,18 +104,7 @@ __device__ __forceinline__ int* ctr(const StepArgs& A, int l, int op) { return A
 
 // One consumer thread waits (bounded) until *cnt >= target, then the 256 consumers proceed.
 static __device__ void wait_dep(const StepArgs& A, const int* cnt, int target, int tid) {
-  if (tid == 0 && ld_acquire(cnt) < target && !ld_volatile(A.abort_flag)) {
-    const uint64_t t0 = globaltimer();
-    for (uint32_t i = 0;; ++i) {
-      if (ld_acquire(cnt) >= target) break;
-      if (ld_volatile(A.abort_flag)) break;
-      if ((i & 255u) == 255u && globaltimer() - t0 > kWaitLimitNs) {
-        atomicOr(A.err, kErrDep);
-        atomicExch(A.abort_flag, 1);
-        break;
-      }
-    }
-  }
+  if (tid == 0) wait_count_ge(cnt, target, A.abort_flag, A.err, kErrDep);
   named_bar(kBarConsumers, kConsumers);
 }
 

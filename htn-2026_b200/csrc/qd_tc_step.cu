@@ -115,17 +115,7 @@ __device__ __forceinline__ void tstamp(const TcStepArgs& A, int cta, int op, int
 
 // One thread waits (bounded) until *cnt >= target; on expiry it flags the error and the abort flag.
 __device__ bool poll_ctr(const TcStepArgs& A, const int* cnt, int target) {
-  if (ld_acquire(cnt) >= target) return true;
-  const uint64_t t0 = globaltimer();
-  for (uint32_t i = 0;; ++i) {
-    if (ld_acquire(cnt) >= target) return true;
-    if (ld_volatile(A.abort_flag)) return false;
-    if ((i & 255u) == 255u && globaltimer() - t0 > kWaitLimitNs) {
-      atomicOr(A.err, kErrDep);
-      atomicExch(A.abort_flag, 1);
-      return false;
-    }
-  }
+  return wait_count_ge(cnt, target, A.abort_flag, A.err, kErrDep);
 }
 // ... and the 256 consumers proceed together
 __device__ void wait_consumers(const TcStepArgs& A, const int* cnt, int target, int tid) {
