@@ -57,7 +57,7 @@ def _args():
                    help="also time the end-to-end run with exact token-tree speculation of this many nodes per tree "
                         "(batch 1; reported as e2e_tree, not the headline)")
     p.add_argument("--kernel", default=None, choices=["qkv", "o", "gu", "down", "lm", "attn", "attn_stream", "attn_tc", "step",
-                                                      "prefill_gu", "prefill_attn", "prefill_fwd"],
+                                                      "prefill_gu", "prefill_attn", "prefill_fwd", "tree_verify"],
                    help="time one decode kernel alone (small profiling case; random packed weights on the GPU)")
     p.add_argument("--launches", type=int, default=8)
     p.add_argument("--trace", action="store_true",
@@ -538,6 +538,59 @@ def run_prefill_forward(a):
                       "library_launches_per_forward": sum(1 for name, _ in rec if not name.endswith("_plan"))}))
 
 
+def run_tree_verify(a):
+    """Token-tree verify forwards (`--layers` layers, `--batch` sequences of `--prompt` tokens, one tree of
+    `--tree` nodes per sequence cut to 64 // batch; random-init weights): the prompt forward, then
+    `--launches` verifies of full trees at the prompt's end, each with its host round trip (upload of
+    the trees, launches, greedy tokens back). Prints avg ms per verify and the library launches of one
+    verify; one further verify runs inside the NVTX range "tree_verify" for a launch-list capture."""
+    import random
+
+    import torch
+
+    import engine as E
+    from decode_b200 import tree as TT
+
+    B, S = a.batch, a.prompt
+    state, cfg = make_model(a.layers)
+    eng = E.Engine.from_state_dict(state, cfg, "cuda:0")
+    del state
+    eng.tree = a.tree or 32
+    st = eng._build(B, S, max(2, a.new))
+    tv = st.tree
+    prompt = synth_prompt(B, S)
+    with torch.inference_mode():
+        eng._upload_prompt(st, prompt)
+        eng._enqueue_prefill(st)
+    rnd = random.Random(0)
+    trees = []
+    for b in range(B):
+        t = TT.TokenTree(prompt[b][-1], tv.T)
+        while len(t) < tv.T:
+            t.insert([rnd.randrange(cfg["vocab_size"]) for _ in range(rnd.randrange(1, tv.depth + 1))], tv.depth)
+        trees.append(t)
+    pos0s = [S - 1] * B
+    for _ in range(3):
+        tv(eng, st, trees, pos0s)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(a.launches):
+        tv(eng, st, trees, pos0s)
+    e.record()
+    e.synchronize()
+    torch.cuda.nvtx.range_push("tree_verify")  # one more verify, as an NVTX range for a launch-list capture
+    tv(eng, st, trees, pos0s)
+    torch.cuda.nvtx.range_pop()
+    eng.check_device_errors(st)
+    n_calls = len(tv.calls)
+    print(json.dumps({"kernel": "tree_verify", "layers": a.layers, "batch": B, "prompt": S, "tree_nodes": tv.T,
+                      "rows": tv.M, "launches": a.launches, "avg_ms": round(s.elapsed_time(e) / a.launches, 3),
+                      "library_launches_per_verify": n_calls,
+                      "note": "each verify includes its host round trip; the engine build runs 2 verifies and "
+                              "this mode 3 more before the timed ones"}))
+
+
 def qdlib_recording():
     from decode_b200 import lib as qdlib
 
@@ -592,6 +645,8 @@ def run_kernel(a):
         return run_step_kernel(a)
     if a.kernel == "prefill_fwd":
         return run_prefill_forward(a)
+    if a.kernel == "tree_verify":
+        return run_tree_verify(a)
     if a.kernel in ("prefill_gu", "prefill_attn"):
         return run_prefill_kernel(a)
     H, I, V, nq, nkv, D, B, L = 2560, 9728, 151936, 32, 8, 128, a.batch, a.layers

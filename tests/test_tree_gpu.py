@@ -44,10 +44,13 @@ def _masks_i32(masks):
     return [m - (1 << 32) if m >= 1 << 31 else m for m in masks]
 
 
-@pytest.mark.parametrize("T,prefixes", [(1, [1]), (8, [37]), (16, [200]), (32, [511]), (32, [0]),
-                                        (16, [5, 300, 0, 77]), (32, [100, 3]), (8, [9, 1000, 64, 2, 0, 513, 31, 8])])
+@pytest.mark.parametrize("T,prefixes", [(1, [1]), (8, [37]), (16, [200]), (32, [511]), (32, [0]), (32, [4000]),
+                                        (16, [5, 300, 0, 77]), (32, [100, 3]), (8, [9, 1000, 64, 2, 0, 513, 31, 8]),
+                                        (2, [7000] + [0] * 31)])
 def test_tree_attention_matches_oracle(T, prefixes):
-    """B sequences, each with its own prefix length and tree; slots past each sequence's tree are NaN."""
+    """B sequences, each with its own prefix length and tree; slots past each sequence's tree are NaN.
+    The split-K partition follows each row's prefix on the device: long and short prefixes share a launch
+    (the last case: one sequence of 7000 cached keys among 31 empty ones)."""
     from decode_b200 import ops
 
     B = len(prefixes)
@@ -283,7 +286,9 @@ def test_batched_tree_verify_accepts_each_sequences_own_continuation(eng2):
     """Three sequences whose trees hold their own greedy continuations to different depths (one sequence
     sits a round out as finished): each walk accepts exactly its branch, the compaction moves each
     sequence's K/V, and the next rounds - at positions that now differ per sequence - continue with every
-    sequence's plain greedy tokens."""
+    sequence's plain greedy tokens. A walk may stop early only where the plain run's own top-2 gap is
+    within the parity bound (a near tie the verify's summation order may flip); that sequence then
+    leaves the test."""
     from decode_b200 import synth, tree as TT
 
     eng, cfg = eng2
@@ -303,11 +308,13 @@ def test_batched_tree_verify_accepts_each_sequences_own_continuation(eng2):
         torch.cuda.synchronize()
         assert st.tok.tolist() == [plain[b][0] for b in range(B)]
         out = [[plain[b][0]] for b in range(B)]
+        tol = max(5e-2, 2 * load_golden("config0")["self_drift"]["max_logsoftmax_diff"])
+        active = [True] * B
         rnd = random.Random(5)
         for rnd_i in range(4):
             trees, pos0s, branches = [], [], []
             for b in range(B):
-                if b == 1 and rnd_i == 1:
+                if (b == 1 and rnd_i == 1) or not active[b]:
                     # sits this round out at its own root slot: the inert rows write slots that its next
                     # round writes again before any query reads them
                     trees.append(None)
@@ -329,12 +336,20 @@ def test_batched_tree_verify_accepts_each_sequences_own_continuation(eng2):
                     paths.append(None)
                     continue
                 emitted, path = trees[b].walk(greedy[b])
-                assert path == branches[b], (rnd_i, b, path, branches[b])
                 paths.append(path)
+                if path != branches[b]:
+                    t = len(out[b]) + len(path)  # the plain step whose token the verify did not repeat
+                    top2 = logits[t][b].float().topk(2).values
+                    gap = float(top2[0] - top2[1])
+                    assert path == branches[b][:len(path)] and gap <= tol, (rnd_i, b, t, gap, path, branches[b])
+                    active[b] = False
+                    continue
                 out[b] += emitted
             commit(paths, pos0s)
-        tol = max(5e-2, 2 * load_golden("config0")["self_drift"]["max_logsoftmax_diff"])
+        assert sum(active) >= 2, active
         for b in range(B):
+            if not active[b]:
+                continue
             assert len(out[b]) > 12
             ok, where = _tie_ok(out[b], plain[b][:len(out[b])], logits, tol, b)
             assert ok, (b, where)
