@@ -580,6 +580,10 @@ struct alignas(64) PrefillAttnArgs {
   int qrow0;  // q tensor-map row of position 0 is -qrow0 (0: q holds every position; q0: only q0..S-1)
   float scale_log2;
   int* err;
+  // token-tree rows (optional): the rows q0..S-1 are the nodes of one draft tree (S - q0 <= 32), and key
+  // q0 + j is visible to the row at position q only if bit j of anc[q - q0] is set (its ancestors and
+  // itself); keys before q0 follow the causal rule
+  const uint32_t* anc;
 };
 
 struct PaLayout {
@@ -779,6 +783,8 @@ __global__ void __launch_bounds__(kPaThreads, 1) prefill_attn_kernel(const __gri
       int i, h, qt;
       pa_unit(a, u, &i, &h, &qt);
       const int q = qt * kPaTile + r;  // query position within the sequence
+      // a token-tree row's ancestor mask over the keys q0.. (every key for rows outside the tree)
+      const uint32_t tmask = (a.anc && q >= a.q0 && q < a.S) ? __ldg(a.anc + (q - a.q0)) : 0xffffffffu;
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; j <= qt; ++j) {
         const int tt = t + j, b = tt & 1;
@@ -794,6 +800,13 @@ __global__ void __launch_bounds__(kPaThreads, 1) prefill_attn_kernel(const __gri
 #pragma unroll
           for (int e = 0; e < 64; ++e)
             if (64 * grp + e > r) own[e] = __float_as_uint(-INFINITY);
+        }
+        if (a.anc && (int64_t)kPaTile * (j + 1) > a.q0) {  // tree keys in this tile: the ancestor mask
+#pragma unroll
+          for (int e = 0; e < 64; ++e) {
+            const int64_t bit = (int64_t)kPaTile * j + 64 * grp + e - a.q0;
+            if (bit >= 0 && bit < 32 && !((tmask >> bit) & 1u)) own[e] = __float_as_uint(-INFINITY);
+          }
         }
         float mx;
         {  // four independent max chains
@@ -1535,7 +1548,8 @@ extern "C" int qd_tree_qk_rope(const void* qkv, int64_t ldqkv, int batch, int T,
 
 static int prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, bool q_compact, int nq_heads,
                         int nkv_heads, const void* k_cache, const void* v_cache, int64_t cap, int64_t cs_b,
-                        int64_t cs_h, float scale, void* out, int64_t ldo, int* err, cudaStream_t stream);
+                        int64_t cs_h, float scale, void* out, int64_t ldo, int* err, cudaStream_t stream,
+                        const uint32_t* anc = nullptr);
 
 extern "C" int qd_prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, int nq_heads,
                                int nkv_heads, const void* k_cache, const void* v_cache, int64_t cap, int64_t cs_b,
@@ -1551,9 +1565,19 @@ extern "C" int qd_prefill_attn_rows(const void* q, int64_t ldq, int batch, int64
                       out, ldo, err, stream);
 }
 
+extern "C" int qd_tree_attn_rows(const void* q, int64_t ldq, int64_t S, int64_t q_begin, const uint32_t* anc,
+                                 int nq_heads, int nkv_heads, const void* k_cache, const void* v_cache, int64_t cap,
+                                 int64_t cs_h, float scale, void* out, int64_t ldo, int* err, cudaStream_t stream) {
+  if (!anc) return set_error(QD_ERR_ARG, "tree attention rows: null ancestor masks");
+  if (S - q_begin < 1 || S - q_begin > 32) return set_error(QD_ERR_ARG, "tree attention rows: 1 to 32 tree rows");
+  return prefill_attn(q, ldq, 1, S, q_begin, true, nq_heads, nkv_heads, k_cache, v_cache, cap,
+                      (int64_t)nkv_heads * cs_h, cs_h, scale, out, ldo, err, stream, anc);
+}
+
 static int prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_t q_begin, bool q_compact, int nq_heads,
                         int nkv_heads, const void* k_cache, const void* v_cache, int64_t cap, int64_t cs_b,
-                        int64_t cs_h, float scale, void* out, int64_t ldo, int* err, cudaStream_t stream) {
+                        int64_t cs_h, float scale, void* out, int64_t ldo, int* err, cudaStream_t stream,
+                        const uint32_t* anc) {
   if (!q || !k_cache || !v_cache || !out) return set_error(QD_ERR_ARG, "null pointer");
   if (batch < 1 || S < 1 || S > cap || q_begin < 0 || q_begin >= S || nq_heads < 1 || nkv_heads < 1 ||
       nq_heads % nkv_heads || ldq < (int64_t)nq_heads * 128 || ldo < (int64_t)nq_heads * 128 || ldq % 8 ||
@@ -1606,7 +1630,8 @@ static int prefill_attn(const void* q, int64_t ldq, int batch, int64_t S, int64_
   a.units = (int)units;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.err = err;
-  if (env_int("QD_PREFILL_ATTN", 1) == 2 && (nq_heads / nkv_heads) % 2 == 0) {  // ping-pong variant
+  a.anc = anc;
+  if (!anc && env_int("QD_PREFILL_ATTN", 1) == 2 && (nq_heads / nkv_heads) % 2 == 0) {  // ping-pong variant
     a.units = (int)(units / 2);  // a unit covers two query heads of one KV head
     const int smem = PpLayout::total + 1024;
     if (int rc = set_max_dynamic_smem((const void*)prefill_attn_pp_kernel, smem)) return rc;

@@ -94,6 +94,8 @@ PROTOTYPES = {
                                 c_int64, c_void_p, c_void_p]),
     "qd_tree_attn": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int64, c_int64,
                              c_int64, c_void_p, c_void_p, c_float, c_void_p, c_int64, c_void_p, c_void_p]),
+    "qd_tree_attn_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int, c_void_p, c_void_p,
+                                  c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_void_p]),
     "qd_tree_compact": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int, c_int64, c_int, c_int64, c_int64, c_void_p,
                                 c_int, c_void_p]),
     "qd_prefill_qk_rope": (c_int, [c_void_p, c_int64, c_int, c_int64, c_int, c_int, c_void_p, c_void_p, c_float,

@@ -330,6 +330,16 @@ def tree_attn(q, B: int, T: int, nq: int, nkv: int, k_cache, v_cache, prefix, an
     return out
 
 
+def tree_attn_rows(q, T: int, pos0: int, anc, nq: int, nkv: int, k_cache, v_cache, out, err=None):
+    """Ancestor-masked attention of one sequence's T tree rows on the tensor cores (qd_tree_attn_rows):
+    node t at slot pos0 + t; q / out [T, nq * 128]; caches [nkv, cap, 128]; anc device uint32 [T] (int32)."""
+    _check_bf16(q, k_cache, v_cache, out)
+    assert anc.dtype == torch.int32 and anc.numel() >= T and k_cache.stride() == v_cache.stride()
+    L.call("qd_tree_attn_rows", _ptr(q), q.stride(0), pos0 + T, pos0, _ptr(anc), nq, nkv, _ptr(k_cache), _ptr(v_cache),
+           k_cache.shape[-2], k_cache.stride(-3), 1.0 / math.sqrt(128), _ptr(out), out.stride(0), _ptr(err), _stream())
+    return out
+
+
 def tree_compact(k_all, v_all, moves, n: int):
     """Move the accepted paths' K/V rows of every layer (qd_tree_compact): caches [layers, B, nkv, cap, 128];
     moves device int32 [n, 3] (sequence, source slot, destination slot), applied in order."""

@@ -72,6 +72,9 @@ SPEC_GATE = os.environ.get("ENGINE_SPEC_GATE", "1") != "0"
 TREE_T = int(os.environ.get("ENGINE_TREE_T", "0"))
 TREE_DEPTH = int(os.environ.get("ENGINE_TREE_DEPTH", "12"))
 TREE_MAX_ROWS = 64
+# the tree attention of a single sequence: "tc" = the tensor-core prompt attention with the ancestor mask
+# (qd_tree_attn_rows), "cuda" = the CUDA-core kernel that batches of trees use (qd_tree_attn)
+TREE_ATTN = os.environ.get("ENGINE_TREE_ATTN", "tc")
 # "persistent": one launch per decode step (qd_decode_step); "kernels": 1 + 5 x layers + 1 launches;
 # "tc": the tensor-core kernels (used from TC_MIN_BATCH up): one persistent launch per step, or the
 # chain of 1 + 7 x layers + 2 launches (TC_STEP)
@@ -341,10 +344,11 @@ class _TreeVerify:
     830-936): the B x T nodes run as activation rows (row b * T + i = node i of sequence b) through the
     tcgen05 projections; node i's q/k are rotated at prefix[b] + depth(i) and its K/V written to slot
     prefix[b] + i of its sequence (qd_tree_qk_rope); every node attends to its sequence's cached prefix and
-    to its ancestors (qd_tree_attn); the LM head's argmax gives the greedy token at every node. After the
-    walks, the accepted nodes' K/V move to consecutive slots (qd_tree_compact). The per-round inputs
-    (tokens, positions, masks, prefixes) live in device buffers, so the ~8 x layers + 3 launches are
-    recorded once and replayed unchanged."""
+    to its ancestors (qd_tree_attn; for one sequence the tensor-core qd_tree_attn_rows); the LM head's
+    argmax gives the greedy token at every node. After the walks, the accepted nodes' K/V move to
+    consecutive slots (qd_tree_compact). The per-round inputs (tokens, positions, masks, prefixes) live in
+    device buffers, so the ~8 x layers + 3 launches are recorded once and replayed, only the tensor-core
+    tree attention's root slot (a host argument) patched per round."""
 
     def __init__(self, eng: "Engine", st: "_State", T: int):
         if not 2 <= T <= 32:
@@ -382,6 +386,8 @@ class _TreeVerify:
         self.out_host = torch.zeros((M,), dtype=torch.int64, pin_memory=pin)
         self.event = torch.cuda.Event()
         self.calls = None
+        self.rows_attn = B == 1 and TREE_ATTN == "tc"
+        self.root1 = 0
 
     def _enqueue(self, eng: "Engine", st: "_State") -> None:
         B, T, nq, nkv, eps, err, pdl = self.B, self.T, eng.nq, eng.nkv, eng.eps, st.err, USE_PDL
@@ -392,7 +398,10 @@ class _TreeVerify:
             self.qkv_op(self.xp_h, eng.w_qkv[i], self.qkv, err=err, pdl=pdl)
             ops.tree_qk_rope(self.qkv, B, T, self.prefix, self.rope_pos, nq, nkv, eng.qn[i], eng.kn[i], eps, st.cos,
                              st.sin, self.q, kc, vc, err=err)
-            ops.tree_attn(self.q, B, T, nq, nkv, kc, vc, self.prefix, self.anc, self.att, err=err)
+            if self.rows_attn:  # root slot patched per round at launch (recorded at 0)
+                ops.tree_attn_rows(self.q, T, 0, self.anc, nq, nkv, kc[0], vc[0], self.att, err=err)
+            else:
+                ops.tree_attn(self.q, B, T, nq, nkv, kc, vc, self.prefix, self.anc, self.att, err=err)
             self.o(self.xp_a.pack(self.att, None, eps, pdl), eng.w_o[i], self.x, res=self.x, err=err, pdl=pdl)
             self.xp_h.pack(self.x, eng.ln2[i], eps, pdl)
             self.gu(self.xp_h, eng.w_gu[i], self.xp_i, err=err, pdl=pdl)
@@ -407,14 +416,20 @@ class _TreeVerify:
                                                                 for i in range(M)] + [root_slot] * B
         self.tok.zero_()
         self.ints.copy_(torch.tensor(ints, dtype=torch.int32))
+        self.root1 = root_slot
 
     def launch(self, eng: "Engine", st: "_State") -> None:
-        """Run the verify forward on the current stream over the device buffers' current contents."""
+        """Run the verify forward on the current stream over the device buffers' current contents (and, for
+        the tensor-core tree attention of one sequence, the host's root slot self.root1)."""
         if self.calls is None:
             with qdlib.recording() as rec:
                 self._enqueue(eng, st)
             self.calls = qdlib.bind(rec)
+            self.rows_calls = [c[2] for c in self.calls if c[1] == "qd_tree_attn_rows"]
         stream = torch.cuda.current_stream().cuda_stream
+        for args in self.rows_calls:
+            args[2] = self.root1 + self.T  # keys end
+            args[3] = self.root1           # first tree row's position
         for _, _, args in self.calls:
             args[-1] = stream
         qdlib.replay(self.calls)
@@ -435,6 +450,7 @@ class _TreeVerify:
             tok += t
             pos += [pos0s[b] + x for x in d]
             anc += [x - (1 << 32) if x >= 1 << 31 else x for x in m]  # 32-bit masks as int32 (two's complement)
+        self.root1 = pos0s[0]
         with torch.inference_mode():
             self.tok_host.copy_(torch.tensor(tok, dtype=torch.int64))
             self.ints_host.copy_(torch.tensor(pos + anc + list(pos0s), dtype=torch.int32))

@@ -324,6 +324,13 @@ int qd_tree_qk_rope(const void* qkv, int64_t ldqkv, int batch, int T, const int3
 int qd_tree_attn(const void* q, int64_t ldq, int batch, int T, int nq_heads, int nkv_heads, const void* k_cache,
                  const void* v_cache, int64_t cap, int64_t cs_b, int64_t cs_h, const int32_t* prefix,
                  const uint32_t* anc, float scale, void* out, int64_t ldo, int* err, cudaStream_t stream);
+/* qd_tree_attn for one sequence on the tensor cores: the T = S - q_begin tree rows (q [T, nq * 128],
+ * row stride ldq; node t at slot q_begin + t) attend to the keys [0, q_begin) and to the tree slots of
+ * their ancestors (anc: device uint32 [T]); caches [nkv][cap][128] (head stride cs_h). The prompt
+ * attention kernel (qd_prefill_attn_rows) with the ancestor mask applied in its softmax; 1 <= T <= 32. */
+int qd_tree_attn_rows(const void* q, int64_t ldq, int64_t S, int64_t q_begin, const uint32_t* anc, int nq_heads,
+                      int nkv_heads, const void* k_cache, const void* v_cache, int64_t cap, int64_t cs_h, float scale,
+                      void* out, int64_t ldo, int* err, cudaStream_t stream);
 int qd_tree_compact(void* k_cache, void* v_cache, int layers, int64_t layer_stride, int batch, int64_t cs_b,
                     int nkv_heads, int64_t cs_h, int64_t cap, const int32_t* moves, int n, cudaStream_t stream);
 

@@ -86,6 +86,43 @@ def test_tree_attention_matches_oracle(T, prefixes):
     assert worst < 2e-2, worst
 
 
+@pytest.mark.parametrize("T,prefix", [(1, 1), (8, 37), (32, 0), (32, 100), (32, 127), (16, 128), (32, 500),
+                                      (32, 2000)])
+def test_tree_attention_rows_on_tensor_cores_matches_oracle(T, prefix):
+    """qd_tree_attn_rows (the prompt attention kernel with the ancestor mask): every node's output against
+    the oracle's SDPA and an fp32 reference over the cached prefix plus its ancestors, within 2e-2 (the
+    prompt attention's tolerance); trees that straddle a 128-key tile boundary included. Slots past the
+    tree hold NaN, so a read of any of them shows."""
+    from decode_b200 import ops
+
+    cap = prefix + T + 40
+    g = torch.Generator().manual_seed(T * 7 + prefix)
+    tree = _random_tree(T, prefix + 3)
+    _, _, masks = tree.padded(T)
+    kc = torch.full((NKV, cap, D), float("nan"), dtype=BF16)
+    vc = torch.full((NKV, cap, D), float("nan"), dtype=BF16)
+    kc[:, :prefix + T] = torch.randn((NKV, prefix + T, D), generator=g).to(BF16)
+    vc[:, :prefix + T] = torch.randn((NKV, prefix + T, D), generator=g).to(BF16)
+    q = torch.randn((T, NQ * D), generator=g).to(BF16)
+    out = torch.full((T, NQ * D), float("nan"), dtype=BF16, device=DEV)
+    anc = torch.tensor(_masks_i32(masks), dtype=torch.int32, device=DEV)
+    err = torch.zeros((1,), dtype=torch.int32, device=DEV)
+    ops.tree_attn_rows(q.to(DEV), T, prefix, anc, NQ, NKV, kc.to(DEV), vc.to(DEV), out, err=err)
+    o = out.float().cpu()
+    assert int(err.item()) == 0 and torch.isfinite(o).all()
+    worst = 0.0
+    for i in range(T):
+        keys = list(range(prefix)) + [prefix + j for j in range(T) if (masks[i] >> j) & 1]
+        k = kc[:, keys][None]
+        v = vc[:, keys][None]
+        ref = Q.attention_decode(q[i].view(1, NQ, D), k, v, len(keys)).float().view(-1)
+        qg = q[i].float().view(NKV, 4, D)
+        p = torch.softmax(torch.einsum("hgd,hnd->hgn", qg, k[0].float()) / math.sqrt(D), -1)
+        ref32 = torch.einsum("hgn,hnd->hgd", p, v[0].float()).reshape(-1)
+        worst = max(worst, (o[i] - ref).abs().max().item(), (o[i] - ref32).abs().max().item())
+    assert worst < 2e-2, worst
+
+
 def test_tree_attention_flags_a_tree_past_the_cache():
     """A sequence whose tree would reach past the cache gets zeros and the position error; the other
     sequence is computed as usual (the kernel checks the device-side prefix before any cache read)."""
@@ -228,6 +265,8 @@ def test_tree_verify_accepts_the_models_own_continuation(eng2, T, depth):
         assert int(st.tok.item()) == P[0]
         emitted_all = [P[0]]
         rnd = random.Random(T)
+        tol = max(5e-2, 2 * load_golden("config0")["self_drift"]["max_logsoftmax_diff"])
+        flipped = False
         for _ in range(2):
             pos0 = S + len(emitted_all) - 1  # position of the last emitted token (the root)
             tree = TT.TokenTree(emitted_all[-1], T)
@@ -237,16 +276,23 @@ def test_tree_verify_accepts_the_models_own_continuation(eng2, T, depth):
                 tree.insert([rnd.randrange(1000) for _ in range(rnd.randrange(1, depth))], depth)
             greedy, commit = tv(eng, st, [tree], [pos0])
             emitted, path = tree.walk(greedy[0])
-            assert path == branch, (path, branch)
             commit([path], [pos0])
+            if path != branch:
+                # the walk may stop early only at a near tie of the plain run (summation order)
+                t = len(emitted_all) + len(path)
+                top2 = logits[t][0].float().topk(2).values
+                gap = float(top2[0] - top2[1])
+                assert path == branch[:len(path)] and gap <= tol, (t, gap, path, branch)
+                flipped = True
+                break
             emitted_all += emitted
             assert emitted_all == P[:len(emitted_all)], (emitted_all, P[:len(emitted_all)])
-        # continue with plain decode steps from the compacted cache
-        n = N - len(emitted_all)
-        rest = list(eng._plain_steps(st, emitted_all[-1], S + len(emitted_all) - 1, n))
-        tol = max(5e-2, 2 * load_golden("config0")["self_drift"]["max_logsoftmax_diff"])
-        ok, where = _tie_ok(emitted_all + rest, P, logits, tol)
-        assert ok, where
+        if not flipped:
+            # continue with plain decode steps from the compacted cache
+            n = N - len(emitted_all)
+            rest = list(eng._plain_steps(st, emitted_all[-1], S + len(emitted_all) - 1, n))
+            ok, where = _tie_ok(emitted_all + rest, P, logits, tol)
+            assert ok, where
         eng.check_device_errors(st)
     finally:
         eng.tree = 0
