@@ -802,8 +802,13 @@ def step_timeline(eng, st, cfg, peak):
     layers = list(range(2, L - 2)) if L > 5 else list(range(1, L))
     med = lambda v: round(statistics.median(v), 2) if v else None  # noqa: E731
     rows = {}
+    def pct5(v):  # min, quartiles, max of the per-CTA values
+        v = sorted(v)
+        n = len(v)
+        return [v[0], v[n // 4], v[n // 2], v[(3 * n) // 4], v[-1]]
+
     for k, name in enumerate(OPS):
-        wait, stage, work, issue, span = [], [], [], [], []
+        wait, stage, work, issue, span, done_dist, issue_dist = [], [], [], [], [], [], []
         for l in layers:
             op, prev = 1 + 5 * l + k, 1 + 5 * l + k - 1
             prev_done = float(t[:, prev, 2].max())
@@ -811,6 +816,9 @@ def step_timeline(eng, st, cfg, peak):
             done = float(t[:, op, 2].max())
             wait.append(ready - prev_done)
             span.append(done - prev_done)
+            done_dist.append(pct5((t[:, op, 2] - prev_done).tolist()))
+            if name != "attn":
+                issue_dist.append(pct5((t[:, op, 3] - prev_done).tolist()))
             if name != "attn":  # the attention op records no `staged` stamp and streams no weights
                 staged = float(t[:, op, 1].max())
                 stage.append(staged - ready)
@@ -819,7 +827,13 @@ def step_timeline(eng, st, cfg, peak):
                 issue.append(float(t[:, op, 3].max()) - float(t[:, prev_proj, 3].max()))
         rows[name] = {"wait_us": med(wait), "stage_us": med(stage), "work_us": med(work), "span_us": med(span),
                       "producer_issue_interval_us": med(issue),
-                      "stream_us_at_peak": round(wbytes[name] / (peak * 1e3), 2)}
+                      "stream_us_at_peak": round(wbytes[name] / (peak * 1e3), 2),
+                      # per-CTA spread, each quantile the median over the layers, relative to the previous
+                      # op's last done: when the CTAs finished (flushes and epilogues included) and when
+                      # their producers issued the op's last weight block
+                      "cta_done_min_q1_med_q3_max_us": [med([d[i] for d in done_dist]) for i in range(5)],
+                      "cta_last_block_issued_min_q1_med_q3_max_us":
+                          [med([d[i] for d in issue_dist]) for i in range(5)] if issue_dist else None}
     layer_us = [float(t[:, 1 + 5 * (l + 1), 0].max()) - float(t[:, 1 + 5 * l, 0].max()) for l in layers[:-1]]
     lm = 1 + 5 * L
     return {"timeline": "persistent step, per-op medians over layers %d..%d" % (layers[0], layers[-1]),
