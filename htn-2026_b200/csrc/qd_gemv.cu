@@ -278,6 +278,9 @@ extern "C" int qd_gemv(const void* x, int64_t ldx, const void* w_packed, int64_t
   a.res = static_cast<const __nv_bfloat16*>(res);
   a.ldr = ldr;
   a.err = err;
+  // residual projections sum their split-K partials in fixed point, as the persistent step does, so the
+  // two paths give the same bits
+  a.fx_numerics = mode == MODE_RES ? 1 : 0;
   return launch_any(a, mode, m, pdl, stream);
 }
 

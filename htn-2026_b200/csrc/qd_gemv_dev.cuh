@@ -33,6 +33,7 @@ constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;  // + one producer warp
 constexpr int kBarConsumers = 1;           // named barrier of the 256 consumer threads
 constexpr int kStageBatch = 5;             // activation chunks per thread in flight (k <= 10240 in one pass)
+constexpr int kFxStage = 1;                // stage_x_fx: chunks per thread in flight
 constexpr int kNormPre = 2;                // RMSNorm weight chunks per thread preloaded (k <= 4096); more are
                                            // loaded in the normalising pass
 
@@ -58,6 +59,15 @@ struct GemvArgs {
   int m_act;       // activation rows that are real (<= M; the tensor-core path pads M to 16s)
   int out_npad;    // SWIGLU: 0 = row-major out; else out is the next projection's packed operand
   int* done;       // optional: +1 (release) per finalized row group
+  // RES epilogue with fixed-point group sums (CUDA-core kernels): a row group's total is
+  // fx_to_float(sum over its segments of fx_of(partial)), an exact integer sum and so independent of the
+  // order the partials are added in. fx_numerics alone: the last arriver sums the stored partials that
+  // way. fx (persistent step): no CTA finalizes - every segment adds its rows into fx ([m][n] int64)
+  // with integer atomics and its K-block count into *fx_ctr (release), and the next op's staging applies
+  // the epilogue from the sums itself.
+  int fx_numerics;
+  int64_t* fx;
+  int* fx_ctr;
   int pos_ready;   // QKV: flags[2] already holds the position and aux its cos/sin rows
   // QKV
   const __nv_bfloat16 *q_norm, *k_norm, *cos, *sin;
@@ -77,6 +87,12 @@ struct GemvArgs {
   int* cta_idx;
   int* lm_ticket;
 };
+
+// Fixed-point partial sums: value * 2^32 rounded to int64 (exact for |value| < 2^31 at a resolution of
+// 2^-32, far below a BF16 output's rounding), added with integer atomics (associative, so the sum does
+// not depend on the order of the contributions) and converted back with one rounding to fp32.
+__device__ __forceinline__ long long fx_of(float v) { return __float2ll_rn(v * 4294967296.0f); }
+__device__ __forceinline__ float fx_to_float(long long s) { return __ll2float_rn(s) * 2.3283064365386963e-10f; }
 
 // Ring of 16 KiB blocks in shared memory with a full and an empty mbarrier per slot.
 struct Ring {
@@ -218,6 +234,84 @@ __device__ void stage_x(const GemvArgs& a, __nv_bfloat16* xs, float* wsum, int t
         if (j * kConsumers + tid < kv8) norm_chunk(j * kConsumers + tid, nwv[j]);
       for (int q = kNormPre * kConsumers + tid; q < kv8; q += kConsumers)
         norm_chunk(q, *reinterpret_cast<const uint4*>(a.norm_w + q * 8));
+    }
+    named_bar(kBarConsumers, kConsumers);
+  }
+}
+
+// stage_x for an input that is a deferred residual sum (persistent step): x = bf16(res + bf16(sum)) with
+// res = a.x (the residual stream before the projection) and sum = fx_to_float(fxs) (the projection's
+// fixed-point group sums) - the RES epilogue's arithmetic - then RMSNorm-ed as stage_x does. This CTA
+// also writes its share of x (chunks q = cta, cta + G, ...) to xw, the residual stream's next buffer.
+// 256 threads; kFxStage chunks of 8 values (and their 8 sums) per thread in flight.
+template <int M>
+__device__ void stage_x_fx(const GemvArgs& a, const int64_t* fxs, __nv_bfloat16* xw, int cta, int G,
+                           __nv_bfloat16* xs, float* wsum, int tid) {
+  const int warp = tid >> 5, lane = tid & 31;
+  const int kv8 = (int)(a.k >> 3);
+  for (int m = 0; m < M; ++m) {
+    float sq = 0.f;
+    for (int q0 = 0; q0 < kv8; q0 += kFxStage * kConsumers) {
+      uint4 rv[kFxStage];
+      longlong2 sv[kFxStage][4];
+#pragma unroll
+      for (int j = 0; j < kFxStage; ++j) {
+        const int q = q0 + j * kConsumers + tid;
+        if (q < kv8) {
+          rv[j] = ld_cg_v4(a.x + m * a.ldx + q * 8);
+          const longlong2* sp = reinterpret_cast<const longlong2*>(fxs + (int64_t)m * a.k + q * 8);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sv[j][e] = __ldcg(sp + e);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kFxStage; ++j) {
+        const int q = q0 + j * kConsumers + tid;
+        if (q >= kv8) continue;
+        const uint32_t ru[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float lo = bf16r(bf_lo(ru[e]) + bf16r(fx_to_float(sv[j][e].x)));
+          const float hi = bf16r(bf_hi(ru[e]) + bf16r(fx_to_float(sv[j][e].y)));
+          o[e] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
+          if (a.norm_w) {
+            sq = fmaf(lo, lo, sq);
+            sq = fmaf(hi, hi, sq);
+          }
+        }
+        const uint4 v = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(xs + (int64_t)m * a.k + q * 8) = v;
+        if (xw && q % G == cta) *reinterpret_cast<uint4*>(xw + m * a.ldx + q * 8) = v;
+      }
+    }
+    if (a.norm_w) {
+      sq = warp_sum(sq);
+      if (lane == 0) wsum[m * kConsumerWarps + warp] = sq;
+    }
+  }
+  named_bar(kBarConsumers, kConsumers);
+  if (a.norm_w) {
+    for (int m = 0; m < M; ++m) {
+      float ss = 0.f;
+#pragma unroll
+      for (int w8 = 0; w8 < kConsumerWarps; ++w8) ss += wsum[m * kConsumerWarps + w8];
+      const float rstd = 1.0f / sqrtf(ss / (float)a.k + a.eps);
+      for (int q = tid; q < kv8; q += kConsumers) {
+        uint4* p = reinterpret_cast<uint4*>(xs + (int64_t)m * a.k + q * 8);
+        const uint4 xv = *p;
+        const uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + q * 8);
+        const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
+        const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float lo = bf16r(bf_lo(wu[e]) * bf16r(bf_lo(xu[e]) * rstd));
+          const float hi = bf16r(bf_hi(wu[e]) * bf16r(bf_hi(xu[e]) * rstd));
+          o[e] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
+        }
+        *p = make_uint4(o[0], o[1], o[2], o[3]);
+      }
     }
     named_bar(kBarConsumers, kConsumers);
   }
@@ -390,13 +484,30 @@ __device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum
 // A CTA's segment of row group g (blocks seg_first..b) is reduced into red[m * 128 + r]. If the segment is
 // the whole group, run the epilogue; otherwise store the partial, take the group's ticket, and the CTA
 // that completes the group sums all partials in CTA order and runs the epilogue. 256 consumer threads.
-template <int M, int MODE>
+template <int M, int MODE, bool DEFER = false>
 __device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64_t b, int cta, float* red,
                               float* wsum, float* lmv, int* lmi, float* aux, int* flags, int tid) {
   const int64_t gb0 = (int64_t)g * a.kblocks;
   const int nseg_blk = (int)(b + 1 - seg_first);
   bool finalized = false;
-  if (seg_first == gb0 && nseg_blk == a.kblocks) {
+  if constexpr (DEFER) {  // every segment into the fixed-point sums (a.fx), no epilogue here
+    for (int idx = tid; idx < a.m_act * kBlockRows; idx += kConsumers) {
+      unsigned long long* dst = reinterpret_cast<unsigned long long*>(a.fx + (int64_t)(idx >> 7) * a.n +
+                                                                      (int64_t)g * kBlockRows + (idx & 127));
+      atomicAdd(dst, (unsigned long long)fx_of(red[idx]));
+    }
+    named_bar(kBarConsumers, kConsumers);
+    if (tid == 0) red_release_add(a.fx_ctr, nseg_blk);  // releases this CTA's additions
+    named_bar(kBarConsumers, kConsumers);
+    return;
+  }
+  if (MODE == MODE_RES && a.fx_numerics && seg_first == gb0 && nseg_blk == a.kblocks) {
+    // the whole group in this CTA: the value a fixed-point sum of one contribution gives
+    for (int idx = tid; idx < a.m_act * kBlockRows; idx += kConsumers) red[idx] = fx_to_float(fx_of(red[idx]));
+    named_bar(kBarConsumers, kConsumers);
+    finalize_group<M, MODE>(a, g, red, wsum, lmv, lmi, aux, flags, tid);
+    finalized = true;
+  } else if (seg_first == gb0 && nseg_blk == a.kblocks) {
     finalize_group<M, MODE>(a, g, red, wsum, lmv, lmi, aux, flags, tid);
     finalized = true;
   } else {
@@ -427,28 +538,61 @@ __device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64
       float res_pre[res_per<M>()];
       if constexpr (MODE == MODE_RES) load_res<M>(a, g, tid, res_pre);  // in flight with the partials
       float4 acc[kPer];
+      if (MODE == MODE_RES && a.fx_numerics) {  // fixed-point group sums (see GemvArgs::fx_numerics)
+        long long iacc[kPer][4];
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int s0 = 0; s0 < nseg; s0 += kSB) {
-        float4 v[kSB][kPer];
+        for (int j = 0; j < kPer; ++j)
 #pragma unroll
-        for (int b2 = 0; b2 < kSB; ++b2)
+          for (int e = 0; e < 4; ++e) iacc[j][e] = 0;
+        for (int s0 = 0; s0 < nseg; s0 += kSB) {
+          float4 v[kSB][kPer];
 #pragma unroll
-          for (int j = 0; j < kPer; ++j) {
-            const int q = tid + j * kConsumers;
-            v[b2][j] = (s0 + b2 < nseg && q < kVec) ? __ldcg(pbase + (int64_t)(s0 + b2) * kVec + q)
-                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
+          for (int b2 = 0; b2 < kSB; ++b2)
 #pragma unroll
-        for (int b2 = 0; b2 < kSB; ++b2)
-#pragma unroll
-          for (int j = 0; j < kPer; ++j)
-            if (s0 + b2 < nseg) {
-              acc[j].x += v[b2][j].x;
-              acc[j].y += v[b2][j].y;
-              acc[j].z += v[b2][j].z;
-              acc[j].w += v[b2][j].w;
+            for (int j = 0; j < kPer; ++j) {
+              const int q = tid + j * kConsumers;
+              v[b2][j] = (s0 + b2 < nseg && q < kVec) ? __ldcg(pbase + (int64_t)(s0 + b2) * kVec + q)
+                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
             }
+#pragma unroll
+          for (int b2 = 0; b2 < kSB; ++b2)
+#pragma unroll
+            for (int j = 0; j < kPer; ++j)
+              if (s0 + b2 < nseg) {
+                iacc[j][0] += fx_of(v[b2][j].x);
+                iacc[j][1] += fx_of(v[b2][j].y);
+                iacc[j][2] += fx_of(v[b2][j].z);
+                iacc[j][3] += fx_of(v[b2][j].w);
+              }
+        }
+#pragma unroll
+        for (int j = 0; j < kPer; ++j)
+          acc[j] = make_float4(fx_to_float(iacc[j][0]), fx_to_float(iacc[j][1]), fx_to_float(iacc[j][2]),
+                               fx_to_float(iacc[j][3]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s0 = 0; s0 < nseg; s0 += kSB) {
+          float4 v[kSB][kPer];
+#pragma unroll
+          for (int b2 = 0; b2 < kSB; ++b2)
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+              const int q = tid + j * kConsumers;
+              v[b2][j] = (s0 + b2 < nseg && q < kVec) ? __ldcg(pbase + (int64_t)(s0 + b2) * kVec + q)
+                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+          for (int b2 = 0; b2 < kSB; ++b2)
+#pragma unroll
+            for (int j = 0; j < kPer; ++j)
+              if (s0 + b2 < nseg) {
+                acc[j].x += v[b2][j].x;
+                acc[j].y += v[b2][j].y;
+                acc[j].z += v[b2][j].z;
+                acc[j].w += v[b2][j].w;
+              }
+        }
       }
 #pragma unroll
       for (int j = 0; j < kPer; ++j) {
@@ -489,7 +633,7 @@ __device__ __forceinline__ void qkv_prologue(const GemvArgs& a, float* aux, int*
 
 // Consume this CTA's blocks of one projection from the ring (in issue order), flushing a segment
 // at every row-group end; ring position (slot, phase) carries across projections.
-template <int M, int MODE>
+template <int M, int MODE, bool DEFER = false>
 __device__ void consume_blocks(const GemvArgs& a, const Ring& R, int& slot, int& phase, int cta,
                                const __nv_bfloat16* xs, float* red, float* wsum, float* lmv, int* lmi, int* flags,
                                float* aux, int tid, bool& ok) {
@@ -569,7 +713,7 @@ __device__ void consume_blocks(const GemvArgs& a, const Ring& R, int& slot, int&
         if (c == 0) red[m * kBlockRows + 16 * warp + rsub + 4 * i] = v;
       }
     named_bar(kBarConsumers, kConsumers);
-    flush_segment<M, MODE>(a, g, seg_first, b, cta, red, wsum, lmv, lmi, aux, flags, tid);
+    flush_segment<M, MODE, DEFER>(a, g, seg_first, b, cta, red, wsum, lmv, lmi, aux, flags, tid);
     seg_first = b + 1;
   }
 }

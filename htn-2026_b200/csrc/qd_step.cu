@@ -7,12 +7,16 @@
 // ring of 16 KiB blocks: weights never depend on activations, so HBM keeps streaming the next
 // projection while the consumers wait for the current one's inputs. The eight consumer warps walk
 // the same op sequence; before each op, one thread waits (bounded) on the completion counter of the
-// op that produces its input, e.g. gate_up waits until all 20 row groups of the O projection are
-// finalized. Counters are bumped with release semantics by whoever finalizes a row group (a GEMV
-// epilogue) or merges a (sequence, KV head) (attention); all cross-CTA activations are read with
-// L2 (.cg) loads after an acquire. The per-op arithmetic is exactly the per-projection kernels'
-// (qd_gemv_dev.cuh, qd_attn_dev.cuh) with the same stream-K partition and the same attention splits,
-// so the two paths produce bit-identical tokens and logits.
+// op that produces its input, e.g. down waits until all row groups of gate_up are finalized. Counters
+// are bumped with release semantics by whoever finalizes a row group (a GEMV epilogue) or merges a
+// (sequence, KV head) (attention); all cross-CTA activations are read with L2 (.cg) loads after an
+// acquire. The residual projections (O, down) finalize nothing: every CTA adds its partial sums into
+// fixed-point group sums with integer atomics and its K-block count into the op's counter, and the next
+// op's staging (gate/up, the next layer's QKV, the LM head) applies the residual add itself once the
+// count is complete - no last-arriving CTA's reduction sits between the two ops. The per-op arithmetic
+// is the per-projection kernels' (qd_gemv_dev.cuh, qd_attn_dev.cuh; their residual projections sum
+// their partials in the same fixed point) with the same stream-K partition and attention splits, so
+// the two paths produce bit-identical tokens and logits.
 //
 // Failure handling: every wait is bounded (1 s); a dependency wait that expires sets QD_DEVERR_DEP
 // and an abort flag that makes every later wait return at once, so a broken step finishes (with
@@ -45,6 +49,11 @@ struct StepArgs {
   int smax[K_KINDS];
   int64_t total[K_KINDS];
   int o_merge;       // 1: attention leaves split partials, the O projection's CTAs merge them
+  // The O and down projections leave their outputs as fixed-point group sums (fx_o, fx_d: [M][H] int64)
+  // and the next op's staging applies the residual add; the residual stream alternates between x (a
+  // layer's input) and xb (after its O projection)
+  __nv_bfloat16* xb;
+  int64_t *fx_o, *fx_d;
   int* counters;
   int* abort_flag;
   int* tickets;
@@ -178,7 +187,7 @@ static __device__ GemvArgs gemv_op(const StepArgs& A, int kind, int l) {
   a.smax = A.smax[kind];
   a.total = A.total[kind];
   if (kind == K_QKV) {
-    a.x = A.x;
+    a.x = l > 0 ? A.xb : A.x;  // the residual stream before the previous layer's down projection
     a.ldx = A.H;
     a.k = A.H;
     a.n = (int64_t)(A.nq + 2 * A.nkv) * 128;
@@ -209,7 +218,9 @@ static __device__ GemvArgs gemv_op(const StepArgs& A, int kind, int l) {
     a.ldo = A.H;
     a.res = A.x;
     a.ldr = A.H;
-    a.done = ctr(A, l, 2);
+    a.fx_numerics = 1;
+    a.fx = A.fx_o;
+    a.fx_ctr = ctr(A, l, 2);
   } else if (kind == K_GU) {
     a.x = A.x;
     a.ldx = A.H;
@@ -230,9 +241,11 @@ static __device__ GemvArgs gemv_op(const StepArgs& A, int kind, int l) {
     a.ldo = A.H;
     a.res = A.x;
     a.ldr = A.H;
-    a.done = ctr(A, l, 4);
+    a.fx_numerics = 1;
+    a.fx = A.fx_d;
+    a.fx_ctr = ctr(A, l, 4);
   } else {  // LM head
-    a.x = A.x;
+    a.x = A.xb;
     a.ldx = A.H;
     a.k = A.H;
     a.n = A.vocab_rows;
@@ -401,6 +414,12 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
     }
     stamp(A, cta, 0, 2, tid);
     const int team = warp >> 2, team_tid = tid & (kAttnThreads - 1);
+    // this CTA's share of a [M][H] fixed-point sum buffer, cleared with plain stores (the CTA's later
+    // releases publish them before any other CTA adds into the buffer again)
+    auto zero_share = [&](int64_t* buf) {
+      const int64_t E = (int64_t)M * A.H, e0 = E * cta / G, e1 = E * (cta + 1) / G;
+      for (int64_t e = e0 + tid; e < e1; e += kConsumers) buf[e] = 0;
+    };
     const int units = M * A.nkv * A.splits;
     const int64_t len = attn_len_of(A, pos);
     int64_t achunk;
@@ -433,11 +452,14 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
         }
       }
       // QKV projection + q/k norm + RoPE + K/V append
-      wait_dep(A, l == 0 ? A.counters : ctr(A, l - 1, 4), l == 0 ? M : A.H / kBlockRows, tid);
+      wait_dep(A, l == 0 ? A.counters : ctr(A, l - 1, 4), l == 0 ? M : (int)A.total[K_DOWN], tid);
       stamp(A, cta, 1 + 5 * l, 0, tid);
       {
         const GemvArgs op = gemv_op<M>(A, K_QKV, l);
-        stage_x<M>(op, xs, wsum, tid);
+        if (l > 0)  // x = previous layer's (x after O) + down's sums; this CTA's share to x
+          stage_x_fx<M>(op, A.fx_d, A.x, cta, G, xs, wsum, tid);
+        else
+          stage_x<M>(op, xs, wsum, tid);
         stamp(A, cta, 1 + 5 * l, 1, tid);
         consume_blocks<M, MODE_QKV>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
       }
@@ -470,6 +492,9 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
         at.partials_only = A.o_merge;
         const int per_b = A.nkv * A.splits;
         wait_dep(A, ctr(A, l, 0), A.nq + 2 * A.nkv, tid);
+        // every CTA has contributed to this layer's QKV, so all have staged the down sums they read: clear
+        // this CTA's share for the next layer's down
+        if (l > 0) zero_share(A.fx_d);
         stamp(A, cta, 2 + 5 * l, 0, tid);
         for (int u = cta + team * G; u < units; u += 2 * G) {
           const int b = u / per_b, rem = u - b * per_b;
@@ -487,41 +512,44 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
         else
           stage_x<M>(op, xs, wsum, tid);
         stamp(A, cta, 3 + 5 * l, 1, tid);
-        consume_blocks<M, MODE_RES>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
+        consume_blocks<M, MODE_RES, true>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
       }
       stamp(A, cta, 3 + 5 * l, 2, tid);
       // gate_up + SwiGLU
-      wait_dep(A, ctr(A, l, 2), A.H / kBlockRows, tid);
+      wait_dep(A, ctr(A, l, 2), (int)A.total[K_O], tid);
       stamp(A, cta, 4 + 5 * l, 0, tid);
       {
         const GemvArgs op = gemv_op<M>(A, K_GU, l);
-        stage_x<M>(op, xs, wsum, tid);
+        stage_x_fx<M>(op, A.fx_o, A.xb, cta, G, xs, wsum, tid);  // x after O = x + O's sums; share to xb
         stamp(A, cta, 4 + 5 * l, 1, tid);
         consume_blocks<M, MODE_SWIGLU>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
       }
       stamp(A, cta, 4 + 5 * l, 2, tid);
       // down projection + residual
       wait_dep(A, ctr(A, l, 3), 2 * A.I / kBlockRows, tid);
+      zero_share(A.fx_o);  // every CTA has staged gate/up, so O's sums are read: clear this CTA's share
       stamp(A, cta, 5 + 5 * l, 0, tid);
       {
         const GemvArgs op = gemv_op<M>(A, K_DOWN, l);
         stage_x<M>(op, xs, wsum, tid);
         stamp(A, cta, 5 + 5 * l, 1, tid);
-        consume_blocks<M, MODE_RES>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
+        consume_blocks<M, MODE_RES, true>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
       }
       stamp(A, cta, 5 + 5 * l, 2, tid);
     }
     // LM head + argmax + position advance; the last CTA also clears the counters for the next step
-    wait_dep(A, ctr(A, A.L - 1, 4), A.H / kBlockRows, tid);
+    wait_dep(A, ctr(A, A.L - 1, 4), (int)A.total[K_DOWN], tid);
     stamp(A, cta, 1 + 5 * A.L, 0, tid);
     {
       const GemvArgs op = gemv_op<M>(A, K_LM, 0);
-      stage_x<M>(op, xs, wsum, tid);
+      stage_x_fx<M>(op, A.fx_d, nullptr, cta, G, xs, wsum, tid);
       stamp(A, cta, 1 + 5 * A.L, 1, tid);
       consume_blocks<M, MODE_LM>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
       stamp(A, cta, 1 + 5 * A.L, 2, tid);
       if (lm_global_argmax<M>(op, cta, wsum, lmv, lmi, flags, tid)) {
         for (int i = tid; i < 1 + 5 * A.L; i += kConsumers) A.counters[i] = 0;
+        // every CTA has staged the LM head's input: the last down's sums start the next step clear
+        for (int64_t e = tid; e < (int64_t)M * A.H; e += kConsumers) A.fx_d[e] = 0;
       }
     }
   }
@@ -535,7 +563,7 @@ struct StepPlan {
   int smax[K_KINDS];
   int64_t total[K_KINDS];
   int64_t off_counters, off_abort, off_tickets, off_lm_ticket, off_cta_val, off_cta_idx, off_partials, off_attn_acc,
-      off_attn_ml, off_attn_tickets, bytes;
+      off_attn_ml, off_attn_tickets, off_xb, off_fx_o, off_fx_d, bytes;
 };
 
 static int step_plan(const qd_step_desc* d, StepPlan* p) {
@@ -593,6 +621,9 @@ static int step_plan(const qd_step_desc* d, StepPlan* p) {
   p->off_attn_acc = take(B * nq * ap.splits * 128 * 4);
   p->off_attn_ml = take(B * nq * ap.splits * 2 * 4);
   p->off_attn_tickets = take(B * nkv * 4);
+  p->off_xb = take(B * H * 2);
+  p->off_fx_o = take(B * H * 8);
+  p->off_fx_d = take(B * H * 8);
   p->bytes = off;
   // O-side attention merge: the most query heads one O CTA reads, times the splits, must fit the
   // attention shared memory (free while O stages its input); heads as bits of a 32-bit mask
@@ -742,6 +773,9 @@ extern "C" int qd_decode_step(const qd_step_desc* d, void* scratch, int64_t scra
   a.attn_acc = reinterpret_cast<float*>(sc + p.off_attn_acc);
   a.attn_ml = reinterpret_cast<float*>(sc + p.off_attn_ml);
   a.attn_tickets = reinterpret_cast<int*>(sc + p.off_attn_tickets);
+  a.xb = reinterpret_cast<__nv_bfloat16*>(sc + p.off_xb);
+  a.fx_o = reinterpret_cast<int64_t*>(sc + p.off_fx_o);
+  a.fx_d = reinterpret_cast<int64_t*>(sc + p.off_fx_d);
   switch (d->batch) {
     case 1: return launch_step<1>(a, p.smem, stream);
     case 2: return launch_step<2>(a, p.smem, stream);

@@ -109,8 +109,13 @@ def test_gemv_residual_in_place(n, k, m):
     plan = ops.Gemv(m, n, k, ops.Gemv.RES, DEV)
     xr = res.to(DEV).clone()
     plan(x.to(DEV), ops.pack_matrix(w.to(DEV)), xr, res=xr)                 # out aliases res (x += ...)
-    ref = (res.float() + _gemv_ref(x, w, None, 0).to(BF16).float()).to(BF16)
-    _assert_bf16_close(xr, ref)
+    y = _gemv_ref(x, w, None, 0).to(BF16).float()
+    ref = (res.float() + y).to(BF16)
+    # bf16(y) may round one ulp apart at a tie (fp32 against fp64 sums), and that ulp can carry into the
+    # rounded sum
+    diff = (xr.float().cpu() - ref.float()).abs()
+    tol = RTOL * (ref.float().abs() + y.abs()) + 1e-3
+    assert not (diff > tol).any(), f"{int((diff > tol).sum())} mismatches, max diff {float(diff.max()):.4g}"
 
 
 @pytest.mark.parametrize("inter,k", [(9728, 2560), (128, 128), (320, 192)])
