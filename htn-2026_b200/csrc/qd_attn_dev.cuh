@@ -79,8 +79,9 @@ struct __align__(16) AttnSmem {
 
 // One unit on a team of 128 threads (team thread id `tid`, named barrier `bar_id`); `len` is the valid
 // length (attn_len). Units past the splits in use at this length return at once.
+// q_ready: the caller has already put the unit's 4 query heads (BF16 values as floats) into sm.qs.
 static __device__ void attn_unit(const AttnArgs& a, int b, int kvh, int split, int tid, int bar_id, AttnSmem& sm,
-                                 int64_t len) {
+                                 int64_t len, bool q_ready = false) {
   const int warp = tid >> 5, lane = tid & 31;
   int64_t chunk;
   const int n_use = attn_active(a, len, &chunk);
@@ -89,10 +90,12 @@ static __device__ void attn_unit(const AttnArgs& a, int b, int kvh, int split, i
   int64_t end = start + chunk;
   if (end > len) end = len;
 
-  for (int h = 0; h < kGroup; ++h) {
-    const __nv_bfloat16* qp = a.q + ((int64_t)b * a.nq + kvh * kGroup + h) * kHeadDim;
-    const uint16_t u = __ldcg(reinterpret_cast<const unsigned short*>(qp) + tid);
-    sm.qs[h][tid] = __uint_as_float((uint32_t)u << 16);
+  if (!q_ready) {
+    for (int h = 0; h < kGroup; ++h) {
+      const __nv_bfloat16* qp = a.q + ((int64_t)b * a.nq + kvh * kGroup + h) * kHeadDim;
+      const uint16_t u = __ldcg(reinterpret_cast<const unsigned short*>(qp) + tid);
+      sm.qs[h][tid] = __uint_as_float((uint32_t)u << 16);
+    }
   }
   named_bar(bar_id, kAttnThreads);
 

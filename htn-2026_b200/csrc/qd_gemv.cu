@@ -319,6 +319,7 @@ extern "C" int qd_qkv_rope_append(const void* x, int64_t ldx, const void* w_pack
   a.cs_h = cs_h;
   a.raw_out = static_cast<__nv_bfloat16*>(raw_out);
   a.err = err;
+  a.fx_numerics = 1;  // fixed-point split-K sums, as the persistent step's deferred QKV
   return launch_any(a, MODE_QKV, m, pdl, stream);
 }
 

@@ -59,7 +59,7 @@ struct GemvArgs {
   int m_act;       // activation rows that are real (<= M; the tensor-core path pads M to 16s)
   int out_npad;    // SWIGLU: 0 = row-major out; else out is the next projection's packed operand
   int* done;       // optional: +1 (release) per finalized row group
-  // RES epilogue with fixed-point group sums (CUDA-core kernels): a row group's total is
+  // RES and QKV epilogues with fixed-point group sums (CUDA-core kernels): a row group's total is
   // fx_to_float(sum over its segments of fx_of(partial)), an exact integer sum and so independent of the
   // order the partials are added in. fx_numerics alone: the last arriver sums the stored partials that
   // way. fx (persistent step): no CTA finalizes - every segment adds its rows into fx ([m][n] int64)
@@ -501,7 +501,7 @@ __device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64
     named_bar(kBarConsumers, kConsumers);
     return;
   }
-  if (MODE == MODE_RES && a.fx_numerics && seg_first == gb0 && nseg_blk == a.kblocks) {
+  if ((MODE == MODE_RES || MODE == MODE_QKV) && a.fx_numerics && seg_first == gb0 && nseg_blk == a.kblocks) {
     // the whole group in this CTA: the value a fixed-point sum of one contribution gives
     for (int idx = tid; idx < a.m_act * kBlockRows; idx += kConsumers) red[idx] = fx_to_float(fx_of(red[idx]));
     named_bar(kBarConsumers, kConsumers);
@@ -538,7 +538,7 @@ __device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64
       float res_pre[res_per<M>()];
       if constexpr (MODE == MODE_RES) load_res<M>(a, g, tid, res_pre);  // in flight with the partials
       float4 acc[kPer];
-      if (MODE == MODE_RES && a.fx_numerics) {  // fixed-point group sums (see GemvArgs::fx_numerics)
+      if ((MODE == MODE_RES || MODE == MODE_QKV) && a.fx_numerics) {  // fixed-point group sums (fx_numerics)
         long long iacc[kPer][4];
 #pragma unroll
         for (int j = 0; j < kPer; ++j)

@@ -54,6 +54,10 @@ struct StepArgs {
   // layer's input) and xb (after its O projection)
   __nv_bfloat16* xb;
   int64_t *fx_o, *fx_d;
+  // The QKV projection likewise leaves fixed-point sums (fx_q: [M][(nq + 2 nkv) * 128]); each attention
+  // unit applies the QKV epilogue (per-head RMSNorm, RoPE) to its own query heads, and the unit that
+  // covers the new position also to the new key / value, which it appends to the cache
+  int64_t* fx_q;
   int* counters;
   int* abort_flag;
   int* tickets;
@@ -206,8 +210,10 @@ static __device__ GemvArgs gemv_op(const StepArgs& A, int kind, int l) {
     a.v_cache = A.vc + l * A.c_ls;
     a.cs_b = A.cs_b;
     a.cs_h = A.cs_h;
-    a.done = ctr(A, l, 0);
     a.pos_ready = 1;
+    a.fx_numerics = 1;
+    a.fx = A.fx_q;
+    a.fx_ctr = ctr(A, l, 0);
   } else if (kind == K_O) {
     a.x = A.attn;
     a.ldx = (int64_t)A.nq * 128;
@@ -297,6 +303,55 @@ __device__ __forceinline__ int attn_active_of(const StepArgs& A, int64_t len, in
   t.chunk = A.chunk;
   t.keys_per_split = A.keys_per_split;
   return attn_active(t, len, chunk);
+}
+
+// The QKV epilogue of one attention unit from the fixed-point QKV sums - the arithmetic of
+// finalize_group's QKV mode: BF16 projection output, per-head RMSNorm (sum of squares per 32 rows, the 4
+// slices added in order), q_norm / k_norm, RoPE at position p with every product rounded to BF16. The
+// unit's 4 query heads go to sm.qs (BF16 values as floats); with `append` (the unit whose keys include
+// the new position) the new key and value of KV head kvh are written to the cache at p. A team of 128
+// threads, one per dimension r; named barrier bar_id. cs: cos[0..127], sin[128..255] at p.
+static __device__ void qkv_heads_from_sums(const StepArgs& A, int l, int b, int kvh, bool append, int64_t p,
+                                           const float* cs, int r, int bar_id, AttnSmem& sm) {
+  const int64_t nqkv = (int64_t)(A.nq + 2 * A.nkv) * 128;
+  const int64_t* row = A.fx_q + (int64_t)b * nqkv;
+  const int lane = r & 31, w = r >> 5;
+  const int nh = append ? kGroup + 1 : kGroup;  // 4 query heads, then the key head
+  float* ys = &sm.wacc[0][0][0];                 // [5][128] normalised values (partner exchange)
+  float* wsq = ys + (kGroup + 1) * kHeadDim;     // [5][4] per-slice sums of squares
+  float v[kGroup + 1];
+  for (int hh = 0; hh < nh; ++hh) {
+    const int g = hh < kGroup ? kvh * kGroup + hh : A.nq + kvh;
+    v[hh] = bf16r(fx_to_float(__ldcg(row + (int64_t)g * kHeadDim + r)));
+  }
+  const float vv = append ? bf16r(fx_to_float(__ldcg(row + (int64_t)(A.nq + A.nkv + kvh) * kHeadDim + r))) : 0.f;
+  const float nwq = bf16_to_f(A.qn[(int64_t)l * kHeadDim + r]), nwk = bf16_to_f(A.kn[(int64_t)l * kHeadDim + r]);
+  for (int hh = 0; hh < nh; ++hh) {
+    const float sq = warp_sum(v[hh] * v[hh]);
+    if (lane == 0) wsq[hh * 4 + w] = sq;
+  }
+  named_bar(bar_id, kAttnThreads);
+  for (int hh = 0; hh < nh; ++hh) {
+    const float var = (wsq[hh * 4 + 0] + wsq[hh * 4 + 1] + wsq[hh * 4 + 2] + wsq[hh * 4 + 3]) / 128.0f;
+    const float rstd = 1.0f / sqrtf(var + A.eps);
+    ys[hh * kHeadDim + r] = bf16r((hh < kGroup ? nwq : nwk) * bf16r(v[hh] * rstd));
+  }
+  named_bar(bar_id, kAttnThreads);
+  const float c = cs[r], sn = cs[128 + r];
+  for (int hh = 0; hh < nh; ++hh) {
+    const float y = ys[hh * kHeadDim + r], yp = ys[hh * kHeadDim + (r ^ 64)];
+    // q*cos + rotate_half(q)*sin with every product a BF16 tensor (rotate_half = cat(-q2, q1))
+    const float rot = (r < 64) ? bf16r(-yp * sn) : bf16r(yp * sn);
+    const __nv_bfloat16 o = __float2bfloat16_rn(bf16r(y * c) + rot);
+    if (hh < kGroup) {
+      sm.qs[hh][r] = __bfloat162float(o);
+    } else if (p >= 0) {
+      const int64_t off = (int64_t)l * A.c_ls + (int64_t)b * A.cs_b + (int64_t)kvh * A.cs_h + p * kHeadDim + r;
+      A.kc[off] = o;
+      A.vc[off] = __float2bfloat16_rn(vv);
+    }
+  }
+  named_bar(bar_id, kAttnThreads);  // queries complete, the new key / value written, before the unit reads
 }
 
 template <int M>
@@ -416,8 +471,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
     const int team = warp >> 2, team_tid = tid & (kAttnThreads - 1);
     // this CTA's share of a [M][H] fixed-point sum buffer, cleared with plain stores (the CTA's later
     // releases publish them before any other CTA adds into the buffer again)
-    auto zero_share = [&](int64_t* buf) {
-      const int64_t E = (int64_t)M * A.H, e0 = E * cta / G, e1 = E * (cta + 1) / G;
+    auto zero_share = [&](int64_t* buf, int64_t row_elems) {
+      const int64_t E = (int64_t)M * row_elems, e0 = E * cta / G, e1 = E * (cta + 1) / G;
       for (int64_t e = e0 + tid; e < e1; e += kConsumers) buf[e] = 0;
     };
     const int units = M * A.nkv * A.splits;
@@ -461,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
         else
           stage_x<M>(op, xs, wsum, tid);
         stamp(A, cta, 1 + 5 * l, 1, tid);
-        consume_blocks<M, MODE_QKV>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
+        consume_blocks<M, MODE_QKV, true>(op, R, slot, phase, cta, xs, red, wsum, lmv, lmi, flags, aux, tid, ok);
       }
       stamp(A, cta, 1 + 5 * l, 2, tid);
       // attention: units (sequence, KV head, split) over CTAs, two teams of 4 warps per CTA. The cached
@@ -491,19 +546,23 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
         at.keys_per_split = A.keys_per_split;
         at.partials_only = A.o_merge;
         const int per_b = A.nkv * A.splits;
-        wait_dep(A, ctr(A, l, 0), A.nq + 2 * A.nkv, tid);
+        wait_dep(A, ctr(A, l, 0), (int)A.total[K_QKV], tid);
         // every CTA has contributed to this layer's QKV, so all have staged the down sums they read: clear
         // this CTA's share for the next layer's down
-        if (l > 0) zero_share(A.fx_d);
+        if (l > 0) zero_share(A.fx_d, A.H);
         stamp(A, cta, 2 + 5 * l, 0, tid);
         for (int u = cta + team * G; u < units; u += 2 * G) {
-          const int b = u / per_b, rem = u - b * per_b;
-          attn_unit(at, b, rem / A.splits, rem % A.splits, team_tid, 2 + team, asm_team[team], len);
+          const int b = u / per_b, rem = u - b * per_b, kvh = rem / A.splits, sp = rem % A.splits;
+          if (sp >= n_use) continue;  // beyond the splits in use at this length (attn_unit would return)
+          qkv_heads_from_sums(A, l, b, kvh, sp == n_use - 1, flags[2], aux, team_tid, 2 + team, asm_team[team]);
+          attn_unit(at, b, kvh, sp, team_tid, 2 + team, asm_team[team], len, true);
         }
       }
       stamp(A, cta, 2 + 5 * l, 2, tid);
       // O projection + residual
       wait_dep(A, ctr(A, l, 1), A.o_merge ? M * A.nkv * n_use : M * A.nkv, tid);
+      // every attention unit has read its QKV sums: clear this CTA's share for the next layer's QKV
+      zero_share(A.fx_q, (int64_t)(A.nq + 2 * A.nkv) * 128);
       stamp(A, cta, 3 + 5 * l, 0, tid);
       {
         const GemvArgs op = gemv_op<M>(A, K_O, l);
@@ -527,7 +586,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       stamp(A, cta, 4 + 5 * l, 2, tid);
       // down projection + residual
       wait_dep(A, ctr(A, l, 3), 2 * A.I / kBlockRows, tid);
-      zero_share(A.fx_o);  // every CTA has staged gate/up, so O's sums are read: clear this CTA's share
+      zero_share(A.fx_o, A.H);  // every CTA has staged gate/up, so O's sums are read: clear this CTA's share
       stamp(A, cta, 5 + 5 * l, 0, tid);
       {
         const GemvArgs op = gemv_op<M>(A, K_DOWN, l);
@@ -563,7 +622,7 @@ struct StepPlan {
   int smax[K_KINDS];
   int64_t total[K_KINDS];
   int64_t off_counters, off_abort, off_tickets, off_lm_ticket, off_cta_val, off_cta_idx, off_partials, off_attn_acc,
-      off_attn_ml, off_attn_tickets, off_xb, off_fx_o, off_fx_d, bytes;
+      off_attn_ml, off_attn_tickets, off_xb, off_fx_o, off_fx_d, off_fx_q, bytes;
 };
 
 static int step_plan(const qd_step_desc* d, StepPlan* p) {
@@ -624,6 +683,7 @@ static int step_plan(const qd_step_desc* d, StepPlan* p) {
   p->off_xb = take(B * H * 2);
   p->off_fx_o = take(B * H * 8);
   p->off_fx_d = take(B * H * 8);
+  p->off_fx_q = take(B * n_rows[K_QKV] * 8);
   p->bytes = off;
   // O-side attention merge: the most query heads one O CTA reads, times the splits, must fit the
   // attention shared memory (free while O stages its input); heads as bits of a 32-bit mask
@@ -776,6 +836,7 @@ extern "C" int qd_decode_step(const qd_step_desc* d, void* scratch, int64_t scra
   a.xb = reinterpret_cast<__nv_bfloat16*>(sc + p.off_xb);
   a.fx_o = reinterpret_cast<int64_t*>(sc + p.off_fx_o);
   a.fx_d = reinterpret_cast<int64_t*>(sc + p.off_fx_d);
+  a.fx_q = reinterpret_cast<int64_t*>(sc + p.off_fx_q);
   switch (d->batch) {
     case 1: return launch_step<1>(a, p.smem, stream);
     case 2: return launch_step<2>(a, p.smem, stream);
