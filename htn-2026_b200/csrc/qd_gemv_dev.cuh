@@ -484,7 +484,9 @@ __device__ void finalize_group(const GemvArgs& a, int g, float* red, float* wsum
 // A CTA's segment of row group g (blocks seg_first..b) is reduced into red[m * 128 + r]. If the segment is
 // the whole group, run the epilogue; otherwise store the partial, take the group's ticket, and the CTA
 // that completes the group sums all partials in CTA order and runs the epilogue. 256 consumer threads.
-template <int M, int MODE, bool DEFER = false>
+// FXSUM: the fixed-point group sums are compiled in (the CUDA-core kernels, M <= 8 activation rows; the
+// tensor-core kernels, whose N is 16..64, never use them and so carry none of their registers).
+template <int M, int MODE, bool DEFER = false, bool FXSUM = (M <= 8)>
 __device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64_t b, int cta, float* red,
                               float* wsum, float* lmv, int* lmi, float* aux, int* flags, int tid) {
   const int64_t gb0 = (int64_t)g * a.kblocks;
@@ -501,7 +503,8 @@ __device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64
     named_bar(kBarConsumers, kConsumers);
     return;
   }
-  if ((MODE == MODE_RES || MODE == MODE_QKV) && a.fx_numerics && seg_first == gb0 && nseg_blk == a.kblocks) {
+  if (FXSUM && (MODE == MODE_RES || MODE == MODE_QKV) && a.fx_numerics && seg_first == gb0 &&
+      nseg_blk == a.kblocks) {
     // the whole group in this CTA: the value a fixed-point sum of one contribution gives
     for (int idx = tid; idx < a.m_act * kBlockRows; idx += kConsumers) red[idx] = fx_to_float(fx_of(red[idx]));
     named_bar(kBarConsumers, kConsumers);
@@ -538,7 +541,10 @@ __device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64
       float res_pre[res_per<M>()];
       if constexpr (MODE == MODE_RES) load_res<M>(a, g, tid, res_pre);  // in flight with the partials
       float4 acc[kPer];
-      if ((MODE == MODE_RES || MODE == MODE_QKV) && a.fx_numerics) {  // fixed-point group sums (fx_numerics)
+      bool fx_done = false;
+      if constexpr (FXSUM && (MODE == MODE_RES || MODE == MODE_QKV)) {
+       if (a.fx_numerics) {  // fixed-point group sums (fx_numerics)
+        fx_done = true;
         long long iacc[kPer][4];
 #pragma unroll
         for (int j = 0; j < kPer; ++j)
@@ -569,7 +575,9 @@ __device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64
         for (int j = 0; j < kPer; ++j)
           acc[j] = make_float4(fx_to_float(iacc[j][0]), fx_to_float(iacc[j][1]), fx_to_float(iacc[j][2]),
                                fx_to_float(iacc[j][3]));
-      } else {
+       }
+      }
+      if (!fx_done) {
 #pragma unroll
         for (int j = 0; j < kPer; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int s0 = 0; s0 < nseg; s0 += kSB) {
