@@ -64,6 +64,10 @@ struct alignas(64) TcStepArgs {
   int* lm_ticket;
   float *apart_acc, *apart_ml;
   int* atickets;
+  // The O and down projections leave fixed-point group sums ([M][H] int64) and the packer of each row
+  // applies the residual add (x row += sums) before normalising it - no last-arriving CTA's reduction
+  // between the projection and the next op
+  int64_t *fx_o, *fx_d;
   uint64_t* trace;
 };
 
@@ -175,7 +179,8 @@ __device__ GemvArgs pop(const TcStepArgs& A, int kind, int l) {
     a.ldo = A.H;
     a.res = A.x;
     a.ldr = A.H;
-    a.done = pctr(A, l, kind == P_O ? 3 : 6);
+    a.fx = kind == P_O ? A.fx_o : A.fx_d;
+    a.fx_ctr = pctr(A, l, kind == P_O ? 3 : 6);
   } else if (kind == P_GU) {
     a.x_packed = reinterpret_cast<const char*>(A.xh);
     a.out = A.xi;
@@ -287,7 +292,7 @@ __device__ void mma_gemm(const TcStepArgs& A, const GemvArgs& op, int cta, char*
   }
 }
 
-template <int N, int MODE>
+template <int N, int MODE, bool DEFER = false>
 __device__ void epilogue_gemm(const TcStepArgs& A, const GemvArgs& op, int cta, char* smem, const TcStepLayout& Ly,
                               uint32_t bars, uint32_t tmem, int& buf, int (&fph)[2], int tid) {
   const int nst = A.nst, warp = tid >> 5, lane = tid & 31;
@@ -336,7 +341,7 @@ __device__ void epilogue_gemm(const TcStepArgs& A, const GemvArgs& op, int cta, 
     if (lane == 0) mbar_arrive(acce0 + 8u * buf);
     buf ^= 1;
     named_bar(kBarConsumers, kConsumers);
-    flush_segment<N, MODE>(op, g, seg_first, b, cta, red, wsum, lmv, lmi, aux, flags, tid);
+    flush_segment<N, MODE, DEFER>(op, g, seg_first, b, cta, red, wsum, lmv, lmi, aux, flags, tid);
     seg_first = b + 1;
   }
   if constexpr (MODE == MODE_LM) {
@@ -347,15 +352,33 @@ __device__ void epilogue_gemm(const TcStepArgs& A, const GemvArgs& op, int cta, 
 }
 
 // RMSNorm of whole activation rows (this CTA's rows cta, cta + G, ...) into the packed operand,
-// qd_pack_act's arithmetic (256 threads). Signals one count per row.
+// qd_pack_act's arithmetic (256 threads). Signals one count per row. With fxs (a residual projection's
+// fixed-point sums), each row first gets the projection's RES epilogue, x = bf16(x + bf16(sum)), written
+// back to x in place (this CTA is the row's only reader), and its sums are cleared for the next use.
 __device__ void pack_rows_norm(const TcStepArgs& A, const __nv_bfloat16* norm_w, int* ctr, int npad, int cta,
-                               float* wsum, int tid) {
+                               float* wsum, int tid, int64_t* fxs = nullptr) {
   const int warp = tid >> 5, lane = tid & 31;
   const int k8 = A.H >> 3;
   for (int m = cta; m < A.m_act; m += A.grid) {
     float sq = 0.f;
     for (int qq = tid; qq < k8; qq += kConsumers) {
-      const uint4 v = ld_cg_v4(A.x + (int64_t)m * A.H + qq * 8);
+      uint4 v = ld_cg_v4(A.x + (int64_t)m * A.H + qq * 8);
+      if (fxs) {
+        longlong2* sp = reinterpret_cast<longlong2*>(fxs + (int64_t)m * A.H + qq * 8);
+        const longlong2 sv[4] = {__ldcg(sp), __ldcg(sp + 1), __ldcg(sp + 2), __ldcg(sp + 3)};
+        const uint32_t ru[4] = {v.x, v.y, v.z, v.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float lo = bf16r(bf_lo(ru[e]) + bf16r(fx_to_float(sv[e].x)));
+          const float hi = bf16r(bf_hi(ru[e]) + bf16r(fx_to_float(sv[e].y)));
+          o[e] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
+        }
+        v = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(A.x + (int64_t)m * A.H + qq * 8) = v;  // re-read below by this thread
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sp[e] = make_longlong2(0, 0);
+      }
       const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -812,9 +835,9 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_step_kernel(const __grid_cons
       signal_done(A.counters, tid);
     }
     for (int l = 0; l < A.L; ++l) {
-      wait_consumers(A, l == 0 ? A.counters : pctr(A, l - 1, 6), l == 0 ? M : A.H / kBlockRows, tid);
+      wait_consumers(A, l == 0 ? A.counters : pctr(A, l - 1, 6), l == 0 ? M : (int)A.total[P_DOWN], tid);
       tstamp(A, cta, 1 + 7 * l, 0, tid);
-      pack_rows_norm(A, A.ln1 + (int64_t)l * A.H, pctr(A, l, 0), N, cta, wsum, tid);
+      pack_rows_norm(A, A.ln1 + (int64_t)l * A.H, pctr(A, l, 0), N, cta, wsum, tid, l == 0 ? nullptr : A.fx_d);
       epilogue_gemm<N, MODE_QKV>(A, pop<N>(A, P_QKV, l), cta, smem, Ly, bars, tmem, buf, fph, tid);
       tstamp(A, cta, 2 + 7 * l, 0, tid);
       if (tid == 0) mbar_arrive(aregfree);  // `red` is free: the attention ring may fill
@@ -822,17 +845,17 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_step_kernel(const __grid_cons
       if (warp < 4) softmax_attn(A, aw, l, cta, smem, Ly, abars, tS0, tO0, agi, tid);
       tstamp(A, cta, 3 + 7 * l, 0, tid);
       named_bar(kBarConsumers, kConsumers);  // the attention ring is drained before `red` is reused
-      epilogue_gemm<N, MODE_RES>(A, pop<N>(A, P_O, l), cta, smem, Ly, bars, tmem, buf, fph, tid);
+      epilogue_gemm<N, MODE_RES, true>(A, pop<N>(A, P_O, l), cta, smem, Ly, bars, tmem, buf, fph, tid);
       tstamp(A, cta, 4 + 7 * l, 0, tid);
-      wait_consumers(A, pctr(A, l, 3), A.H / kBlockRows, tid);
-      pack_rows_norm(A, A.ln2 + (int64_t)l * A.H, pctr(A, l, 4), N, cta, wsum, tid);
+      wait_consumers(A, pctr(A, l, 3), (int)A.total[P_O], tid);
+      pack_rows_norm(A, A.ln2 + (int64_t)l * A.H, pctr(A, l, 4), N, cta, wsum, tid, A.fx_o);
       epilogue_gemm<N, MODE_SWIGLU>(A, pop<N>(A, P_GU, l), cta, smem, Ly, bars, tmem, buf, fph, tid);
       tstamp(A, cta, 5 + 7 * l, 0, tid);
-      epilogue_gemm<N, MODE_RES>(A, pop<N>(A, P_DOWN, l), cta, smem, Ly, bars, tmem, buf, fph, tid);
+      epilogue_gemm<N, MODE_RES, true>(A, pop<N>(A, P_DOWN, l), cta, smem, Ly, bars, tmem, buf, fph, tid);
       tstamp(A, cta, 6 + 7 * l, 0, tid);
     }
-    wait_consumers(A, pctr(A, A.L - 1, 6), A.H / kBlockRows, tid);
-    pack_rows_norm(A, A.fnorm, final_pack_ctr(A), N, cta, wsum, tid);
+    wait_consumers(A, pctr(A, A.L - 1, 6), (int)A.total[P_DOWN], tid);
+    pack_rows_norm(A, A.fnorm, final_pack_ctr(A), N, cta, wsum, tid, A.fx_d);
     epilogue_gemm<N, MODE_LM>(A, pop<N>(A, P_LM, 0), cta, smem, Ly, bars, tmem, buf, fph, tid);
     tstamp(A, cta, 2 + 7 * A.L, 0, tid);
   }
@@ -870,7 +893,7 @@ struct TcStepPlan {
   int64_t wn[P_KINDS], wk[P_KINDS], total[P_KINDS];
   int smax[P_KINDS];
   int64_t off_counters, off_abort, off_tickets, off_lm_ticket, off_cta_val, off_cta_idx, off_partials, off_aacc,
-      off_aml, off_atickets, bytes;
+      off_aml, off_atickets, off_fx_o, off_fx_d, bytes;
 };
 
 static int tc_step_plan(const qd_step_desc* d, TcStepPlan* p) {
@@ -928,6 +951,8 @@ static int tc_step_plan(const qd_step_desc* d, TcStepPlan* p) {
   p->off_aacc = take(pairs * asmax * kGroup * kHeadDim * 4);
   p->off_aml = take(pairs * asmax * kGroup * 2 * 4);
   p->off_atickets = take(pairs * 4);
+  p->off_fx_o = take(B * H * 8);
+  p->off_fx_d = take(B * H * 8);
   p->bytes = off;
   return QD_OK;
 }
@@ -1046,6 +1071,8 @@ extern "C" int qd_tc_decode_step(const qd_step_desc* d, void* xh, void* xa, void
   char* sc = static_cast<char*>(scratch);
   a.counters = reinterpret_cast<int*>(sc + p.off_counters);
   a.abort_flag = reinterpret_cast<int*>(sc + p.off_abort);
+  a.fx_o = reinterpret_cast<int64_t*>(sc + p.off_fx_o);
+  a.fx_d = reinterpret_cast<int64_t*>(sc + p.off_fx_d);
   a.tickets = reinterpret_cast<int*>(sc + p.off_tickets);
   a.lm_ticket = reinterpret_cast<int*>(sc + p.off_lm_ticket);
   a.cta_val = reinterpret_cast<float*>(sc + p.off_cta_val);
