@@ -499,7 +499,7 @@ __device__ void flush_segment(const GemvArgs& a, int g, int64_t seg_first, int64
       atomicAdd(dst, (unsigned long long)fx_of(red[idx]));
     }
     named_bar(kBarConsumers, kConsumers);
-    if (tid == 0) red_release_add(a.fx_ctr, nseg_blk);  // releases this CTA's additions
+    if (tid == 0 && a.fx_ctr) red_release_add(a.fx_ctr, nseg_blk);  // releases this CTA's additions
     named_bar(kBarConsumers, kConsumers);
     return;
   }

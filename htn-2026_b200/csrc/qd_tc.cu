@@ -76,7 +76,7 @@ constexpr int tmem_cols() {  // two accumulators of N fp32 columns, power of two
   return 2 * N <= 32 ? 32 : (2 * N <= 64 ? 64 : (2 * N <= 128 ? 128 : 256));
 }
 
-template <int N, int MODE>
+template <int N, int MODE, bool DEFER = false>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemv_kernel(const __grid_constant__ GemvArgs a) {
   extern __shared__ __align__(1024) char smem_raw[];
   // the 128-byte swizzle is a function of the shared address: operand tiles must sit on 1 KiB boundaries
@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemv_kernel(const __grid_con
         flags[3] = 8 + 8 * (n_seg < 7 ? n_seg : 6);  // trace slot base of this segment's flush phases
       }
       named_bar(kBarConsumers, kConsumers);
-      flush_segment<N, MODE>(a, g, seg_first, b, cta, red, wsum, lmv, lmi, aux, flags, tid);
+      flush_segment<N, MODE, DEFER>(a, g, seg_first, b, cta, red, wsum, lmv, lmi, aux, flags, tid);
       if (tid == 0 && n_seg < 7) TC_STAMP(13 + 8 * n_seg);
       ++n_seg;
       seg_first = b + 1;
@@ -330,6 +330,74 @@ __global__ void __launch_bounds__(256) pack_act_kernel(const __grid_constant__ P
   }
 }
 
+// The residual add a QD_EPI_RES_SUMS projection left behind, then the packing of qd_pack_act: row m of x
+// becomes bf16(x + bf16(sum)) (written back to x), its sums are cleared for the next projection, and the
+// row is RMSNorm-ed (optional) into the packed operand. One CTA of 256 threads per row.
+struct PackResArgs {
+  __nv_bfloat16* x;
+  int64_t ldx, k;
+  int64_t* fxs;  // [m_act][k]
+  const __nv_bfloat16* norm_w;
+  float eps;
+  __nv_bfloat16* xpk;
+  int n_pad;
+};
+
+__global__ void __launch_bounds__(256) pack_act_res_kernel(const __grid_constant__ PackResArgs a) {
+  __shared__ float wsum[8];
+  grid_dep_wait();
+  grid_dep_launch();
+  const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int k8 = (int)(a.k >> 3);
+  float sq = 0.f;
+  for (int q = tid; q < k8; q += 256) {
+    const uint4 v = ld_cg_v4(a.x + m * a.ldx + q * 8);
+    longlong2* sp = reinterpret_cast<longlong2*>(a.fxs + m * a.k + q * 8);
+    const longlong2 sv[4] = {__ldcg(sp), __ldcg(sp + 1), __ldcg(sp + 2), __ldcg(sp + 3)};
+    const uint32_t ru[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float lo = bf16r(bf_lo(ru[e]) + bf16r(fx_to_float(sv[e].x)));
+      const float hi = bf16r(bf_hi(ru[e]) + bf16r(fx_to_float(sv[e].y)));
+      o[e] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
+      sq = fmaf(lo, lo, sq);
+      sq = fmaf(hi, hi, sq);
+    }
+    *reinterpret_cast<uint4*>(a.x + m * a.ldx + q * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sp[e] = make_longlong2(0, 0);
+  }
+  float rstd = 1.f;
+  if (a.norm_w) {
+    sq = warp_sum(sq);
+    if (lane == 0) wsum[warp] = sq;
+    __syncthreads();
+    float ss = 0.f;
+#pragma unroll
+    for (int w8 = 0; w8 < 8; ++w8) ss += wsum[w8];
+    rstd = 1.0f / sqrtf(ss / (float)a.k + a.eps);
+  }
+  for (int q = tid; q < k8; q += 256) {
+    uint4 v = ld_cg_v4(a.x + m * a.ldx + q * 8);  // this thread's own write above
+    if (a.norm_w) {
+      const uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + q * 8);
+      const uint32_t xu[4] = {v.x, v.y, v.z, v.w};
+      const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float lo = bf16r(bf_lo(wu[e]) * bf16r(bf_lo(xu[e]) * rstd));
+        const float hi = bf16r(bf_hi(wu[e]) * bf16r(bf_hi(xu[e]) * rstd));
+        o[e] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
+      }
+      v = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    const int kb = q >> 3, c = q & 7;
+    *reinterpret_cast<uint4*>(a.xpk + ((int64_t)kb * a.n_pad + m) * 64 + ((c ^ (m & 7)) << 3)) = v;
+  }
+}
+
 // ------------------------------------------------------------------ host side
 static int tc_ctas_per_sm() {
   const int c = env_int("QD_TC_CTAS_PER_SM", 1);
@@ -375,21 +443,21 @@ static bool tc_plan(int64_t n_rows, int64_t k, int n_pad, int grid_hint, Plan* p
   return p->nst >= 2;
 }
 
-template <int N, int MODE>
+template <int N, int MODE, bool DEFER = false>
 static int tc_launch_nm(const GemvArgs& a, int pdl, cudaStream_t stream) {
-  auto kern = tc_gemv_kernel<N, MODE>;
+  auto kern = tc_gemv_kernel<N, MODE, DEFER>;
   const int smem = tc_layout(N, a.nst).total + 1024;  // + alignment slack
   if (int rc = set_max_dynamic_smem((const void*)kern, smem)) return rc;
   return launch_kernel((const void*)kern, dim3(a.grid), dim3(kTcThreads), smem, pdl, stream, (void*)&a);
 }
 
-template <int MODE>
+template <int MODE, bool DEFER = false>
 static int tc_launch_mode(const GemvArgs& a, int N, int pdl, cudaStream_t stream) {
   switch (N) {
-    case 16: return tc_launch_nm<16, MODE>(a, pdl, stream);
-    case 32: return tc_launch_nm<32, MODE>(a, pdl, stream);
-    case 48: return tc_launch_nm<48, MODE>(a, pdl, stream);
-    case 64: return tc_launch_nm<64, MODE>(a, pdl, stream);
+    case 16: return tc_launch_nm<16, MODE, DEFER>(a, pdl, stream);
+    case 32: return tc_launch_nm<32, MODE, DEFER>(a, pdl, stream);
+    case 48: return tc_launch_nm<48, MODE, DEFER>(a, pdl, stream);
+    case 64: return tc_launch_nm<64, MODE, DEFER>(a, pdl, stream);
   }
   return set_error(QD_ERR_UNSUPPORTED, "n_pad %d not in {16, 32, 48, 64}", N);
 }
@@ -460,6 +528,25 @@ extern "C" int qd_pack_act(const void* x, int64_t ldx, int m_act, int n_pad, int
   return launch_kernel((const void*)pack_act_kernel, dim3(m_act), dim3(256), 0, pdl, stream, &a);
 }
 
+extern "C" int qd_pack_act_res(void* x, int64_t ldx, int m_act, int n_pad, int64_t k, void* fx_sums,
+                               const void* norm_w, float eps, void* xpk, int pdl, cudaStream_t stream) {
+  if (!x || !xpk || !fx_sums || !aligned16(x) || !aligned16(xpk) || !aligned16(fx_sums) ||
+      (norm_w && !aligned16(norm_w)))
+    return set_error(QD_ERR_ARG, "pack_act_res: null or unaligned pointer");
+  if (m_act < 1 || m_act > n_pad || k % kBlockCols || ldx < k || ldx % 8)
+    return set_error(QD_ERR_ARG, "pack_act_res: bad sizes");
+  PackResArgs a = {};
+  a.x = static_cast<__nv_bfloat16*>(x);
+  a.ldx = ldx;
+  a.k = k;
+  a.fxs = static_cast<int64_t*>(fx_sums);
+  a.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
+  a.eps = eps;
+  a.xpk = static_cast<__nv_bfloat16*>(xpk);
+  a.n_pad = n_pad;
+  return launch_kernel((const void*)pack_act_res_kernel, dim3(m_act), dim3(256), 0, pdl, stream, &a);
+}
+
 extern "C" int qd_tc_gemv_plan(int64_t n, int64_t k, int n_pad, int grid_hint, int* grid, int64_t* scratch_bytes) {
   Plan p;
   if (!tc_plan(n, k, n_pad, grid_hint, &p))
@@ -489,6 +576,11 @@ extern "C" int qd_tc_gemv(const void* xpk, int n_pad, int m_act, const void* w_p
     mode = MODE_SWIGLU;
     if (!aligned16(out)) return set_error(QD_ERR_ARG, "packed out must be 16-byte aligned");
     a.out_npad = n_pad;
+  } else if (epilogue == QD_EPI_RES_SUMS) {
+    // the residual add is left to the next qd_pack_act_res: out = fixed-point sums [m_act][n] int64
+    if (!aligned16(out)) return set_error(QD_ERR_ARG, "sums must be 16-byte aligned");
+    a.fx = static_cast<int64_t*>(out);
+    return tc_launch_mode<MODE_RES, true>(a, n_pad, pdl, stream);
   } else {
     return set_error(QD_ERR_ARG, "unknown epilogue %d", epilogue);
   }

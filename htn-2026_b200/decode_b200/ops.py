@@ -201,6 +201,16 @@ class PackedActivations:
                int(pdl), _stream())
         return self
 
+    def pack_res(self, x, sums, norm_w=None, eps: float = 1e-6, pdl=True):
+        """x += the deferred residual sums of a RES_SUMS projection (qd_pack_act_res: x written back, the
+        sums cleared), then pack as `pack` does."""
+        _check_bf16(x, norm_w)
+        assert x.shape == (self.m, self.k) and x.stride(1) == 1
+        assert sums.dtype == torch.int64 and sums.is_contiguous() and sums.numel() >= self.m * self.k
+        L.call("qd_pack_act_res", _ptr(x), x.stride(0), self.m, self.n_pad, self.k, _ptr(sums), _ptr(norm_w), eps,
+               _ptr(self.t), int(pdl), _stream())
+        return self
+
 
 class _TcOp:
     def __init__(self, n_pad: int, n: int, k: int, device, grid: int = 0):
@@ -215,6 +225,7 @@ class TcGemv(_TcOp):
     `out` is the next projection's PackedActivations, written directly by the epilogue."""
 
     STORE, RES, SWIGLU, SWIGLU_PACKED = L.QD_EPI_STORE, L.QD_EPI_RES, L.QD_EPI_SWIGLU, L.QD_EPI_SWIGLU_PACKED
+    RES_SUMS = L.QD_EPI_RES_SUMS  # `out` = int64 fixed-point sums [m, n], applied by PackedActivations.pack_res
 
     def __init__(self, m: int, n: int, k: int, epilogue: int, device, grid: int = 0):
         self.m, self.n, self.k, self.epilogue, self.n_pad = m, n, k, epilogue, tc_n_pad(m)
@@ -224,6 +235,12 @@ class TcGemv(_TcOp):
         if self.epilogue == self.SWIGLU_PACKED:
             assert isinstance(out, PackedActivations) and out.m == self.m and out.k == self.n // 2
             out = out.t
+        if self.epilogue == self.RES_SUMS:
+            assert out.dtype == torch.int64 and out.is_contiguous() and out.numel() >= self.m * self.n
+            _check_bf16(w)
+            L.call("qd_tc_gemv", _ptr(xp.t), self.n_pad, self.m, _ptr(w), self.n, self.k, _ptr(out), 0, None, 0,
+                   self.epilogue, self.grid, _ptr(self.scratch), self.scratch.numel(), _ptr(err), int(pdl), _stream())
+            return out
         _check_bf16(w, out, res)
         assert xp.m == self.m and xp.k == self.k and out.stride(-1) == 1
         ldo = out.stride(0) if out.dim() > 1 else 0

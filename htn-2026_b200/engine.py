@@ -206,10 +206,12 @@ class _State:
             self.xp_a = ops.PackedActivations(B, nq * D, dev)
             self.xp_i = ops.PackedActivations(B, I, dev)
             self.qkv = ops.TcQkvRopeAppend(B, H, nq, nkv, dev)
-            self.o = ops.TcGemv(B, H, nq * D, ops.TcGemv.RES, dev)
+            # the residual projections leave fixed-point sums that the next packing applies
+            self.o = ops.TcGemv(B, H, nq * D, ops.TcGemv.RES_SUMS, dev)
             self.gu = ops.TcGemv(B, 2 * I, H, ops.TcGemv.SWIGLU_PACKED, dev)
-            self.down = ops.TcGemv(B, H, I, ops.TcGemv.RES, dev)
+            self.down = ops.TcGemv(B, H, I, ops.TcGemv.RES_SUMS, dev)
             self.lm = ops.TcLmHeadArgmax(B, eng.vocab, H, dev)
+            self.res_sums = torch.zeros((B, H), dtype=torch.int64, device=dev)
         else:
             self.attn = ops.DecodeAttention(B, nq, nkv, cap, dev)
             self.qkv = ops.QkvRopeAppend(B, H, nq, nkv, dev, eps=eng.eps)
@@ -642,18 +644,23 @@ class Engine:
         """Layers and LM head on the tensor-core kernels: each projection reads its activations packed
         into the MMA operand layout - RMSNorm-ed by a packing kernel before QKV, gate/up and the LM head,
         written packed directly by the attention and SwiGLU epilogues before O and down."""
-        B, eps = st.B, self.eps
+        B, eps, sums = st.B, self.eps, st.res_sums
+        # O and down leave their outputs as fixed-point sums; the packing for the next projection adds them
+        # to the residual stream x (and clears them), so no split-K last arriver sits between the two
         for i in range(self.n_layers):
             kc, vc = st.k_all[i], st.v_all[i]
-            st.xp_h.pack(st.x, self.ln1[i], eps, pdl)
+            if i == 0:
+                st.xp_h.pack(st.x, self.ln1[i], eps, pdl)
+            else:
+                st.xp_h.pack_res(st.x, sums, self.ln1[i], eps, pdl)
             st.qkv(st.xp_h, self.w_qkv[i], self.qn[i], self.kn[i], st.cos, st.sin, st.pos, st.q, kc, vc, err=err,
                    pdl=pdl)
             st.attn(st.q, kc, vc, st.pos, st.xp_a, err=err, pdl=pdl)       # written packed for O
-            st.o(st.xp_a, self.w_o[i], st.x, res=st.x, err=err, pdl=pdl)
-            st.xp_h.pack(st.x, self.ln2[i], eps, pdl)
+            st.o(st.xp_a, self.w_o[i], sums, err=err, pdl=pdl)
+            st.xp_h.pack_res(st.x, sums, self.ln2[i], eps, pdl)
             st.gu(st.xp_h, self.w_gu[i], st.xp_i, err=err, pdl=pdl)        # SwiGLU written packed for down
-            st.down(st.xp_i, self.w_down[i], st.x, res=st.x, err=err, pdl=pdl)
-        st.xp_h.pack(st.x, self.final_norm, eps, pdl)
+            st.down(st.xp_i, self.w_down[i], sums, err=err, pdl=pdl)
+        st.xp_h.pack_res(st.x, sums, self.final_norm, eps, pdl)
         st.lm(st.xp_h, self.e_packed, st.tok, st.pos, inc_pos=True, logits=logits, err=err, pdl=pdl)
 
     def check_device_errors(self, st: _State) -> None:
@@ -666,6 +673,8 @@ class Engine:
                          st.tstep_logits, *extra):
                 if plan is not None:
                     plan.scratch.zero_()
+            if getattr(st, "res_sums", None) is not None:  # deferred residual sums may be half added
+                st.res_sums.zero_()
             st.err.zero_()
             raise RuntimeError(f"decode kernels reported a device error: {qdlib.describe_device_error(code)}")
 

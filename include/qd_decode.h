@@ -33,7 +33,7 @@ enum {
   QD_ERR_UNSUPPORTED = 4  /* shape outside what the kernels are built for */
 };
 
-enum { QD_EPI_STORE = 0, QD_EPI_RES = 1, QD_EPI_SWIGLU = 2, QD_EPI_SWIGLU_PACKED = 3 };
+enum { QD_EPI_STORE = 0, QD_EPI_RES = 1, QD_EPI_SWIGLU = 2, QD_EPI_SWIGLU_PACKED = 3, QD_EPI_RES_SUMS = 4 };
 
 enum {
   QD_DEVERR_WAIT_FULL = 1,
@@ -152,6 +152,14 @@ int qd_tc_gemv_plan(int64_t n, int64_t k, int n_pad, int grid_hint, int* grid, i
 int qd_tc_gemv(const void* xpk, int n_pad, int m_act, const void* w_packed, int64_t n, int64_t k, void* out,
                int64_t ldo, const void* res, int64_t ldr, int epilogue, int grid, void* scratch,
                int64_t scratch_bytes, int* err, int pdl, cudaStream_t stream);
+/* QD_EPI_RES_SUMS (qd_tc_gemv): the residual add is deferred - `out` is an int64 [m_act][n] buffer of
+ * fixed-point group sums (value * 2^32, zero on entry), which every CTA adds its split-K partials into
+ * with integer atomics (order-independent, so deterministic); res / ldo are unused. qd_pack_act_res
+ * then applies it: x row m = bf16(x + bf16(sum)) (written back to x), the sums cleared to zero, and the
+ * row packed as qd_pack_act does (RMSNorm-ed when norm_w is given). This takes the split-K last
+ * arriver's reduction off the path between a residual projection and the next one. */
+int qd_pack_act_res(void* x, int64_t ldx, int m_act, int n_pad, int64_t k, void* fx_sums, const void* norm_w,
+                    float eps, void* xpk, int pdl, cudaStream_t stream);
 /* qd_qkv_rope_append from packed activations (plan with n = (nq + 2 nkv) * 128). */
 int qd_tc_qkv_rope_append(const void* xpk, int n_pad, int m_act, const void* w_packed, int64_t k, const void* q_norm,
                           const void* k_norm, const void* cos, const void* sin, const int64_t* pos, int64_t cap,

@@ -250,3 +250,36 @@ def test_tc_swiglu_packed_output_is_packed_rowmajor(m):
     ops.TcGemv(m, 2 * inter, k, ops.TcGemv.SWIGLU_PACKED, DEV)(xp, w, packed)
     ref = ops.PackedActivations(m, inter, DEV).pack(row)
     assert torch.equal(packed.t.view(torch.int16), ref.t.view(torch.int16))
+
+
+@pytest.mark.parametrize("n,k", [(2560, 4096), (2560, 9728)])
+@pytest.mark.parametrize("m", [13, 32, 64])
+def test_tc_gemv_deferred_residual_sums(n, k, m):
+    """QD_EPI_RES_SUMS + qd_pack_act_res: the projection's split-K partials go into fixed-point sums, the
+    packing adds them to the residual stream (x written back) and clears them; x against the fp64
+    reference as in the residual test, the packed operand equal to packing the new x, the sums zero after,
+    and a second round on the cleared sums gives the same bytes."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(n + k + 7 * m)
+    x, w, res = _rand((m, k), 1.0, g), _rand((n, k), 0.02, g), _rand((m, n), 1.0, g)
+    nw = (1.0 + 0.1 * torch.randn(n, generator=g)).to(BF16).to(DEV)
+    xp = ops.PackedActivations(m, k, DEV).pack(x.to(DEV))
+    wp = ops.pack_matrix(w.to(DEV))
+    plan = ops.TcGemv(m, n, k, ops.TcGemv.RES_SUMS, DEV)
+    sums = torch.zeros((m, n), dtype=torch.int64, device=DEV)
+    outs = []
+    for _ in range(2):
+        xr = res.to(DEV).clone()
+        plan(xp, wp, sums)
+        packed = ops.PackedActivations(m, n, DEV).pack_res(xr, sums, nw)
+        torch.cuda.synchronize()
+        assert int(sums.abs().sum()) == 0
+        outs.append((xr.clone(), packed.t.clone()))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    xr, pk = outs[0]
+    y = _gemv_ref(x, w, None, 0).to(BF16).float()
+    ref = (res.float() + y).to(BF16)
+    diff = (xr.float().cpu() - ref.float()).abs()
+    tol = RTOL * (ref.float().abs() + y.abs()) + 1e-3
+    assert not (diff > tol).any(), f"{int((diff > tol).sum())} mismatches, max diff {float(diff.max()):.4g}"
+    assert torch.equal(pk, ops.PackedActivations(m, n, DEV).pack(xr, nw).t)
