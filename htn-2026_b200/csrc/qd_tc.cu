@@ -398,6 +398,62 @@ __global__ void __launch_bounds__(256) pack_act_res_kernel(const __grid_constant
   }
 }
 
+// The QKV epilogue (the decode QKV GEMV's arithmetic: BF16 projection output, per-head RMSNorm with
+// the sum of squares taken per 32 rows and the 4 slices added in order, q_norm / k_norm, RoPE at the
+// decode position with every product rounded to BF16, q store, K/V append) applied to the fixed-point
+// sums a QD_EPI_STORE_SUMS projection left, which it clears. One CTA of 128 threads (one per dimension)
+// per (head, row).
+struct QkvSumsArgs {
+  int64_t* sums;  // [m_act][(nq + 2 nkv) * 128]
+  int64_t lds;
+  const __nv_bfloat16 *qn, *kn, *cos, *sin;
+  const int64_t* pos;
+  int64_t cap;
+  int nq, nkv;
+  float eps;
+  __nv_bfloat16 *q_out, *k_cache, *v_cache;
+  int64_t cs_b, cs_h;
+  int* err;
+};
+
+__global__ void __launch_bounds__(128) qkv_rope_sums_kernel(const __grid_constant__ QkvSumsArgs a) {
+  __shared__ float wsq[4];
+  __shared__ float ys[128];
+  grid_dep_wait();
+  grid_dep_launch();
+  const int g = blockIdx.x, m = blockIdx.y, r = threadIdx.x, lane = r & 31, w = r >> 5;
+  int64_t* sp = a.sums + (int64_t)m * a.lds + (int64_t)g * 128 + r;
+  const float v = bf16r(fx_to_float(__ldcg(sp)));
+  *sp = 0;  // the sums start the next projection clear
+  const int64_t p = ld_cg_s64(a.pos);
+  if (p < 0 || p >= a.cap) {  // the same for every thread: flagged, nothing written
+    if (r == 0 && g == 0 && m == 0 && a.err) atomicOr(a.err, QD_DEVERR_POS);
+    return;
+  }
+  if (g >= a.nq + a.nkv) {  // V head: into the cache as is
+    a.v_cache[(int64_t)m * a.cs_b + (int64_t)(g - a.nq - a.nkv) * a.cs_h + p * 128 + r] = __float2bfloat16_rn(v);
+    return;
+  }
+  const float sq = warp_sum(v * v);
+  if (lane == 0) wsq[w] = sq;
+  __syncthreads();
+  const float var = (wsq[0] + wsq[1] + wsq[2] + wsq[3]) / 128.0f;
+  const float rstd = 1.0f / sqrtf(var + a.eps);
+  const float nw = bf16_to_f(g < a.nq ? a.qn[r] : a.kn[r]);
+  const float y = bf16r(nw * bf16r(v * rstd));
+  ys[r] = y;
+  __syncthreads();
+  const float yp = ys[r ^ 64];
+  const float c = bf16_to_f(a.cos[p * 128 + r]), sn = bf16_to_f(a.sin[p * 128 + r]);
+  // q*cos + rotate_half(q)*sin with every product a BF16 tensor (rotate_half = cat(-q2, q1))
+  const float rot = (r < 64) ? bf16r(-yp * sn) : bf16r(yp * sn);
+  const __nv_bfloat16 o = __float2bfloat16_rn(bf16r(y * c) + rot);
+  if (g < a.nq)
+    a.q_out[((int64_t)m * a.nq + g) * 128 + r] = o;
+  else
+    a.k_cache[(int64_t)m * a.cs_b + (int64_t)(g - a.nq) * a.cs_h + p * 128 + r] = o;
+}
+
 // ------------------------------------------------------------------ host side
 static int tc_ctas_per_sm() {
   const int c = env_int("QD_TC_CTAS_PER_SM", 1);
@@ -547,6 +603,37 @@ extern "C" int qd_pack_act_res(void* x, int64_t ldx, int m_act, int n_pad, int64
   return launch_kernel((const void*)pack_act_res_kernel, dim3(m_act), dim3(256), 0, pdl, stream, &a);
 }
 
+extern "C" int qd_qkv_rope_sums(void* sums, int64_t lds, int m_act, int nq_heads, int nkv_heads, const void* q_norm,
+                                const void* k_norm, float eps, const void* cos, const void* sin, const int64_t* pos,
+                                int64_t cap, void* q_out, void* k_cache, void* v_cache, int64_t cs_b, int64_t cs_h,
+                                int* err, int pdl, cudaStream_t stream) {
+  if (!sums || !q_norm || !k_norm || !cos || !sin || !pos || !q_out || !k_cache || !v_cache)
+    return set_error(QD_ERR_ARG, "qkv_rope_sums: null pointer");
+  if (m_act < 1 || m_act > 65535 || nq_heads < 1 || nkv_heads < 1 || lds < (int64_t)(nq_heads + 2 * nkv_heads) * 128 ||
+      cap < 1 || cs_h < cap * 128 || cs_b < (int64_t)nkv_heads * cs_h)
+    return set_error(QD_ERR_ARG, "qkv_rope_sums: bad sizes");
+  QkvSumsArgs a = {};
+  a.sums = static_cast<int64_t*>(sums);
+  a.lds = lds;
+  a.qn = static_cast<const __nv_bfloat16*>(q_norm);
+  a.kn = static_cast<const __nv_bfloat16*>(k_norm);
+  a.cos = static_cast<const __nv_bfloat16*>(cos);
+  a.sin = static_cast<const __nv_bfloat16*>(sin);
+  a.pos = pos;
+  a.cap = cap;
+  a.nq = nq_heads;
+  a.nkv = nkv_heads;
+  a.eps = eps;
+  a.q_out = static_cast<__nv_bfloat16*>(q_out);
+  a.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  a.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  a.cs_b = cs_b;
+  a.cs_h = cs_h;
+  a.err = err;
+  return launch_kernel((const void*)qkv_rope_sums_kernel, dim3(nq_heads + 2 * nkv_heads, m_act), dim3(128), 0, pdl,
+                       stream, &a);
+}
+
 extern "C" int qd_tc_gemv_plan(int64_t n, int64_t k, int n_pad, int grid_hint, int* grid, int64_t* scratch_bytes) {
   Plan p;
   if (!tc_plan(n, k, n_pad, grid_hint, &p))
@@ -576,6 +663,11 @@ extern "C" int qd_tc_gemv(const void* xpk, int n_pad, int m_act, const void* w_p
     mode = MODE_SWIGLU;
     if (!aligned16(out)) return set_error(QD_ERR_ARG, "packed out must be 16-byte aligned");
     a.out_npad = n_pad;
+  } else if (epilogue == QD_EPI_STORE_SUMS) {
+    // the projection output stays as fixed-point sums for a following kernel (qd_qkv_rope_sums)
+    if (!aligned16(out)) return set_error(QD_ERR_ARG, "sums must be 16-byte aligned");
+    a.fx = static_cast<int64_t*>(out);
+    return tc_launch_mode<MODE_STORE, true>(a, n_pad, pdl, stream);
   } else if (epilogue == QD_EPI_RES_SUMS) {
     // the residual add is left to the next qd_pack_act_res: out = fixed-point sums [m_act][n] int64
     if (!aligned16(out)) return set_error(QD_ERR_ARG, "sums must be 16-byte aligned");

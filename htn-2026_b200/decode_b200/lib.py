@@ -59,6 +59,9 @@ PROTOTYPES = {
                                   c_void_p, c_int, c_void_p, c_int64, c_int, c_void_p, c_int64, c_void_p, c_int,
                                   c_void_p]),
     "qd_pack_act": (c_int, [c_void_p, c_int64, c_int, c_int, c_int64, c_void_p, c_float, c_void_p, c_int, c_void_p]),
+    "qd_qkv_rope_sums": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_float, c_void_p,
+                                 c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
+                                 c_int, c_void_p]),
     "qd_pack_act_res": (c_int, [c_void_p, c_int64, c_int, c_int, c_int64, c_void_p, c_void_p, c_float, c_void_p,
                                 c_int, c_void_p]),
     "qd_tc_gemv_plan": (c_int, [c_int64, c_int64, c_int, c_int, P_INT, P_I64]),
@@ -113,7 +116,7 @@ PROTOTYPES = {
 }
 
 QD_OK, QD_ERR_ARG, QD_ERR_SCRATCH, QD_ERR_CUDA, QD_ERR_UNSUPPORTED = 0, 1, 2, 3, 4
-QD_EPI_STORE, QD_EPI_RES, QD_EPI_SWIGLU, QD_EPI_SWIGLU_PACKED, QD_EPI_RES_SUMS = 0, 1, 2, 3, 4
+QD_EPI_STORE, QD_EPI_RES, QD_EPI_SWIGLU, QD_EPI_SWIGLU_PACKED, QD_EPI_RES_SUMS, QD_EPI_STORE_SUMS = 0, 1, 2, 3, 4, 5
 DEVERR = {1: "wait for a weight block timed out", 2: "wait for a free ring slot timed out",
           4: "drain of in-flight copies timed out", 8: "token id out of range",
           16: "decode position outside the cache", 32: "a wait for another CTA's results timed out",

@@ -226,6 +226,7 @@ class TcGemv(_TcOp):
 
     STORE, RES, SWIGLU, SWIGLU_PACKED = L.QD_EPI_STORE, L.QD_EPI_RES, L.QD_EPI_SWIGLU, L.QD_EPI_SWIGLU_PACKED
     RES_SUMS = L.QD_EPI_RES_SUMS  # `out` = int64 fixed-point sums [m, n], applied by PackedActivations.pack_res
+    STORE_SUMS = L.QD_EPI_STORE_SUMS  # `out` = int64 fixed-point sums [m, n], applied by qkv_rope_sums
 
     def __init__(self, m: int, n: int, k: int, epilogue: int, device, grid: int = 0):
         self.m, self.n, self.k, self.epilogue, self.n_pad = m, n, k, epilogue, tc_n_pad(m)
@@ -235,7 +236,7 @@ class TcGemv(_TcOp):
         if self.epilogue == self.SWIGLU_PACKED:
             assert isinstance(out, PackedActivations) and out.m == self.m and out.k == self.n // 2
             out = out.t
-        if self.epilogue == self.RES_SUMS:
+        if self.epilogue in (self.RES_SUMS, self.STORE_SUMS):
             assert out.dtype == torch.int64 and out.is_contiguous() and out.numel() >= self.m * self.n
             _check_bf16(w)
             L.call("qd_tc_gemv", _ptr(xp.t), self.n_pad, self.m, _ptr(w), self.n, self.k, _ptr(out), 0, None, 0,
@@ -364,6 +365,19 @@ def tree_compact(k_all, v_all, moves, n: int):
     assert k_all.dim() == 5 and k_all.stride() == v_all.stride() and moves.dtype == torch.int32
     L.call("qd_tree_compact", _ptr(k_all), _ptr(v_all), k_all.shape[0], k_all.stride(0), k_all.shape[1],
            k_all.stride(1), k_all.shape[2], k_all.stride(2), k_all.shape[3], _ptr(moves), n, _stream())
+
+
+def qkv_rope_sums(sums, m: int, nq: int, nkv: int, q_norm, k_norm, eps: float, cos, sin, pos, q_out, k_cache,
+                  v_cache, err=None, pdl=True):
+    """The QKV epilogue applied to a STORE_SUMS projection's fixed-point sums (qd_qkv_rope_sums), which
+    it clears: q_out [m, nq, 128]; K/V appended at *pos into caches [B, nkv, cap, 128]."""
+    _check_bf16(q_norm, k_norm, cos, sin, q_out, k_cache, v_cache)
+    assert sums.dtype == torch.int64 and sums.stride(-1) == 1 and pos.dtype == torch.int64
+    assert k_cache.stride(2) == 128 and k_cache.stride() == v_cache.stride()
+    L.call("qd_qkv_rope_sums", _ptr(sums), sums.stride(0), m, nq, nkv, _ptr(q_norm), _ptr(k_norm), eps, _ptr(cos),
+           _ptr(sin), _ptr(pos), k_cache.shape[2], _ptr(q_out), _ptr(k_cache), _ptr(v_cache), k_cache.stride(0),
+           k_cache.stride(1), _ptr(err), int(pdl), _stream())
+    return q_out
 
 
 def argmax_rows(logits, n: int, out):

@@ -212,6 +212,9 @@ class _State:
             self.down = ops.TcGemv(B, H, I, ops.TcGemv.RES_SUMS, dev)
             self.lm = ops.TcLmHeadArgmax(B, eng.vocab, H, dev)
             self.res_sums = torch.zeros((B, H), dtype=torch.int64, device=dev)
+            # the chain's QKV: the projection into fixed-point sums, then the epilogue kernel
+            self.qkv_mm = ops.TcGemv(B, (nq + 2 * nkv) * D, H, ops.TcGemv.STORE_SUMS, dev)
+            self.qkv_sums = torch.zeros((B, (nq + 2 * nkv) * D), dtype=torch.int64, device=dev)
         else:
             self.attn = ops.DecodeAttention(B, nq, nkv, cap, dev)
             self.qkv = ops.QkvRopeAppend(B, H, nq, nkv, dev, eps=eng.eps)
@@ -653,8 +656,9 @@ class Engine:
                 st.xp_h.pack(st.x, self.ln1[i], eps, pdl)
             else:
                 st.xp_h.pack_res(st.x, sums, self.ln1[i], eps, pdl)
-            st.qkv(st.xp_h, self.w_qkv[i], self.qn[i], self.kn[i], st.cos, st.sin, st.pos, st.q, kc, vc, err=err,
-                   pdl=pdl)
+            st.qkv_mm(st.xp_h, self.w_qkv[i], st.qkv_sums, err=err, pdl=pdl)
+            ops.qkv_rope_sums(st.qkv_sums, B, self.nq, self.nkv, self.qn[i], self.kn[i], eps, st.cos, st.sin, st.pos,
+                              st.q, kc, vc, err=err, pdl=pdl)
             st.attn(st.q, kc, vc, st.pos, st.xp_a, err=err, pdl=pdl)       # written packed for O
             st.o(st.xp_a, self.w_o[i], sums, err=err, pdl=pdl)
             st.xp_h.pack_res(st.x, sums, self.ln2[i], eps, pdl)
@@ -669,12 +673,14 @@ class Engine:
             # counters and tickets may be left mid-step: clear every scratch buffer before raising
             extra = [v for side in (st.verify, st.tree) if side is not None
                      for v in (side.qkv_op, side.o, side.gu, side.down, side.lm)]
-            for plan in (st.qkv, st.attn, st.o, st.gu, st.down, st.lm, st.step, st.step_logits, st.tstep,
+            for plan in (st.qkv, getattr(st, "qkv_mm", None), st.attn, st.o, st.gu, st.down, st.lm, st.step,
+                         st.step_logits, st.tstep,
                          st.tstep_logits, *extra):
                 if plan is not None:
                     plan.scratch.zero_()
-            if getattr(st, "res_sums", None) is not None:  # deferred residual sums may be half added
-                st.res_sums.zero_()
+            for sums in (getattr(st, "res_sums", None), getattr(st, "qkv_sums", None)):
+                if sums is not None:  # deferred fixed-point sums may be half added
+                    sums.zero_()
             st.err.zero_()
             raise RuntimeError(f"decode kernels reported a device error: {qdlib.describe_device_error(code)}")
 

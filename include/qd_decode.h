@@ -33,7 +33,14 @@ enum {
   QD_ERR_UNSUPPORTED = 4  /* shape outside what the kernels are built for */
 };
 
-enum { QD_EPI_STORE = 0, QD_EPI_RES = 1, QD_EPI_SWIGLU = 2, QD_EPI_SWIGLU_PACKED = 3, QD_EPI_RES_SUMS = 4 };
+enum {
+  QD_EPI_STORE = 0,
+  QD_EPI_RES = 1,
+  QD_EPI_SWIGLU = 2,
+  QD_EPI_SWIGLU_PACKED = 3,
+  QD_EPI_RES_SUMS = 4,
+  QD_EPI_STORE_SUMS = 5
+};
 
 enum {
   QD_DEVERR_WAIT_FULL = 1,
@@ -160,6 +167,15 @@ int qd_tc_gemv(const void* xpk, int n_pad, int m_act, const void* w_packed, int6
  * arriver's reduction off the path between a residual projection and the next one. */
 int qd_pack_act_res(void* x, int64_t ldx, int m_act, int n_pad, int64_t k, void* fx_sums, const void* norm_w,
                     float eps, void* xpk, int pdl, cudaStream_t stream);
+/* QD_EPI_STORE_SUMS (qd_tc_gemv): the projection output stays as fixed-point sums in `out` (int64
+ * [m_act][n], zero on entry), as for QD_EPI_RES_SUMS. qd_qkv_rope_sums applies the QKV epilogue to them
+ * - the arithmetic of qd_tc_qkv_rope_append's (per-head RMSNorm, RoPE at *pos, q to q_out [m][nq][128],
+ * K/V appended at *pos) - and clears them: the decode QKV of the tensor-core chain without a split-K
+ * last arriver. A position outside [0, cap) flags QD_DEVERR_POS and writes nothing. */
+int qd_qkv_rope_sums(void* sums, int64_t lds, int m_act, int nq_heads, int nkv_heads, const void* q_norm,
+                     const void* k_norm, float eps, const void* cos, const void* sin, const int64_t* pos, int64_t cap,
+                     void* q_out, void* k_cache, void* v_cache, int64_t cs_b, int64_t cs_h, int* err, int pdl,
+                     cudaStream_t stream);
 /* qd_qkv_rope_append from packed activations (plan with n = (nq + 2 nkv) * 128). */
 int qd_tc_qkv_rope_append(const void* xpk, int n_pad, int m_act, const void* w_packed, int64_t k, const void* q_norm,
                           const void* k_norm, const void* cos, const void* sin, const int64_t* pos, int64_t cap,

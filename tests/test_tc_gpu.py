@@ -283,3 +283,54 @@ def test_tc_gemv_deferred_residual_sums(n, k, m):
     tol = RTOL * (ref.float().abs() + y.abs()) + 1e-3
     assert not (diff > tol).any(), f"{int((diff > tol).sum())} mismatches, max diff {float(diff.max()):.4g}"
     assert torch.equal(pk, ops.PackedActivations(m, n, DEV).pack(xr, nw).t)
+
+
+@pytest.mark.parametrize("m", [13, 64])
+@pytest.mark.parametrize("pos", [0, 700])
+def test_tc_qkv_store_sums_then_rope_epilogue(m, pos):
+    """QD_EPI_STORE_SUMS + qd_qkv_rope_sums (the chain's QKV without a split-K last arriver) against the
+    fused qd_tc_qkv_rope_append on the same inputs: q, k and v within the rope tolerance (the projection
+    sums differ only in summation order, fixed point against fp32), the sums cleared, the rest of the
+    cache untouched, and a second round on the cleared sums giving the same bytes."""
+    ops = _ops()
+    H, nq, nkv, D, cap, eps = 2560, 32, 8, 128, 1024, 1e-6
+    g = torch.Generator().manual_seed(m * 31 + pos)
+    x = _rand((m, H), 1.0, g)
+    w = _rand(((nq + 2 * nkv) * D, H), 0.02, g)
+    ln = (1.0 + 0.1 * torch.randn(H, generator=g)).to(BF16).to(DEV)
+    qn = (1.0 + 0.1 * torch.randn(D, generator=g)).to(BF16).to(DEV)
+    kn = (1.0 + 0.1 * torch.randn(D, generator=g)).to(BF16).to(DEV)
+    cos, sin = (t.to(DEV) for t in Q.rope_tables(cap, D, 5e6))
+    xp = ops.PackedActivations(m, H, DEV).pack(x.to(DEV), norm_w=ln)
+    wp = ops.pack_matrix(w.to(DEV))
+    posd = torch.tensor([pos], dtype=torch.int64, device=DEV)
+
+    def caches():
+        return (torch.full((m, nkv, cap, D), float("nan"), dtype=BF16, device=DEV),
+                torch.full((m, nkv, cap, D), float("nan"), dtype=BF16, device=DEV),
+                torch.empty((m, nq, D), dtype=BF16, device=DEV))
+
+    kr, vr, qr = caches()
+    raw = torch.empty((m, (nq + 2 * nkv) * D), dtype=BF16, device=DEV)
+    ops.TcQkvRopeAppend(m, H, nq, nkv, DEV)(xp, wp, qn, kn, cos, sin, posd, qr, kr, vr, raw_out=raw)
+    mm = ops.TcGemv(m, (nq + 2 * nkv) * D, H, ops.TcGemv.STORE_SUMS, DEV)
+    sums = torch.zeros((m, (nq + 2 * nkv) * D), dtype=torch.int64, device=DEV)
+    outs = []
+    for _ in range(2):
+        kc, vc, q = caches()
+        mm(xp, wp, sums)
+        ops.qkv_rope_sums(sums, m, nq, nkv, qn, kn, eps, cos, sin, posd, q, kc, vc)
+        torch.cuda.synchronize()
+        assert int(sums.abs().sum()) == 0
+        outs.append((q.clone(), kc[:, :, pos].clone(), vc[:, :, pos].clone()))
+        others = torch.ones(cap, dtype=torch.bool)
+        others[pos] = False
+        assert torch.isnan(kc[:, :, others].float()).all() and torch.isnan(vc[:, :, others].float()).all()
+    for a, b in zip(outs[0], outs[1]):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    rc = raw.cpu()
+    y_q = Q.rms_norm(rc, qn.cpu(), eps, nq)
+    y_k = Q.rms_norm(rc[:, nq * D:], kn.cpu(), eps, nkv)
+    _assert_rope_close(outs[0][0], qr.cpu(), y_q, cos[pos].cpu(), sin[pos].cpu())
+    _assert_rope_close(outs[0][1], kr[:, :, pos].cpu(), y_k, cos[pos].cpu(), sin[pos].cpu())
+    _assert_bf16_close(outs[0][2], vr[:, :, pos])
