@@ -756,6 +756,10 @@ def run_step_kernel(a):
             step()
         e.record()
         e.synchronize()
+        torch.cuda.nvtx.range_push("decode_step")  # one more step, as an NVTX range for launch-list captures
+        step()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
     eng.check_device_errors(st)
     us = s.elapsed_time(e) / a.launches * 1e3
     nbytes = weight_bytes(cfg) + B * kv_bytes_per_token(cfg) * (S + 3 + a.launches / 2 + 1)

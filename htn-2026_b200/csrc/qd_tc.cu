@@ -349,24 +349,65 @@ __global__ void __launch_bounds__(256) pack_act_res_kernel(const __grid_constant
   grid_dep_launch();
   const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int k8 = (int)(a.k >> 3);
+  // this thread's first chunks q = tid + 256 j (j < kCh): residual, sums and norm weights all requested
+  // before any is used, the new values kept in registers for the normalising pass; a row wider than
+  // kCh chunks per thread (k > 4096) takes the rest chunk by chunk and re-reads its values
+  constexpr int kCh = 2;
+  uint4 xv[kCh], wv[kCh];
+  longlong2 sv[kCh][4];
   float sq = 0.f;
-  for (int q = tid; q < k8; q += 256) {
-    const uint4 v = ld_cg_v4(a.x + m * a.ldx + q * 8);
-    longlong2* sp = reinterpret_cast<longlong2*>(a.fxs + m * a.k + q * 8);
-    const longlong2 sv[4] = {__ldcg(sp), __ldcg(sp + 1), __ldcg(sp + 2), __ldcg(sp + 3)};
-    const uint32_t ru[4] = {v.x, v.y, v.z, v.w};
-    uint32_t o[4];
+  {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float lo = bf16r(bf_lo(ru[e]) + bf16r(fx_to_float(sv[e].x)));
-      const float hi = bf16r(bf_hi(ru[e]) + bf16r(fx_to_float(sv[e].y)));
-      o[e] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
-      sq = fmaf(lo, lo, sq);
-      sq = fmaf(hi, hi, sq);
+    for (int j = 0; j < kCh; ++j) {
+      const int q = j * 256 + tid;
+      if (q < k8) {
+        xv[j] = ld_cg_v4(a.x + m * a.ldx + q * 8);
+        const longlong2* sp = reinterpret_cast<const longlong2*>(a.fxs + m * a.k + q * 8);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sv[j][e] = __ldcg(sp + e);
+        if (a.norm_w) wv[j] = *reinterpret_cast<const uint4*>(a.norm_w + q * 8);
+      }
     }
-    *reinterpret_cast<uint4*>(a.x + m * a.ldx + q * 8) = make_uint4(o[0], o[1], o[2], o[3]);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) sp[e] = make_longlong2(0, 0);
+    for (int j = 0; j < kCh; ++j) {
+      const int q = j * 256 + tid;
+      if (q >= k8) continue;
+      const uint32_t ru[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float lo = bf16r(bf_lo(ru[e]) + bf16r(fx_to_float(sv[j][e].x)));
+        const float hi = bf16r(bf_hi(ru[e]) + bf16r(fx_to_float(sv[j][e].y)));
+        o[e] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
+        sq = fmaf(lo, lo, sq);
+        sq = fmaf(hi, hi, sq);
+      }
+      xv[j] = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4*>(a.x + m * a.ldx + q * 8) = xv[j];
+      longlong2* sp = reinterpret_cast<longlong2*>(a.fxs + m * a.k + q * 8);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sp[e] = make_longlong2(0, 0);
+    }
+  }
+  if (k8 > kCh * 256) {  // the remaining chunks of a wide row
+    for (int q = kCh * 256 + tid; q < k8; q += 256) {
+      const uint4 v = ld_cg_v4(a.x + m * a.ldx + q * 8);
+      longlong2* sp = reinterpret_cast<longlong2*>(a.fxs + m * a.k + q * 8);
+      const longlong2 s4[4] = {__ldcg(sp), __ldcg(sp + 1), __ldcg(sp + 2), __ldcg(sp + 3)};
+      const uint32_t ru[4] = {v.x, v.y, v.z, v.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float lo = bf16r(bf_lo(ru[e]) + bf16r(fx_to_float(s4[e].x)));
+        const float hi = bf16r(bf_hi(ru[e]) + bf16r(fx_to_float(s4[e].y)));
+        o[e] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
+        sq = fmaf(lo, lo, sq);
+        sq = fmaf(hi, hi, sq);
+      }
+      *reinterpret_cast<uint4*>(a.x + m * a.ldx + q * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sp[e] = make_longlong2(0, 0);
+    }
   }
   float rstd = 1.f;
   if (a.norm_w) {
@@ -379,11 +420,18 @@ __global__ void __launch_bounds__(256) pack_act_res_kernel(const __grid_constant
     rstd = 1.0f / sqrtf(ss / (float)a.k + a.eps);
   }
   for (int q = tid; q < k8; q += 256) {
-    uint4 v = ld_cg_v4(a.x + m * a.ldx + q * 8);  // this thread's own write above
+    const int j = (q - tid) >> 8;  // which register chunk, when the row fits in registers
+    uint4 v, w;
+    if (k8 <= kCh * 256) {
+      v = j == 0 ? xv[0] : xv[1];
+      w = j == 0 ? wv[0] : wv[1];
+    } else {
+      v = ld_cg_v4(a.x + m * a.ldx + q * 8);  // this thread's own write above
+      if (a.norm_w) w = *reinterpret_cast<const uint4*>(a.norm_w + q * 8);
+    }
     if (a.norm_w) {
-      const uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + q * 8);
       const uint32_t xu[4] = {v.x, v.y, v.z, v.w};
-      const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+      const uint32_t wu[4] = {w.x, w.y, w.z, w.w};
       uint32_t o[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -422,15 +470,26 @@ __global__ void __launch_bounds__(128) qkv_rope_sums_kernel(const __grid_constan
   grid_dep_wait();
   grid_dep_launch();
   const int g = blockIdx.x, m = blockIdx.y, r = threadIdx.x, lane = r & 31, w = r >> 5;
+  // everything that does not depend on the position in one round trip: the position, this element's
+  // sum, its norm weight; then the RoPE row
   int64_t* sp = a.sums + (int64_t)m * a.lds + (int64_t)g * 128 + r;
-  const float v = bf16r(fx_to_float(__ldcg(sp)));
-  *sp = 0;  // the sums start the next projection clear
   const int64_t p = ld_cg_s64(a.pos);
-  if (p < 0 || p >= a.cap) {  // the same for every thread: flagged, nothing written
+  const long long sraw = __ldcg(sp);
+  const bool vhead = g >= a.nq + a.nkv;
+  const __nv_bfloat16 nwb = vhead ? __float2bfloat16_rn(0.f) : (g < a.nq ? a.qn[r] : a.kn[r]);
+  const bool in = p >= 0 && p < a.cap;  // the same for every thread
+  float c = 0.f, sn = 0.f;
+  if (in && !vhead) {
+    c = bf16_to_f(a.cos[p * 128 + r]);
+    sn = bf16_to_f(a.sin[p * 128 + r]);
+  }
+  const float v = bf16r(fx_to_float(sraw));
+  *sp = 0;  // the sums start the next projection clear
+  if (!in) {  // flagged, nothing written
     if (r == 0 && g == 0 && m == 0 && a.err) atomicOr(a.err, QD_DEVERR_POS);
     return;
   }
-  if (g >= a.nq + a.nkv) {  // V head: into the cache as is
+  if (vhead) {  // V head: into the cache as is
     a.v_cache[(int64_t)m * a.cs_b + (int64_t)(g - a.nq - a.nkv) * a.cs_h + p * 128 + r] = __float2bfloat16_rn(v);
     return;
   }
@@ -439,12 +498,10 @@ __global__ void __launch_bounds__(128) qkv_rope_sums_kernel(const __grid_constan
   __syncthreads();
   const float var = (wsq[0] + wsq[1] + wsq[2] + wsq[3]) / 128.0f;
   const float rstd = 1.0f / sqrtf(var + a.eps);
-  const float nw = bf16_to_f(g < a.nq ? a.qn[r] : a.kn[r]);
-  const float y = bf16r(nw * bf16r(v * rstd));
+  const float y = bf16r(bf16_to_f(nwb) * bf16r(v * rstd));
   ys[r] = y;
   __syncthreads();
   const float yp = ys[r ^ 64];
-  const float c = bf16_to_f(a.cos[p * 128 + r]), sn = bf16_to_f(a.sin[p * 128 + r]);
   // q*cos + rotate_half(q)*sin with every product a BF16 tensor (rotate_half = cat(-q2, q1))
   const float rot = (r < 64) ? bf16r(-yp * sn) : bf16r(yp * sn);
   const __nv_bfloat16 o = __float2bfloat16_rn(bf16r(y * c) + rot);
