@@ -11,8 +11,9 @@
 //                                                operand, P the K-major one
 // and the fp32 accumulator of each (dim, head) lives in the thread of that dim: acc = acc * alpha + O.
 // K and V move through a 3-stage ring by TMA (4-D tensor maps over the [B, nkv, cap, 128] cache, two
-// 64-dim boxes of 128 keys per operand, 128-byte swizzle); keys past the cache read as zeros and V rows
-// past the valid length are zeroed in shared memory before P.V. Warps 0-3 run softmax and the
+// 64-dim boxes of 128 keys per operand, 128-byte swizzle; a pair's last, partial chunk only as many
+// 32-key boxes as hold keys); keys past the cache read as zeros, scores of keys past the valid length
+// are masked and those V rows zeroed in shared memory before P.V. Warps 0-3 run softmax and the
 // epilogue (tensor-memory lanes 0-127), warp 4 issues the copies, warp 5 issues the MMAs. No
 // multicast anywhere.
 #include <cuda.h>
@@ -28,6 +29,8 @@ constexpr int kTKeys = 128;                // keys per chunk (the q.k MMA's M)
 constexpr int kTBox = kTKeys * 128;        // one [128 keys][64 dims] BF16 box: 16 KiB
 constexpr int kTStage = 4 * kTBox;         // K dims 0-63, K dims 64-127, V dims 0-63, V dims 64-127
 constexpr int kTStages = 3;
+constexpr int kTTailKeys = 32;             // a pair's last, partial chunk is copied in boxes of 32 keys
+constexpr int kTTailBox = kTTailKeys * 128;  // [32 keys][64 dims] BF16: 4 KiB
 constexpr int kTN = 16;                    // MMA N: the 4 query heads of the KV head + 12 zero rows
 constexpr int kTThreads = 192;
 constexpr int kTSO = 3;                    // S / O accumulator sets in tensor memory
@@ -36,7 +39,8 @@ constexpr int kTSoftBar = 1;               // named barrier of warps 0-3
 constexpr int kTStageMax = 160;            // merge staging: 3 x 4 x smax floats
 
 struct alignas(64) TcAttnArgs {
-  CUtensorMap tk, tv;
+  CUtensorMap tk, tv;            // boxes of 128 keys
+  CUtensorMap tk_tail, tv_tail;  // boxes of kTTailKeys keys
   const __nv_bfloat16* q;
   const int64_t* pos;
   __nv_bfloat16* out;
@@ -91,8 +95,10 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int cta = blockIdx.x;
 
-  grid_dep_wait();  // q and the new token's K/V come from the preceding kernel
-  grid_dep_launch();
+  // With pdl, q and the new token's K/V (each pair's last chunk) come from the preceding kernel; the
+  // position and the keys before it were written before that kernel started (it waited on its own
+  // predecessor before letting this grid in). So the set-up and the copies of chunks that are not a
+  // pair's last go out before the dependency wait, overlapping the preceding kernel's tail.
   const int64_t len = attn_len_at(ld_cg_s64(a.pos), a.cap, a.err, tid == 0 && cta == 0);
   const int nch = (int)((len + kTKeys - 1) / kTKeys);
   const int pairs = a.batch * a.nkv;
@@ -147,15 +153,37 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
       const uint64_t pol = policy_evict_first();
       int pair = (int)(c_begin / nch), ci = (int)(c_begin - (int64_t)pair * nch);
       int slot = 0, round = 0, issued = 0;
+      bool dep_done = false;
       for (int i = 0; i < n; ++i) {
         if (round > 0 && !mbar_wait(empty_bar(slot), (round - 1) & 1, a.err, kErrWaitEmpty)) break;
+        if (!dep_done && ci == nch - 1) {  // this chunk holds the row the preceding kernel appends
+          grid_dep_wait();
+          dep_done = true;
+        }
         const int b = pair / a.nkv, kvh = pair - b * a.nkv, k0 = ci * kTKeys;
         const uint32_t st = sbase + Ly::stages + slot * kTStage;
-        mbar_arrive_expect_tx(full_bar(slot), kTStage);  // rows past the cache are zero-filled, counted
-        tma_load_4d(st, &a.tk, 0, k0, kvh, b, full_bar(slot), pol);
-        tma_load_4d(st + kTBox, &a.tk, 64, k0, kvh, b, full_bar(slot), pol);
-        tma_load_4d(st + 2 * kTBox, &a.tv, 0, k0, kvh, b, full_bar(slot), pol);
-        tma_load_4d(st + 3 * kTBox, &a.tv, 64, k0, kvh, b, full_bar(slot), pol);
+        const int64_t nk = len - k0;
+        if (nk >= kTKeys) {
+          mbar_arrive_expect_tx(full_bar(slot), kTStage);  // rows past the cache are zero-filled, counted
+          tma_load_4d(st, &a.tk, 0, k0, kvh, b, full_bar(slot), pol);
+          tma_load_4d(st + kTBox, &a.tk, 64, k0, kvh, b, full_bar(slot), pol);
+          tma_load_4d(st + 2 * kTBox, &a.tv, 0, k0, kvh, b, full_bar(slot), pol);
+          tma_load_4d(st + 3 * kTBox, &a.tv, 64, k0, kvh, b, full_bar(slot), pol);
+        } else {
+          // the pair's last chunk: only the 32-key row blocks that hold keys (at 4 KiB steps the
+          // 128-byte swizzle pattern is that of the full box); the rows left stale are masked in the
+          // softmax (K) and zeroed before P.V (V)
+          const int nb = (int)((nk + kTTailKeys - 1) / kTTailKeys);
+          mbar_arrive_expect_tx(full_bar(slot), (uint32_t)(4 * nb * kTTailBox));
+          for (int j = 0; j < nb; ++j) {
+            const uint32_t r = (uint32_t)(j * kTTailBox);
+            const int kj = k0 + j * kTTailKeys;
+            tma_load_4d(st + r, &a.tk_tail, 0, kj, kvh, b, full_bar(slot), pol);
+            tma_load_4d(st + kTBox + r, &a.tk_tail, 64, kj, kvh, b, full_bar(slot), pol);
+            tma_load_4d(st + 2 * kTBox + r, &a.tv_tail, 0, kj, kvh, b, full_bar(slot), pol);
+            tma_load_4d(st + 3 * kTBox + r, &a.tv_tail, 64, kj, kvh, b, full_bar(slot), pol);
+          }
+        }
         ++issued;
         if (++ci == nch) {
           ci = 0;
@@ -243,6 +271,8 @@ __global__ void __launch_bounds__(kTThreads, 1) attn_tc_kernel(const __grid_cons
       if (lane == 0) mbar_arrive(qready_bar);
       if (pr + 1 <= pair_last) load_q(pr + 1);
     };
+    grid_dep_wait();  // q comes from the preceding kernel
+    grid_dep_launch();
     load_q(pair);
     auto reset_state = [&]() {
 #pragma unroll
@@ -452,12 +482,12 @@ static int64_t tc_attn_scratch(int pairs, int smax, int64_t* off_ml, int64_t* of
 }
 
 static bool encode_cache_map(CUtensorMap* m, const void* base, int batch, int nkv, int64_t cap, int64_t cs_b,
-                             int64_t cs_h) {
+                             int64_t cs_h, int box_keys) {
   const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (!encode) return false;
   const cuuint64_t dims[4] = {(cuuint64_t)kHeadDim, (cuuint64_t)cap, (cuuint64_t)nkv, (cuuint64_t)batch};
   const cuuint64_t strides[3] = {(cuuint64_t)kHeadDim * 2, (cuuint64_t)cs_h * 2, (cuuint64_t)cs_b * 2};
-  const cuuint32_t box[4] = {64, (cuuint32_t)kTKeys, 1, 1};
+  const cuuint32_t box[4] = {64, (cuuint32_t)box_keys, 1, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
                                             strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -505,8 +535,10 @@ extern "C" int qd_attn_decode_tc(const void* q, const void* k_cache, const void*
   if (scratch_bytes < need)
     return set_error(QD_ERR_SCRATCH, "scratch %lld B < %lld B", (long long)scratch_bytes, (long long)need);
   TcAttnArgs a = {};
-  if (!encode_cache_map(&a.tk, k_cache, batch, nkv_heads, cap, cs_b, cs_h) ||
-      !encode_cache_map(&a.tv, v_cache, batch, nkv_heads, cap, cs_b, cs_h))
+  if (!encode_cache_map(&a.tk, k_cache, batch, nkv_heads, cap, cs_b, cs_h, kTKeys) ||
+      !encode_cache_map(&a.tv, v_cache, batch, nkv_heads, cap, cs_b, cs_h, kTKeys) ||
+      !encode_cache_map(&a.tk_tail, k_cache, batch, nkv_heads, cap, cs_b, cs_h, kTTailKeys) ||
+      !encode_cache_map(&a.tv_tail, v_cache, batch, nkv_heads, cap, cs_b, cs_h, kTTailKeys))
     return set_error(QD_ERR_CUDA, "cuTensorMapEncodeTiled failed for the KV cache");
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.pos = pos;

@@ -220,7 +220,10 @@ int qd_attn_decode_stream(const void* q, const void* k_cache, const void* v_cach
  * the CUDA cores between the two MMAs, probabilities rounded to BF16. Same inputs, outputs, merge and
  * error behaviour; grid_hint <= 0 picks one CTA per SM; grid / smax must be qd_attn_tc_plan's values.
  * out_npad = 0: out is [batch, nq, 128]; out_npad = 16..64 (>= batch, multiple of 16): out is the packed
- * activation operand of the O projection, [nq * 2][out_npad][64] tiles (qd_pack_act's layout). */
+ * activation operand of the O projection, [nq * 2][out_npad][64] tiles (qd_pack_act's layout).
+ * With pdl = 1 the kernel reads *pos and copies the cached keys / values of every chunk that does not
+ * hold position *pos before it waits on the preceding kernel, so those, and *pos, must be written
+ * before that kernel starts; the preceding kernel may write q and the new row at *pos. */
 int qd_attn_tc_plan(int batch, int nkv_heads, int64_t cap, int grid_hint, int* grid, int* smax,
                     int64_t* scratch_bytes);
 int qd_attn_decode_tc(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, void* out,
