@@ -28,7 +28,10 @@ def _rand(shape, std, gen):
 @pytest.mark.parametrize("B,L,cap,grid", [(1, 1, 384, 0), (1, 33, 384, 0), (1, 384, 384, 0), (3, 200, 256, 0),
                                           (8, 1000, 1024, 0), (2, 64, 65, 0), (1, 4096, 8192, 0),
                                           (64, 1280, 1536, 0), (5, 777, 800, 7), (5, 777, 800, 37),
-                                          (16, 300, 320, 1000), (32, 1024, 1024, 0)])
+                                          (16, 300, 320, 1000), (32, 1024, 1024, 0),
+                                          # the tensor-core kernel's last chunk in 32-key boxes: exactly
+                                          # one box, a box one key short, a box past the capacity
+                                          (2, 160, 192, 0), (4, 255, 256, 0), (3, 70, 72, 0)])
 @pytest.mark.parametrize("kind", ["stream", "tc"])
 def test_stream_attention_matches_oracle(B, L, cap, grid, kind):
     from decode_b200 import ops
