@@ -35,6 +35,19 @@ sys.path.insert(0, os.path.join(REPO, "htn-2026_b200"))
 METRIC = "decode tokens/s (bs1 latency ms/token; bs64 aggregate) and % of HBM roofline"
 
 
+def rank_reduce(x: float, op: str, device) -> float:
+    """x reduced over the ranks of the default process group ("max" or "min"; a float32 tensor on
+    `device`, so every rank takes the same collective step); x itself without one, or with one rank."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return x
+    t = torch.tensor([x], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.MIN)
+    return float(t.item())
+
+
 def _args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -283,11 +296,7 @@ def run_ours(a):
         torch.cuda.synchronize()
         eng.check_device_errors(st)
     ms = t_s.elapsed_time(t_e)
-    ms_max = ms
-    if world > 1:
-        tt = torch.tensor([ms], device=f"cuda:{local}")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms_max = float(tt.item())
+    ms_max = rank_reduce(ms, "max", f"cuda:{local}")
     ms_step = ms_max / K
     value = world * B * K / (ms_max / 1e3)
 
@@ -304,9 +313,7 @@ def run_ours(a):
         dec = stamps[-1] - stamps[0]
         e2e_val = B * (n_e2e - 1) / dec if n_e2e > 1 else 0.0
         if world > 1:
-            tt = torch.tensor([e2e_val], device=f"cuda:{local}")
-            dist.all_reduce(tt, op=dist.ReduceOp.MIN)
-            e2e_val = float(tt.item()) * world
+            e2e_val = rank_reduce(e2e_val, "min", f"cuda:{local}") * world
         e2e = {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": round(B * S * 8 / n_e2e, 1),
                "d2h_bytes_per_step": B * 8, "ttft_ms": 1e3 * (stamps[0] - t0),
                "total_tokens_per_s_incl_prefill": world * B * n_e2e / total,
@@ -488,11 +495,7 @@ def config4_leg(eng, cfg, a, world, rank, local, peak):
             dist.barrier()
         eng.check_device_errors(st)
     ms = t_s.elapsed_time(t_e)
-    ms_max = ms
-    if world > 1:
-        tt = torch.tensor([ms], device=f"cuda:{local}")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms_max = float(tt.item())
+    ms_max = rank_reduce(ms, "max", f"cuda:{local}")
     L_avg = S + W + K / 2
     step_bytes = weight_bytes(cfg) + b * kv_bytes_per_token(cfg) * (L_avg + 1)
     per_gpu = step_bytes / (ms / K / 1e3) / 1e9
