@@ -38,6 +38,44 @@ def test_header_declares_and_library_exports_every_symbol(lib):
     assert set(L.PROTOTYPES) <= set(syms)
 
 
+def header_prototypes():
+    """{name: (return type, [parameter types])} of every qd_* prototype in the header."""
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = re.sub(r"//[^\n]*", "", text)
+    out = {}
+    for m in re.finditer(r"([A-Za-z_][\w\s*]*?)\b(qd_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text):
+        params = [p.strip() for p in m.group(3).split(",")]
+        if params in ([""], ["void"]):
+            params = []
+        types = [p if p.endswith("*") else re.sub(r"\s*\b\w+$", "", p) for p in params]  # drop the name
+        out[m.group(2)] = (" ".join(m.group(1).split()), [" ".join(t.split()) for t in types])
+    return out
+
+
+def _ctype_matches(c_type: str, ct) -> bool:
+    if "*" in c_type or c_type == "cudaStream_t":  # any pointer, the stream handle included
+        return ct in (ctypes.c_void_p, ctypes.c_char_p) or (isinstance(ct, type) and issubclass(ct, ctypes._Pointer))
+    return ct is {"int": ctypes.c_int, "int64_t": ctypes.c_int64, "float": ctypes.c_float,
+                  "double": ctypes.c_double}[c_type]
+
+
+def test_ctypes_table_matches_every_header_prototype():
+    """decode_b200/lib.py's PROTOTYPES (the table every Python call goes through) against the header:
+    the same entry points, the same number of parameters and a matching C type for each, and the
+    same return type, so a changed signature cannot leave a stale ctypes binding behind."""
+    from decode_b200 import lib as L
+
+    protos = header_prototypes()
+    assert sorted(protos) == sorted(L.PROTOTYPES)
+    for name, (ret, params) in protos.items():
+        restype, argtypes = L.PROTOTYPES[name]
+        assert len(argtypes) == len(params), (name, params, argtypes)
+        for i, (c_type, ct) in enumerate(zip(params, argtypes)):
+            assert _ctype_matches(c_type, ct), (name, i, c_type, ct)
+        assert _ctype_matches(ret, restype), (name, ret, restype)
+
+
 def test_version_and_errors(lib):
     assert b"sm_100a" in lib.qd_version()
     g, nb = ctypes.c_int(0), ctypes.c_int64(0)
