@@ -76,6 +76,30 @@ def test_ctypes_table_matches_every_header_prototype():
         assert _ctype_matches(ret, restype), (name, ret, restype)
 
 
+def test_step_desc_mirrors_the_header_struct():
+    """decode_b200/lib.py's StepDesc against qd_step_desc in the header: the same field names in the same
+    order, pointers as pointers, int64_t / double as themselves (so the same offsets and size)."""
+    from decode_b200 import lib as L
+
+    text = open(HEADER).read()
+    body = re.search(r"typedef struct qd_step_desc \{(.*?)\} qd_step_desc;", text, flags=re.S).group(1)
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    fields = []
+    for decl in body.split(";"):
+        decl = " ".join(decl.split())
+        if not decl:
+            continue
+        m = re.match(r"((?:const )?[A-Za-z_0-9]+\s*\**)\s*(.*)", decl)
+        ctype, names = m.group(1).replace(" ", ""), [n.strip() for n in m.group(2).split(",")]
+        for n in names:
+            kind = "ptr" if ctype.endswith("*") else {"int64_t": "i64", "double": "f64"}[ctype]
+            fields.append((n, kind))
+    ours = [(n, "ptr" if t is ctypes.c_void_p else {ctypes.c_int64: "i64", ctypes.c_double: "f64"}[t])
+            for n, t in L.StepDesc._fields_]
+    assert ours == fields
+    assert ctypes.sizeof(L.StepDesc) == 8 * len(fields)
+
+
 def test_version_and_errors(lib):
     assert b"sm_100a" in lib.qd_version()
     g, nb = ctypes.c_int(0), ctypes.c_int64(0)
