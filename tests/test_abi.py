@@ -100,6 +100,41 @@ def test_step_desc_mirrors_the_header_struct():
     assert ctypes.sizeof(L.StepDesc) == 8 * len(fields)
 
 
+def test_integration_stubs_bind_the_header_signatures():
+    """The reference-side ctypes stubs in INTEGRATION.md, executed against a stand-in library object:
+    every argtypes list they set has the header prototype's parameter count and kinds."""
+    import types
+
+    class StandIn:
+        def __init__(self):
+            self.fns = {}
+
+        def __getattr__(self, name):
+            return self.fns.setdefault(name, types.SimpleNamespace())
+
+    text = open(os.path.join(REPO, "INTEGRATION.md")).read()
+    blocks = re.findall(r"```python\n(.*?)```", text, flags=re.S)
+    stand_in = StandIn()
+    ns = {}
+    ran = 0
+    for b in blocks:
+        if "_lib." not in b:
+            continue  # the engine usage example (needs a checkpoint)
+        b = re.sub(r"_lib = ctypes\.CDLL\([^)]*\)", "_lib = __stand_in__", b)
+        ns["__stand_in__"] = stand_in
+        exec(compile(b, "INTEGRATION.md", "exec"), ns)
+        ran += 1
+    assert ran >= 3
+    protos = header_prototypes()
+    bound = {n: f.argtypes for n, f in stand_in.fns.items() if hasattr(f, "argtypes")}
+    assert len(bound) >= 6
+    for name, argtypes in bound.items():
+        params = protos[name][1]
+        assert len(argtypes) == len(params), (name, params, argtypes)
+        for i, (c_type, ct) in enumerate(zip(params, argtypes)):
+            assert _ctype_matches(c_type, ct), (name, i, c_type, ct)
+
+
 def test_version_and_errors(lib):
     assert b"sm_100a" in lib.qd_version()
     g, nb = ctypes.c_int(0), ctypes.c_int64(0)
