@@ -1,12 +1,16 @@
-"""bench.py's multi-rank host logic on the CPU: the reduction over ranks that the torchrun launch uses
-for its timings (max of the per-rank device times; min of the per-rank end-to-end rates), run on two
-`gloo` ranks, and the reference arm's rule that only rank 0 works and prints. No GPU is used."""
+"""bench.py's host-side contract on the CPU: the reduction over ranks that the torchrun launch uses for
+its timings (max of the per-rank device times; min of the per-rank end-to-end rates), run on two
+`gloo` ranks; the reference arm's rule that only rank 0 works and prints; and the reference arm's one
+JSON line on a one-layer model. No GPU is used."""
 
 import argparse
 import datetime
+import json
 import multiprocessing as mp
 import os
 import socket
+import subprocess
+import sys
 
 import bench
 
@@ -58,3 +62,23 @@ def test_reference_arm_runs_on_rank_0_only(monkeypatch, capsys):
     a = argparse.Namespace(layers=36, batch=1, prompt=128, steps=3, warmup=3, cpu_steps=96, gpus=2)
     assert bench.run_reference(a) is None  # returns before building the model
     assert capsys.readouterr().out == ""
+
+
+def test_reference_arm_prints_one_contract_line():
+    """`bench.py --impl reference` (the host-core arm the driver runs beside ours) on a one-layer model:
+    exactly one JSON line with the contract's keys, its cpu_baseline and e2e describing the same run."""
+    cmd = [sys.executable, os.path.join(os.path.dirname(bench.__file__), "bench.py"), "--impl", "reference",
+           "--layers", "1", "--prompt", "8", "--steps", "2", "--warmup", "1", "--cpu-steps", "2"]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=300, env={**os.environ, "RANK": "0"})
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["metric"] == bench.METRIC and d["higher_is_better"] is True
+    assert d["steps"] == 2 and d["warmup"] == 1 and d["value"] > 0
+    cb = d["cpu_baseline"]
+    assert cb["value"] == d["value"] and cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"]
+    assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
